@@ -1,0 +1,391 @@
+#!/usr/bin/env python
+"""bench.py -- flat kNN queries/s (C2: 1M x 128 cosine, k=100) and k-means
+iterations/s (C3) on B200, through libvrs's C ABI.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched by torchrun (one process per GPU); each rank holds a row
+shard of the base (GpuShardMode::Sharded) and the ranks meet in an NCCL
+all-gather + GPU merge inside vrs_knn_search. Prints one JSON line on rank 0.
+
+A step is one vrs_knn_search of the 10,000 C2 queries against the whole
+(sharded) 1,000,000 x 128 base. `value` times steps whose queries and
+results stay in HBM; `e2e` times the same call with pinned host buffers
+(H2D of the queries and D2H of the results inside the timed region).
+The base (512 MB of f32) is larger than L2, so no flush is needed between
+steps. Inputs are seeded Philox4x32-10 draws generated on the device, the
+same bits the CPU oracle consumes.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vector-rs_b200", "python"))
+
+import numpy as np  # noqa: E402
+
+N_BASE, DIM, N_QUERY, K = 1_000_000, 128, 10_000, 100
+COS = 2
+CPU_SAMPLE_QUERIES = 1000
+KM_N, KM_D, KM_K, KM_ITERS, KM_SIGMA = 1_000_000, 128, 1024, 20, 0.1
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-kmeans", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--n-base", type=int, default=N_BASE)
+    ap.add_argument("--n-query", type=int, default=N_QUERY)
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during a timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=5)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def host_gen(vc, kind, seed, stream, rows, d, threads=None):
+    """Host copy of generator rows, produced in parallel chunks."""
+    from concurrent.futures import ThreadPoolExecutor
+    out = np.empty((rows, d), np.float32)
+    nt = threads or os.cpu_count() or 1
+    chunk = max(1, -(-rows // (nt * 4)))
+
+    def work(r0):
+        n = min(chunk, rows - r0)
+        out[r0:r0 + n] = vc.gen_rows_host(kind, seed, stream, r0, n, d)
+
+    with ThreadPoolExecutor(nt) as ex:
+        list(ex.map(work, range(0, rows, chunk)))
+    return out
+
+
+def cpu_leg(base, queries, k, sample):
+    """Timed oracle (restated reference CPU path) on a query sample."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
+    cores = os.cpu_count() or 1
+    qs = queries[:sample]
+    t0 = time.perf_counter()
+    d, i = oracle.knn_search(base, qs, k, COS, nthreads=cores)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"{sample} of the {N_QUERY} C2 queries against the full {len(base)}-row base "
+                      f"(AVX-512 restatement of search_batch_cpu, {cores} threads)",
+            "seconds": dt}, (d, i)
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import vector_cuda as vc
+    seed = vc.config_seed(1)
+    base = host_gen(vc, vc.GEN_NORMAL_UNIT, seed, 0, args.n_base, DIM)
+    queries = host_gen(vc, vc.GEN_NORMAL_UNIT, seed, 1, min(args.n_query, 2000), DIM)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
+    cores = os.cpu_count() or 1
+    per_step = 100
+    for w in range(args.warmup):
+        oracle.knn_search(base, queries[:16], K, COS, nthreads=cores)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        q0 = (s * per_step) % (len(queries) - per_step + 1)
+        oracle.knn_search(base, queries[q0:q0 + per_step], K, COS, nthreads=cores)
+    dt = time.perf_counter() - t0
+    v = per_step * args.steps / dt
+    line = {
+        "impl": "reference", "metric": "flat kNN queries/s (1M x 128 cosine, k=100)", "value": v,
+        "unit": "queries/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (Philox4x32-10, C2 distribution)",
+        "config": {"workload": "C2 cosine flat kNN, base 1,000,000 x 128 unit rows, k=100",
+                   "n_base": args.n_base, "queries_per_step": per_step, "k": K},
+        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": cores, "kind": "port",
+                         "sample": f"{per_step} queries per step against the full base, "
+                                   f"{cores} threads (reference Rust cannot build here: "
+                                   "no cargo; oracle restatement of search_batch_cpu)"},
+        "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import torch
+    import vector_cuda as vc
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=dev)
+    uid = [vc.Comm.unique_id() if rank == 0 else None]
+    if dist:
+        dist.broadcast_object_list(uid, src=0)
+    comm = vc.Comm.init(uid[0], world, rank, local)
+
+    # ---------------------------------------------------------------- data
+    n_base, n_q = args.n_base, args.n_query
+    seed = vc.config_seed(1)
+    chunk = -(-n_base // world)
+    r0, r1 = min(n_base, rank * chunk), min(n_base, (rank + 1) * chunk)
+    shard = torch.empty((max(r1 - r0, 1), DIM), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(vc.GEN_NORMAL_UNIT, seed, 0, r0, r1 - r0, DIM, shard.data_ptr())
+    q_dev = torch.empty((n_q, DIM), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(vc.GEN_NORMAL_UNIT, seed, 1, 0, n_q, DIM, q_dev.data_ptr())
+    torch.cuda.synchronize()
+    eng = vc.DistributedKnnEngine.create_rank(comm, None, DIM, r0, n_base, vc.GpuShardMode.Sharded,
+                                              vc.DistanceMetric.CosineSimilarity,
+                                              device_ptr=shard.data_ptr(), n_local=r1 - r0)
+    stream = torch.cuda.current_stream(dev)
+    eng.set_stream(stream.cuda_stream)
+    out_d = torch.empty((n_q, K), dtype=torch.float32, device=dev)
+    out_i = torch.empty((n_q, K), dtype=torch.int32, device=dev)
+
+    def step_dev():
+        return eng.search_device(q_dev.data_ptr(), n_q, K, out_d.data_ptr(), out_i.data_ptr())
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step_dev()
+    barrier()
+    vc.profile_reset()
+    vc.profile_enable(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step_dev()
+        ev1.record(stream)
+        barrier()
+    vc.profile_enable(False)
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    scan_ms, scan_n = vc.profile_read("knn_scan")
+    sel_ms, sel_n = vc.profile_read("knn_select")
+    merge_ms, merge_n = vc.profile_read("knn_merge")
+    launches = vc.profile_read("*")[1]
+    value = n_q * args.steps / (ms / 1e3)
+
+    # ----------------------------------------------------------- e2e (host)
+    q_host = torch.empty((n_q, DIM), dtype=torch.float32, pin_memory=True)
+    q_host.copy_(q_dev.cpu())
+    hd = torch.empty((n_q, K), dtype=torch.float32, pin_memory=True)
+    hi = torch.empty((n_q, K), dtype=torch.int32, pin_memory=True)
+
+    def step_host():
+        kk = np.ctypeslib.ctypes.c_int32()
+        vc._check(vc.lib().vrs_knn_search_ex(eng._h, vc.ctypes.c_void_p(q_host.data_ptr()), n_q, K,
+                                            vc.ctypes.c_void_p(hd.data_ptr()),
+                                            vc.ctypes.c_void_p(hi.data_ptr()),
+                                            vc.ctypes.byref(kk), 0))
+
+    for _ in range(max(1, args.warmup // 2)):
+        step_host()
+    barrier()
+    with ClockSampler(local) as clk2:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step_host()
+        ev1.record(stream)
+        barrier()
+    ms_e2e = max_over_ranks(ev0.elapsed_time(ev1))
+    e2e = n_q * args.steps / (ms_e2e / 1e3)
+
+    # ------------------------------------------------------------ roofline
+    pk, pk_kind = peaks()
+    flops_per_launch = 2.0 * (r1 - r0) * DIM * n_q  # algorithmic: 2*N_local*D per query
+    per_launch_ms = scan_ms / max(scan_n, 1)
+    achieved = flops_per_launch / (per_launch_ms / 1e3) / 1e12
+    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    roofline = {"bound": "tensor", "kernel": "knn_scan", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"{pk_kind} bf16 dense (sustained)",
+                "per_launch_ms": per_launch_ms, "launches": scan_n,
+                "flops_per_launch": flops_per_launch, "traffic": None,
+                "note": "scan = fused distance + bounded top-k candidates (f32 CUDA-core path); "
+                        "select+merge ms per launch: %.3f / %.3f" % (
+                            sel_ms / max(sel_n, 1), merge_ms / max(merge_n, 1))}
+
+    line = {
+        "metric": "flat kNN queries/s (1M x 128 cosine, k=100)", "value": value,
+        "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: Philox4x32-10 N(0,1) rows L2-normalised (f64), generated on device",
+        "config": {"workload": "C2 cosine flat kNN: base 1,000,000 x 128, 10,000 queries, k=100, "
+                               "GpuShardMode::Sharded over N GPUs",
+                   "n_base": n_base, "queries_per_step": n_q, "k": K, "dim": DIM,
+                   "parallelism": f"row-sharded x{world} + NCCL all-gather merge",
+                   "l2": "inputs larger than L2 (512 MB f32 base), no flush"},
+        "roofline": roofline,
+        "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": n_q * DIM * 4,
+                "d2h_bytes_per_step": n_q * K * 8, "ms_per_step": ms_e2e / args.steps},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+        "clocks_e2e": clk2.summary(),
+    }
+
+    # ------------------------------------------------------- k-means (C3)
+    if not args.no_kmeans:
+        km_seed = vc.config_seed(2)
+        kchunk = -(-KM_N // world)
+        k0, k1 = min(KM_N, rank * kchunk), min(KM_N, (rank + 1) * kchunk)
+        cent = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)
+        vc.gen_rows_device(vc.GEN_NORMAL, km_seed, 2, 0, KM_K, KM_D, cent.data_ptr())
+        xs = torch.empty((max(k1 - k0, 1), KM_D), dtype=torch.float32, device=dev)
+        vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, 0, k0, k1 - k0, KM_D, xs.data_ptr(),
+                           cent.data_ptr(), KM_K, KM_SIGMA)
+        init = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)
+        vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, 0, 0, KM_K, KM_D, init.data_ptr(),
+                           cent.data_ptr(), KM_K, KM_SIGMA)
+        init_h = init.cpu().numpy()
+        torch.cuda.synchronize()
+        vc.kmeans_fit_rank(comm, None, KM_N, KM_D, KM_K, init_h, 2, 0.0,
+                           vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(), n_local=k1 - k0)
+        barrier()
+        vc.profile_reset()
+        vc.profile_enable(True)
+        t0 = time.perf_counter()
+        res = vc.kmeans_fit_rank(comm, None, KM_N, KM_D, KM_K, init_h, KM_ITERS, 0.0,
+                                 vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(),
+                                 n_local=k1 - k0)
+        barrier()
+        km_s = max_over_ranks(time.perf_counter() - t0)
+        vc.profile_enable(False)
+        a_ms, a_n = vc.profile_read("kmeans_assign")
+        u_ms, u_n = vc.profile_read("kmeans_update")
+        a_flops = 2.0 * (k1 - k0) * KM_K * KM_D
+        a_ach = a_flops / (a_ms / max(a_n, 1) / 1e3) / 1e12
+        line["kmeans"] = {
+            "metric": "k-means iterations/s (C3: 1M x 128, K=1024, 20 iterations)",
+            "value": res.iterations / km_s, "unit": "iterations/s", "iterations": res.iterations,
+            "inertia": res.inertia, "seconds": km_s,
+            "timing": "host wall clock around vrs_kmeans_fit_rank (data resident in HBM, "
+                      "includes per-iteration convergence readback), max over ranks",
+            "assign_roofline": {"bound": "tensor", "achieved": a_ach, "peak": peak,
+                                "unit": "TFLOP/s", "frac": a_ach / peak,
+                                "per_launch_ms": a_ms / max(a_n, 1), "launches": a_n},
+            "update_ms_per_launch": u_ms / max(u_n, 1)}
+
+    # ------------------------------------------------------- CPU baseline
+    if rank == 0 and world == 1 and not args.no_cpu:
+        base_h = shard[: r1 - r0].cpu().numpy()
+        q_h = q_dev[:CPU_SAMPLE_QUERIES].cpu().numpy()
+        cb, (do, io) = cpu_leg(base_h, q_h, K, CPU_SAMPLE_QUERIES)
+        line["cpu_baseline"] = cb
+        gi = out_i[:CPU_SAMPLE_QUERIES].cpu().numpy().view(np.uint32)
+        gd = out_d[:CPU_SAMPLE_QUERIES].cpu().numpy()
+        line["parity_sample"] = {
+            "queries": CPU_SAMPLE_QUERIES,
+            "ids_equal_frac": float((gi == io).mean()),
+            "dist_bit_equal_frac": float((gd.view(np.uint32) == do.view(np.uint32)).mean())}
+
+    eng.close()
+    comm.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,124 @@
+"""ctypes wrapper for the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+Loads ``oracle/_build/liboracle.so`` (built by ``oracle/Makefile``). Only
+``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
+import this module; the product never does.
+
+The functions restate VectorRS's CPU paths (see ``vrs_oracle.c``):
+``knn_search`` = ``CudaKnnEngine::search_batch_cpu``
+(crates/vector-cuda/src/knn.rs:312-377), ``kmeans_fit`` =
+``CudaKMeansEngine::fit_cpu`` (crates/vector-cuda/src/kmeans.rs:240-357),
+``topk_reduce`` = ``CollectiveOps::top_k_reduce``
+(crates/vector-cuda/src/ddp/collective.rs:115-159), ``distance`` = the
+AVX-512 pair kernels of crates/vector-simd/src/avx512.rs.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_lib = None
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.orc_distance.restype = ctypes.c_float
+        L.orc_distance.argtypes = [ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        L.orc_rank_key.restype = ctypes.c_float
+        L.orc_rank_key.argtypes = [ctypes.c_int, _f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        L.orc_has_avx512.restype = ctypes.c_int
+        L.orc_knn_search.restype = ctypes.c_int
+        L.orc_knn_search.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _f32p, ctypes.c_int64,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     _f32p, _u32p, ctypes.POINTER(ctypes.c_int)]
+        L.orc_topk_reduce.restype = ctypes.c_int
+        L.orc_topk_reduce.argtypes = [_f32p, _u32p, _i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      _f32p, _u32p]
+        L.orc_kmeans_fit.restype = ctypes.c_int
+        L.orc_kmeans_fit.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _f32p,
+                                     ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int, _f32p, ctypes.c_void_p,
+                                     ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double)]
+        _lib = L
+    return _lib
+
+
+def has_avx512() -> bool:
+    return bool(lib().orc_has_avx512())
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def distance(metric: int, a, b, use_simd: int = -1) -> float:
+    a, b = _f32(a).ravel(), _f32(b).ravel()
+    assert a.size == b.size
+    return float(lib().orc_distance(int(metric), a, b, a.size, use_simd))
+
+
+def rank_key(metric: int, a, b, use_simd: int = -1) -> float:
+    a, b = _f32(a).ravel(), _f32(b).ravel()
+    return float(lib().orc_rank_key(int(metric), a, b, a.size, use_simd))
+
+
+def knn_search(base, queries, k: int, metric: int, nthreads: int | None = None, use_simd: int = -1):
+    """Returns (dist[nq,k'], ids[nq,k']) best-first, k' = min(k, n)."""
+    base, queries = _f32(base), _f32(queries)
+    n, d = base.shape
+    nq = queries.shape[0]
+    kk = max(0, min(k, n))
+    out_d = np.zeros((nq, max(kk, 1)), np.float32)
+    out_i = np.zeros((nq, max(kk, 1)), np.uint32)
+    ok = ctypes.c_int(0)
+    lib().orc_knn_search(base, n, d, queries, nq, int(k), int(metric),
+                         int(nthreads or os.cpu_count() or 1), use_simd, out_d, out_i, ctypes.byref(ok))
+    return out_d[:, :ok.value], out_i[:, :ok.value]
+
+
+def topk_reduce(lists, k: int, metric: int):
+    """lists: sequence of (dists, ids) per rank, in rank order."""
+    lens = np.array([len(d) for d, _ in lists] or [0], np.int32)
+    dists = _f32(np.concatenate([np.asarray(d, np.float32) for d, _ in lists]) if lists else np.zeros(1))
+    ids = np.ascontiguousarray(np.concatenate([np.asarray(i, np.uint32) for _, i in lists]) if lists
+                               else np.zeros(1, np.uint32), dtype=np.uint32)
+    out_d = np.zeros(max(k, 1), np.float32)
+    out_i = np.zeros(max(k, 1), np.uint32)
+    m = lib().orc_topk_reduce(dists, ids, lens, len(lists), int(k), int(metric), out_d, out_i)
+    return out_d[:m], out_i[:m]
+
+
+def kmeans_fit(x, k: int, init, max_iters: int, tol: float, metric: int,
+               nthreads: int | None = None, use_simd: int = -1):
+    """Returns (centroids[k',d], assign[n], iterations, inertia(f64))."""
+    x = _f32(x)
+    n, d = x.shape
+    kk = max(0, min(k, n))
+    init = _f32(init).reshape(-1)
+    cent = np.zeros(max(kk * d, 1), np.float32)
+    assign = np.zeros(max(n, 1), np.int32)
+    it = ctypes.c_int(0)
+    inertia = ctypes.c_double(0.0)
+    kk = lib().orc_kmeans_fit(x, n, d, int(k), init, int(max_iters), float(tol), int(metric),
+                              int(nthreads or os.cpu_count() or 1), use_simd, cent,
+                              assign.ctypes.data, ctypes.byref(it), ctypes.byref(inertia))
+    return cent[:kk * d].reshape(kk, d), assign[:n], it.value, inertia.value

@@ -1,0 +1,68 @@
+"""CPU tests of the C ABI: the library loads, exports every function that
+include/vrs.h declares, and reports errors the way CudaError does
+(crates/vector-cuda/src/error.rs:7-29) without needing a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "vrs.h")).read()
+    return sorted(set(re.findall(r"VRS_API\s+[\w\s\*]+?\b(vrs_\w+)\s*\(", src)))
+
+
+def test_header_declares_api():
+    names = _declared()
+    for n in ["vrs_knn_create", "vrs_knn_search", "vrs_knn_destroy", "vrs_kmeans_fit",
+              "vrs_device_count", "vrs_last_error", "vrs_comm_init", "vrs_knn_create_rank",
+              "vrs_kmeans_fit_rank", "vrs_gen_rows_host", "vrs_gen_rows_device"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(vc):
+    out = subprocess.run(["nm", "-D", "--defined-only", vc.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r" T (vrs_\w+)", out))
+    missing = [n for n in _declared() if n not in exported]
+    assert not missing, missing
+    L = ctypes.CDLL(vc.LIB_PATH)
+    for n in _declared():
+        assert getattr(L, n) is not None
+
+
+def test_device_count_and_errors_without_gpu(vc):
+    n = vc.CudaDeviceContext.device_count()
+    assert n >= 0
+    req = n + 100
+    with pytest.raises(vc.CudaError) as e:
+        vc.DistributedKnnEngine.try_new(np.zeros(8, np.float32), 2, req, vc.GpuShardMode.Sharded,
+                                        vc.DistanceMetric.L2Squared)
+    assert e.value.kind == "InsufficientDevices"
+    assert e.value.requested == req and e.value.available == n
+    with pytest.raises(vc.CudaError) as e:
+        vc.DistributedKMeansEngine.try_new(req)
+    assert e.value == vc.CudaError(1, "", requested=req, available=n)
+
+
+def test_invalid_config_rejected(vc):
+    L = vc.lib()
+    h = ctypes.c_void_p()
+    # bad metric code
+    st = L.vrs_knn_create(None, 0, 4, 1, 0, 42, ctypes.byref(h))
+    assert st in (1, 5)
+    assert L.vrs_last_error()
+    # null out_k
+    assert L.vrs_knn_search(None, None, 0, 1, None, None, None) == 5
+
+
+def test_metric_higher_is_better(vc):
+    L = vc.lib()
+    assert [L.vrs_metric_higher_is_better(m) for m in range(10)] == [0, 1, 1, 0, 0, 0, 0, 0, 0, 0]
+    assert [vc.DistanceMetric(m).higher_is_better() for m in range(10)] == \
+        [False, True, True] + [False] * 7

@@ -1,0 +1,1003 @@
+// capi.cu -- the C ABI of libvrs (include/vrs.h): kNN and k-means engines,
+// per-GPU shards, the single-process NCCL clique (one host thread drives
+// every GPU; replaces the rayon-over-ranks loops of
+// crates/vector-cuda/src/ddp/distributed_knn.rs:155-231 and
+// crates/vector-cuda/src/ddp/distributed_kmeans.rs:108-330) and the
+// one-process-per-GPU rank mode.
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <thread>
+#include <vector>
+
+#include "vrs_exact.cuh"
+#include "vrs_internal.cuh"
+
+namespace vrs {
+
+static thread_local std::string g_err;
+
+void set_error(int status, const std::string& msg) {
+  (void)status;
+  g_err = msg;
+}
+
+int cuda_status(cudaError_t e) {
+  switch (e) {
+    case cudaErrorMemoryAllocation: return VRS_ERR_OOM;
+    case cudaErrorNoDevice:
+    case cudaErrorInsufficientDriver: return VRS_ERR_HARDWARE_NOT_AVAILABLE;
+    case cudaErrorInvalidDevice: return VRS_ERR_DEVICE_NOT_FOUND;
+    default: return VRS_ERR_DRIVER;
+  }
+}
+
+static int fail(int st, const std::string& m) {
+  set_error(st, m);
+  return st;
+}
+
+#define VRS_NCCL(call)                                                                   \
+  do {                                                                                   \
+    ncclResult_t _r = (call);                                                            \
+    if (_r != ncclSuccess && _r != ncclInProgress)                                       \
+      return ::vrs::fail(VRS_ERR_NCCL, std::string(#call) + ": " + ncclGetErrorString(_r)); \
+  } while (0)
+
+// Growable device buffer bound to one device.
+struct DBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  DBuf() = default;
+  DBuf(const DBuf&) = delete;
+  DBuf& operator=(const DBuf&) = delete;
+  ~DBuf() { release(); }
+  int reserve(size_t bytes) {
+    if (bytes <= cap && p) return VRS_OK;
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+    bytes = std::max<size_t>(bytes, 256);
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+      p = nullptr;
+      return fail(cuda_status(e), "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    }
+    cap = bytes;
+    return VRS_OK;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+  template <class T>
+  T* as() const {
+    return reinterpret_cast<T*>(p);
+  }
+};
+
+static int round_up(int x, int m) { return (x + m - 1) / m * m; }
+static int next_pow2(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// Polls a communicator until its pending NCCL calls are enqueued (a
+// non-blocking communicator may return ncclInProgress), or it reports an
+// error, or `timeout_s` passes (then the communicator is aborted).
+static int nccl_ready(ncclComm_t comm, double timeout_s) {
+  if (!comm) return VRS_OK;
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t ar = ncclSuccess;
+    ncclCommGetAsyncError(comm, &ar);
+    if (ar == ncclSuccess) return VRS_OK;
+    if (ar != ncclInProgress) {
+      ncclCommAbort(comm);
+      return fail(VRS_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(ar));
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
+      ncclCommAbort(comm);
+      return fail(VRS_ERR_TIMEOUT, "NCCL call not enqueued within " + std::to_string(timeout_s) + " s");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+// Bounded wait for work enqueued on `s`, watching an NCCL communicator for
+// asynchronous errors (a rank that died or never joined). Aborts the
+// communicator and reports VRS_ERR_TIMEOUT after `timeout_s`.
+static int stream_wait(cudaStream_t s, ncclComm_t comm, double timeout_s) {
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    if (comm) {
+      ncclResult_t ar = ncclSuccess;
+      ncclCommGetAsyncError(comm, &ar);
+      if (ar != ncclSuccess && ar != ncclInProgress) {
+        ncclCommAbort(comm);
+        return fail(VRS_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(ar));
+      }
+      if (ar == ncclSuccess) {
+        cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return VRS_OK;
+        if (e != cudaErrorNotReady)
+          return fail(cuda_status(e), std::string("stream: ") + cudaGetErrorString(e));
+      }
+    } else {
+      cudaError_t e = cudaStreamQuery(s);
+      if (e == cudaSuccess) return VRS_OK;
+      if (e != cudaErrorNotReady) return fail(cuda_status(e), std::string("stream: ") + cudaGetErrorString(e));
+    }
+    double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s) {
+      if (comm) ncclCommAbort(comm);
+      return fail(VRS_ERR_TIMEOUT, "device wait exceeded " + std::to_string(timeout_s) + " s");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(comm ? 50 : 5));
+  }
+}
+
+static double env_timeout() {
+  const char* e = getenv("VRS_TIMEOUT_S");
+  return e ? atof(e) : 300.0;
+}
+
+}  // namespace vrs
+
+using namespace vrs;
+
+struct vrs_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 1, rank = 0, device = 0;
+  cudaStream_t stream = nullptr;
+};
+
+// ============================================================== kNN engine
+namespace {
+
+struct KnnShard {
+  int device = 0;
+  cudaStream_t stream = nullptr;      // stream in use
+  cudaStream_t own_stream = nullptr;  // stream created for this shard
+  ncclComm_t comm = nullptr;  // clique or rank communicator (not owned here)
+  int64_t n_local = 0;
+  int64_t offset = 0;
+  DBuf base, base_aux;
+  // per-search scratch
+  DBuf q_in, q, q_aux, cand, cnt, overflow, pairs, gathered, out_dist, out_id;
+};
+
+}  // namespace
+
+struct vrs_knn {
+  int64_t n_global = 0;
+  int d = 0, dp = 0, metric = 0, mode = 0, g = 1;
+  std::vector<std::unique_ptr<KnnShard>> shards;
+  bool rank_mode = false;
+  vrs_comm* comm = nullptr;  // rank mode
+  std::vector<ncclComm_t> clique;  // owned (single process, g > 1)
+  ~vrs_knn() {
+    for (auto& s : shards) {
+      cudaSetDevice(s->device);
+      cudaStreamSynchronize(s->stream);
+      for (DBuf* b : {&s->base, &s->base_aux, &s->q_in, &s->q, &s->q_aux, &s->cand, &s->cnt,
+                      &s->overflow, &s->pairs, &s->gathered, &s->out_dist, &s->out_id})
+        b->release();
+      if (s->own_stream) cudaStreamDestroy(s->own_stream);
+    }
+    for (ncclComm_t c : clique) ncclCommDestroy(c);
+  }
+};
+
+namespace {
+
+int valid_metric(int m) { return m >= 0 && m <= 9; }
+
+// Uploads (or copies) one shard's rows into the padded layout.
+int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
+  VRS_CUDA(cudaSetDevice(s->device));
+  size_t nb = (size_t)std::max<int64_t>(s->n_local, 1) * h->dp * sizeof(float);
+  VRS_TRY(s->base.reserve(nb));
+  VRS_TRY(s->base_aux.reserve((size_t)std::max<int64_t>(s->n_local, 1) * sizeof(float)));
+  if (s->n_local == 0) return VRS_OK;
+  const int transform = h->metric == vrs_exact::kHell ? 1 : 0;
+  // Stage in chunks to bound the temporary buffer.
+  const int64_t chunk = std::max<int64_t>(1, (int64_t)(256ll << 20) / (h->d * (int64_t)sizeof(float)));
+  DBuf stage;
+  for (int64_t r0 = 0; r0 < s->n_local; r0 += chunk) {
+    int64_t rows_c = std::min(chunk, s->n_local - r0);
+    const float* src = rows + r0 * h->d;
+    if (mem == VRS_MEM_HOST) {
+      int st = stage.reserve((size_t)rows_c * h->d * sizeof(float));
+      if (st) return st;
+      VRS_CUDA(cudaMemcpyAsync(stage.p, src, (size_t)rows_c * h->d * sizeof(float),
+                               cudaMemcpyHostToDevice, s->stream));
+      src = stage.as<float>();
+    }
+    VRS_TRY(launch_pad_rows(src, rows_c, h->d, h->dp, s->base.as<float>() + r0 * h->dp, transform,
+                            s->stream));
+    VRS_CUDA(cudaStreamSynchronize(s->stream));
+  }
+  stage.release();
+  if (h->metric == vrs_exact::kCos)
+    VRS_TRY(launch_cos_norms(s->base.as<float>(), s->n_local, h->d, h->dp, s->base_aux.as<float>(),
+                             s->stream));
+  VRS_CUDA(cudaStreamSynchronize(s->stream));
+  return VRS_OK;
+}
+
+struct ScanPlan {
+  int nseg, cap, max_sort;
+  int64_t seg_len;
+};
+
+ScanPlan plan_scan(int64_t n_local, int nq, int kk) {
+  ScanPlan p;
+  p.cap = next_pow2(std::max(512, 2 * kk + 128));
+  int qtiles = (nq + 31) / 32;
+  int want = std::max(1, (148 * 8 + qtiles - 1) / qtiles);
+  int max_seg = std::max(1, std::min(64, 16384 / std::max(kk, 1)));
+  int nseg = std::min(want, max_seg);
+  int64_t seg_len = (n_local + nseg - 1) / nseg;
+  seg_len = std::max<int64_t>(256, (seg_len + 63) / 64 * 64);
+  p.nseg = (int)std::max<int64_t>(1, (n_local + seg_len - 1) / seg_len);
+  p.seg_len = seg_len;
+  p.max_sort = std::min(16384, next_pow2(std::max(256, p.nseg * kk)));
+  return p;
+}
+
+// Local top-k' of queries already in s->q_in ([nq][d], device) against this
+// shard. Writes either final results (out_dist/out_id, device) or merge pairs
+// (out_pairs, device). Sets *overflow when a query needs the fallback.
+int shard_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
+                 Cand* out_pairs) {
+  cudaStream_t st = s->stream;
+  VRS_TRY(s->q.reserve((size_t)nq * h->dp * sizeof(float)));
+  VRS_TRY(s->q_aux.reserve((size_t)nq * sizeof(float)));
+  VRS_TRY(launch_pad_rows(s->q_in.as<float>(), nq, h->d, h->dp, s->q.as<float>(),
+                          h->metric == vrs_exact::kHell ? 1 : 0, st));
+  if (h->metric == vrs_exact::kCos)
+    VRS_TRY(launch_cos_norms(s->q.as<float>(), nq, h->d, h->dp, s->q_aux.as<float>(), st));
+  ScanPlan p = plan_scan(s->n_local, nq, kk);
+  VRS_TRY(s->cand.reserve((size_t)p.nseg * nq * p.cap * sizeof(Cand)));
+  VRS_TRY(s->cnt.reserve((size_t)p.nseg * nq * sizeof(int)));
+  VRS_TRY(s->overflow.reserve((size_t)(nq + 1) * sizeof(int)));
+  VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)p.nseg * nq * sizeof(int), st));
+  VRS_CUDA(cudaMemsetAsync(s->overflow.p, 0, (size_t)(nq + 1) * sizeof(int), st));
+  KnnScanArgs a{};
+  a.base = s->base.as<float>();
+  a.base_aux = s->base_aux.as<float>();
+  a.n = s->n_local;
+  a.d = h->d;
+  a.dp = h->dp;
+  a.q = s->q.as<float>();
+  a.q_aux = s->q_aux.as<float>();
+  a.q_index = nullptr;
+  a.nq = nq;
+  a.k = kk;
+  a.seg_len = p.seg_len;
+  a.nseg = p.nseg;
+  a.cand = s->cand.as<Cand>();
+  a.cnt = s->cnt.as<int>();
+  a.overflow = s->overflow.as<int>();
+  a.cap = p.cap;
+  a.metric = h->metric;
+  a.kind = kExactScores;
+  a.rho = 1.0f;
+  a.absm = nullptr;
+  if (s->n_local > 0) {
+    ProfToken t = prof_begin("knn_scan", st);
+    VRS_TRY(launch_knn_scan_exact(a, st));
+    prof_end(t, st);
+  }
+  KnnSelectArgs sa{};
+  sa.base = a.base;
+  sa.base_aux = a.base_aux;
+  sa.d = h->d;
+  sa.dp = h->dp;
+  sa.q = a.q;
+  sa.q_aux = a.q_aux;
+  sa.q_index = nullptr;
+  sa.nq = nq;
+  sa.k = kk;
+  sa.nseg = s->n_local > 0 ? p.nseg : 0;
+  sa.cand = a.cand;
+  sa.cnt = a.cnt;
+  sa.overflow = a.overflow;
+  sa.cap = p.cap;
+  sa.metric = h->metric;
+  sa.kind = a.kind;
+  sa.rho = 1.0f;
+  sa.absm = nullptr;
+  sa.id_offset = (uint32_t)s->offset;
+  sa.out_dist = out_dist;
+  sa.out_id = out_id;
+  sa.out_pairs = out_pairs;
+  sa.max_sort = p.max_sort;
+  ProfToken t = prof_begin("knn_select", st);
+  VRS_TRY(launch_knn_select(sa, st));
+  prof_end(t, st);
+  return VRS_OK;
+}
+
+int check_overflow(KnnShard* s, int nq) {
+  std::vector<int> f(nq);
+  if (nq == 0) return VRS_OK;
+  VRS_CUDA(cudaMemcpyAsync(f.data(), s->overflow.p, (size_t)nq * sizeof(int), cudaMemcpyDeviceToHost,
+                           s->stream));
+  VRS_CUDA(cudaStreamSynchronize(s->stream));
+  for (int i = 0; i < nq; i++)
+    if (f[i]) return fail(VRS_ERR_DRIVER, "candidate list overflow for query " + std::to_string(i));
+  return VRS_OK;
+}
+
+int64_t query_batch(int kk) {
+  (void)kk;
+  return 16384;
+}
+
+int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, float* out_dist,
+                    uint32_t* out_id, int32_t* out_k, int mem) {
+  if (!h || !out_k) return fail(VRS_ERR_INVALID_CONFIG, "null handle or out_k");
+  *out_k = 0;
+  if (nq < 0 || k < 0) return fail(VRS_ERR_INVALID_CONFIG, "negative nq or k");
+  if (nq == 0 || k == 0 || h->n_global == 0) return VRS_OK;
+  const int kk = (int)std::min<int64_t>(k, h->n_global);
+  if (kk > 2048) return fail(VRS_ERR_INVALID_CONFIG, "k' > 2048 is not supported");
+  if (!queries || !out_dist || !out_id) return fail(VRS_ERR_INVALID_CONFIG, "null buffer");
+  const bool dev_io = mem == VRS_MEM_DEVICE;
+  if (dev_io && !h->rank_mode && h->shards.size() > 1)
+    return fail(VRS_ERR_INVALID_CONFIG, "device buffers need a single-GPU or rank-mode handle");
+  const cudaMemcpyKind h2d = dev_io ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  const cudaMemcpyKind d2h = dev_io ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+  const int64_t QB = query_batch(kk);
+  const double tmo = env_timeout();
+  const int G = (int)h->shards.size();
+  const int nranks = h->rank_mode ? h->comm->nranks : G;
+
+  for (int64_t q0 = 0; q0 < nq; q0 += QB) {
+    const int nb = (int)std::min<int64_t>(QB, nq - q0);
+    const float* qsrc = queries + q0 * h->d;
+    float* odst = out_dist + q0 * kk;
+    uint32_t* oid = out_id + q0 * kk;
+    if (h->mode == VRS_SHARDED) {
+      // Every shard scores all queries; per-shard top-k' lists meet in an
+      // all-gather and a G-way merge.
+      for (int r = 0; r < G; r++) {
+        KnnShard* s = h->shards[r].get();
+        VRS_CUDA(cudaSetDevice(s->device));
+        VRS_TRY(s->q_in.reserve((size_t)nb * h->d * sizeof(float)));
+        VRS_CUDA(cudaMemcpyAsync(s->q_in.p, qsrc, (size_t)nb * h->d * sizeof(float), h2d, s->stream));
+        VRS_TRY(s->out_dist.reserve((size_t)nb * kk * sizeof(float)));
+        VRS_TRY(s->out_id.reserve((size_t)nb * kk * sizeof(uint32_t)));
+        if (nranks == 1) {
+          VRS_TRY(shard_search(h, s, nb, kk, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr));
+        } else {
+          VRS_TRY(s->pairs.reserve((size_t)nb * kk * sizeof(Cand)));
+          VRS_TRY(s->gathered.reserve((size_t)nranks * nb * kk * sizeof(Cand)));
+          VRS_TRY(shard_search(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>()));
+        }
+      }
+      if (nranks > 1) {
+        VRS_NCCL(ncclGroupStart());
+        for (int r = 0; r < G; r++) {
+          KnnShard* s = h->shards[r].get();
+          VRS_NCCL(ncclAllGather(s->pairs.p, s->gathered.p, (size_t)nb * kk, ncclUint64, s->comm,
+                                 s->stream));
+        }
+        VRS_NCCL(ncclGroupEnd());
+        for (int r = 0; r < G; r++) VRS_TRY(nccl_ready(h->shards[r]->comm, tmo));
+        // Rank mode: every rank merges. Clique: GPU 0 merges.
+        KnnShard* s0 = h->shards[0].get();
+        VRS_CUDA(cudaSetDevice(s0->device));
+        ProfToken t = prof_begin("knn_merge", s0->stream);
+        VRS_TRY(launch_merge_pairs(s0->gathered.as<Cand>(), nranks, nb, kk, h->metric,
+                                   s0->out_dist.as<float>(), s0->out_id.as<uint32_t>(), s0->stream));
+        prof_end(t, s0->stream);
+      }
+      for (int r = 0; r < G; r++) {
+        KnnShard* s = h->shards[r].get();
+        VRS_CUDA(cudaSetDevice(s->device));
+        VRS_TRY(stream_wait(s->stream, nranks > 1 ? s->comm : nullptr, tmo));
+        VRS_TRY(check_overflow(s, nb));
+      }
+      KnnShard* s0 = h->shards[0].get();
+      VRS_CUDA(cudaSetDevice(s0->device));
+      VRS_CUDA(cudaMemcpyAsync(odst, s0->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s0->stream));
+      VRS_CUDA(cudaMemcpyAsync(oid, s0->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s0->stream));
+      VRS_CUDA(cudaStreamSynchronize(s0->stream));
+    } else {
+      // Replicated: query chunks of ceil(nb / ranks) (distributed_knn.rs:201-229).
+      const int chunk = (nb + nranks - 1) / nranks;
+      for (int r = 0; r < G; r++) {
+        KnnShard* s = h->shards[r].get();
+        const int rank = h->rank_mode ? h->comm->rank : r;
+        const int c0 = std::min(nb, rank * chunk), c1 = std::min(nb, c0 + chunk);
+        const int nc = c1 - c0;
+        VRS_CUDA(cudaSetDevice(s->device));
+        VRS_TRY(s->out_dist.reserve((size_t)std::max(nb, 1) * kk * sizeof(float)));
+        VRS_TRY(s->out_id.reserve((size_t)std::max(nb, 1) * kk * sizeof(uint32_t)));
+        VRS_TRY(s->q_in.reserve((size_t)std::max(nc, 1) * h->d * sizeof(float)));
+        VRS_TRY(s->pairs.reserve((size_t)std::max(chunk, 1) * kk * sizeof(Cand)));
+        if (nc > 0)
+          VRS_CUDA(cudaMemcpyAsync(s->q_in.p, qsrc + (int64_t)c0 * h->d, (size_t)nc * h->d * sizeof(float),
+                                   h2d, s->stream));
+        if (!h->rank_mode) {
+          if (nc > 0)
+            VRS_TRY(shard_search(h, s, nc, kk, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr));
+        } else {
+          // Pad the chunk with empty pairs so every rank sends the same count.
+          VRS_CUDA(cudaMemsetAsync(s->pairs.p, 0xff, (size_t)chunk * kk * sizeof(Cand), s->stream));
+          if (nc > 0) VRS_TRY(shard_search(h, s, nc, kk, nullptr, nullptr, s->pairs.as<Cand>()));
+          VRS_TRY(s->gathered.reserve((size_t)nranks * chunk * kk * sizeof(Cand)));
+          VRS_NCCL(ncclAllGather(s->pairs.p, s->gathered.p, (size_t)chunk * kk, ncclUint64, s->comm,
+                                 s->stream));
+          VRS_TRY(nccl_ready(s->comm, tmo));
+          VRS_TRY(launch_finish_pairs(s->gathered.as<Cand>(), (int64_t)nb * kk, h->metric,
+                                      s->out_dist.as<float>(), s->out_id.as<uint32_t>(), s->stream));
+        }
+      }
+      for (int r = 0; r < G; r++) {
+        KnnShard* s = h->shards[r].get();
+        const int rank = h->rank_mode ? h->comm->rank : r;
+        const int c0 = std::min(nb, rank * chunk), c1 = std::min(nb, c0 + chunk);
+        VRS_CUDA(cudaSetDevice(s->device));
+        VRS_TRY(stream_wait(s->stream, h->rank_mode ? s->comm : nullptr, tmo));
+        if (c1 > c0) VRS_TRY(check_overflow(s, c1 - c0));
+        if (h->rank_mode) {
+          VRS_CUDA(cudaMemcpyAsync(odst, s->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s->stream));
+          VRS_CUDA(cudaMemcpyAsync(oid, s->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s->stream));
+        } else if (c1 > c0) {
+          VRS_CUDA(cudaMemcpyAsync(odst + (int64_t)c0 * kk, s->out_dist.p, (size_t)(c1 - c0) * kk * sizeof(float),
+                                   d2h, s->stream));
+          VRS_CUDA(cudaMemcpyAsync(oid + (int64_t)c0 * kk, s->out_id.p,
+                                   (size_t)(c1 - c0) * kk * sizeof(uint32_t), d2h, s->stream));
+        }
+        VRS_CUDA(cudaStreamSynchronize(s->stream));
+      }
+    }
+  }
+  *out_k = kk;
+  return VRS_OK;
+}
+
+int available_devices() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+}  // namespace
+
+// ================================================================ C ABI
+extern "C" {
+
+int vrs_device_count(int32_t* out_count) {
+  if (!out_count) return fail(VRS_ERR_INVALID_CONFIG, "null out_count");
+  *out_count = available_devices();
+  return VRS_OK;
+}
+
+const char* vrs_last_error(void) { return g_err.c_str(); }
+
+int vrs_metric_higher_is_better(int32_t metric) { return vrs_exact::higher_is_better(metric) ? 1 : 0; }
+
+int vrs_knn_create(const float* base, int64_t n, int32_t d, int32_t num_gpus, int32_t mode,
+                   int32_t metric, vrs_knn** out) {
+  if (!out) return fail(VRS_ERR_INVALID_CONFIG, "null out");
+  *out = nullptr;
+  if (num_gpus < 1) return fail(VRS_ERR_INVALID_CONFIG, "num_gpus must be at least 1");
+  if (d < 1 || n < 0 || (n > 0 && !base)) return fail(VRS_ERR_INVALID_CONFIG, "bad base/dimension");
+  if (n > 0xfffffffeLL) return fail(VRS_ERR_INVALID_CONFIG, "ids are u32: n must be < 2^32-1");
+  if (!valid_metric(metric) || (mode != VRS_SHARDED && mode != VRS_REPLICATED))
+    return fail(VRS_ERR_INVALID_CONFIG, "bad metric or mode");
+  int avail = available_devices();
+  if (num_gpus > avail)
+    return fail(VRS_ERR_INSUFFICIENT_DEVICES, "Insufficient hardware GPUs: requested " +
+                                                  std::to_string(num_gpus) + " device(s), but only " +
+                                                  std::to_string(avail) + " physical GPU(s) found");
+  std::unique_ptr<vrs_knn> h(new vrs_knn());
+  h->n_global = n;
+  h->d = d;
+  h->dp = round_up(d, 8);
+  h->metric = metric;
+  h->mode = mode;
+  const int g = (int)std::max<int64_t>(1, std::min<int64_t>(num_gpus, std::max<int64_t>(n, 1)));
+  h->g = g;
+  const int64_t chunk = (n + g - 1) / g;
+  for (int r = 0; r < g; r++) {
+    auto s = std::make_unique<KnnShard>();
+    s->device = r;
+    VRS_CUDA(cudaSetDevice(r));
+    VRS_CUDA(cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking));
+    s->stream = s->own_stream;
+    if (mode == VRS_SHARDED) {
+      int64_t b = std::min(n, r * chunk), e = std::min(n, b + chunk);
+      s->offset = b;
+      s->n_local = e - b;
+    } else {
+      s->offset = 0;
+      s->n_local = n;
+    }
+    h->shards.push_back(std::move(s));
+    VRS_TRY(shard_upload(h.get(), h->shards.back().get(), base + h->shards.back()->offset * d,
+                         VRS_MEM_HOST));
+  }
+  if (g > 1 && mode == VRS_SHARDED) {
+    h->clique.resize(g);
+    std::vector<int> devs(g);
+    for (int r = 0; r < g; r++) devs[r] = r;
+    VRS_NCCL(ncclCommInitAll(h->clique.data(), g, devs.data()));
+    for (int r = 0; r < g; r++) h->shards[r]->comm = h->clique[r];
+  }
+  *out = h.release();
+  return VRS_OK;
+}
+
+int vrs_knn_search(vrs_knn* h, const float* queries, int64_t nq, int32_t k, float* out_dist,
+                   uint32_t* out_id, int32_t* out_k) {
+  return knn_search_impl(h, queries, nq, k, out_dist, out_id, out_k, VRS_MEM_HOST);
+}
+
+int vrs_knn_search_ex(vrs_knn* h, const float* queries, int64_t nq, int32_t k, float* out_dist,
+                      uint32_t* out_id, int32_t* out_k, int32_t mem) {
+  if (mem != VRS_MEM_HOST && mem != VRS_MEM_DEVICE) return fail(VRS_ERR_INVALID_CONFIG, "bad mem flag");
+  return knn_search_impl(h, queries, nq, k, out_dist, out_id, out_k, mem);
+}
+
+int vrs_knn_info(const vrs_knn* h, int64_t* num_vectors, int32_t* dimension, int32_t* num_gpus,
+                 int32_t* mode, int32_t* metric) {
+  if (!h) return fail(VRS_ERR_INVALID_CONFIG, "null handle");
+  if (num_vectors) *num_vectors = h->n_global;
+  if (dimension) *dimension = h->d;
+  if (num_gpus) *num_gpus = h->rank_mode ? h->comm->nranks : h->g;
+  if (mode) *mode = h->mode;
+  if (metric) *metric = h->metric;
+  return VRS_OK;
+}
+
+void vrs_knn_destroy(vrs_knn* h) { delete h; }
+
+int vrs_knn_set_stream(vrs_knn* h, void* cuda_stream) {
+  if (!h) return fail(VRS_ERR_INVALID_CONFIG, "null handle");
+  if (h->shards.size() != 1) return fail(VRS_ERR_INVALID_CONFIG, "set_stream needs a single-GPU or rank-mode handle");
+  KnnShard* s = h->shards[0].get();
+  VRS_CUDA(cudaSetDevice(s->device));
+  VRS_CUDA(cudaStreamSynchronize(s->stream));
+  s->stream = cuda_stream ? (cudaStream_t)cuda_stream : s->own_stream;
+  return VRS_OK;
+}
+
+int vrs_comm_unique_id(uint8_t out_id[128]) {
+  if (!out_id) return fail(VRS_ERR_INVALID_CONFIG, "null id buffer");
+  ncclUniqueId id;
+  VRS_NCCL(ncclGetUniqueId(&id));
+  static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
+  memcpy(out_id, &id, 128);
+  return VRS_OK;
+}
+
+int vrs_comm_init(const uint8_t id[128], int32_t nranks, int32_t rank, int32_t device, vrs_comm** out) {
+  if (!out || !id || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(VRS_ERR_INVALID_CONFIG, "bad comm arguments");
+  *out = nullptr;
+  int avail = available_devices();
+  if (device < 0 || device >= avail)
+    return fail(VRS_ERR_DEVICE_NOT_FOUND, "CUDA device with ordinal " + std::to_string(device) +
+                                              " was not found or could not be initialized");
+  std::unique_ptr<vrs_comm> c(new vrs_comm());
+  c->nranks = nranks;
+  c->rank = rank;
+  c->device = device;
+  VRS_CUDA(cudaSetDevice(device));
+  VRS_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  ncclUniqueId uid;
+  memcpy(&uid, id, 128);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = ncclCommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(VRS_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    ncclCommGetAsyncError(c->comm, &st);
+    if (st == ncclSuccess) break;
+    if (st != ncclInProgress) {
+      ncclCommAbort(c->comm);
+      return fail(VRS_ERR_NCCL, std::string("NCCL init: ") + ncclGetErrorString(st));
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > env_timeout()) {
+      ncclCommAbort(c->comm);
+      return fail(VRS_ERR_TIMEOUT, "NCCL init timed out (a rank never joined)");
+    }
+    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+  }
+  *out = c.release();
+  return VRS_OK;
+}
+
+void vrs_comm_destroy(vrs_comm* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->comm) ncclCommDestroy(c->comm);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+int vrs_knn_create_rank(vrs_comm* comm, const float* shard, int64_t n_local, int64_t global_offset,
+                        int64_t n_global, int32_t d, int32_t mode, int32_t metric, int32_t mem,
+                        vrs_knn** out) {
+  if (!out || !comm) return fail(VRS_ERR_INVALID_CONFIG, "null comm or out");
+  *out = nullptr;
+  if (d < 1 || n_local < 0 || n_global < n_local || global_offset < 0 || (n_local > 0 && !shard))
+    return fail(VRS_ERR_INVALID_CONFIG, "bad shard arguments");
+  if (n_global > 0xfffffffeLL) return fail(VRS_ERR_INVALID_CONFIG, "ids are u32: n must be < 2^32-1");
+  if (!valid_metric(metric) || (mode != VRS_SHARDED && mode != VRS_REPLICATED))
+    return fail(VRS_ERR_INVALID_CONFIG, "bad metric or mode");
+  if (mem != VRS_MEM_HOST && mem != VRS_MEM_DEVICE) return fail(VRS_ERR_INVALID_CONFIG, "bad mem flag");
+  std::unique_ptr<vrs_knn> h(new vrs_knn());
+  h->n_global = n_global;
+  h->d = d;
+  h->dp = round_up(d, 8);
+  h->metric = metric;
+  h->mode = mode;
+  h->g = 1;
+  h->rank_mode = true;
+  h->comm = comm;
+  auto s = std::make_unique<KnnShard>();
+  s->device = comm->device;
+  s->comm = comm->comm;
+  s->n_local = n_local;
+  s->offset = global_offset;
+  VRS_CUDA(cudaSetDevice(comm->device));
+  VRS_CUDA(cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking));
+  s->stream = s->own_stream;
+  h->shards.push_back(std::move(s));
+  VRS_TRY(shard_upload(h.get(), h->shards[0].get(), shard, mem));
+  *out = h.release();
+  return VRS_OK;
+}
+
+}  // extern "C"
+
+// ============================================================ k-means
+namespace {
+
+constexpr int kSumSlots = 513;  // launch_sum_f64 partials + result
+
+struct KmShard {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  ncclComm_t comm = nullptr;
+  int64_t n_local = 0;
+  DBuf x, xr, x_aux, assign, dist, acc, cent, cent_r, cent_aux, shift, scal, red;
+  ~KmShard() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (DBuf* b : {&x, &xr, &x_aux, &assign, &dist, &acc, &cent, &cent_r, &cent_aux, &shift, &scal, &red})
+      b->release();
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+struct KmParams {
+  int64_t n_global;
+  int d, dp, k, max_iters, metric;
+  float tol;
+  int nranks;  // participants in the all-reduce (shards in a clique, or ranks)
+  bool rank_mode;
+};
+
+int km_prepare_shard(const KmParams& P, KmShard* s, const float* rows, int mem) {
+  VRS_CUDA(cudaSetDevice(s->device));
+  const size_t nx = (size_t)std::max<int64_t>(s->n_local, 1);
+  VRS_TRY(s->x.reserve(nx * P.dp * sizeof(float)));
+  VRS_TRY(s->assign.reserve(nx * sizeof(int32_t)));
+  VRS_TRY(s->dist.reserve(nx * sizeof(float)));
+  VRS_TRY(s->x_aux.reserve(nx * sizeof(float)));
+  VRS_TRY(s->acc.reserve(((size_t)P.k * P.dp + P.k) * sizeof(unsigned long long)));
+  VRS_TRY(s->cent.reserve((size_t)P.k * P.dp * sizeof(float)));
+  VRS_TRY(s->cent_r.reserve((size_t)P.k * P.dp * sizeof(float)));
+  VRS_TRY(s->cent_aux.reserve((size_t)P.k * sizeof(float)));
+  VRS_TRY(s->shift.reserve((size_t)P.k * sizeof(float)));
+  VRS_TRY(s->scal.reserve(4 * sizeof(float)));
+  VRS_TRY(s->red.reserve(kSumSlots * sizeof(double)));
+  if (s->n_local > 0) {
+    const float* src = rows;
+    DBuf stage;
+    if (mem == VRS_MEM_HOST) {
+      VRS_TRY(stage.reserve((size_t)s->n_local * P.d * sizeof(float)));
+      VRS_CUDA(cudaMemcpyAsync(stage.p, rows, (size_t)s->n_local * P.d * sizeof(float),
+                               cudaMemcpyHostToDevice, s->stream));
+      src = stage.as<float>();
+    }
+    VRS_TRY(launch_pad_rows(src, s->n_local, P.d, P.dp, s->x.as<float>(), 0, s->stream));
+    VRS_CUDA(cudaStreamSynchronize(s->stream));
+    stage.release();
+    if (P.metric == vrs_exact::kHell) {
+      VRS_TRY(s->xr.reserve(nx * P.dp * sizeof(float)));
+      VRS_TRY(launch_pad_rows(s->x.as<float>(), s->n_local, P.dp, P.dp, s->xr.as<float>(), 1, s->stream));
+    }
+    if (P.metric == vrs_exact::kCos)
+      VRS_TRY(launch_cos_norms(s->x.as<float>(), s->n_local, P.d, P.dp, s->x_aux.as<float>(), s->stream));
+  }
+  return VRS_OK;
+}
+
+// Shared Lloyd loop over 1..G shards (clique) or one shard per rank.
+int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_host,
+           float* out_centroids, int32_t* out_assign_local, int32_t* out_iters, double* out_inertia) {
+  const double tmo = env_timeout();
+  const int G = (int)shards.size();
+  const bool coll = P.nranks > 1;
+  // Initial centroids (padded) on every shard.
+  {
+    std::vector<float> padded((size_t)P.k * P.dp, 0.0f);
+    for (int c = 0; c < P.k; c++)
+      memcpy(&padded[(size_t)c * P.dp], init_host + (size_t)c * P.d, P.d * sizeof(float));
+    for (KmShard* s : shards) {
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_CUDA(cudaMemcpyAsync(s->cent.p, padded.data(), padded.size() * sizeof(float),
+                               cudaMemcpyHostToDevice, s->stream));
+      VRS_CUDA(cudaStreamSynchronize(s->stream));
+    }
+  }
+  // Fixed-point scale from the global max |x|.
+  float gmax = 0.0f;
+  for (KmShard* s : shards) {
+    VRS_CUDA(cudaSetDevice(s->device));
+    VRS_TRY(launch_abs_max(s->x.as<float>(), s->n_local, P.d, P.dp, s->scal.as<float>(), s->stream));
+  }
+  if (coll) {
+    VRS_NCCL(ncclGroupStart());
+    for (KmShard* s : shards)
+      VRS_NCCL(ncclAllReduce(s->scal.p, s->scal.p, 1, ncclFloat32, ncclMax, s->comm, s->stream));
+    VRS_NCCL(ncclGroupEnd());
+  }
+  for (KmShard* s : shards) {
+    VRS_CUDA(cudaSetDevice(s->device));
+    VRS_TRY(stream_wait(s->stream, coll ? s->comm : nullptr, tmo));
+    float m = 0;
+    VRS_CUDA(cudaMemcpy(&m, s->scal.p, sizeof(float), cudaMemcpyDeviceToHost));
+    gmax = std::max(gmax, m);
+  }
+  int scale_exp = 0;
+  if (gmax > 0.0f) {
+    double lim = 61.0 - std::log2((double)std::max<int64_t>(P.n_global, 1) * (double)gmax);
+    scale_exp = (int)std::floor(lim);
+    scale_exp = std::max(-200, std::min(100, scale_exp));
+  }
+  const size_t acc_elems = (size_t)P.k * P.dp + P.k;
+  int iters = 0;
+  for (int it = 0; it < P.max_iters; it++) {
+    iters = it + 1;
+    for (KmShard* s : shards) {
+      VRS_CUDA(cudaSetDevice(s->device));
+      const float* cent_ops = s->cent.as<float>();
+      const float* x_ops = s->x.as<float>();
+      if (P.metric == vrs_exact::kHell) {
+        VRS_TRY(launch_pad_rows(s->cent.as<float>(), P.k, P.dp, P.dp, s->cent_r.as<float>(), 1, s->stream));
+        cent_ops = s->cent_r.as<float>();
+        x_ops = s->xr.as<float>();
+      }
+      if (P.metric == vrs_exact::kCos)
+        VRS_TRY(launch_cos_norms(s->cent.as<float>(), P.k, P.d, P.dp, s->cent_aux.as<float>(), s->stream));
+      ProfToken t = prof_begin("kmeans_assign", s->stream);
+      VRS_TRY(launch_kmeans_assign_exact(x_ops, s->n_local, P.d, P.dp, cent_ops, s->cent_aux.as<float>(),
+                                         s->x_aux.as<float>(), P.k, P.metric, s->assign.as<int32_t>(),
+                                         s->dist.as<float>(), s->stream));
+      prof_end(t, s->stream);
+      VRS_CUDA(cudaMemsetAsync(s->acc.p, 0, acc_elems * sizeof(unsigned long long), s->stream));
+      unsigned long long* sums = s->acc.as<unsigned long long>();
+      VRS_TRY(launch_kmeans_accumulate(s->x.as<float>(), s->n_local, P.d, P.dp, s->assign.as<int32_t>(), P.k,
+                                       scale_exp, sums, sums + (size_t)P.k * P.dp, s->stream));
+    }
+    if (coll) {
+      VRS_NCCL(ncclGroupStart());
+      for (KmShard* s : shards)
+        VRS_NCCL(ncclAllReduce(s->acc.p, s->acc.p, acc_elems, ncclUint64, ncclSum, s->comm, s->stream));
+      VRS_NCCL(ncclGroupEnd());
+      for (KmShard* s : shards) VRS_TRY(nccl_ready(s->comm, tmo));
+    }
+    for (KmShard* s : shards) {
+      VRS_CUDA(cudaSetDevice(s->device));
+      unsigned long long* sums = s->acc.as<unsigned long long>();
+      ProfToken t = prof_begin("kmeans_update", s->stream);
+      VRS_TRY(launch_kmeans_update(sums, sums + (size_t)P.k * P.dp, P.k, P.d, P.dp, scale_exp,
+                                   s->cent.as<float>(), s->shift.as<float>(), s->scal.as<float>() + 1,
+                                   s->stream));
+      prof_end(t, s->stream);
+    }
+    float max_shift = 0.0f;
+    for (KmShard* s : shards) {
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_TRY(stream_wait(s->stream, coll ? s->comm : nullptr, tmo));
+    }
+    VRS_CUDA(cudaSetDevice(shards[0]->device));
+    VRS_CUDA(cudaMemcpy(&max_shift, shards[0]->scal.as<float>() + 1, sizeof(float), cudaMemcpyDeviceToHost));
+    if (max_shift <= P.tol) break;
+  }
+  // Inertia of the last assignment step: deterministic per-shard f64 sums,
+  // added in rank order.
+  double inertia = 0.0;
+  if (iters > 0) {
+    std::vector<double> parts;
+    for (KmShard* s : shards) {
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_TRY(launch_sum_f64(s->dist.as<float>(), s->n_local, s->red.as<double>(), s->stream));
+    }
+    if (P.rank_mode && coll) {
+      KmShard* s = shards[0];
+      DBuf g;
+      VRS_TRY(g.reserve((size_t)P.nranks * sizeof(double)));
+      VRS_NCCL(ncclAllGather(s->red.as<double>() + (kSumSlots - 1), g.p, 1, ncclFloat64, s->comm, s->stream));
+      VRS_TRY(stream_wait(s->stream, s->comm, tmo));
+      parts.resize(P.nranks);
+      VRS_CUDA(cudaMemcpy(parts.data(), g.p, P.nranks * sizeof(double), cudaMemcpyDeviceToHost));
+      g.release();
+    } else {
+      for (KmShard* s : shards) {
+        VRS_CUDA(cudaSetDevice(s->device));
+        VRS_TRY(stream_wait(s->stream, nullptr, tmo));
+        double v = 0;
+        VRS_CUDA(cudaMemcpy(&v, s->red.as<double>() + (kSumSlots - 1), sizeof(double), cudaMemcpyDeviceToHost));
+        parts.push_back(v);
+      }
+    }
+    for (double v : parts) inertia += v;
+  }
+  // Outputs.
+  {
+    KmShard* s0 = shards[0];
+    VRS_CUDA(cudaSetDevice(s0->device));
+    std::vector<float> padded((size_t)P.k * P.dp);
+    VRS_CUDA(cudaMemcpy(padded.data(), s0->cent.p, padded.size() * sizeof(float), cudaMemcpyDeviceToHost));
+    for (int c = 0; c < P.k; c++)
+      memcpy(out_centroids + (size_t)c * P.d, &padded[(size_t)c * P.dp], P.d * sizeof(float));
+  }
+  if (out_assign_local) {
+    int64_t off = 0;
+    for (KmShard* s : shards) {
+      VRS_CUDA(cudaSetDevice(s->device));
+      if (s->n_local > 0) {
+        if (iters > 0)
+          VRS_CUDA(cudaMemcpy(out_assign_local + off, s->assign.p, (size_t)s->n_local * sizeof(int32_t),
+                              cudaMemcpyDeviceToHost));
+        else
+          memset(out_assign_local + off, 0, (size_t)s->n_local * sizeof(int32_t));
+      }
+      off += s->n_local;
+    }
+  }
+  *out_iters = iters;
+  *out_inertia = inertia;
+  return VRS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vrs_kmeans_fit(const float* x, int64_t n, int32_t d, int32_t k, const float* init,
+                   int32_t max_iters, float tol, int32_t metric, int32_t num_gpus,
+                   float* out_centroids, int32_t* out_assign, int32_t* out_k, int32_t* out_iters,
+                   double* out_inertia) {
+  if (!out_k || !out_iters || !out_inertia) return fail(VRS_ERR_INVALID_CONFIG, "null output");
+  *out_k = 0;
+  *out_iters = 0;
+  *out_inertia = 0.0;
+  if (num_gpus < 1) return fail(VRS_ERR_INVALID_CONFIG, "num_gpus must be at least 1");
+  int avail = available_devices();
+  if (num_gpus > avail)
+    return fail(VRS_ERR_INSUFFICIENT_DEVICES, "Insufficient hardware GPUs: requested " +
+                                                  std::to_string(num_gpus) + " device(s), but only " +
+                                                  std::to_string(avail) + " physical GPU(s) found");
+  if (d < 1 || n < 0 || k < 0 || max_iters < 0 || !valid_metric(metric))
+    return fail(VRS_ERR_INVALID_CONFIG, "bad k-means arguments");
+  if (n == 0 || k == 0) return VRS_OK;
+  if (!x || !out_centroids) return fail(VRS_ERR_INVALID_CONFIG, "null buffer");
+  KmParams P;
+  P.n_global = n;
+  P.d = d;
+  P.dp = round_up(d, 8);
+  P.k = (int)std::min<int64_t>(k, n);
+  P.max_iters = max_iters;
+  P.metric = metric;
+  P.tol = tol;
+  const int g = (int)std::min<int64_t>(num_gpus, n);
+  P.nranks = g;
+  P.rank_mode = false;
+  std::vector<std::unique_ptr<KmShard>> own;
+  std::vector<KmShard*> shards;
+  std::vector<ncclComm_t> clique;
+  const int64_t chunk = (n + g - 1) / g;
+  for (int r = 0; r < g; r++) {
+    auto s = std::make_unique<KmShard>();
+    s->device = r;
+    VRS_CUDA(cudaSetDevice(r));
+    VRS_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+    int64_t b = std::min(n, r * chunk), e = std::min(n, b + chunk);
+    s->n_local = e - b;
+    VRS_TRY(km_prepare_shard(P, s.get(), x + b * d, VRS_MEM_HOST));
+    shards.push_back(s.get());
+    own.push_back(std::move(s));
+  }
+  if (g > 1) {
+    clique.resize(g);
+    std::vector<int> devs(g);
+    for (int r = 0; r < g; r++) devs[r] = r;
+    VRS_NCCL(ncclCommInitAll(clique.data(), g, devs.data()));
+    for (int r = 0; r < g; r++) shards[r]->comm = clique[r];
+  }
+  const float* init_ptr = init ? init : x;  // NULL -> first k' points
+  int st = km_run(P, shards, init_ptr, out_centroids, out_assign, out_iters, out_inertia);
+  own.clear();
+  for (ncclComm_t c : clique) ncclCommDestroy(c);
+  if (st == VRS_OK) *out_k = P.k;
+  return st;
+}
+
+int vrs_kmeans_fit_rank(vrs_comm* comm, const float* x_local, int64_t n_local, int64_t n_global,
+                        int32_t d, int32_t k, const float* init, int32_t max_iters, float tol,
+                        int32_t metric, int32_t mem, float* out_centroids, int32_t* out_assign,
+                        int32_t* out_k, int32_t* out_iters, double* out_inertia) {
+  if (!comm || !out_k || !out_iters || !out_inertia) return fail(VRS_ERR_INVALID_CONFIG, "null argument");
+  *out_k = 0;
+  *out_iters = 0;
+  *out_inertia = 0.0;
+  if (d < 1 || n_local < 0 || n_global < n_local || k < 0 || max_iters < 0 || !valid_metric(metric) ||
+      (mem != VRS_MEM_HOST && mem != VRS_MEM_DEVICE))
+    return fail(VRS_ERR_INVALID_CONFIG, "bad k-means arguments");
+  if (n_global == 0 || k == 0) return VRS_OK;
+  if ((n_local > 0 && !x_local) || !out_centroids) return fail(VRS_ERR_INVALID_CONFIG, "null buffer");
+  KmParams P;
+  P.n_global = n_global;
+  P.d = d;
+  P.dp = round_up(d, 8);
+  P.k = (int)std::min<int64_t>(k, n_global);
+  P.max_iters = max_iters;
+  P.metric = metric;
+  P.tol = tol;
+  P.nranks = comm->nranks;
+  P.rank_mode = true;
+  auto s = std::make_unique<KmShard>();
+  s->device = comm->device;
+  s->comm = comm->comm;
+  s->n_local = n_local;
+  VRS_CUDA(cudaSetDevice(comm->device));
+  VRS_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+  VRS_TRY(km_prepare_shard(P, s.get(), x_local, mem));
+  std::vector<float> init_buf((size_t)P.k * d);
+  if (init) {
+    memcpy(init_buf.data(), init, init_buf.size() * sizeof(float));
+  } else {
+    // First k' global rows live on rank 0; broadcast them.
+    DBuf tmp;
+    VRS_TRY(tmp.reserve(init_buf.size() * sizeof(float)));
+    if (comm->rank == 0) {
+      if (n_local < P.k) return fail(VRS_ERR_INVALID_CONFIG, "rank 0 holds fewer than k rows; pass init");
+      VRS_CUDA(cudaMemcpy2DAsync(tmp.p, d * sizeof(float), s->x.p, P.dp * sizeof(float), d * sizeof(float),
+                                 P.k, cudaMemcpyDeviceToDevice, s->stream));
+    }
+    VRS_NCCL(ncclBroadcast(tmp.p, tmp.p, init_buf.size(), ncclFloat32, 0, s->comm, s->stream));
+    VRS_TRY(stream_wait(s->stream, s->comm, env_timeout()));
+    VRS_CUDA(cudaMemcpy(init_buf.data(), tmp.p, init_buf.size() * sizeof(float), cudaMemcpyDeviceToHost));
+    tmp.release();
+  }
+  std::vector<KmShard*> shards{s.get()};
+  int st = km_run(P, shards, init_buf.data(), out_centroids, out_assign, out_iters, out_inertia);
+  if (st == VRS_OK) *out_k = P.k;
+  return st;
+}
+
+}  // extern "C"

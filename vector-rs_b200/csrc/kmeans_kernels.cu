@@ -1,0 +1,214 @@
+// kmeans_kernels.cu -- CUDA-core kernels of the Lloyd k-means path.
+//   * kmeans_assign_exact: per point, the nearest centroid under the
+//     reference's exact pair arithmetic (find_nearest,
+//     crates/vector-cuda/src/kmeans.rs:361-407: strict comparison, lowest
+//     index wins ties, argmax for dot/cosine);
+//   * kmeans_accumulate: per-cluster sums as 64-bit fixed-point integers
+//     (value * 2^s rounded), so the sum is exact, independent of the order
+//     in which points arrive, and identical across GPUs after an integer
+//     NCCL all-reduce; counts as 64-bit integers;
+//   * kmeans_update: mean = (float)(sum / count) in f64, squared shift in f32
+//     summed over dimensions in order (kmeans.rs:318-331); an empty cluster
+//     keeps its centroid (reference kernel kernels/kmeans.cu:350-356);
+//   * deterministic f64 reduction for the inertia; |x| maximum for the
+//     fixed-point scale.
+// Reference kernels replaced: kmeans_zero_accumulators,
+// kmeans_assign_and_accumulate, kmeans_update_centroids
+// (crates/vector-cuda/src/kernels/kmeans.cu:22-395).
+#include "vrs_exact.cuh"
+#include "vrs_internal.cuh"
+
+namespace vrs {
+namespace {
+
+template <int METRIC>
+__global__ void __launch_bounds__(128) kmeans_assign_exact_kernel(
+    const float* __restrict__ x, int64_t n, int d, int dp, const float* __restrict__ cent,
+    const float* __restrict__ cent_aux, const float* __restrict__ x_aux, int k,
+    int32_t* __restrict__ assign, float* __restrict__ dist) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float* v = x + i * dp;
+  const float va = METRIC == vrs_exact::kCos ? x_aux[i] : 0.0f;
+  const bool hib = vrs_exact::higher_is_better(METRIC);
+  int best = 0;
+  float best_key = hib ? -INFINITY : INFINITY;
+  for (int c = 0; c < k; c++) {
+    const float ca = METRIC == vrs_exact::kCos ? cent_aux[c] : 0.0f;
+    float key = vrs_exact::rank_key(METRIC, v, cent + (int64_t)c * dp, d, va, ca);
+    if (hib ? key > best_key : key < best_key) {
+      best_key = key;
+      best = c;
+    }
+  }
+  assign[i] = best;
+  dist[i] = vrs_exact::finish(METRIC, best_key);
+}
+
+__global__ void kmeans_accumulate_kernel(const float* __restrict__ x, int64_t n, int d, int dp,
+                                         const int32_t* __restrict__ assign, int scale_exp,
+                                         unsigned long long* __restrict__ sums,
+                                         unsigned long long* __restrict__ counts) {
+  // One warp per point: lanes stride over dimensions.
+  int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  int c = assign[w];
+  const float* v = x + w * dp;
+  unsigned long long* s = sums + (int64_t)c * dp;
+  for (int j = lane; j < d; j += 32) {
+    long long q = __double2ll_rn(ldexp((double)v[j], scale_exp));
+    atomicAdd(&s[j], (unsigned long long)q);
+  }
+  if (lane == 0) atomicAdd(&counts[c], 1ull);
+}
+
+__global__ void kmeans_update_kernel(const unsigned long long* __restrict__ sums,
+                                     const unsigned long long* __restrict__ counts, int k, int d,
+                                     int dp, int scale_exp, float* __restrict__ cent,
+                                     float* __restrict__ shift, float* __restrict__ max_shift) {
+  int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= k) return;
+  unsigned long long cnt = counts[c];
+  if (cnt == 0) {
+    shift[c] = 0.0f;
+    return;
+  }
+  double inv_scale = ldexp(1.0, -scale_exp);
+  float sh = 0.0f;
+  for (int j = 0; j < d; j++) {
+    double sum = (double)(long long)sums[(int64_t)c * dp + j] * inv_scale;
+    float val = (float)(sum / (double)cnt);
+    float old = cent[(int64_t)c * dp + j];
+    float diff = __fsub_rn(val, old);
+    sh = __fadd_rn(sh, __fmul_rn(diff, diff));
+    cent[(int64_t)c * dp + j] = val;
+  }
+  shift[c] = sh;
+  // Non-negative floats order like their bit patterns.
+  atomicMax(reinterpret_cast<unsigned int*>(max_shift), __float_as_uint(sh));
+}
+
+__global__ void abs_max_kernel(const float* __restrict__ x, int64_t n, int d, int dp,
+                               unsigned int* __restrict__ out) {
+  float m = 0.0f;
+  int64_t total = n * dp;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int c = (int)(i % dp);
+    if (c < d) m = fmaxf(m, fabsf(x[i]));
+  }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+constexpr int kSumBlocks = 512;
+constexpr int kSumThreads = 256;
+
+// Deterministic f64 sum: fixed partition of indices over a fixed grid, fixed
+// in-block tree, then one block sums the partials in a fixed tree.
+__global__ void sum_f64_stage1(const float* __restrict__ v, int64_t n, double* __restrict__ part) {
+  __shared__ double s[kSumThreads];
+  double acc = 0.0;
+  for (int64_t i = blockIdx.x * (int64_t)kSumThreads + threadIdx.x; i < n;
+       i += (int64_t)kSumBlocks * kSumThreads)
+    acc = __dadd_rn(acc, (double)v[i]);
+  s[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = kSumThreads / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) s[threadIdx.x] = __dadd_rn(s[threadIdx.x], s[threadIdx.x + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[blockIdx.x] = s[0];
+}
+
+__global__ void sum_f64_stage2(double* __restrict__ part, double* __restrict__ out) {
+  __shared__ double s[kSumBlocks];
+  for (int i = threadIdx.x; i < kSumBlocks; i += blockDim.x) s[i] = part[i];
+  __syncthreads();
+  for (int w = kSumBlocks / 2; w > 0; w >>= 1) {
+    for (int i = threadIdx.x; i < w; i += blockDim.x) s[i] = __dadd_rn(s[i], s[i + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out = s[0];
+}
+
+template <int M>
+struct AssignL {
+  static int run(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
+                 const float* x_aux, int k, int32_t* assign, float* dist, cudaStream_t s) {
+    kmeans_assign_exact_kernel<M><<<(unsigned)((n + 127) / 128), 128, 0, s>>>(
+        x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist);
+    VRS_CUDA(cudaGetLastError());
+    count_launch();
+    return VRS_OK;
+  }
+};
+
+}  // namespace
+
+int launch_kmeans_assign_exact(const float* x, int64_t n, int d, int dp, const float* cent,
+                               const float* cent_aux, const float* x_aux, int k, int metric,
+                               int32_t* assign, float* dist, cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  switch (metric) {
+    case 0: return AssignL<0>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 1: return AssignL<1>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 2: return AssignL<2>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 3: return AssignL<3>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 4: return AssignL<4>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 5: return AssignL<5>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 6: return AssignL<6>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 7: return AssignL<7>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 8: return AssignL<8>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+    case 9: return AssignL<9>::run(x, n, d, dp, cent, cent_aux, x_aux, k, assign, dist, s);
+  }
+  set_error(VRS_ERR_INVALID_CONFIG, "unknown metric");
+  return VRS_ERR_INVALID_CONFIG;
+}
+
+int launch_kmeans_accumulate(const float* x, int64_t n, int d, int dp, const int32_t* assign, int k,
+                             int scale_exp, unsigned long long* sums, unsigned long long* counts,
+                             cudaStream_t s) {
+  (void)k;
+  if (n == 0) return VRS_OK;
+  int64_t threads = n * 32;
+  kmeans_accumulate_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      x, n, d, dp, assign, scale_exp, sums, counts);
+  VRS_CUDA(cudaGetLastError());
+    count_launch();
+  return VRS_OK;
+}
+
+int launch_kmeans_update(const unsigned long long* sums, const unsigned long long* counts, int k,
+                         int d, int dp, int scale_exp, float* cent, float* shift, float* max_shift,
+                         cudaStream_t s) {
+  VRS_CUDA(cudaMemsetAsync(max_shift, 0, sizeof(float), s));
+  kmeans_update_kernel<<<(k + 127) / 128, 128, 0, s>>>(sums, counts, k, d, dp, scale_exp, cent,
+                                                       shift, max_shift);
+  VRS_CUDA(cudaGetLastError());
+    count_launch();
+  return VRS_OK;
+}
+
+int launch_abs_max(const float* x, int64_t n, int d, int dp, float* out, cudaStream_t s) {
+  VRS_CUDA(cudaMemsetAsync(out, 0, sizeof(float), s));
+  if (n == 0) return VRS_OK;
+  abs_max_kernel<<<148 * 8, 256, 0, s>>>(x, n, d, dp, reinterpret_cast<unsigned int*>(out));
+  VRS_CUDA(cudaGetLastError());
+    count_launch();
+  return VRS_OK;
+}
+
+// out must have room for kSumBlocks + 1 doubles; the sum lands in out[kSumBlocks].
+int launch_sum_f64(const float* v, int64_t n, double* out, cudaStream_t s) {
+  sum_f64_stage1<<<kSumBlocks, kSumThreads, 0, s>>>(v, n, out);
+  VRS_CUDA(cudaGetLastError());
+    count_launch();
+  sum_f64_stage2<<<1, 256, 0, s>>>(out, out + kSumBlocks);
+  VRS_CUDA(cudaGetLastError());
+    count_launch();
+  return VRS_OK;
+}
+
+}  // namespace vrs

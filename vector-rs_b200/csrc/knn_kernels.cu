@@ -1,0 +1,562 @@
+// knn_kernels.cu -- CUDA-core kernels of the flat kNN path:
+//   * knn_scan_exact: streams the shard, scores (query, row) pairs in the
+//     reference's exact arithmetic order, and keeps per-(segment, query)
+//     candidate lists bounded by a running k-th best (radix-select
+//     compaction); the Q x N score matrix never reaches HBM;
+//   * knn_select: per query, gathers the segment lists, selects the k-th
+//     best, re-ranks the survivors exactly and sorts by (score, id);
+//   * merge_pairs: G-way merge of per-rank top-k lists after the NCCL
+//     all-gather (replaces CollectiveOps::top_k_reduce,
+//     crates/vector-cuda/src/ddp/collective.rs:115-159);
+//   * small layout kernels (row padding, Hellinger roots, cosine norms).
+// Reference kernels these replace: knn_compute_distance_matrix and
+// knn_topk_select, crates/vector-cuda/src/kernels/knn.cu:21-305.
+#include <float.h>
+
+#include "vrs_exact.cuh"
+#include "vrs_internal.cuh"
+
+namespace vrs {
+namespace {
+
+constexpr int kScanThreads = 256;
+constexpr int kScanQT = 32;  // query slots per CTA
+constexpr int kScanNT = 64;  // rows per tile
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ bool cand_less(const Cand& x, const Cand& y) {
+  return x.hs < y.hs || (x.hs == y.hs && x.id < y.id);
+}
+
+__device__ __forceinline__ int warp_incl_scan(int v) {
+  int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int t = __shfl_up_sync(kFull, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+// Given a 256-bin histogram in shared memory and a 1-based rank kk, one
+// warp finds the digit holding the kk-th element and the count of elements
+// in smaller digits. All 32 lanes return the same values.
+__device__ __forceinline__ void warp_find_digit(const int* hist, int kk, int* digit, int* before) {
+  int lane = threadIdx.x & 31;
+  int local[8];
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    local[j] = hist[8 * lane + j];
+    s += local[j];
+  }
+  int incl = warp_incl_scan(s);
+  int excl = incl - s;
+  unsigned m = __ballot_sync(kFull, excl < kk && kk <= incl);
+  int src = m ? __ffs(m) - 1 : 31;
+  int dg = 255, bf = 0;
+  if (lane == src) {
+    int acc = excl;
+    dg = 8 * lane + 7;
+    bf = acc;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      if (acc + local[j] >= kk) {
+        dg = 8 * lane + j;
+        bf = acc;
+        break;
+      }
+      acc += local[j];
+    }
+  }
+  *digit = __shfl_sync(kFull, dg, src);
+  *before = __shfl_sync(kFull, bf, src);
+}
+
+// Warp radix select over a global-memory list. BY_ID = false: value =
+// ord_key(hs) over all entries. BY_ID = true: value = id over the entries
+// whose ord_key(hs) == match. Returns the kk-th smallest value (1-based)
+// and, in *less, how many participating entries are strictly smaller.
+template <bool BY_ID>
+__device__ uint32_t warp_select(const Cand* list, int c, int kk, uint32_t match, int* hist,
+                                int* less) {
+  int lane = threadIdx.x & 31;
+  uint32_t prefix = 0, pmask = 0;
+  int below = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) hist[b] = 0;
+    __syncwarp();
+    for (int i = lane; i < c; i += 32) {
+      Cand e = list[i];
+      uint32_t hk = ord_key(e.hs);
+      uint32_t v = BY_ID ? e.id : hk;
+      bool part = BY_ID ? (hk == match) : true;
+      if (part && (v & pmask) == prefix) atomicAdd(&hist[(v >> shift) & 255], 1);
+    }
+    __syncwarp();
+    int digit, before;
+    warp_find_digit(hist, kk, &digit, &before);
+    kk -= before;
+    below += before;
+    prefix |= (uint32_t)digit << shift;
+    pmask |= 0xffu << shift;
+    __syncwarp();
+  }
+  *less = below;
+  return prefix;
+}
+
+// In-place stream compaction of a warp-owned global list; returns the new count.
+template <class Pred>
+__device__ int warp_filter(Cand* list, int c, Pred keep_fn) {
+  int lane = threadIdx.x & 31;
+  int out = 0;
+  for (int base = 0; base < c; base += 32) {
+    int i = base + lane;
+    Cand e;
+    bool keep = false;
+    if (i < c) {
+      e = list[i];
+      keep = keep_fn(e);
+    }
+    unsigned m = __ballot_sync(kFull, keep);
+    if (keep) list[out + __popc(m & ((1u << lane) - 1))] = e;
+    out += __popc(m);
+  }
+  __syncwarp();
+  return out;
+}
+
+struct KeepExact {
+  uint32_t kth, id_sel;
+  __device__ bool operator()(const Cand& e) const {
+    uint32_t k = ord_key(e.hs);
+    return k < kth || (k == kth && e.id <= id_sel);
+  }
+};
+struct KeepBound {
+  float b;
+  __device__ bool operator()(const Cand& e) const { return e.hs <= b; }
+};
+
+// Shrinks one (segment, query) list once it is nearly full. Exact scores
+// keep exactly the k best by (score, id); approximate scores keep every
+// entry within the acceptance bound of the k-th best (and flag overflow when
+// near-ties leave no room).
+__device__ void warp_compact(const KnnScanArgs& a, Cand* list, int c, float absm, int* hist,
+                             int* new_c, float* new_bound, bool* ovf) {
+  int less;
+  uint32_t kth = warp_select<false>(list, c, a.k, 0, hist, &less);
+  float tau = ord_inv(kth);
+  if (a.kind == kExactScores) {
+    int less2;
+    uint32_t id_sel = warp_select<true>(list, c, a.k - less, kth, hist, &less2);
+    *new_c = warp_filter(list, c, KeepExact{kth, id_sel});
+    *new_bound = tau;
+    *ovf = false;
+  } else {
+    float b = accept_bound(a.kind, tau, a.rho, absm);
+    *new_c = warp_filter(list, c, KeepBound{b});
+    *new_bound = b;
+    *ovf = *new_c > a.cap - kScanNT;
+  }
+}
+
+template <int METRIC>
+__device__ __forceinline__ float pair_key(const float* q, const float* x, int d, float qa, float xa) {
+  return vrs_exact::rank_key(METRIC, q, x, d, qa, xa);
+}
+
+template <int METRIC>
+__global__ void __launch_bounds__(kScanThreads) knn_scan_exact_kernel(KnnScanArgs a) {
+  __shared__ float s_bound[kScanQT];
+  __shared__ int s_cnt[kScanQT];
+  __shared__ int s_hist[kScanThreads / 32][256];
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int qt0 = blockIdx.x * kScanQT;
+  const int seg = blockIdx.y;
+  const int64_t row_begin = (int64_t)seg * a.seg_len;
+  const int64_t row_end = min(a.n, row_begin + a.seg_len);
+  if (tid < kScanQT) {
+    s_bound[tid] = INFINITY;
+    s_cnt[tid] = 0;
+  }
+  __syncthreads();
+  const int qs = tid >> 3;
+  const int slot = qt0 + qs;
+  const bool valid = slot < a.nq;
+  const int qrow = valid ? (a.q_index ? a.q_index[slot] : slot) : 0;
+  const float* qp = a.q + (int64_t)qrow * a.dp;
+  const float qa = (METRIC == vrs_exact::kCos && valid) ? a.q_aux[qrow] : 0.0f;
+  Cand* list = a.cand + ((int64_t)seg * a.nq + (valid ? slot : 0)) * a.cap;
+
+  for (int64_t t0 = row_begin; t0 < row_end; t0 += kScanNT) {
+    const float bound = s_bound[qs];
+#pragma unroll 1
+    for (int j = 0; j < kScanNT / 8; j++) {
+      const int64_t row = t0 + (tid & 7) + 8 * j;
+      if (valid && row < row_end) {
+        const float* xp = a.base + row * a.dp;
+        const float xa = (METRIC == vrs_exact::kCos) ? a.base_aux[row] : 0.0f;
+        const float key = pair_key<METRIC>(qp, xp, a.d, qa, xa);
+        const float hs = vrs_exact::heap_score(METRIC, key);
+        if (hs < bound) {
+          int pos = atomicAdd(&s_cnt[qs], 1);
+          list[pos] = Cand{hs, (uint32_t)row};
+        }
+      }
+    }
+    __syncthreads();
+    for (int s = warp; s < kScanQT; s += kScanThreads / 32) {
+      int c = s_cnt[s];
+      if (qt0 + s < a.nq && c > a.cap - kScanNT) {
+        Cand* l = a.cand + ((int64_t)seg * a.nq + qt0 + s) * a.cap;
+        int nc;
+        float nb;
+        bool ovf;
+        warp_compact(a, l, c, 0.0f, s_hist[warp], &nc, &nb, &ovf);
+        if ((threadIdx.x & 31) == 0) {
+          s_cnt[s] = nc;
+          s_bound[s] = nb;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // Final compaction so the select step sees at most ~k entries per segment.
+  for (int s = warp; s < kScanQT; s += kScanThreads / 32) {
+    int c = s_cnt[s];
+    if (qt0 + s < a.nq && c > a.k) {
+      Cand* l = a.cand + ((int64_t)seg * a.nq + qt0 + s) * a.cap;
+      int nc;
+      float nb;
+      bool ovf;
+      warp_compact(a, l, c, 0.0f, s_hist[warp], &nc, &nb, &ovf);
+      if ((threadIdx.x & 31) == 0) s_cnt[s] = nc;
+    }
+  }
+  __syncthreads();
+  if (tid < kScanQT && qt0 + tid < a.nq) a.cnt[(int64_t)seg * a.nq + qt0 + tid] = s_cnt[tid];
+}
+
+// ------------------------------------------------------------------ select
+// Block-wide radix select over a shared-memory list (same contract as
+// warp_select with BY_ID = false).
+__device__ uint32_t block_select(const Cand* buf, int c, int kk, int* hist, int* s_res) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  uint32_t prefix = 0, pmask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    for (int i = tid; i < c; i += blockDim.x) {
+      uint32_t v = ord_key(buf[i].hs);
+      if ((v & pmask) == prefix) atomicAdd(&hist[(v >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int digit, before;
+      warp_find_digit(hist, kk, &digit, &before);
+      if (tid == 0) {
+        s_res[0] = digit;
+        s_res[1] = before;
+      }
+    }
+    __syncthreads();
+    kk -= s_res[1];
+    prefix |= (uint32_t)s_res[0] << shift;
+    pmask |= 0xffu << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Block compaction of a shared list with a predicate; returns the new count.
+template <class Pred>
+__device__ int block_filter(Cand* buf, int c, Pred keep_fn, int* s_warp_tot) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  int out = 0;
+  for (int base = 0; base < c; base += blockDim.x) {
+    int i = base + tid;
+    Cand e;
+    bool keep = false;
+    if (i < c) {
+      e = buf[i];
+      keep = keep_fn(e);
+    }
+    unsigned m = __ballot_sync(kFull, keep);
+    if (lane == 0) s_warp_tot[warp] = __popc(m);
+    __syncthreads();
+    int woff = 0, tot = 0;
+    for (int w = 0; w < nw; w++) {
+      if (w < warp) woff += s_warp_tot[w];
+      tot += s_warp_tot[w];
+    }
+    __syncthreads();
+    if (keep) buf[out + woff + __popc(m & ((1u << lane) - 1))] = e;
+    out += tot;
+    __syncthreads();
+  }
+  return out;
+}
+
+__device__ void block_bitonic_sort(Cand* s, int P) {
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        int ixj = i ^ j;
+        if (ixj > i) {
+          bool asc = (i & k) == 0;
+          Cand x = s[i], y = s[ixj];
+          if (cand_less(y, x) == asc) {
+            s[i] = y;
+            s[ixj] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+template <int METRIC>
+__global__ void __launch_bounds__(256) knn_select_kernel(KnnSelectArgs a) {
+  extern __shared__ Cand sbuf[];
+  __shared__ int s_hist[256];
+  __shared__ int s_res[4];
+  __shared__ int s_wt[32];
+  __shared__ int s_off[65];
+  const int slot = blockIdx.x;
+  const int tid = threadIdx.x;
+  if (a.overflow[slot]) return;
+  const int qrow = a.q_index ? a.q_index[slot] : slot;
+  if (tid == 0) {
+    int tot = 0;
+    for (int s = 0; s < a.nseg; s++) {
+      s_off[s] = tot;
+      tot += a.cnt[(int64_t)s * a.nq + slot];
+    }
+    s_off[a.nseg] = tot;
+  }
+  __syncthreads();
+  int total = s_off[a.nseg];
+  if (total > a.max_sort) {
+    if (tid == 0) a.overflow[slot] = 1;
+    return;
+  }
+  for (int s = 0; s < a.nseg; s++) {
+    const Cand* l = a.cand + ((int64_t)s * a.nq + slot) * a.cap;
+    int c = s_off[s + 1] - s_off[s];
+    for (int i = tid; i < c; i += blockDim.x) sbuf[s_off[s] + i] = l[i];
+  }
+  __syncthreads();
+  // k-th best scan score over all segments -> acceptance bound -> survivors.
+  int R = total;
+  if (total > a.k) {
+    uint32_t kth = block_select(sbuf, total, a.k, s_hist, s_res);
+    float tau = ord_inv(kth);
+    float absm = a.kind == kAbsMargin ? a.absm[qrow] : 0.0f;
+    float b = accept_bound(a.kind, tau, a.rho, absm);
+    R = block_filter(sbuf, total, KeepBound{b}, s_wt);
+  }
+  // Exact re-rank of approximate survivors in the reference's order.
+  if (a.kind != kExactScores) {
+    const float* qp = a.q + (int64_t)qrow * a.dp;
+    const float qa = METRIC == vrs_exact::kCos ? a.q_aux[qrow] : 0.0f;
+    for (int i = tid; i < R; i += blockDim.x) {
+      uint32_t row = sbuf[i].id;
+      const float xa = METRIC == vrs_exact::kCos ? a.base_aux[row] : 0.0f;
+      float key = vrs_exact::rank_key(METRIC, qp, a.base + (int64_t)row * a.dp, a.d, qa, xa);
+      sbuf[i].hs = vrs_exact::heap_score(METRIC, key);
+    }
+    __syncthreads();
+  }
+  int P = 1;
+  while (P < R) P <<= 1;
+  if (P > a.max_sort) {
+    if (tid == 0) a.overflow[slot] = 1;
+    return;
+  }
+  for (int i = R + tid; i < P; i += blockDim.x) sbuf[i] = Cand{INFINITY, 0xffffffffu};
+  __syncthreads();
+  block_bitonic_sort(sbuf, P);
+  for (int r = tid; r < a.k; r += blockDim.x) {
+    Cand e = r < R ? sbuf[r] : Cand{INFINITY, 0xffffffffu};
+    uint32_t gid = e.id == 0xffffffffu ? 0xffffffffu : e.id + a.id_offset;
+    if (a.out_pairs) a.out_pairs[(int64_t)slot * a.k + r] = Cand{e.hs, gid};
+    if (a.out_dist) {
+      float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
+      a.out_dist[(int64_t)slot * a.k + r] = e.id == 0xffffffffu ? NAN : vrs_exact::finish(METRIC, key);
+      a.out_id[(int64_t)slot * a.k + r] = gid;
+    }
+  }
+}
+
+// --------------------------------------------------------------- merge
+template <int METRIC>
+__global__ void __launch_bounds__(256) merge_pairs_kernel(const Cand* g, int nlists, int nq, int k,
+                                                           float* out_dist, uint32_t* out_id) {
+  extern __shared__ Cand sbuf[];
+  const int q = blockIdx.x;
+  const int T = nlists * k;
+  int P = 1;
+  while (P < T) P <<= 1;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    if (i < T) {
+      int l = i / k, r = i % k;
+      sbuf[i] = g[((int64_t)l * nq + q) * k + r];
+    } else {
+      sbuf[i] = Cand{INFINITY, 0xffffffffu};
+    }
+  }
+  __syncthreads();
+  block_bitonic_sort(sbuf, P);
+  for (int r = threadIdx.x; r < k; r += blockDim.x) {
+    Cand e = sbuf[r];
+    float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
+    out_dist[(int64_t)q * k + r] = e.id == 0xffffffffu ? NAN : vrs_exact::finish(METRIC, key);
+    out_id[(int64_t)q * k + r] = e.id;
+  }
+}
+
+template <int METRIC>
+__global__ void finish_pairs_kernel(const Cand* p, int64_t count, float* out_dist, uint32_t* out_id) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= count) return;
+  Cand e = p[i];
+  float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
+  out_dist[i] = e.id == 0xffffffffu ? NAN : vrs_exact::finish(METRIC, key);
+  out_id[i] = e.id;
+}
+
+// ------------------------------------------------------------- layout
+__global__ void pad_rows_kernel(const float* __restrict__ src, int64_t rows, int d, int dp,
+                                float* __restrict__ dst, int transform) {
+  int64_t total = rows * dp;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / dp;
+    int c = (int)(i - r * dp);
+    float v = c < d ? src[r * d + c] : 0.0f;
+    if (transform == 1) v = vrs_exact::root_abs(v);
+    dst[i] = v;
+  }
+}
+
+__global__ void cos_norms_kernel(const float* __restrict__ x, int64_t rows, int d, int dp,
+                                 float* __restrict__ out) {
+  int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r < rows) out[r] = vrs_exact::cos_norm_sq(x + r * dp, d);
+}
+
+template <template <int> class F, class... Args>
+int dispatch_metric(int metric, Args... args) {
+  switch (metric) {
+    case 0: return F<0>::run(args...);
+    case 1: return F<1>::run(args...);
+    case 2: return F<2>::run(args...);
+    case 3: return F<3>::run(args...);
+    case 4: return F<4>::run(args...);
+    case 5: return F<5>::run(args...);
+    case 6: return F<6>::run(args...);
+    case 7: return F<7>::run(args...);
+    case 8: return F<8>::run(args...);
+    case 9: return F<9>::run(args...);
+  }
+  set_error(VRS_ERR_INVALID_CONFIG, "unknown metric code " + std::to_string(metric));
+  return VRS_ERR_INVALID_CONFIG;
+}
+
+template <int M>
+struct ScanExactL {
+  static int run(const KnnScanArgs& a, cudaStream_t s) {
+    dim3 grid((a.nq + kScanQT - 1) / kScanQT, a.nseg);
+    knn_scan_exact_kernel<M><<<grid, kScanThreads, 0, s>>>(a);
+    VRS_CUDA(cudaGetLastError());
+    count_launch();
+    return VRS_OK;
+  }
+};
+
+template <int M>
+struct SelectL {
+  static int run(const KnnSelectArgs& a, cudaStream_t s) {
+    size_t smem = (size_t)a.max_sort * sizeof(Cand);
+    VRS_CUDA(cudaFuncSetAttribute(knn_select_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    knn_select_kernel<M><<<a.nq, 256, smem, s>>>(a);
+    VRS_CUDA(cudaGetLastError());
+    count_launch();
+    return VRS_OK;
+  }
+};
+
+template <int M>
+struct MergeL {
+  static int run(const Cand* g, int nlists, int nq, int k, float* od, uint32_t* oi, cudaStream_t s) {
+    int P = 1;
+    while (P < nlists * k) P <<= 1;
+    size_t smem = (size_t)P * sizeof(Cand);
+    VRS_CUDA(cudaFuncSetAttribute(merge_pairs_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    merge_pairs_kernel<M><<<nq, 256, smem, s>>>(g, nlists, nq, k, od, oi);
+    VRS_CUDA(cudaGetLastError());
+    count_launch();
+    return VRS_OK;
+  }
+};
+
+template <int M>
+struct FinishL {
+  static int run(const Cand* p, int64_t count, float* od, uint32_t* oi, cudaStream_t s) {
+    if (count == 0) return VRS_OK;
+    finish_pairs_kernel<M><<<(unsigned)((count + 255) / 256), 256, 0, s>>>(p, count, od, oi);
+    VRS_CUDA(cudaGetLastError());
+    count_launch();
+    return VRS_OK;
+  }
+};
+
+}  // namespace
+
+int launch_knn_scan_exact(const KnnScanArgs& a, cudaStream_t s) {
+  if (a.nq == 0 || a.n == 0) return VRS_OK;
+  return dispatch_metric<ScanExactL>(a.metric, a, s);
+}
+
+int launch_knn_select(const KnnSelectArgs& a, cudaStream_t s) {
+  if (a.nq == 0) return VRS_OK;
+  return dispatch_metric<SelectL>(a.metric, a, s);
+}
+
+int launch_merge_pairs(const Cand* gathered, int nlists, int nq, int k, int metric, float* out_dist,
+                       uint32_t* out_id, cudaStream_t s) {
+  if (nq == 0 || k == 0) return VRS_OK;
+  return dispatch_metric<MergeL>(metric, gathered, nlists, nq, k, out_dist, out_id, s);
+}
+
+int launch_finish_pairs(const Cand* pairs, int64_t count, int metric, float* out_dist,
+                        uint32_t* out_id, cudaStream_t s) {
+  return dispatch_metric<FinishL>(metric, pairs, count, out_dist, out_id, s);
+}
+
+int launch_pad_rows(const float* src, int64_t rows, int d, int dp, float* dst, int transform,
+                    cudaStream_t s) {
+  if (rows == 0) return VRS_OK;
+  int64_t total = rows * dp;
+  int64_t nblk = (total + 255) / 256;
+  unsigned blocks = (unsigned)(nblk < 148 * 64 ? nblk : 148 * 64);
+  pad_rows_kernel<<<blocks, 256, 0, s>>>(src, rows, d, dp, dst, transform);
+  VRS_CUDA(cudaGetLastError());
+    count_launch();
+  return VRS_OK;
+}
+
+int launch_cos_norms(const float* x, int64_t rows, int d, int dp, float* out, cudaStream_t s) {
+  if (rows == 0) return VRS_OK;
+  cos_norms_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, s>>>(x, rows, d, dp, out);
+  VRS_CUDA(cudaGetLastError());
+    count_launch();
+  return VRS_OK;
+}
+
+}  // namespace vrs
