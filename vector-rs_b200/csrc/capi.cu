@@ -16,6 +16,7 @@
 
 #include "vrs_exact.cuh"
 #include "vrs_internal.cuh"
+#include "vrs_tc.cuh"
 
 namespace vrs {
 
@@ -169,8 +170,18 @@ struct KnnShard {
   int64_t n_local = 0;
   int64_t offset = 0;
   DBuf base, base_aux;
+  // tensor-core operands (GEMM-form metrics, d <= 128)
+  bool use_tc = false;
+  int num_sms = 148;
+  int n_tiny = 0;
+  DBuf xb, xn, xmax, tiny, ntiny;
+  DBuf pb, pn;                  // pivot rows (every pivot_stride-th row)
+  int64_t pivot_m = 0, pivot_stride = 1;
+  DBuf tmin, ibound;            // per-search pivot-pass outputs
   // per-search scratch
   DBuf q_in, q, q_aux, cand, cnt, overflow, pairs, gathered, out_dist, out_id;
+  DBuf qb, absm, err, qindex;
+  int last_nq = 0, last_kk = 0, last_nseg = 0, last_cap = 0;
 };
 
 }  // namespace
@@ -187,7 +198,9 @@ struct vrs_knn {
       cudaSetDevice(s->device);
       cudaStreamSynchronize(s->stream);
       for (DBuf* b : {&s->base, &s->base_aux, &s->q_in, &s->q, &s->q_aux, &s->cand, &s->cnt,
-                      &s->overflow, &s->pairs, &s->gathered, &s->out_dist, &s->out_id})
+                      &s->overflow, &s->pairs, &s->gathered, &s->out_dist, &s->out_id, &s->xb,
+                      &s->xn, &s->xmax, &s->tiny, &s->ntiny, &s->qb, &s->absm, &s->err, &s->qindex, &s->pb,
+                      &s->pn, &s->tmin, &s->ibound})
         b->release();
       if (s->own_stream) cudaStreamDestroy(s->own_stream);
     }
@@ -229,6 +242,39 @@ int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
     VRS_TRY(launch_cos_norms(s->base.as<float>(), s->n_local, h->d, h->dp, s->base_aux.as<float>(),
                              s->stream));
   VRS_CUDA(cudaStreamSynchronize(s->stream));
+  VRS_CUDA(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, s->device));
+  if (tc::tc_supported(h->metric, h->d) && !getenv("VRS_DISABLE_TC")) {
+    const int d16 = tc::tc_d16(h->d);
+    const int64_t npad = (s->n_local + 127) / 128 * 128 + 128;
+    VRS_TRY(s->xb.reserve((size_t)s->n_local * d16 * 2));
+    VRS_TRY(s->xn.reserve((size_t)npad * sizeof(float)));
+    VRS_TRY(s->xmax.reserve(sizeof(unsigned int)));
+    VRS_TRY(s->tiny.reserve((size_t)tc::kTinyCap * sizeof(uint32_t)));
+    VRS_TRY(s->ntiny.reserve(sizeof(int)));
+    VRS_CUDA(cudaMemsetAsync(s->xn.p, 0, (size_t)npad * sizeof(float), s->stream));
+    VRS_CUDA(cudaMemsetAsync(s->xmax.p, 0, sizeof(unsigned int), s->stream));
+    VRS_CUDA(cudaMemsetAsync(s->ntiny.p, 0, sizeof(int), s->stream));
+    VRS_TRY(tc::tc_base_prep(s->base.as<float>(), s->n_local, h->d, h->dp, h->metric, s->xb.p,
+                             s->xn.as<float>(), s->xmax.as<unsigned int>(), s->tiny.as<uint32_t>(),
+                             s->ntiny.as<int>(), tc::kTinyCap, s->stream));
+    VRS_CUDA(cudaMemcpyAsync(&s->n_tiny, s->ntiny.p, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+    VRS_CUDA(cudaStreamSynchronize(s->stream));
+    s->use_tc = s->n_tiny <= tc::kTinyCap;
+    if (!s->use_tc) {
+      s->xb.release();
+    } else {
+      s->pivot_m = tc::tc_pivot_rows(s->n_local, &s->pivot_stride);
+      if (s->pivot_stride > 1) {
+        const int64_t ppad = (s->pivot_m + 127) / 128 * 128 + 128;
+        VRS_TRY(s->pb.reserve((size_t)s->pivot_m * d16 * 2));
+        VRS_TRY(s->pn.reserve((size_t)ppad * sizeof(float)));
+        VRS_CUDA(cudaMemsetAsync(s->pn.p, 0, (size_t)ppad * sizeof(float), s->stream));
+        VRS_TRY(tc::tc_pivot_gather(s->xb.p, s->xn.as<float>(), s->pivot_m, s->pivot_stride, h->d, s->pb.p,
+                                    s->pn.as<float>(), s->stream));
+        VRS_CUDA(cudaStreamSynchronize(s->stream));
+      }
+    }
+  }
   return VRS_OK;
 }
 
@@ -255,21 +301,16 @@ ScanPlan plan_scan(int64_t n_local, int nq, int kk) {
 // Local top-k' of queries already in s->q_in ([nq][d], device) against this
 // shard. Writes either final results (out_dist/out_id, device) or merge pairs
 // (out_pairs, device). Sets *overflow when a query needs the fallback.
-int shard_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
-                 Cand* out_pairs) {
+// Launches the exact-order CUDA-core scan + select for `nq` query slots.
+// q_index (device, nullable) maps slots to query rows of s->q; results land
+// in the rows the slots name. `ovf` receives per-slot overflow flags.
+int launch_exact_search(vrs_knn* h, KnnShard* s, int nq, int kk, const int* q_index, int* ovf,
+                        float* out_dist, uint32_t* out_id, Cand* out_pairs) {
   cudaStream_t st = s->stream;
-  VRS_TRY(s->q.reserve((size_t)nq * h->dp * sizeof(float)));
-  VRS_TRY(s->q_aux.reserve((size_t)nq * sizeof(float)));
-  VRS_TRY(launch_pad_rows(s->q_in.as<float>(), nq, h->d, h->dp, s->q.as<float>(),
-                          h->metric == vrs_exact::kHell ? 1 : 0, st));
-  if (h->metric == vrs_exact::kCos)
-    VRS_TRY(launch_cos_norms(s->q.as<float>(), nq, h->d, h->dp, s->q_aux.as<float>(), st));
   ScanPlan p = plan_scan(s->n_local, nq, kk);
   VRS_TRY(s->cand.reserve((size_t)p.nseg * nq * p.cap * sizeof(Cand)));
   VRS_TRY(s->cnt.reserve((size_t)p.nseg * nq * sizeof(int)));
-  VRS_TRY(s->overflow.reserve((size_t)(nq + 1) * sizeof(int)));
   VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)p.nseg * nq * sizeof(int), st));
-  VRS_CUDA(cudaMemsetAsync(s->overflow.p, 0, (size_t)(nq + 1) * sizeof(int), st));
   KnnScanArgs a{};
   a.base = s->base.as<float>();
   a.base_aux = s->base_aux.as<float>();
@@ -278,14 +319,14 @@ int shard_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint3
   a.dp = h->dp;
   a.q = s->q.as<float>();
   a.q_aux = s->q_aux.as<float>();
-  a.q_index = nullptr;
+  a.q_index = q_index;
   a.nq = nq;
   a.k = kk;
   a.seg_len = p.seg_len;
   a.nseg = p.nseg;
   a.cand = s->cand.as<Cand>();
   a.cnt = s->cnt.as<int>();
-  a.overflow = s->overflow.as<int>();
+  a.overflow = ovf;
   a.cap = p.cap;
   a.metric = h->metric;
   a.kind = kExactScores;
@@ -303,16 +344,16 @@ int shard_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint3
   sa.dp = h->dp;
   sa.q = a.q;
   sa.q_aux = a.q_aux;
-  sa.q_index = nullptr;
+  sa.q_index = q_index;
   sa.nq = nq;
   sa.k = kk;
   sa.nseg = s->n_local > 0 ? p.nseg : 0;
   sa.cand = a.cand;
   sa.cnt = a.cnt;
-  sa.overflow = a.overflow;
+  sa.overflow = ovf;
   sa.cap = p.cap;
   sa.metric = h->metric;
-  sa.kind = a.kind;
+  sa.kind = kExactScores;
   sa.rho = 1.0f;
   sa.absm = nullptr;
   sa.id_offset = (uint32_t)s->offset;
@@ -320,20 +361,133 @@ int shard_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint3
   sa.out_id = out_id;
   sa.out_pairs = out_pairs;
   sa.max_sort = p.max_sort;
+  sa.tiny = nullptr;
+  sa.n_tiny = 0;
   ProfToken t = prof_begin("knn_select", st);
   VRS_TRY(launch_knn_select(sa, st));
   prof_end(t, st);
   return VRS_OK;
 }
 
-int check_overflow(KnnShard* s, int nq) {
-  std::vector<int> f(nq);
+// Launches the tensor-core scan + exact re-rank select for all nq queries.
+int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
+                     Cand* out_pairs) {
+  cudaStream_t st = s->stream;
+  const int d16 = tc::tc_d16(h->d);
+  const int nq_alloc = (nq + 255) / 256 * 256;
+  VRS_TRY(s->qb.reserve((size_t)nq_alloc * d16 * 2));
+  VRS_TRY(s->absm.reserve((size_t)nq * sizeof(float)));
+  VRS_TRY(s->err.reserve(sizeof(int)));
+  if (nq_alloc > nq)
+    VRS_CUDA(cudaMemsetAsync((char*)s->qb.p + (size_t)nq * d16 * 2, 0, (size_t)(nq_alloc - nq) * d16 * 2, st));
+  VRS_CUDA(cudaMemsetAsync(s->err.p, 0, sizeof(int), st));
+  VRS_TRY(tc::tc_query_prep(s->q.as<float>(), nq, h->d, h->dp, h->metric, s->xmax.as<unsigned int>(),
+                            s->qb.p, s->absm.as<float>(), s->overflow.as<int>(), st));
+  tc::TcPlan p = tc::tc_plan(s->n_local, nq, kk, s->num_sms);
+  VRS_TRY(s->cand.reserve((size_t)p.nseg * nq * p.cap * sizeof(Cand)));
+  VRS_TRY(s->cnt.reserve((size_t)p.nseg * nq * sizeof(int)));
+  VRS_TRY(s->ibound.reserve((size_t)nq * sizeof(float)));
+  VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)p.nseg * nq * sizeof(int), st));
+  if (s->n_local > 0) {
+    // Pivot pass: per-query starting bound from the k-th smallest tile
+    // minimum over every pivot_stride-th row.
+    const void* pb = s->pivot_stride > 1 ? s->pb.p : s->xb.p;
+    const float* pn = s->pivot_stride > 1 ? s->pn.as<float>() : s->xn.as<float>();
+    const int ntile = (int)((s->pivot_m + 127) / 128);
+    tc::TcPlan pp = tc::tc_plan(s->pivot_m, nq, kk, s->num_sms);
+    VRS_TRY(s->tmin.reserve((size_t)ntile * nq * sizeof(float)));
+    ProfToken t0 = prof_begin("knn_pivot", st);
+    VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, pb, s->pivot_m, h->d, pn, h->metric, nq, kk, pp, nullptr,
+                        nullptr, s->overflow.as<int>(), s->absm.as<float>(), s->err.as<int>(),
+                        s->tmin.as<float>(), nullptr, st));
+    VRS_TRY(tc::tc_tau(s->tmin.as<float>(), ntile, nq, kk, s->absm.as<float>(), s->ibound.as<float>(), st));
+    prof_end(t0, st);
+    ProfToken t = prof_begin("knn_scan", st);
+    VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, s->xb.p, s->n_local, h->d, s->xn.as<float>(), h->metric, nq, kk,
+                        p, s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(),
+                        s->absm.as<float>(), s->err.as<int>(), nullptr, s->ibound.as<float>(), st));
+    prof_end(t, st);
+  }
+  KnnSelectArgs sa{};
+  sa.base = s->base.as<float>();
+  sa.base_aux = s->base_aux.as<float>();
+  sa.d = h->d;
+  sa.dp = h->dp;
+  sa.q = s->q.as<float>();
+  sa.q_aux = s->q_aux.as<float>();
+  sa.q_index = nullptr;
+  sa.nq = nq;
+  sa.k = kk;
+  sa.nseg = s->n_local > 0 ? p.nseg : 0;
+  sa.cand = s->cand.as<Cand>();
+  sa.cnt = s->cnt.as<int>();
+  sa.overflow = s->overflow.as<int>();
+  sa.cap = p.cap;
+  sa.metric = h->metric;
+  sa.kind = kAbsMargin;
+  sa.rho = 1.0f;
+  sa.absm = s->absm.as<float>();
+  sa.id_offset = (uint32_t)s->offset;
+  sa.out_dist = out_dist;
+  sa.out_id = out_id;
+  sa.out_pairs = out_pairs;
+  sa.max_sort = std::min(16384, next_pow2(std::max(512, p.nseg * (kk + 160) + s->n_tiny)));
+  sa.tiny = s->tiny.as<uint32_t>();
+  sa.n_tiny = h->metric == vrs_exact::kCos ? s->n_tiny : 0;
+  ProfToken t = prof_begin("knn_select", st);
+  VRS_TRY(launch_knn_select(sa, st));
+  prof_end(t, st);
+  return VRS_OK;
+}
+
+// Phase 1 (asynchronous): local top-k' of the queries in s->q_in ([nq][d],
+// device). Writes final results (out_dist/out_id) or merge pairs (out_pairs).
+int shard_search_launch(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
+                        Cand* out_pairs) {
+  cudaStream_t st = s->stream;
+  VRS_TRY(s->q.reserve((size_t)nq * h->dp * sizeof(float)));
+  VRS_TRY(s->q_aux.reserve((size_t)nq * sizeof(float)));
+  VRS_TRY(s->overflow.reserve((size_t)(2 * nq + 1) * sizeof(int)));
+  VRS_CUDA(cudaMemsetAsync(s->overflow.p, 0, (size_t)(2 * nq + 1) * sizeof(int), st));
+  VRS_TRY(launch_pad_rows(s->q_in.as<float>(), nq, h->d, h->dp, s->q.as<float>(),
+                          h->metric == vrs_exact::kHell ? 1 : 0, st));
+  if (h->metric == vrs_exact::kCos)
+    VRS_TRY(launch_cos_norms(s->q.as<float>(), nq, h->d, h->dp, s->q_aux.as<float>(), st));
+  s->last_nq = nq;
+  s->last_kk = kk;
+  if (s->use_tc) return launch_tc_search(h, s, nq, kk, out_dist, out_id, out_pairs);
+  return launch_exact_search(h, s, nq, kk, nullptr, s->overflow.as<int>(), out_dist, out_id, out_pairs);
+}
+
+// Phase 2 (synchronous): queries whose candidate lists overflowed (or whose
+// tensor-core bound does not apply) are redone with the exact-order scan.
+int shard_search_finish(vrs_knn* h, KnnShard* s, float* out_dist, uint32_t* out_id, Cand* out_pairs,
+                        double tmo) {
+  const int nq = s->last_nq, kk = s->last_kk;
   if (nq == 0) return VRS_OK;
+  std::vector<int> f(nq);
+  int err = 0;
   VRS_CUDA(cudaMemcpyAsync(f.data(), s->overflow.p, (size_t)nq * sizeof(int), cudaMemcpyDeviceToHost,
                            s->stream));
-  VRS_CUDA(cudaStreamSynchronize(s->stream));
+  if (s->use_tc)
+    VRS_CUDA(cudaMemcpyAsync(&err, s->err.p, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+  VRS_TRY(stream_wait(s->stream, nullptr, tmo));
+  if (err) return fail(VRS_ERR_TIMEOUT, "tensor-core scan gave up waiting (stage code " + std::to_string(err) + ")");
+  std::vector<int> idx;
   for (int i = 0; i < nq; i++)
-    if (f[i]) return fail(VRS_ERR_DRIVER, "candidate list overflow for query " + std::to_string(i));
+    if (f[i]) idx.push_back(i);
+  if (idx.empty()) return VRS_OK;
+  const int nf = (int)idx.size();
+  VRS_TRY(s->qindex.reserve((size_t)nf * sizeof(int)));
+  VRS_CUDA(cudaMemcpyAsync(s->qindex.p, idx.data(), (size_t)nf * sizeof(int), cudaMemcpyHostToDevice,
+                           s->stream));
+  int* ovf2 = s->overflow.as<int>() + nq;
+  VRS_TRY(launch_exact_search(h, s, nf, kk, s->qindex.as<int>(), ovf2, out_dist, out_id, out_pairs));
+  std::vector<int> f2(nf);
+  VRS_CUDA(cudaMemcpyAsync(f2.data(), ovf2, (size_t)nf * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+  VRS_TRY(stream_wait(s->stream, nullptr, tmo));
+  for (int i = 0; i < nf; i++)
+    if (f2[i]) return fail(VRS_ERR_DRIVER, "exact fallback overflowed for query " + std::to_string(idx[i]));
   return VRS_OK;
 }
 
@@ -377,12 +531,20 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         VRS_TRY(s->out_dist.reserve((size_t)nb * kk * sizeof(float)));
         VRS_TRY(s->out_id.reserve((size_t)nb * kk * sizeof(uint32_t)));
         if (nranks == 1) {
-          VRS_TRY(shard_search(h, s, nb, kk, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr));
+          VRS_TRY(shard_search_launch(h, s, nb, kk, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr));
         } else {
           VRS_TRY(s->pairs.reserve((size_t)nb * kk * sizeof(Cand)));
           VRS_TRY(s->gathered.reserve((size_t)nranks * nb * kk * sizeof(Cand)));
-          VRS_TRY(shard_search(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>()));
+          VRS_TRY(shard_search_launch(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>()));
         }
+      }
+      for (int r = 0; r < G; r++) {
+        KnnShard* s = h->shards[r].get();
+        VRS_CUDA(cudaSetDevice(s->device));
+        if (nranks == 1)
+          VRS_TRY(shard_search_finish(h, s, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr, tmo));
+        else
+          VRS_TRY(shard_search_finish(h, s, nullptr, nullptr, s->pairs.as<Cand>(), tmo));
       }
       if (nranks > 1) {
         VRS_NCCL(ncclGroupStart());
@@ -405,7 +567,6 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         KnnShard* s = h->shards[r].get();
         VRS_CUDA(cudaSetDevice(s->device));
         VRS_TRY(stream_wait(s->stream, nranks > 1 ? s->comm : nullptr, tmo));
-        VRS_TRY(check_overflow(s, nb));
       }
       KnnShard* s0 = h->shards[0].get();
       VRS_CUDA(cudaSetDevice(s0->device));
@@ -428,13 +589,24 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         if (nc > 0)
           VRS_CUDA(cudaMemcpyAsync(s->q_in.p, qsrc + (int64_t)c0 * h->d, (size_t)nc * h->d * sizeof(float),
                                    h2d, s->stream));
+        s->last_nq = 0;
         if (!h->rank_mode) {
           if (nc > 0)
-            VRS_TRY(shard_search(h, s, nc, kk, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr));
+            VRS_TRY(shard_search_launch(h, s, nc, kk, s->out_dist.as<float>(), s->out_id.as<uint32_t>(),
+                                        nullptr));
         } else {
           // Pad the chunk with empty pairs so every rank sends the same count.
           VRS_CUDA(cudaMemsetAsync(s->pairs.p, 0xff, (size_t)chunk * kk * sizeof(Cand), s->stream));
-          if (nc > 0) VRS_TRY(shard_search(h, s, nc, kk, nullptr, nullptr, s->pairs.as<Cand>()));
+          if (nc > 0) VRS_TRY(shard_search_launch(h, s, nc, kk, nullptr, nullptr, s->pairs.as<Cand>()));
+        }
+      }
+      for (int r = 0; r < G; r++) {
+        KnnShard* s = h->shards[r].get();
+        VRS_CUDA(cudaSetDevice(s->device));
+        if (!h->rank_mode) {
+          VRS_TRY(shard_search_finish(h, s, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr, tmo));
+        } else {
+          VRS_TRY(shard_search_finish(h, s, nullptr, nullptr, s->pairs.as<Cand>(), tmo));
           VRS_TRY(s->gathered.reserve((size_t)nranks * chunk * kk * sizeof(Cand)));
           VRS_NCCL(ncclAllGather(s->pairs.p, s->gathered.p, (size_t)chunk * kk, ncclUint64, s->comm,
                                  s->stream));
@@ -449,7 +621,6 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         const int c0 = std::min(nb, rank * chunk), c1 = std::min(nb, c0 + chunk);
         VRS_CUDA(cudaSetDevice(s->device));
         VRS_TRY(stream_wait(s->stream, h->rank_mode ? s->comm : nullptr, tmo));
-        if (c1 > c0) VRS_TRY(check_overflow(s, c1 - c0));
         if (h->rank_mode) {
           VRS_CUDA(cudaMemcpyAsync(odst, s->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s->stream));
           VRS_CUDA(cudaMemcpyAsync(oid, s->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s->stream));

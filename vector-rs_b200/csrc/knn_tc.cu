@@ -1,0 +1,558 @@
+// knn_tc.cu -- tensor-core (tcgen05) fused distance + candidate scan for the
+// GEMM-form metrics (squared L2, Mahalanobis = sqrt L2, dot, cosine).
+//
+// Each CTA owns 256 queries (two M=128 bf16 operand tiles, loaded once by
+// TMA) and streams 128-row bf16 tiles of one base segment through a 4-stage
+// TMA ring. One thread issues tcgen05.mma into two 128x128 f32 accumulators
+// per tile, double-buffered in TMEM (4 x 128 = 512 columns). Eight epilogue
+// warps read their lanes with tcgen05.ld (one thread = one query), form the
+// approximate heap score (L2: |x|^2 - 2 q.x, similarity: -q.x), and append
+// (score, row) to the query's segment list only when the score is within the
+// query's acceptance bound; lists are shrunk in place by a warp radix select
+// when nearly full. The Q x N score matrix never reaches HBM.
+//
+// Correctness: bf16 products carry a bounded error; a row can belong to the
+// exact top-k only if its approximate score is within `absm[q]` of the k-th
+// best approximate score, so every such row is kept and later re-ranked in
+// the reference's exact f32 arithmetic (knn_select in knn_kernels.cu).
+//
+// Replaces knn_compute_distance_matrix + knn_topk_select,
+// crates/vector-cuda/src/kernels/knn.cu:21-305.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "tc_common.cuh"
+#include "vrs_exact.cuh"
+#include "vrs_internal.cuh"
+#include "vrs_select.cuh"
+#include "vrs_tc.cuh"
+
+namespace vrs {
+namespace tc {
+namespace {
+
+constexpr int BM = 128;        // queries per accumulator
+constexpr int NACC = 2;        // accumulators per CTA (256 queries)
+constexpr int BN = 128;        // base rows per tile
+constexpr int KBW = 64;        // bf16 elements per K-block (one 128-byte swizzle row)
+constexpr int MAX_KBLK = 2;    // D <= 128 on this path
+constexpr int STAGES = 4;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + EPI_WARPS * 32;
+constexpr uint32_t BLK_A = BM * 128;  // bytes of one K-block of a 128-row tile
+constexpr uint32_t BLK_B = BN * 128;
+constexpr size_t SMEM_A = (size_t)NACC * MAX_KBLK * BLK_A;
+constexpr size_t SMEM_B = (size_t)STAGES * MAX_KBLK * BLK_B;
+constexpr size_t SMEM_HIST = (size_t)EPI_WARPS * 256 * 4;
+constexpr size_t SMEM_BAR = 256;
+constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_HIST + SMEM_BAR;
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait, then abort
+constexpr uint32_t TMEM_COLS = 512;
+
+struct TcScanArgs {
+  const float* xn;   // |x|^2 per row (L2 mode), zero padded to a multiple of BN
+  int64_t n;
+  int nq;
+  int ksteps;        // ceil(D / 16)
+  int kblk;          // ceil(D16 / 64)
+  int64_t seg_len;   // multiple of BN
+  Cand* cand;        // [nseg][nq][cap]
+  int* cnt;          // [nseg][nq]
+  int* overflow;     // [nq]
+  int cap;
+  int k;
+  int mode;          // 0: score = |x|^2 - 2 acc; 1: score = -acc
+  const float* absm; // [nq]
+  int* err;          // global error word (0 = ok)
+  // Pivot pass: instead of appending, write each tile's minimum score per
+  // query to tmin[tile][query] (tile = global 128-row tile index).
+  int tilemin;
+  float* tmin;
+  // Starting acceptance bound per query (null: +inf).
+  const float* init_bound;
+};
+
+__device__ __forceinline__ float min32(const float* v) {
+  float m0 = fmin3(v[0], v[1], v[2]), m1 = fmin3(v[3], v[4], v[5]);
+  float m2 = fmin3(v[6], v[7], v[8]), m3 = fmin3(v[9], v[10], v[11]);
+  float m4 = fmin3(v[12], v[13], v[14]), m5 = fmin3(v[15], v[16], v[17]);
+  float m6 = fmin3(v[18], v[19], v[20]), m7 = fmin3(v[21], v[22], v[23]);
+  float m8 = fmin3(v[24], v[25], v[26]), m9 = fmin3(v[27], v[28], v[29]);
+  float a = fmin3(m0, m1, m2), b = fmin3(m3, m4, m5), c = fmin3(m6, m7, m8);
+  float d = fmin3(m9, v[30], v[31]);
+  return fminf(fmin3(a, b, c), d);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    knn_scan_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       TcScanArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + SMEM_A;
+  int* s_hist = (int*)(sB + SMEM_B);
+  uint64_t* bars = (uint64_t*)((uint8_t*)s_hist + SMEM_HIST);
+  uint64_t* full = bars;                // [STAGES] TMA -> MMA
+  uint64_t* empty = bars + STAGES;      // [STAGES] MMA -> TMA
+  uint64_t* tfull = bars + 2 * STAGES;  // [2] MMA -> epilogue
+  uint64_t* tempty = tfull + 2;         // [2] epilogue -> MMA
+  uint64_t* afull = tempty + 2;         // queries loaded
+  uint32_t* s_tmem = (uint32_t*)(afull + 1);
+  volatile int* s_abort = (volatile int*)(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * (BM * NACC);
+  const int seg = blockIdx.y;
+  const int64_t row_begin = (int64_t)seg * a.seg_len;
+  const int64_t row_end = min(a.n, row_begin + a.seg_len);
+  const int ntiles = row_end > row_begin ? (int)((row_end - row_begin + BN - 1) / BN) : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], EPI_WARPS);
+    }
+    mbar_init(afull, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(s_tmem, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    // ---------------------------------------------------- TMA producer
+    if (lane == 0 && ntiles > 0) {
+      mbar_expect_tx(afull, (uint32_t)(NACC * a.kblk) * BLK_A);
+      for (int acc = 0; acc < NACC; acc++)
+        for (int kb = 0; kb < a.kblk; kb++)
+          tma_load_2d(sA + (acc * MAX_KBLK + kb) * BLK_A, &tmA, kb * KBW, q0 + acc * BM, afull);
+      int issued = 0;
+      for (int t = 0; t < ntiles; t++) {
+        const int s = t % STAGES;
+        if (!mbar_wait(&empty[s], ((t / STAGES) & 1) ^ 1, s_abort, a.err, 1, WAIT_NS)) break;
+        mbar_expect_tx(&full[s], (uint32_t)a.kblk * BLK_B);
+        const int y = (int)(row_begin + (int64_t)t * BN);
+        for (int kb = 0; kb < a.kblk; kb++)
+          tma_load_2d(sB + (s * MAX_KBLK + kb) * BLK_B, &tmB, kb * KBW, y, &full[s]);
+        issued = t + 1;
+      }
+      if (*s_abort) {
+        // Drain: wait (bounded) for the loads this thread issued.
+        volatile int dummy = 0;
+        for (int t = max(0, issued - STAGES); t < issued; t++)
+          mbar_wait(&full[t % STAGES], (t / STAGES) & 1, &dummy, a.err, 0, WAIT_NS / 4);
+        mbar_wait(afull, 0, &dummy, a.err, 0, WAIT_NS / 4);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------- MMA issuer
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t idesc = idesc_bf16(BM, BN);
+      bool ok = mbar_wait(afull, 0, s_abort, a.err, 2, WAIT_NS);
+      tc_fence_after();
+      int last = -1;
+      for (int t = 0; ok && t < ntiles; t++) {
+        const int s = t % STAGES, b = t & 1;
+        if (!mbar_wait(&full[s], (t / STAGES) & 1, s_abort, a.err, 3, WAIT_NS)) break;
+        if (!mbar_wait(&tempty[b], ((t >> 1) & 1) ^ 1, s_abort, a.err, 4, WAIT_NS)) break;
+        tc_fence_after();
+        for (int acc = 0; acc < NACC; acc++) {
+          const uint32_t d = tmem + acc * 256 + b * BN;
+          for (int ks = 0; ks < a.ksteps; ks++) {
+            const int kb = ks >> 2, koff = (ks & 3) * 32;
+            const uint64_t ad = smem_desc_sw128(sA + (acc * MAX_KBLK + kb) * BLK_A + koff);
+            const uint64_t bd = smem_desc_sw128(sB + (s * MAX_KBLK + kb) * BLK_B + koff);
+            mma_bf16(d, ad, bd, idesc, ks > 0 ? 1u : 0u);
+          }
+        }
+        mma_commit(&empty[s]);
+        mma_commit(&tfull[b]);
+        last = t;
+      }
+      if (*s_abort && last >= 0) {
+        // Let the last issued MMAs finish before TMEM is released.
+        volatile int dummy = 0;
+        mbar_wait(&tfull[last & 1], (last >> 1) & 1, &dummy, a.err, 0, WAIT_NS / 4);
+      }
+    }
+  } else {
+    // ---------------------------------------------------- epilogue
+    const int ew = warp - 2;
+    const int acc = ew >> 2;
+    const int quad = warp & 3;
+    const int q = q0 + acc * BM + quad * 32 + lane;
+    const bool vq = q < a.nq;
+    Cand* list = a.cand + ((int64_t)blockIdx.y * a.nq + (vq ? q : 0)) * a.cap;
+    int count = 0;
+    float bound = (vq && a.init_bound) ? a.init_bound[q] : INFINITY;
+    const float absm = vq ? a.absm[q] : 0.0f;
+    float tile_min = INFINITY;
+    int* hist = s_hist + ew * 256;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    for (int t = 0; t < ntiles; t++) {
+      const int b = t & 1;
+      const bool ok = mbar_wait(&tfull[b], (t >> 1) & 1, s_abort, a.err, 5, WAIT_NS);
+      if (!__all_sync(sel::kFull, ok)) break;
+      tc_fence_after();
+      const int64_t n0 = row_begin + (int64_t)t * BN;
+      const int64_t rem_cols = row_end - n0;
+      const int valid_cols = rem_cols < BN ? (int)rem_cols : BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + acc * 256 + b * BN + c * 32, v);
+        if (a.mode == 0) {
+          const float4* xp = reinterpret_cast<const float4*>(a.xn + n0 + c * 32);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; j4++) {
+            const float4 x4 = __ldg(xp + j4);
+            v[4 * j4 + 0] = fmaf(-2.0f, v[4 * j4 + 0], x4.x);
+            v[4 * j4 + 1] = fmaf(-2.0f, v[4 * j4 + 1], x4.y);
+            v[4 * j4 + 2] = fmaf(-2.0f, v[4 * j4 + 2], x4.z);
+            v[4 * j4 + 3] = fmaf(-2.0f, v[4 * j4 + 3], x4.w);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j++) v[j] = -v[j];
+        }
+        const int cb = valid_cols - c * 32;
+        if (cb < 32) {
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (j >= cb) v[j] = INFINITY;
+        }
+        const float m = min32(v);
+        tile_min = fminf(tile_min, m);
+        if (!a.tilemin && vq && m <= bound) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            if (j < cb && v[j] <= bound) list[count++] = Cand{v[j], (uint32_t)(n0 + c * 32 + j)};
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+      if (a.tilemin) {
+        if (vq) a.tmin[(row_begin / BN + t) * (int64_t)a.nq + q] = tile_min;
+        tile_min = INFINITY;
+        continue;
+      }
+      // Shrink lists that could overflow on the next tile.
+      unsigned need = __ballot_sync(sel::kFull, vq && count > a.cap - BN);
+      while (need) {
+        const int l = __ffs(need) - 1;
+        need &= need - 1;
+        const int lc = __shfl_sync(sel::kFull, count, l);
+        const float la = __shfl_sync(sel::kFull, absm, l);
+        Cand* ll = reinterpret_cast<Cand*>(
+            __shfl_sync(sel::kFull, reinterpret_cast<unsigned long long>(list), l));
+        __syncwarp();
+        int less;
+        const uint32_t kth = sel::warp_select<false>(ll, lc, a.k, 0, hist, &less);
+        const float bnd = __fadd_ru(ord_inv(kth), la);
+        const int nc = sel::warp_filter(ll, lc, sel::KeepBound{bnd});
+        if (lane == l) {
+          count = nc;
+          bound = bnd;
+          if (nc > a.cap - BN) {
+            a.overflow[q] = 1;
+            count = 0;
+            bound = -INFINITY;
+          }
+        }
+      }
+    }
+    if (vq && !a.tilemin) a.cnt[(int64_t)blockIdx.y * a.nq + q] = count;
+    if (vq && *s_abort) a.overflow[q] = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ prep
+// Base rows -> bf16 operand rows (cosine: unit-normalised), |x|^2 for the L2
+// epilogue, max |x| for the margins, and the list of near-zero cosine rows.
+__global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int d, int dp, int d16,
+                                    int metric, __nv_bfloat16* __restrict__ xb,
+                                    float* __restrict__ xn, unsigned int* __restrict__ xmax_bits,
+                                    uint32_t* __restrict__ tiny, int* __restrict__ n_tiny,
+                                    int tiny_cap) {
+  int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const float* v = x + r * dp;
+  __nv_bfloat16* o = xb + r * d16;
+  float scale = 1.0f;
+  if (metric == vrs_exact::kCos) {
+    const float sx = sqrtf(vrs_exact::cos_norm_sq(v, d));
+    if (!(sx >= kTinyNorm)) {
+      int i = atomicAdd(n_tiny, 1);
+      if (i < tiny_cap) tiny[i] = (uint32_t)r;
+      scale = 0.0f;
+    } else {
+      scale = 1.0f / sx;
+    }
+  }
+  double ss = 0.0;
+  for (int j = 0; j < d16; j++) {
+    float e = j < d ? v[j] : 0.0f;
+    ss += (double)e * (double)e;
+    o[j] = __float2bfloat16_rn(metric == vrs_exact::kCos ? e * scale : e);
+  }
+  if (xn) xn[r] = (float)ss;
+  atomicMax(xmax_bits, __float_as_uint((float)sqrt(ss)));
+}
+
+// Queries -> bf16 operand rows and per-query acceptance margins (heap-score
+// units). Near-zero cosine queries are routed to the exact fallback.
+__global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d, int dp, int d16,
+                                     int metric, const unsigned int* __restrict__ xmax_bits,
+                                     __nv_bfloat16* __restrict__ qb, float* __restrict__ absm,
+                                     int* __restrict__ overflow) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nq) return;
+  const float* v = q + (int64_t)i * dp;
+  __nv_bfloat16* o = qb + (int64_t)i * d16;
+  float scale = 1.0f;
+  if (metric == vrs_exact::kCos) {
+    const float sq = sqrtf(vrs_exact::cos_norm_sq(v, d));
+    if (!(sq >= kTinyNorm)) {
+      overflow[i] = 1;
+      scale = 0.0f;
+    } else {
+      scale = 1.0f / sq;
+    }
+  }
+  double ss = 0.0;
+  for (int j = 0; j < d16; j++) {
+    float e = j < d ? v[j] : 0.0f;
+    ss += (double)e * (double)e;
+    o[j] = __float2bfloat16_rn(metric == vrs_exact::kCos ? e * scale : e);
+  }
+  const double X = (double)__uint_as_float(*xmax_bits);
+  const double Q = sqrt(ss);
+  const double u = 0x1p-24;
+  const double c_tc = 0x1p-8 + 0x1p-17 + (double)(d16 + 2) * 0x1p-22;
+  const double g = (double)(d + 4) * u * 1.01;
+  double e;
+  if (metric == vrs_exact::kCos) {
+    e = c_tc + 8.0 * u + 4.0 * g;
+  } else if (metric == vrs_exact::kDot) {
+    e = (c_tc + 2.0 * g) * Q * X;
+  } else {  // squared L2 / Mahalanobis scores |x|^2 - 2 q.x
+    e = 2.0 * c_tc * Q * X + 8.0 * g * (Q + X) * (Q + X);
+  }
+  absm[i] = (float)(2.0 * e * 1.25) * (1.0f + 0x1p-20f);
+}
+
+// Starting bound per query: the k-th smallest pivot-tile minimum. Each tile
+// minimum is the score of a distinct pivot row, so at least k rows score
+// <= tau and the exact k-th best is <= tau; anything in the exact top-k thus
+// has approximate score <= tau + absm.
+__global__ void __launch_bounds__(256) tc_tau_kernel(const float* __restrict__ tmin, int ntile, int nq,
+                                                     int k, const float* __restrict__ absm,
+                                                     float* __restrict__ init_bound) {
+  extern __shared__ Cand buf[];
+  __shared__ int s_hist[256];
+  __shared__ int s_res[4];
+  const int q = blockIdx.x;
+  if (ntile < k) {
+    if (threadIdx.x == 0) init_bound[q] = INFINITY;
+    return;
+  }
+  for (int t = threadIdx.x; t < ntile; t += blockDim.x) buf[t] = Cand{tmin[(int64_t)t * nq + q], 0u};
+  __syncthreads();
+  const uint32_t kth = sel::block_select(buf, ntile, k, s_hist, s_res);
+  if (threadIdx.x == 0) {
+    const float tau = ord_inv(kth);
+    init_bound[q] = isfinite(tau) ? __fadd_ru(tau, absm[q]) : INFINITY;
+  }
+}
+
+// Gathers every `stride`-th bf16 operand row (and |x|^2) into the pivot set.
+__global__ void tc_pivot_gather_kernel(const __nv_bfloat16* __restrict__ xb, const float* __restrict__ xn,
+                                       int64_t m, int64_t stride, int d16,
+                                       __nv_bfloat16* __restrict__ pb, float* __restrict__ pn) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= m * d16) return;
+  int64_t r = i / d16;
+  int c = (int)(i - r * d16);
+  pb[i] = xb[r * stride * d16 + c];
+  if (c == 0 && xn) pn[r] = xn[r * stride];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// bf16 [rows][d16] row-major, box 64 x 128, 128-byte swizzle, zero OOB fill.
+int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error(VRS_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
+    return VRS_ERR_DRIVER;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)d16, (cuuint64_t)std::max<int64_t>(rows, 1)};
+  cuuint64_t strides[1] = {(cuuint64_t)d16 * 2};
+  cuuint32_t box[2] = {(cuuint32_t)KBW, (cuuint32_t)BM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error(VRS_ERR_DRIVER, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return VRS_ERR_DRIVER;
+  }
+  return VRS_OK;
+}
+
+}  // namespace
+
+bool tc_supported(int metric, int d) {
+  return d >= 1 && d <= 128 &&
+         (metric == vrs_exact::kL2 || metric == vrs_exact::kMaha || metric == vrs_exact::kDot ||
+          metric == vrs_exact::kCos);
+}
+
+int tc_d16(int d) { return (d + 15) / 16 * 16; }
+
+int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* xn,
+                 unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  tc_base_prep_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(
+      x, n, d, dp, tc_d16(d), metric, (__nv_bfloat16*)xb, xn, xmax_bits, tiny, n_tiny, tiny_cap);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+int tc_query_prep(const float* q, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
+                  void* qb, float* absm, int* overflow, cudaStream_t s) {
+  if (nq == 0) return VRS_OK;
+  tc_query_prep_kernel<<<(nq + 127) / 128, 128, 0, s>>>(q, nq, d, dp, tc_d16(d), metric, xmax_bits,
+                                                         (__nv_bfloat16*)qb, absm, overflow);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, int d, void* pb,
+                    float* pn, cudaStream_t s) {
+  if (m == 0) return VRS_OK;
+  const int d16 = tc_d16(d);
+  const int64_t total = m * d16;
+  tc_pivot_gather_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+      (const __nv_bfloat16*)xb, xn, m, stride, d16, (__nv_bfloat16*)pb, pn);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+int tc_tau(const float* tmin, int ntile, int nq, int k, const float* absm, float* init_bound,
+           cudaStream_t s) {
+  if (nq == 0) return VRS_OK;
+  const size_t smem = (size_t)std::max(ntile, 1) * sizeof(Cand);
+  if (smem > 200 * 1024) {
+    set_error(VRS_ERR_INVALID_CONFIG, "pivot tile count too large");
+    return VRS_ERR_INVALID_CONFIG;
+  }
+  VRS_CUDA(cudaFuncSetAttribute(tc_tau_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  tc_tau_kernel<<<nq, 256, smem, s>>>(tmin, ntile, nq, k, absm, init_bound);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms) {
+  TcPlan p;
+  p.qtiles = (nq + BM * NACC - 1) / (BM * NACC);
+  p.cap = 1024;
+  while (p.cap < 2 * kk + 2 * BN) p.cap *= 2;
+  const int64_t ntile_total = (n + BN - 1) / BN;
+  double best = 1e30;
+  p.nseg = 1;
+  for (int s = 1; s <= 32; s++) {
+    if (s > 1 && ntile_total / s < 8) break;
+    const double waves = (double)p.qtiles * s / num_sms;
+    const double cost = std::ceil(waves) / waves + 0.003 * s;
+    if (cost < best - 1e-9) {
+      best = cost;
+      p.nseg = s;
+    }
+  }
+  const int64_t tiles_per_seg = (ntile_total + p.nseg - 1) / p.nseg;
+  p.seg_len = std::max<int64_t>(1, tiles_per_seg) * BN;
+  p.nseg = (int)std::max<int64_t>(1, (n + p.seg_len - 1) / p.seg_len);
+  return p;
+}
+
+int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn,
+            int metric, int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow,
+            const float* absm, int* err, float* tmin, const float* init_bound, cudaStream_t s) {
+  if (n == 0 || nq == 0) return VRS_OK;
+  const int d16 = tc_d16(d);
+  CUtensorMap tmA, tmB;
+  VRS_TRY(make_tmap(&tmA, qb, nq_rows_alloc, d16));
+  VRS_TRY(make_tmap(&tmB, xb, n, d16));
+  TcScanArgs a;
+  a.xn = xn;
+  a.n = n;
+  a.nq = nq;
+  a.ksteps = (d + 15) / 16;
+  a.kblk = (d16 + KBW - 1) / KBW;
+  a.seg_len = p.seg_len;
+  a.cand = cand;
+  a.cnt = cnt;
+  a.overflow = overflow;
+  a.cap = p.cap;
+  a.k = kk;
+  a.mode = (metric == vrs_exact::kL2 || metric == vrs_exact::kMaha) ? 0 : 1;
+  a.absm = absm;
+  a.err = err;
+  a.tilemin = tmin != nullptr;
+  a.tmin = tmin;
+  a.init_bound = init_bound;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    VRS_CUDA(cudaFuncSetAttribute(knn_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)SMEM_TOTAL));
+    attr_set[dev] = true;
+  }
+  dim3 grid(p.qtiles, p.nseg);
+  knn_scan_tc_kernel<<<grid, THREADS, SMEM_TOTAL, s>>>(tmA, tmB, a);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+}  // namespace tc
+}  // namespace vrs

@@ -125,6 +125,8 @@ struct KnnSelectArgs {
   uint32_t* out_id;      // [nq][k] or null
   Cand* out_pairs;       // [nq][k] or null
   int max_sort;          // shared-memory sort capacity (power of two)
+  const uint32_t* tiny;  // rows always re-ranked exactly (cosine near-zero rows)
+  int n_tiny;
 };
 
 // Launchers (knn_kernels.cu).

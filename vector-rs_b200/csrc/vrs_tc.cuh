@@ -1,0 +1,52 @@
+// vrs_tc.cuh -- host-side interface of the tensor-core scan (knn_tc.cu).
+#pragma once
+#include "vrs_internal.cuh"
+
+namespace vrs {
+namespace tc {
+
+// Cosine rows or queries whose norm is below this go through the exact
+// path: for every other pair sqrt(|q|^2) * sqrt(|x|^2) >= 1e-8 > 1e-9, so
+// the reference's zero guard (crates/vector-simd/src/avx512.rs:218-221)
+// never fires on the tensor-core path.
+constexpr float kTinyNorm = 1e-4f;
+constexpr int kTinyCap = 2048;
+
+struct TcPlan {
+  int qtiles;
+  int nseg;
+  int64_t seg_len;
+  int cap;
+};
+
+bool tc_supported(int metric, int d);
+int tc_d16(int d);
+int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* xn,
+                 unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s);
+int tc_query_prep(const float* q, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
+                  void* qb, float* absm, int* overflow, cudaStream_t s);
+TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms);
+// With tmin != null this is the pivot pass (per-tile minima, no appends);
+// init_bound (nullable) seeds each query's acceptance bound.
+int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn,
+            int metric, int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow,
+            const float* absm, int* err, float* tmin, const float* init_bound, cudaStream_t s);
+int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, int d, void* pb,
+                    float* pn, cudaStream_t s);
+int tc_tau(const float* tmin, int ntile, int nq, int k, const float* absm, float* init_bound,
+           cudaStream_t s);
+// Rows in the pivot set (every stride-th row) for a shard of n rows.
+inline int64_t tc_pivot_rows(int64_t n, int64_t* stride) {
+  int64_t m = n / 16;
+  if (m < 65536) m = 65536;
+  if (m > 2000000) m = 2000000;
+  if (m >= n) {
+    *stride = 1;
+    return n;
+  }
+  *stride = n / m;
+  return n / *stride;
+}
+
+}  // namespace tc
+}  // namespace vrs
