@@ -384,16 +384,17 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   VRS_TRY(tc::tc_query_prep(s->q.as<float>(), nq, h->d, h->dp, h->metric, s->xmax.as<unsigned int>(),
                             s->qb.p, s->absm.as<float>(), s->overflow.as<int>(), st));
   tc::TcPlan p = tc::tc_plan(s->n_local, nq, kk, s->num_sms);
-  VRS_TRY(s->cand.reserve((size_t)p.nseg * nq * p.cap * sizeof(Cand)));
-  VRS_TRY(s->cnt.reserve((size_t)p.nseg * nq * sizeof(int)));
+  const int nlists = 2 * p.nseg;
+  VRS_TRY(s->cand.reserve((size_t)nlists * nq * p.cap * sizeof(Cand)));
+  VRS_TRY(s->cnt.reserve((size_t)nlists * nq * sizeof(int)));
   VRS_TRY(s->ibound.reserve((size_t)nq * sizeof(float)));
-  VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)p.nseg * nq * sizeof(int), st));
+  VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)nlists * nq * sizeof(int), st));
   if (s->n_local > 0) {
     // Pivot pass: per-query starting bound from the k-th smallest tile
     // minimum over every pivot_stride-th row.
     const void* pb = s->pivot_stride > 1 ? s->pb.p : s->xb.p;
     const float* pn = s->pivot_stride > 1 ? s->pn.as<float>() : s->xn.as<float>();
-    const int ntile = (int)((s->pivot_m + 127) / 128);
+    const int ntile = 2 * (int)((s->pivot_m + 127) / 128);  // half-tile minima
     tc::TcPlan pp = tc::tc_plan(s->pivot_m, nq, kk, s->num_sms);
     VRS_TRY(s->tmin.reserve((size_t)ntile * nq * sizeof(float)));
     ProfToken t0 = prof_begin("knn_pivot", st);
@@ -418,7 +419,7 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   sa.q_index = nullptr;
   sa.nq = nq;
   sa.k = kk;
-  sa.nseg = s->n_local > 0 ? p.nseg : 0;
+  sa.nseg = s->n_local > 0 ? nlists : 0;
   sa.cand = s->cand.as<Cand>();
   sa.cnt = s->cnt.as<int>();
   sa.overflow = s->overflow.as<int>();
@@ -431,11 +432,14 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   sa.out_dist = out_dist;
   sa.out_id = out_id;
   sa.out_pairs = out_pairs;
-  sa.max_sort = std::min(16384, next_pow2(std::max(512, p.nseg * (kk + 160) + s->n_tiny)));
+  sa.max_sort = std::min(16384, next_pow2(std::max(512, nlists * (kk + 160) + s->n_tiny)));
   sa.tiny = s->tiny.as<uint32_t>();
   sa.n_tiny = h->metric == vrs_exact::kCos ? s->n_tiny : 0;
   ProfToken t = prof_begin("knn_select", st);
-  VRS_TRY(launch_knn_select(sa, st));
+  if (nlists <= 32 && kk <= 256 && sa.n_tiny <= 256)
+    VRS_TRY(launch_knn_select_warp(sa, st));
+  else
+    VRS_TRY(launch_knn_select(sa, st));
   prof_end(t, st);
   return VRS_OK;
 }

@@ -14,6 +14,7 @@
 #include <float.h>
 
 #include "vrs_exact.cuh"
+#include "vrs_exact_lanes.cuh"
 #include "vrs_internal.cuh"
 #include "vrs_select.cuh"
 
@@ -216,6 +217,131 @@ __global__ void __launch_bounds__(256) knn_select_kernel(KnnSelectArgs a) {
   }
 }
 
+// ------------------------------------------------ select, warp per query
+// For approximate scans (tensor-core path): one warp per query. The k-th
+// best approximate score over the segment lists is found by a warp radix
+// select reading the lists in place; survivors within the acceptance bound
+// are copied to shared memory, re-ranked exactly by half-warps (the 16 lanes
+// are the reference's 16 SIMD lanes, loads coalesced), sorted by
+// (score, id) with a warp bitonic sort, and written out.
+constexpr int kSelWarps = 8;
+constexpr int kSelRmax = 512;
+
+template <int METRIC>
+__global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSelectArgs a) {
+  __shared__ int s_hist[kSelWarps][256];
+  __shared__ Cand s_buf[kSelWarps][kSelRmax];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = blockIdx.x * kSelWarps + warp;
+  if (slot >= a.nq) return;
+  if (a.overflow[slot]) return;
+  const int qrow = a.q_index ? a.q_index[slot] : slot;
+  Cand* buf = s_buf[warp];
+  int* hist = s_hist[warp];
+  const int cnt_l = lane < a.nseg ? a.cnt[(int64_t)lane * a.nq + slot] : 0;
+  int total = cnt_l;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFull, total, o);
+
+  float bound = INFINITY;
+  if (total > a.k) {
+    uint32_t prefix = 0, pmask = 0;
+    int kk = a.k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = lane; b < 256; b += 32) hist[b] = 0;
+      __syncwarp();
+      for (int sgm = 0; sgm < a.nseg; sgm++) {
+        const int cs = __shfl_sync(kFull, cnt_l, sgm);
+        const Cand* l = a.cand + ((int64_t)sgm * a.nq + slot) * a.cap;
+        for (int i = lane; i < cs; i += 32) {
+          const uint32_t v = ord_key(l[i].hs);
+          if ((v & pmask) == prefix) atomicAdd(&hist[(v >> shift) & 255], 1);
+        }
+      }
+      __syncwarp();
+      int digit, before;
+      warp_find_digit(hist, kk, &digit, &before);
+      kk -= before;
+      prefix |= (uint32_t)digit << shift;
+      pmask |= 0xffu << shift;
+      __syncwarp();
+    }
+    const float absm = a.kind == kAbsMargin ? a.absm[qrow] : 0.0f;
+    bound = accept_bound(a.kind, ord_inv(prefix), a.rho, absm);
+  }
+  // Survivors -> shared memory.
+  int R = 0;
+  for (int sgm = 0; sgm < a.nseg; sgm++) {
+    const int cs = __shfl_sync(kFull, cnt_l, sgm);
+    const Cand* l = a.cand + ((int64_t)sgm * a.nq + slot) * a.cap;
+    for (int base = 0; base < cs; base += 32) {
+      const int i = base + lane;
+      Cand e;
+      bool keep = false;
+      if (i < cs) {
+        e = l[i];
+        keep = e.hs <= bound;
+      }
+      const unsigned m = __ballot_sync(kFull, keep);
+      const int pos = R + __popc(m & ((1u << lane) - 1));
+      if (keep && pos < kSelRmax) buf[pos] = e;
+      R += __popc(m);
+    }
+  }
+  if (R + a.n_tiny > kSelRmax) {
+    if (lane == 0) a.overflow[slot] = 1;
+    return;
+  }
+  __syncwarp();
+  // Exact re-rank, two candidates per warp step (one per half-warp); rows
+  // without an error bound (near-zero cosine rows) are scored here too.
+  const float* qp = a.q + (int64_t)qrow * a.dp;
+  const float qa = METRIC == vrs_exact::kCos ? a.q_aux[qrow] : 0.0f;
+  const int half = lane >> 4, hl = lane & 15;
+  const int RT = R + a.n_tiny;
+  for (int it = 0; 2 * it < RT; it++) {
+    const int i = 2 * it + half;
+    const bool act = i < RT;
+    const int ii = act ? i : 2 * it;
+    const uint32_t row = ii < R ? buf[ii].id : a.tiny[ii - R];
+    const float xa = METRIC == vrs_exact::kCos ? a.base_aux[row] : 0.0f;
+    const float key = vrs_exact::lanes::rank_key(METRIC, qp, a.base + (int64_t)row * a.dp, a.d, qa, xa, hl);
+    __syncwarp();
+    if (act && hl == 0) buf[i] = Cand{vrs_exact::heap_score(METRIC, key), row};
+  }
+  __syncwarp();
+  int P = 32;
+  while (P < RT) P <<= 1;
+  for (int i = RT + lane; i < P; i += 32) buf[i] = Cand{INFINITY, 0xffffffffu};
+  __syncwarp();
+  for (int kb = 2; kb <= P; kb <<= 1) {
+    for (int j = kb >> 1; j > 0; j >>= 1) {
+      for (int i = lane; i < P; i += 32) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const bool asc = (i & kb) == 0;
+          const Cand x = buf[i], y = buf[ixj];
+          if (cand_less(y, x) == asc) {
+            buf[i] = y;
+            buf[ixj] = x;
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+  for (int r = lane; r < a.k; r += 32) {
+    const Cand e = r < RT ? buf[r] : Cand{INFINITY, 0xffffffffu};
+    const uint32_t gid = e.id == 0xffffffffu ? 0xffffffffu : e.id + a.id_offset;
+    if (a.out_pairs) a.out_pairs[(int64_t)qrow * a.k + r] = Cand{e.hs, gid};
+    if (a.out_dist) {
+      const float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
+      a.out_dist[(int64_t)qrow * a.k + r] = e.id == 0xffffffffu ? NAN : vrs_exact::finish(METRIC, key);
+      a.out_id[(int64_t)qrow * a.k + r] = gid;
+    }
+  }
+}
+
 // --------------------------------------------------------------- merge
 template <int METRIC>
 __global__ void __launch_bounds__(256) merge_pairs_kernel(const Cand* g, int nlists, int nq, int k,
@@ -316,6 +442,24 @@ struct SelectL {
 };
 
 template <int M>
+struct SelectWarpL {
+  static int run(const KnnSelectArgs& a, cudaStream_t s) {
+    if (M != vrs_exact::kL2 && M != vrs_exact::kMaha && M != vrs_exact::kDot && M != vrs_exact::kCos) {
+      set_error(VRS_ERR_INVALID_CONFIG, "warp select supports L2/Mahalanobis/dot/cosine");
+      return VRS_ERR_INVALID_CONFIG;
+    }
+    if (a.nseg > 32 || a.k > kSelRmax) {
+      set_error(VRS_ERR_INVALID_CONFIG, "warp select needs nseg <= 32 and k <= 512");
+      return VRS_ERR_INVALID_CONFIG;
+    }
+    knn_select_warp_kernel<M><<<(a.nq + kSelWarps - 1) / kSelWarps, kSelWarps * 32, 0, s>>>(a);
+    VRS_CUDA(cudaGetLastError());
+    count_launch();
+    return VRS_OK;
+  }
+};
+
+template <int M>
 struct MergeL {
   static int run(const Cand* g, int nlists, int nq, int k, float* od, uint32_t* oi, cudaStream_t s) {
     int P = 1;
@@ -351,6 +495,11 @@ int launch_knn_scan_exact(const KnnScanArgs& a, cudaStream_t s) {
 int launch_knn_select(const KnnSelectArgs& a, cudaStream_t s) {
   if (a.nq == 0) return VRS_OK;
   return dispatch_metric<SelectL>(a.metric, a, s);
+}
+
+int launch_knn_select_warp(const KnnSelectArgs& a, cudaStream_t s) {
+  if (a.nq == 0) return VRS_OK;
+  return dispatch_metric<SelectWarpL>(a.metric, a, s);
 }
 
 int launch_merge_pairs(const Cand* gathered, int nlists, int nq, int k, int metric, float* out_dist,

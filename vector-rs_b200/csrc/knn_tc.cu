@@ -41,8 +41,9 @@ constexpr int BN = 128;        // base rows per tile
 constexpr int KBW = 64;        // bf16 elements per K-block (one 128-byte swizzle row)
 constexpr int MAX_KBLK = 2;    // D <= 128 on this path
 constexpr int STAGES = 4;
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 16;   // 2 per (TMEM lane quadrant, accumulator): column halves
 constexpr int THREADS = 64 + EPI_WARPS * 32;
+constexpr int HALF_COLS = BN / 2;
 constexpr uint32_t BLK_A = BM * 128;  // bytes of one K-block of a 128-row tile
 constexpr uint32_t BLK_B = BN * 128;
 constexpr size_t SMEM_A = (size_t)NACC * MAX_KBLK * BLK_A;
@@ -60,32 +61,21 @@ struct TcScanArgs {
   int ksteps;        // ceil(D / 16)
   int kblk;          // ceil(D16 / 64)
   int64_t seg_len;   // multiple of BN
-  Cand* cand;        // [nseg][nq][cap]
-  int* cnt;          // [nseg][nq]
+  Cand* cand;        // [nseg * 2][nq][cap]: one list per (segment, column half, query)
+  int* cnt;          // [nseg * 2][nq]
   int* overflow;     // [nq]
   int cap;
   int k;
   int mode;          // 0: score = |x|^2 - 2 acc; 1: score = -acc
   const float* absm; // [nq]
   int* err;          // global error word (0 = ok)
-  // Pivot pass: instead of appending, write each tile's minimum score per
-  // query to tmin[tile][query] (tile = global 128-row tile index).
+  // Pivot pass: instead of appending, write each half tile's minimum score
+  // per query to tmin[2 * tile + half][query] (tile = global 128-row index).
   int tilemin;
   float* tmin;
   // Starting acceptance bound per query (null: +inf).
   const float* init_bound;
 };
-
-__device__ __forceinline__ float min32(const float* v) {
-  float m0 = fmin3(v[0], v[1], v[2]), m1 = fmin3(v[3], v[4], v[5]);
-  float m2 = fmin3(v[6], v[7], v[8]), m3 = fmin3(v[9], v[10], v[11]);
-  float m4 = fmin3(v[12], v[13], v[14]), m5 = fmin3(v[15], v[16], v[17]);
-  float m6 = fmin3(v[18], v[19], v[20]), m7 = fmin3(v[21], v[22], v[23]);
-  float m8 = fmin3(v[24], v[25], v[26]), m9 = fmin3(v[27], v[28], v[29]);
-  float a = fmin3(m0, m1, m2), b = fmin3(m3, m4, m5), c = fmin3(m6, m7, m8);
-  float d = fmin3(m9, v[30], v[31]);
-  return fminf(fmin3(a, b, c), d);
-}
 
 __global__ void __launch_bounds__(THREADS, 1)
     knn_scan_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -192,16 +182,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---------------------------------------------------- epilogue
+    // Warp e owns TMEM lane quadrant (warp % 4) of accumulator (e / 4) % 2
+    // and column half e / 8 of every tile: one thread = one query.
     const int ew = warp - 2;
-    const int acc = ew >> 2;
+    const int acc = (ew >> 2) & 1;
+    const int ch = ew >> 3;
     const int quad = warp & 3;
     const int q = q0 + acc * BM + quad * 32 + lane;
     const bool vq = q < a.nq;
-    Cand* list = a.cand + ((int64_t)blockIdx.y * a.nq + (vq ? q : 0)) * a.cap;
+    const int64_t list_id = ((int64_t)blockIdx.y * 2 + ch) * a.nq + (vq ? q : 0);
+    Cand* list = a.cand + list_id * a.cap;
     int count = 0;
     float bound = (vq && a.init_bound) ? a.init_bound[q] : INFINITY;
     const float absm = vq ? a.absm[q] : 0.0f;
-    float tile_min = INFINITY;
     int* hist = s_hist + ew * 256;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     for (int t = 0; t < ntiles; t++) {
@@ -209,13 +202,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool ok = mbar_wait(&tfull[b], (t >> 1) & 1, s_abort, a.err, 5, WAIT_NS);
       if (!__all_sync(sel::kFull, ok)) break;
       tc_fence_after();
-      const int64_t n0 = row_begin + (int64_t)t * BN;
+      const int64_t n0 = row_begin + (int64_t)t * BN + ch * HALF_COLS;
       const int64_t rem_cols = row_end - n0;
-      const int valid_cols = rem_cols < BN ? (int)rem_cols : BN;
+      const int valid_cols = rem_cols < HALF_COLS ? (int)(rem_cols > 0 ? rem_cols : 0) : HALF_COLS;
+      // Similarity mode keeps raw dot products and tests them against
+      // -bound (score = -acc); L2 mode forms the score |x|^2 - 2 acc.
+      const float nbound = -bound;
+      float tile_min = INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
+      for (int c = 0; c < HALF_COLS / 32; c++) {
         float v[32];
-        tmem_ld32(tmem + lane_base + acc * 256 + b * BN + c * 32, v);
+        tmem_ld32(tmem + lane_base + acc * 256 + b * BN + ch * HALF_COLS + c * 32, v);
+        const int cb = valid_cols - c * 32;
         if (a.mode == 0) {
           const float4* xp = reinterpret_cast<const float4*>(a.xn + n0 + c * 32);
 #pragma unroll
@@ -226,22 +224,56 @@ __global__ void __launch_bounds__(THREADS, 1)
             v[4 * j4 + 2] = fmaf(-2.0f, v[4 * j4 + 2], x4.z);
             v[4 * j4 + 3] = fmaf(-2.0f, v[4 * j4 + 3], x4.w);
           }
-        } else {
+          if (cb < 32) {
 #pragma unroll
-          for (int j = 0; j < 32; j++) v[j] = -v[j];
-        }
-        const int cb = valid_cols - c * 32;
-        if (cb < 32) {
+            for (int j = 0; j < 32; j++)
+              if (j >= cb) v[j] = INFINITY;
+          }
+        } else if (cb < 32) {
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            if (j >= cb) v[j] = INFINITY;
+            if (j >= cb) v[j] = -INFINITY;
         }
-        const float m = min32(v);
-        tile_min = fminf(tile_min, m);
-        if (!a.tilemin && vq && m <= bound) {
+        // Extremum (score-wise best) of each group of 4 columns.
+        float g[8];
+        if (a.mode == 0) {
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            if (j < cb && v[j] <= bound) list[count++] = Cand{v[j], (uint32_t)(n0 + c * 32 + j)};
+          for (int i = 0; i < 8; i++)
+            g[i] = fminf(fminf(v[4 * i], v[4 * i + 1]), fminf(v[4 * i + 2], v[4 * i + 3]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            g[i] = fmaxf(fmaxf(v[4 * i], v[4 * i + 1]), fmaxf(v[4 * i + 2], v[4 * i + 3]));
+        }
+        if (a.tilemin) {
+          float hm = g[0];
+          if (a.mode == 0) {
+#pragma unroll
+            for (int i = 1; i < 8; i++) hm = fminf(hm, g[i]);
+            tile_min = fminf(tile_min, hm);
+          } else {
+#pragma unroll
+            for (int i = 1; i < 8; i++) hm = fmaxf(hm, g[i]);
+            tile_min = fminf(tile_min, -hm);
+          }
+          continue;
+        }
+        // One ballot per group (independent); only groups where some lane
+        // passes take the append path.
+        unsigned gb[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          gb[i] = __ballot_sync(sel::kFull, vq && (a.mode == 0 ? g[i] <= bound : g[i] >= nbound));
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (gb[i]) {
+            const bool gp = (gb[i] >> lane) & 1u;
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+              const int j = 4 * i + jj;
+              const float sc = a.mode == 0 ? v[j] : -v[j];
+              if (gp && j < cb && sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + c * 32 + j)};
+            }
           }
         }
       }
@@ -249,12 +281,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
       if (a.tilemin) {
-        if (vq) a.tmin[(row_begin / BN + t) * (int64_t)a.nq + q] = tile_min;
-        tile_min = INFINITY;
+        if (vq) a.tmin[((row_begin / BN + t) * 2 + ch) * (int64_t)a.nq + q] = tile_min;
         continue;
       }
       // Shrink lists that could overflow on the next tile.
-      unsigned need = __ballot_sync(sel::kFull, vq && count > a.cap - BN);
+      unsigned need = __ballot_sync(sel::kFull, vq && count > a.cap - HALF_COLS);
       while (need) {
         const int l = __ffs(need) - 1;
         need &= need - 1;
@@ -270,7 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == l) {
           count = nc;
           bound = bnd;
-          if (nc > a.cap - BN) {
+          if (nc > a.cap - HALF_COLS) {
             a.overflow[q] = 1;
             count = 0;
             bound = -INFINITY;
@@ -278,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-    if (vq && !a.tilemin) a.cnt[(int64_t)blockIdx.y * a.nq + q] = count;
+    if (vq && !a.tilemin) a.cnt[list_id] = count;
     if (vq && *s_abort) a.overflow[q] = 1;
   }
   tc_fence_before();
@@ -498,7 +529,7 @@ TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms) {
   const int64_t ntile_total = (n + BN - 1) / BN;
   double best = 1e30;
   p.nseg = 1;
-  for (int s = 1; s <= 32; s++) {
+  for (int s = 1; s <= 16; s++) {
     if (s > 1 && ntile_total / s < 8) break;
     const double waves = (double)p.qtiles * s / num_sms;
     const double cost = std::ceil(waves) / waves + 0.003 * s;

@@ -57,13 +57,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                                           int* gerr, int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (;;) {
+  for (uint32_t i = 1;; i++) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (globaltimer_ns() - t0 > limit_ns) {
-      *abort = code;
-      atomicCAS(gerr, 0, code);
-      return false;
+    if ((i & 63) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        *abort = code;
+        atomicCAS(gerr, 0, code);
+        return false;
+      }
     }
   }
 }
@@ -141,6 +143,30 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 64 consecutive 32-bit columns (two x32 loads, one wait).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t r[64];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[32 * h + 0]), "=r"(r[32 * h + 1]), "=r"(r[32 * h + 2]), "=r"(r[32 * h + 3]),
+          "=r"(r[32 * h + 4]), "=r"(r[32 * h + 5]), "=r"(r[32 * h + 6]), "=r"(r[32 * h + 7]),
+          "=r"(r[32 * h + 8]), "=r"(r[32 * h + 9]), "=r"(r[32 * h + 10]), "=r"(r[32 * h + 11]),
+          "=r"(r[32 * h + 12]), "=r"(r[32 * h + 13]), "=r"(r[32 * h + 14]), "=r"(r[32 * h + 15]),
+          "=r"(r[32 * h + 16]), "=r"(r[32 * h + 17]), "=r"(r[32 * h + 18]), "=r"(r[32 * h + 19]),
+          "=r"(r[32 * h + 20]), "=r"(r[32 * h + 21]), "=r"(r[32 * h + 22]), "=r"(r[32 * h + 23]),
+          "=r"(r[32 * h + 24]), "=r"(r[32 * h + 25]), "=r"(r[32 * h + 26]), "=r"(r[32 * h + 27]),
+          "=r"(r[32 * h + 28]), "=r"(r[32 * h + 29]), "=r"(r[32 * h + 30]), "=r"(r[32 * h + 31])
+        : "r"(taddr + 32 * h));
+  }
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle,
 // 8-row groups 1024 bytes apart (SBO), LBO unused (1), descriptor version 1.
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
@@ -163,10 +189,15 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);
 }
 
-// Three-input minimum (PTX ISA 8.8, sm_100+).
+// Three-input minimum / maximum (PTX ISA 8.8, sm_100+).
 __device__ __forceinline__ float fmin3(float a, float b, float c) {
   float r;
   asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
 }
 

@@ -1,0 +1,100 @@
+// vrs_exact_lanes.cuh -- the reference's AVX-512 pair arithmetic computed by
+// a half-warp: lane l (0..15) plays SIMD lane l, loads are coalesced, and the
+// horizontal add is a shuffle halving tree (xor 8, 4, 2, 1), which pairs the
+// same elements as _mm512_reduce_add_ps. Results are bit-identical to
+// vrs_exact.cuh (and to crates/vector-simd/src/avx512.rs). Every lane of the
+// half-warp returns the same value; all 16 lanes must call together.
+#pragma once
+#include "vrs_exact.cuh"
+
+namespace vrs_exact {
+namespace lanes {
+
+__device__ __forceinline__ float hsum16(float v) {
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8, 16));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4, 16));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2, 16));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1, 16));
+  return v;
+}
+
+// avx512::dot_product (avx512.rs:23-76)
+__device__ __forceinline__ float dot(const float* __restrict__ a, const float* __restrict__ b, int n,
+                                     int l) {
+  float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+  const int chunks = n / 64;
+  for (int c = 0; c < chunks; c++) {
+    const float* pa = a + c * 64 + l;
+    const float* pb = b + c * 64 + l;
+    s0 = __fmaf_rn(pa[0], pb[0], s0);
+    s1 = __fmaf_rn(pa[16], pb[16], s1);
+    s2 = __fmaf_rn(pa[32], pb[32], s2);
+    s3 = __fmaf_rn(pa[48], pb[48], s3);
+  }
+  int i = chunks * 64;
+  for (; i + 16 <= n; i += 16) s0 = __fmaf_rn(a[i + l], b[i + l], s0);
+  float r = hsum16(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
+  for (; i < n; i++) r = __fadd_rn(r, __fmul_rn(a[i], b[i]));
+  return r;
+}
+
+// avx512::l2_squared (avx512.rs:87-148)
+__device__ __forceinline__ float l2(const float* __restrict__ a, const float* __restrict__ b, int n,
+                                    int l) {
+  float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+  const int chunks = n / 64;
+  for (int c = 0; c < chunks; c++) {
+    const float* pa = a + c * 64 + l;
+    const float* pb = b + c * 64 + l;
+    float d0 = __fsub_rn(pa[0], pb[0]), d1 = __fsub_rn(pa[16], pb[16]);
+    float d2 = __fsub_rn(pa[32], pb[32]), d3 = __fsub_rn(pa[48], pb[48]);
+    s0 = __fmaf_rn(d0, d0, s0);
+    s1 = __fmaf_rn(d1, d1, s1);
+    s2 = __fmaf_rn(d2, d2, s2);
+    s3 = __fmaf_rn(d3, d3, s3);
+  }
+  int i = chunks * 64;
+  for (; i + 16 <= n; i += 16) {
+    float d = __fsub_rn(a[i + l], b[i + l]);
+    s0 = __fmaf_rn(d, d, s0);
+  }
+  float r = hsum16(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
+  for (; i < n; i++) {
+    float d = __fsub_rn(a[i], b[i]);
+    r = __fadd_rn(r, __fmul_rn(d, d));
+  }
+  return r;
+}
+
+// Dot product in the cosine kernel's order (avx512.rs:161-223).
+__device__ __forceinline__ float cos_dot(const float* __restrict__ a, const float* __restrict__ b,
+                                         int n, int l) {
+  float s0 = 0.0f, s1 = 0.0f;
+  const int chunks = n / 32;
+  for (int c = 0; c < chunks; c++) {
+    const float* pa = a + c * 32 + l;
+    const float* pb = b + c * 32 + l;
+    s0 = __fmaf_rn(pa[0], pb[0], s0);
+    s1 = __fmaf_rn(pa[16], pb[16], s1);
+  }
+  int i = chunks * 32;
+  for (; i + 16 <= n; i += 16) s0 = __fmaf_rn(a[i + l], b[i + l], s0);
+  float r = hsum16(__fadd_rn(s0, s1));
+  for (; i < n; i++) r = __fadd_rn(r, __fmul_rn(a[i], b[i]));
+  return r;
+}
+
+// Rank key for the metrics re-ranked by lanes (others are scanned exactly).
+__device__ __forceinline__ float rank_key(int metric, const float* a, const float* b, int n, float na,
+                                          float nb, int l) {
+  switch (metric) {
+    case kL2:
+    case kMaha: return l2(a, b, n, l);
+    case kDot: return dot(a, b, n, l);
+    case kCos: return cos_finish(cos_dot(a, b, n, l), na, nb);
+  }
+  return 0.0f;
+}
+
+}  // namespace lanes
+}  // namespace vrs_exact

@@ -132,6 +132,9 @@ struct KnnSelectArgs {
 // Launchers (knn_kernels.cu).
 int launch_knn_scan_exact(const KnnScanArgs& a, cudaStream_t s);
 int launch_knn_select(const KnnSelectArgs& a, cudaStream_t s);
+// Warp-per-query select with half-warp exact re-rank (approximate scans of
+// L2 / Mahalanobis / dot / cosine; nseg <= 32, k <= 512).
+int launch_knn_select_warp(const KnnSelectArgs& a, cudaStream_t s);
 int launch_merge_pairs(const Cand* gathered, int nlists, int nq, int k, int metric,
                        float* out_dist, uint32_t* out_id, cudaStream_t s);
 int launch_pad_rows(const float* src, int64_t rows, int d, int dp, float* dst, int transform,

@@ -12,6 +12,8 @@ namespace tc {
 constexpr float kTinyNorm = 1e-4f;
 constexpr int kTinyCap = 2048;
 
+// Each segment keeps two candidate lists per query (one per column half of
+// every tile), so a plan with nseg segments has 2 * nseg lists per query.
 struct TcPlan {
   int qtiles;
   int nseg;
@@ -37,9 +39,9 @@ int tc_tau(const float* tmin, int ntile, int nq, int k, const float* absm, float
            cudaStream_t s);
 // Rows in the pivot set (every stride-th row) for a shard of n rows.
 inline int64_t tc_pivot_rows(int64_t n, int64_t* stride) {
-  int64_t m = n / 16;
+  int64_t m = n / 6;
   if (m < 65536) m = 65536;
-  if (m > 2000000) m = 2000000;
+  if (m > 1600000) m = 1600000;
   if (m >= n) {
     *stride = 1;
     return n;
