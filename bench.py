@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--n-base", type=int, default=N_BASE)
     ap.add_argument("--n-query", type=int, default=N_QUERY)
+    ap.add_argument("--km-n", type=int, default=KM_N, help="k-means points (C3: 1,000,000)")
+    ap.add_argument("--km-iters", type=int, default=KM_ITERS)
+    ap.add_argument("--no-knn", action="store_true", help="skip the kNN measurement")
     return ap.parse_args()
 
 
@@ -326,8 +329,9 @@ def main():
     # ------------------------------------------------------- k-means (C3)
     if not args.no_kmeans:
         km_seed = vc.config_seed(2)
-        kchunk = -(-KM_N // world)
-        k0, k1 = min(KM_N, rank * kchunk), min(KM_N, (rank + 1) * kchunk)
+        KMN = args.km_n
+        kchunk = -(-KMN // world)
+        k0, k1 = min(KMN, rank * kchunk), min(KMN, (rank + 1) * kchunk)
         cent = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)
         vc.gen_rows_device(vc.GEN_NORMAL, km_seed, 2, 0, KM_K, KM_D, cent.data_ptr())
         xs = torch.empty((max(k1 - k0, 1), KM_D), dtype=torch.float32, device=dev)
@@ -338,13 +342,13 @@ def main():
                            cent.data_ptr(), KM_K, KM_SIGMA)
         init_h = init.cpu().numpy()
         torch.cuda.synchronize()
-        vc.kmeans_fit_rank(comm, None, KM_N, KM_D, KM_K, init_h, 2, 0.0,
+        vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, 2, 0.0,
                            vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(), n_local=k1 - k0)
         barrier()
         vc.profile_reset()
         vc.profile_enable(True)
         t0 = time.perf_counter()
-        res = vc.kmeans_fit_rank(comm, None, KM_N, KM_D, KM_K, init_h, KM_ITERS, 0.0,
+        res = vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, args.km_iters, 0.0,
                                  vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(),
                                  n_local=k1 - k0)
         barrier()

@@ -16,6 +16,7 @@
 
 #include "vrs_exact.cuh"
 #include "vrs_internal.cuh"
+#include "vrs_kmeans_tc.cuh"
 #include "vrs_tc.cuh"
 
 namespace vrs {
@@ -852,14 +853,20 @@ constexpr int kSumSlots = 513;  // launch_sum_f64 partials + result
 
 struct KmShard {
   int device = 0;
+  int num_sms = 148;
   cudaStream_t stream = nullptr;
   ncclComm_t comm = nullptr;
   int64_t n_local = 0;
   DBuf x, xr, x_aux, assign, dist, acc, cent, cent_r, cent_aux, shift, scal, red;
+  // tensor-core assignment operands
+  bool use_tc = false;
+  DBuf xb, xq, xtiny, cb, cn, cmax, res, cands, err, ctiny;
+  DBuf segws;  // counting-sort workspace of the centroid sums
   ~KmShard() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
-    for (DBuf* b : {&x, &xr, &x_aux, &assign, &dist, &acc, &cent, &cent_r, &cent_aux, &shift, &scal, &red})
+    for (DBuf* b : {&x, &xr, &x_aux, &assign, &dist, &acc, &cent, &cent_r, &cent_aux, &shift, &scal, &red, &xb,
+                    &xq, &xtiny, &cb, &cn, &cmax, &res, &cands, &err, &ctiny, &segws})
       b->release();
     if (stream) cudaStreamDestroy(stream);
   }
@@ -905,6 +912,25 @@ int km_prepare_shard(const KmParams& P, KmShard* s, const float* rows, int mem) 
     }
     if (P.metric == vrs_exact::kCos)
       VRS_TRY(launch_cos_norms(s->x.as<float>(), s->n_local, P.d, P.dp, s->x_aux.as<float>(), s->stream));
+  }
+  VRS_CUDA(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, s->device));
+  if (kmtc::supported(P.metric, P.d) && !getenv("VRS_DISABLE_TC") && s->n_local > 0) {
+    const int d16 = (P.d + 15) / 16 * 16;
+    const int64_t kpad = (P.k + 127) / 128 * 128 + 128;
+    VRS_TRY(s->xb.reserve((size_t)s->n_local * d16 * 2));
+    VRS_TRY(s->xq.reserve(nx * sizeof(float)));
+    VRS_TRY(s->xtiny.reserve(nx * sizeof(int)));
+    VRS_TRY(s->cb.reserve((size_t)P.k * d16 * 2));
+    VRS_TRY(s->cn.reserve((size_t)kpad * sizeof(float)));
+    VRS_TRY(s->cmax.reserve(2 * sizeof(unsigned int)));
+    VRS_TRY(s->ctiny.reserve(sizeof(int)));
+    VRS_TRY(s->res.reserve(nx * 2 * sizeof(kmtc::Res)));
+    VRS_TRY(s->cands.reserve(nx * 2 * 4 * sizeof(Cand)));
+    VRS_TRY(s->err.reserve(sizeof(int)));
+    VRS_CUDA(cudaMemsetAsync(s->cn.p, 0, (size_t)kpad * sizeof(float), s->stream));
+    VRS_TRY(kmtc::prep_rows(s->x.as<float>(), s->n_local, P.d, P.dp, P.metric, s->xb.p, nullptr,
+                            s->xq.as<float>(), nullptr, s->xtiny.as<int>(), nullptr, s->stream));
+    s->use_tc = true;
   }
   return VRS_OK;
 }
@@ -967,15 +993,53 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
       }
       if (P.metric == vrs_exact::kCos)
         VRS_TRY(launch_cos_norms(s->cent.as<float>(), P.k, P.d, P.dp, s->cent_aux.as<float>(), s->stream));
-      ProfToken t = prof_begin("kmeans_assign", s->stream);
-      VRS_TRY(launch_kmeans_assign_exact(x_ops, s->n_local, P.d, P.dp, cent_ops, s->cent_aux.as<float>(),
-                                         s->x_aux.as<float>(), P.k, P.metric, s->assign.as<int32_t>(),
-                                         s->dist.as<float>(), s->stream));
-      prof_end(t, s->stream);
+      bool tc_done = false;
+      if (s->use_tc) {
+        // Centroid operands for this iteration; a near-zero cosine centroid
+        // sends the iteration to the exact path.
+        int any_tiny = 0;
+        VRS_CUDA(cudaMemsetAsync(s->cmax.p, 0, 2 * sizeof(unsigned int), s->stream));
+        VRS_CUDA(cudaMemsetAsync(s->ctiny.p, 0, sizeof(int), s->stream));
+        VRS_TRY(kmtc::prep_rows(s->cent.as<float>(), P.k, P.d, P.dp, P.metric, s->cb.p,
+                                (P.metric == vrs_exact::kL2 || P.metric == vrs_exact::kMaha) ? s->cn.as<float>()
+                                                                                              : nullptr,
+                                nullptr, s->cmax.as<unsigned int>(), nullptr, s->ctiny.as<int>(), s->stream));
+        if (P.metric == vrs_exact::kCos) {
+          VRS_CUDA(cudaMemcpyAsync(&any_tiny, s->ctiny.p, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+          VRS_CUDA(cudaStreamSynchronize(s->stream));
+        }
+        if (!any_tiny) {
+          VRS_CUDA(cudaMemsetAsync(s->err.p, 0, sizeof(int), s->stream));
+          ProfToken t = prof_begin("kmeans_assign", s->stream);
+          VRS_TRY(kmtc::assign(s->xb.p, s->n_local, s->cb.p, P.k, P.d, s->cn.as<float>(), s->xq.as<float>(),
+                               s->cmax.as<unsigned int>(), P.metric, s->res.as<kmtc::Res>(), s->cands.as<Cand>(),
+                               s->err.as<int>(), s->num_sms, s->stream));
+          prof_end(t, s->stream);
+          ProfToken t2 = prof_begin("kmeans_finalize", s->stream);
+          VRS_TRY(kmtc::finalize(s->x.as<float>(), s->n_local, P.d, P.dp, s->cent.as<float>(),
+                                 s->cent_aux.as<float>(), s->x_aux.as<float>(), P.k, s->xq.as<float>(),
+                                 s->cmax.as<unsigned int>(), P.metric, s->res.as<kmtc::Res>(),
+                                 s->cands.as<Cand>(),
+                                 P.metric == vrs_exact::kCos ? s->xtiny.as<int>() : nullptr,
+                                 s->assign.as<int32_t>(), s->dist.as<float>(), s->stream));
+          prof_end(t2, s->stream);
+          tc_done = true;
+        }
+      }
+      if (!tc_done) {
+        ProfToken t = prof_begin("kmeans_assign", s->stream);
+        VRS_TRY(launch_kmeans_assign_exact(x_ops, s->n_local, P.d, P.dp, cent_ops, s->cent_aux.as<float>(),
+                                           s->x_aux.as<float>(), P.k, P.metric, s->assign.as<int32_t>(),
+                                           s->dist.as<float>(), s->stream));
+        prof_end(t, s->stream);
+      }
       VRS_CUDA(cudaMemsetAsync(s->acc.p, 0, acc_elems * sizeof(unsigned long long), s->stream));
       unsigned long long* sums = s->acc.as<unsigned long long>();
-      VRS_TRY(launch_kmeans_accumulate(s->x.as<float>(), s->n_local, P.d, P.dp, s->assign.as<int32_t>(), P.k,
-                                       scale_exp, sums, sums + (size_t)P.k * P.dp, s->stream));
+      VRS_TRY(s->segws.reserve(kmeans_segsum_ws_bytes(s->n_local, P.k)));
+      ProfToken ts = prof_begin("kmeans_sums", s->stream);
+      VRS_TRY(launch_kmeans_segsum(s->x.as<float>(), s->n_local, P.d, P.dp, s->assign.as<int32_t>(), P.k,
+                                   scale_exp, sums, sums + (size_t)P.k * P.dp, s->segws.as<int>(), s->stream));
+      prof_end(ts, s->stream);
     }
     if (coll) {
       VRS_NCCL(ncclGroupStart());
@@ -997,6 +1061,15 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
     for (KmShard* s : shards) {
       VRS_CUDA(cudaSetDevice(s->device));
       VRS_TRY(stream_wait(s->stream, coll ? s->comm : nullptr, tmo));
+    }
+    for (KmShard* s : shards) {
+      if (!s->use_tc) continue;
+      int err = 0;
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_CUDA(cudaMemcpy(&err, s->err.p, sizeof(int), cudaMemcpyDeviceToHost));
+      if (err)
+        return fail(VRS_ERR_TIMEOUT, "tensor-core k-means assignment gave up waiting (stage code " +
+                                         std::to_string(err) + ")");
     }
     VRS_CUDA(cudaSetDevice(shards[0]->device));
     VRS_CUDA(cudaMemcpy(&max_shift, shards[0]->scal.as<float>() + 1, sizeof(float), cudaMemcpyDeviceToHost));

@@ -89,6 +89,48 @@ __global__ void kmeans_update_kernel(const unsigned long long* __restrict__ sums
   atomicMax(reinterpret_cast<unsigned int*>(max_shift), __float_as_uint(sh));
 }
 
+// Warp per cluster: means in parallel, then the squared shift summed over
+// dimensions in order (f32, separate multiply and add, kmeans.rs:318-331).
+__global__ void kmeans_update_warp_kernel(const unsigned long long* __restrict__ sums,
+                                          const unsigned long long* __restrict__ counts, int k, int d,
+                                          int dp, int scale_exp, float* __restrict__ cent,
+                                          float* __restrict__ shift, float* __restrict__ max_shift) {
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (c >= k) return;
+  const unsigned long long cnt = counts[c];
+  if (cnt == 0) {
+    if (lane == 0) shift[c] = 0.0f;
+    return;
+  }
+  const double inv_scale = ldexp(1.0, -scale_exp);
+  float diff[8];
+#pragma unroll
+  for (int jj = 0; jj < 8; jj++) {
+    const int j = jj * 32 + lane;
+    diff[jj] = 0.0f;
+    if (j < d) {
+      const double sum = (double)(long long)sums[(int64_t)c * dp + j] * inv_scale;
+      const float val = (float)(sum / (double)cnt);
+      diff[jj] = __fsub_rn(val, cent[(int64_t)c * dp + j]);
+      cent[(int64_t)c * dp + j] = val;
+    }
+  }
+  float sh = 0.0f;
+#pragma unroll
+  for (int jj = 0; jj < 8; jj++) {
+    if (jj * 32 >= d) break;
+    for (int t = 0; t < 32; t++) {
+      const float dj = __shfl_sync(0xffffffffu, diff[jj], t);
+      if (jj * 32 + t < d) sh = __fadd_rn(sh, __fmul_rn(dj, dj));
+    }
+  }
+  if (lane == 0) {
+    shift[c] = sh;
+    atomicMax(reinterpret_cast<unsigned int*>(max_shift), __float_as_uint(sh));
+  }
+}
+
 __global__ void abs_max_kernel(const float* __restrict__ x, int64_t n, int d, int dp,
                                unsigned int* __restrict__ out) {
   float m = 0.0f;
@@ -100,6 +142,114 @@ __global__ void abs_max_kernel(const float* __restrict__ x, int64_t n, int d, in
   }
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+// ---------------------------------------------- segmented centroid sums
+// Points are bucketed by cluster (counting sort), then each chunk of at
+// most kChunk points of one cluster is summed by one block in 64-bit fixed
+// point and added to the cluster's sums with one integer atomic per
+// dimension. Integer addition is associative, so the result does not
+// depend on the order of points or blocks.
+constexpr int kChunk = 2048;
+
+__global__ void km_count_kernel(const int32_t* __restrict__ assign, int64_t n, int* __restrict__ counts) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < n) atomicAdd(&counts[assign[i]], 1);
+}
+
+// Single block: exclusive scans of counts (point offsets) and of the chunk
+// counts ceil(count / kChunk) (chunk offsets); zeroes the scatter cursors.
+__global__ void km_scan_kernel(const int* __restrict__ counts, int k, int* __restrict__ off,
+                               int* __restrict__ coff, int* __restrict__ cursor) {
+  __shared__ int s_a[1024], s_b[1024];
+  const int t = threadIdx.x;
+  const int per = (k + 1023) / 1024;
+  int a = 0, b = 0;
+  for (int j = 0; j < per; j++) {
+    int c = t * per + j;
+    if (c < k) {
+      a += counts[c];
+      b += (counts[c] + kChunk - 1) / kChunk;
+    }
+  }
+  s_a[t] = a;
+  s_b[t] = b;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    int va = t >= o ? s_a[t - o] : 0, vb = t >= o ? s_b[t - o] : 0;
+    __syncthreads();
+    s_a[t] += va;
+    s_b[t] += vb;
+    __syncthreads();
+  }
+  int ra = s_a[t] - a, rb = s_b[t] - b;
+  for (int j = 0; j < per; j++) {
+    int c = t * per + j;
+    if (c < k) {
+      off[c] = ra;
+      coff[c] = rb;
+      cursor[c] = 0;
+      ra += counts[c];
+      rb += (counts[c] + kChunk - 1) / kChunk;
+    }
+  }
+  if (t == 1023) {
+    off[k] = s_a[t];
+    coff[k] = s_b[t];
+  }
+}
+
+__global__ void km_scatter_kernel(const int32_t* __restrict__ assign, int64_t n, const int* __restrict__ off,
+                                  int* __restrict__ cursor, int32_t* __restrict__ perm) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < n) {
+    const int c = assign[i];
+    perm[off[c] + atomicAdd(&cursor[c], 1)] = (int32_t)i;
+  }
+}
+
+// One block (4 warps) per chunk; lane l of a warp owns dimensions l + 32 j.
+template <int NJ>
+__global__ void __launch_bounds__(128) km_chunk_sum_kernel(
+    const float* __restrict__ x, int d, int dp, int k, const int* __restrict__ off,
+    const int* __restrict__ coff, const int32_t* __restrict__ perm, int scale_exp,
+    unsigned long long* __restrict__ sums) {
+  __shared__ long long s_part[4][NJ * 32];
+  const int b = blockIdx.x;
+  if (b >= coff[k]) return;
+  int lo = 0, hi = k;  // cluster c with coff[c] <= b < coff[c+1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (coff[mid] <= b) lo = mid; else hi = mid;
+  }
+  const int c = lo;
+  const int p0 = off[c] + (b - coff[c]) * kChunk;
+  const int p1 = min(off[c + 1], p0 + kChunk);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long acc[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; j++) acc[j] = 0;
+  const double scale = ldexp(1.0, scale_exp);
+  for (int p = p0 + warp; p < p1; p += 4) {
+    const float* v = x + (int64_t)perm[p] * dp;
+#pragma unroll
+    for (int j = 0; j < NJ; j++) {
+      const int e = lane + 32 * j;
+      if (e < d) acc[j] += __double2ll_rn((double)v[e] * scale);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NJ; j++) s_part[warp][lane + 32 * j] = acc[j];
+  __syncthreads();
+  for (int e = threadIdx.x; e < d; e += 128) {
+    const long long t = s_part[0][e] + s_part[1][e] + s_part[2][e] + s_part[3][e];
+    if (t) atomicAdd(&sums[(int64_t)c * dp + e], (unsigned long long)t);
+  }
+}
+
+__global__ void km_counts_u64_kernel(const int* __restrict__ counts, int k, unsigned long long* __restrict__ out) {
+  int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < k) out[c] = (unsigned long long)counts[c];
 }
 
 constexpr int kSumBlocks = 512;
@@ -180,12 +330,44 @@ int launch_kmeans_accumulate(const float* x, int64_t n, int d, int dp, const int
   return VRS_OK;
 }
 
+int launch_kmeans_segsum(const float* x, int64_t n, int d, int dp, const int32_t* assign, int k,
+                         int scale_exp, unsigned long long* sums, unsigned long long* counts, int* ws,
+                         cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  if (d > 256) return launch_kmeans_accumulate(x, n, d, dp, assign, k, scale_exp, sums, counts, s);
+  int* cnt = ws;                // [k]
+  int* off = cnt + k;           // [k+1]
+  int* coff = off + k + 1;      // [k+1]
+  int* cursor = coff + k + 1;   // [k]
+  int32_t* perm = cursor + k;   // [n]
+  VRS_CUDA(cudaMemsetAsync(cnt, 0, (size_t)k * sizeof(int), s));
+  const unsigned nb = (unsigned)((n + 255) / 256);
+  km_count_kernel<<<nb, 256, 0, s>>>(assign, n, cnt);
+  km_scan_kernel<<<1, 1024, 0, s>>>(cnt, k, off, coff, cursor);
+  km_scatter_kernel<<<nb, 256, 0, s>>>(assign, n, off, cursor, perm);
+  const unsigned nchunks = (unsigned)((n + kChunk - 1) / kChunk + k);
+  if (d <= 128)
+    km_chunk_sum_kernel<4><<<nchunks, 128, 0, s>>>(x, d, dp, k, off, coff, perm, scale_exp, sums);
+  else
+    km_chunk_sum_kernel<8><<<nchunks, 128, 0, s>>>(x, d, dp, k, off, coff, perm, scale_exp, sums);
+  km_counts_u64_kernel<<<(k + 255) / 256, 256, 0, s>>>(cnt, k, counts);
+  VRS_CUDA(cudaGetLastError());
+  count_launch(5);
+  return VRS_OK;
+}
+
+size_t kmeans_segsum_ws_bytes(int64_t n, int k) { return ((size_t)4 * k + 2 + (size_t)n) * sizeof(int); }
+
 int launch_kmeans_update(const unsigned long long* sums, const unsigned long long* counts, int k,
                          int d, int dp, int scale_exp, float* cent, float* shift, float* max_shift,
                          cudaStream_t s) {
   VRS_CUDA(cudaMemsetAsync(max_shift, 0, sizeof(float), s));
-  kmeans_update_kernel<<<(k + 127) / 128, 128, 0, s>>>(sums, counts, k, d, dp, scale_exp, cent,
-                                                       shift, max_shift);
+  if (d <= 256)
+    kmeans_update_warp_kernel<<<(unsigned)(((int64_t)k * 32 + 127) / 128), 128, 0, s>>>(
+        sums, counts, k, d, dp, scale_exp, cent, shift, max_shift);
+  else
+    kmeans_update_kernel<<<(k + 127) / 128, 128, 0, s>>>(sums, counts, k, d, dp, scale_exp, cent,
+                                                         shift, max_shift);
   VRS_CUDA(cudaGetLastError());
     count_launch();
   return VRS_OK;

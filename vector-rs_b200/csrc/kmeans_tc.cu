@@ -1,0 +1,527 @@
+// kmeans_tc.cu -- tensor-core (tcgen05) k-means assignment for the GEMM-form
+// metrics (squared L2, Mahalanobis, dot, cosine).
+//
+// Persistent CTAs loop over tiles of 256 points (two M=128 bf16 operand
+// tiles, loaded by TMA); the K centroids stream through a 4-stage TMA ring
+// as 128-row bf16 tiles; one thread issues tcgen05.mma into two 128x128 f32
+// TMEM accumulators (double-buffered). Sixteen epilogue warps (one thread =
+// one point, two warps per point splitting each tile's columns) keep the
+// approximate best centroid and every centroid whose approximate score is
+// within the point's error margin of it (at most 4, else the point is
+// flagged). kmeans_finalize then picks the exact argmin among those
+// candidates in the reference's f32 arithmetic (find_nearest,
+// crates/vector-cuda/src/kmeans.rs:361-407: strict comparison, lowest index
+// wins ties) and records the exact distance for the inertia.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "tc_common.cuh"
+#include "vrs_exact.cuh"
+#include "vrs_exact_lanes.cuh"
+#include "vrs_internal.cuh"
+#include "vrs_kmeans_tc.cuh"
+#include "vrs_select.cuh"
+
+namespace vrs {
+namespace kmtc {
+namespace {
+
+using namespace vrs::tc;
+
+constexpr int BM = 128, NACC = 2, BN = 128, KBW = 64, MAX_KBLK = 2, STAGES = 4;
+constexpr int EPI_WARPS = 16;
+constexpr int THREADS = 64 + EPI_WARPS * 32;
+constexpr int HALF_COLS = BN / 2;
+constexpr int NCAND = 4;
+constexpr uint32_t BLK = BM * 128;
+constexpr size_t SMEM_A = (size_t)NACC * MAX_KBLK * BLK;
+constexpr size_t SMEM_B = (size_t)STAGES * MAX_KBLK * BLK;
+constexpr size_t SMEM_CAND = (size_t)EPI_WARPS * 32 * NCAND * sizeof(Cand);
+constexpr size_t SMEM_BAR = 256;
+constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_CAND + SMEM_BAR;
+constexpr uint64_t WAIT_NS = 2000000000ull;
+constexpr uint32_t TMEM_COLS = 512;
+
+struct AssignArgs {
+  const float* cn;          // |c|^2 per centroid (L2 mode), zero padded
+  const float* xq;          // |x| per point (margins)
+  const unsigned int* cmax; // max |c| (float bits)
+  int64_t n;
+  int k;
+  int d;
+  int ksteps, kblk;
+  int mode;                 // 0: score |c|^2 - 2 x.c ; 1: score -x.c
+  int metric;
+  Res* res;                 // [n][2] per (point, column half)
+  Cand* cands;              // [n][2][NCAND]
+  int* err;
+};
+
+// Acceptance margin of one point in score units (same bound as the kNN
+// path, with the centroids as the "base").
+__device__ __forceinline__ float point_margin(int metric, int d, float Q, float X) {
+  const double u = 0x1p-24;
+  const int d16 = (d + 15) / 16 * 16;
+  const double c_tc = 0x1p-8 + 0x1p-17 + (double)(d16 + 2) * 0x1p-22;
+  const double g = (double)(d + 4) * u * 1.01;
+  double e;
+  if (metric == vrs_exact::kCos) {
+    e = c_tc + 8.0 * u + 4.0 * g;
+  } else if (metric == vrs_exact::kDot) {
+    e = (c_tc + 2.0 * g) * (double)Q * (double)X;
+  } else {
+    e = 2.0 * c_tc * (double)Q * (double)X + 8.0 * g * ((double)Q + X) * ((double)Q + X);
+  }
+  return (float)(2.0 * e * 1.25) * (1.0f + 0x1p-20f);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    kmeans_assign_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            AssignArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + SMEM_A;
+  Cand* s_cand = (Cand*)(sB + SMEM_B);
+  uint64_t* bars = (uint64_t*)((uint8_t*)s_cand + SMEM_CAND);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* afull = tempty + 2;
+  uint64_t* aempty = afull + 1;
+  uint32_t* s_tmem = (uint32_t*)(aempty + 1);
+  volatile int* s_abort = (volatile int*)(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nptiles = (int)((a.n + BM * NACC - 1) / (BM * NACC));
+  const int kt = (a.k + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], EPI_WARPS);
+    }
+    mbar_init(afull, 1);
+    mbar_init(aempty, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(s_tmem, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    // ---------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t g = 0;
+      int lp = 0;
+      bool ok = true;
+      for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x, lp++) {
+        if (!mbar_wait(aempty, (lp & 1) ^ 1, s_abort, a.err, 11, WAIT_NS)) break;
+        mbar_expect_tx(afull, (uint32_t)(NACC * a.kblk) * BLK);
+        for (int acc = 0; acc < NACC; acc++)
+          for (int kb = 0; kb < a.kblk; kb++)
+            tma_load_2d(sA + (acc * MAX_KBLK + kb) * BLK, &tmA, kb * KBW, pt * BM * NACC + acc * BM, afull);
+        for (int j = 0; j < kt; j++, g++) {
+          const int s = g % STAGES;
+          if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, s_abort, a.err, 12, WAIT_NS)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], (uint32_t)a.kblk * BLK);
+          for (int kb = 0; kb < a.kblk; kb++)
+            tma_load_2d(sB + (s * MAX_KBLK + kb) * BLK, &tmB, kb * KBW, j * BN, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(BM, BN);
+      uint32_t g = 0;
+      int lp = 0;
+      bool ok = true;
+      int64_t last = -1;
+      for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x, lp++) {
+        if (!mbar_wait(afull, lp & 1, s_abort, a.err, 13, WAIT_NS)) break;
+        tc_fence_after();
+        for (int j = 0; j < kt; j++, g++) {
+          const int s = g % STAGES, b = g & 1;
+          if (!mbar_wait(&full[s], (g / STAGES) & 1, s_abort, a.err, 14, WAIT_NS) ||
+              !mbar_wait(&tempty[b], ((g >> 1) & 1) ^ 1, s_abort, a.err, 15, WAIT_NS)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int acc = 0; acc < NACC; acc++) {
+            const uint32_t d = tmem + acc * 256 + b * BN;
+            for (int ks = 0; ks < a.ksteps; ks++) {
+              const int kb = ks >> 2, koff = (ks & 3) * 32;
+              const uint64_t ad = smem_desc_sw128(sA + (acc * MAX_KBLK + kb) * BLK + koff);
+              const uint64_t bd = smem_desc_sw128(sB + (s * MAX_KBLK + kb) * BLK + koff);
+              mma_bf16(d, ad, bd, idesc, ks > 0 ? 1u : 0u);
+            }
+          }
+          mma_commit(&empty[s]);
+          mma_commit(&tfull[b]);
+          last = g;
+        }
+        if (ok) mma_commit(aempty);
+      }
+      if (*s_abort && last >= 0) {
+        volatile int dummy = 0;
+        mbar_wait(&tfull[last & 1], (uint32_t)((last >> 1) & 1), &dummy, a.err, 0, WAIT_NS / 4);
+      }
+    }
+  } else {
+    // ---------------------------------------------------- epilogue
+    const int ew = warp - 2;
+    const int acc = (ew >> 2) & 1;
+    const int ch = ew >> 3;
+    const int quad = warp & 3;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    Cand* buf = s_cand + (ew * 32 + lane) * NCAND;
+    const float X = __uint_as_float(*a.cmax);
+    uint32_t g = 0;
+    bool ok = true;
+    for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x) {
+      const int64_t p = (int64_t)pt * BM * NACC + acc * BM + quad * 32 + lane;
+      const bool vp = p < a.n;
+      const float absm = vp ? point_margin(a.metric, a.d, a.xq[p], X) : 0.0f;
+      float best = INFINITY;
+      float bound = INFINITY;
+      int cnt = 0, ovf = 0;
+      for (int j = 0; j < kt; j++, g++) {
+        const int b = g & 1;
+        const bool w = mbar_wait(&tfull[b], (g >> 1) & 1, s_abort, a.err, 16, WAIT_NS);
+        if (!__all_sync(sel::kFull, w)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int c0 = j * BN + ch * HALF_COLS;
+        const int rem = a.k - c0;
+        const int valid = rem < HALF_COLS ? (rem > 0 ? rem : 0) : HALF_COLS;
+#pragma unroll 1
+        for (int c = 0; c < HALF_COLS / 32; c++) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + acc * 256 + b * BN + ch * HALF_COLS + c * 32, v);
+          const int cb = valid - c * 32;
+          // scores, smaller is better
+          if (a.mode == 0) {
+            const float4* cp = reinterpret_cast<const float4*>(a.cn + c0 + c * 32);
+#pragma unroll
+            for (int j4 = 0; j4 < 8; j4++) {
+              const float4 x4 = __ldg(cp + j4);
+              v[4 * j4 + 0] = fmaf(-2.0f, v[4 * j4 + 0], x4.x);
+              v[4 * j4 + 1] = fmaf(-2.0f, v[4 * j4 + 1], x4.y);
+              v[4 * j4 + 2] = fmaf(-2.0f, v[4 * j4 + 2], x4.z);
+              v[4 * j4 + 3] = fmaf(-2.0f, v[4 * j4 + 3], x4.w);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = -v[i];
+          }
+          if (cb < 32) {
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+              if (i >= cb) v[i] = INFINITY;
+          }
+          float gm[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) gm[i] = fminf(fminf(v[4 * i], v[4 * i + 1]), fminf(v[4 * i + 2], v[4 * i + 3]));
+          const float cmn = fminf(fminf(fminf(gm[0], gm[1]), fminf(gm[2], gm[3])),
+                                  fminf(fminf(gm[4], gm[5]), fminf(gm[6], gm[7])));
+          // A better chunk minimum tightens the bound; drop candidates that
+          // fall outside it.
+          if (vp && cmn < best) {
+            best = cmn;
+            bound = __fadd_ru(best, absm);
+            int k2 = 0;
+            for (int e = 0; e < cnt; e++) {
+              const Cand ce = buf[e];
+              if (ce.hs <= bound) buf[k2++] = ce;
+            }
+            cnt = k2;
+          }
+          unsigned m = 0;
+#pragma unroll
+          for (int i = 0; i < 8; i++) m |= (vp && gm[i] <= bound) ? (1u << i) : 0u;
+          unsigned um = __reduce_or_sync(sel::kFull, m);
+          while (um) {
+            const int i = __ffs(um) - 1;
+            um &= um - 1;
+            if ((m >> i) & 1u) {
+              float w0 = v[0], w1 = v[1], w2 = v[2], w3 = v[3];
+#pragma unroll
+              for (int t = 1; t < 8; t++) {
+                if (i == t) {
+                  w0 = v[4 * t];
+                  w1 = v[4 * t + 1];
+                  w2 = v[4 * t + 2];
+                  w3 = v[4 * t + 3];
+                }
+              }
+#pragma unroll 1
+              for (int jj = 0; jj < 4; jj++) {
+                const float sc = jj == 0 ? w0 : jj == 1 ? w1 : jj == 2 ? w2 : w3;
+                if (4 * i + jj < cb && sc <= bound) {
+                  if (cnt < NCAND)
+                    buf[cnt++] = Cand{sc, (uint32_t)(c0 + c * 32 + 4 * i + jj)};
+                  else
+                    ovf = 1;
+                }
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
+      }
+      if (!ok) break;
+      if (vp) {
+        Res r;
+        r.best = best;
+        r.bi = cnt > 0 ? buf[0].id : 0xffffffffu;
+        r.cnt = cnt;
+        r.ovf = ovf;
+        a.res[p * 2 + ch] = r;
+        if (!ovf)
+          for (int e = 0; e < cnt; e++) a.cands[(p * 2 + ch) * NCAND + e] = buf[e];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// Exact argmin among each point's candidates (all K centroids when flagged),
+// in the reference's pair arithmetic; writes assignment and exact distance.
+// One half-warp per point: its 16 lanes are the reference's 16 SIMD lanes.
+template <int METRIC>
+__global__ void __launch_bounds__(128) kmeans_finalize_kernel(
+    const float* __restrict__ x, int64_t n, int d, int dp, const float* __restrict__ cent,
+    const float* __restrict__ cent_aux, const float* __restrict__ x_aux, int k,
+    const float* __restrict__ xq, const unsigned int* __restrict__ cmax, const Res* __restrict__ res,
+    const Cand* __restrict__ cands, const int* __restrict__ force_full, int32_t* __restrict__ assign,
+    float* __restrict__ dist) {
+  const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
+  if (i >= n) return;  // whole half-warps leave together
+  const int hl = threadIdx.x & 15;
+  const unsigned mask = 0xffffu << (threadIdx.x & 16);
+  const float* v = x + i * dp;
+  const float va = METRIC == vrs_exact::kCos ? x_aux[i] : 0.0f;
+  const bool hib = vrs_exact::higher_is_better(METRIC);
+  const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
+  int best = 0x7fffffff;
+  float best_key = hib ? -INFINITY : INFINITY;
+  auto consider = [&](uint32_t c) {
+    const float ca = METRIC == vrs_exact::kCos ? cent_aux[c] : 0.0f;
+    const float key =
+        vrs_exact::lanes::rank_key(METRIC, v, cent + (int64_t)c * dp, d, va, ca, hl, mask);
+    const bool better = hib ? (key > best_key || (key == best_key && (int)c < best))
+                            : (key < best_key || (key == best_key && (int)c < best));
+    if (better) {
+      best_key = key;
+      best = (int)c;
+    }
+  };
+  if (r0.ovf || r1.ovf || (force_full && force_full[i])) {
+    for (int c = 0; c < k; c++) consider((uint32_t)c);
+  } else {
+    const float bapprox = fminf(r0.best, r1.best);
+    const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax));
+    const float bound = __fadd_ru(bapprox, absm);
+    for (int h = 0; h < 2; h++) {
+      const Res r = h ? r1 : r0;
+      for (int e = 0; e < r.cnt; e++) {
+        const Cand ce = cands[(i * 2 + h) * NCAND + e];
+        if (ce.hs <= bound) consider(ce.id);
+      }
+    }
+  }
+  if (hl == 0) {
+    assign[i] = best;
+    dist[i] = vrs_exact::finish(METRIC, best_key);
+  }
+}
+
+// Operand rows (bf16; cosine rows unit-normalised), |row|^2 and |row| for
+// points or centroids; max |row| into *maxn; near-zero cosine rows flagged.
+__global__ void km_prep_rows_kernel(const float* __restrict__ x, int64_t n, int d, int dp, int metric,
+                                    __nv_bfloat16* __restrict__ xb, float* __restrict__ sq,
+                                    float* __restrict__ nrm, unsigned int* __restrict__ maxn,
+                                    int* __restrict__ tiny_flag, int* __restrict__ any_tiny) {
+  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int d16 = (d + 15) / 16 * 16;
+  const float* v = x + r * dp;
+  __nv_bfloat16* o = xb + r * d16;
+  float scale = 1.0f;
+  int tiny = 0;
+  if (metric == vrs_exact::kCos) {
+    const float s = sqrtf(vrs_exact::cos_norm_sq(v, d));
+    if (!(s >= 1e-4f)) {
+      tiny = 1;
+      scale = 0.0f;
+    } else {
+      scale = 1.0f / s;
+    }
+  }
+  double ss = 0.0;
+  for (int j = 0; j < d16; j++) {
+    const float e = j < d ? v[j] : 0.0f;
+    ss += (double)e * (double)e;
+    o[j] = __float2bfloat16_rn(metric == vrs_exact::kCos ? e * scale : e);
+  }
+  if (sq) sq[r] = (float)ss;
+  const float nr = (float)sqrt(ss);
+  if (nrm) nrm[r] = nr;
+  if (maxn) atomicMax(maxn, __float_as_uint(nr));
+  if (tiny_flag) tiny_flag[r] = tiny;
+  if (tiny && any_tiny) atomicOr(any_tiny, 1);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error(VRS_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
+    return VRS_ERR_DRIVER;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)d16, (cuuint64_t)std::max<int64_t>(rows, 1)};
+  cuuint64_t strides[1] = {(cuuint64_t)d16 * 2};
+  cuuint32_t box[2] = {(cuuint32_t)KBW, (cuuint32_t)BM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error(VRS_ERR_DRIVER, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return VRS_ERR_DRIVER;
+  }
+  return VRS_OK;
+}
+
+template <int M>
+int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
+                 const float* x_aux, int k, const float* xq, const unsigned int* cmax, const Res* res,
+                 const Cand* cands, const int* force_full, int32_t* assign, float* dist, cudaStream_t s) {
+  kmeans_finalize_kernel<M><<<(unsigned)((n * 16 + 127) / 128), 128, 0, s>>>(
+      x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full, assign, dist);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+}  // namespace
+
+bool supported(int metric, int d) {
+  return d >= 1 && d <= 128 &&
+         (metric == vrs_exact::kL2 || metric == vrs_exact::kMaha || metric == vrs_exact::kDot ||
+          metric == vrs_exact::kCos);
+}
+
+int prep_rows(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* sq, float* nrm,
+              unsigned int* maxn, int* tiny_flag, int* any_tiny, cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  km_prep_rows_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(x, n, d, dp, metric, (__nv_bfloat16*)xb, sq,
+                                                                 nrm, maxn, tiny_flag, any_tiny);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
+           const unsigned int* cmax, int metric, Res* res, Cand* cands, int* err, int num_sms,
+           cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  const int d16 = (d + 15) / 16 * 16;
+  CUtensorMap tmA, tmB;
+  VRS_TRY(make_tmap(&tmA, xb, n, d16));
+  VRS_TRY(make_tmap(&tmB, cb, k, d16));
+  AssignArgs a;
+  a.cn = cn;
+  a.xq = xq;
+  a.cmax = cmax;
+  a.n = n;
+  a.k = k;
+  a.d = d;
+  a.ksteps = (d + 15) / 16;
+  a.kblk = (d16 + KBW - 1) / KBW;
+  a.mode = (metric == vrs_exact::kL2 || metric == vrs_exact::kMaha) ? 0 : 1;
+  a.metric = metric;
+  a.res = res;
+  a.cands = cands;
+  a.err = err;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    VRS_CUDA(cudaFuncSetAttribute(kmeans_assign_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)SMEM_TOTAL));
+    attr_set[dev] = true;
+  }
+  const int nptiles = (int)((n + BM * NACC - 1) / (BM * NACC));
+  const int grid = std::max(1, std::min(nptiles, num_sms));
+  kmeans_assign_tc_kernel<<<grid, THREADS, SMEM_TOTAL, s>>>(tmA, tmB, a);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
+             const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
+             const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  switch (metric) {
+    case vrs_exact::kL2:
+      return finalize_run<vrs_exact::kL2>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full,
+                                          assign_out, dist, s);
+    case vrs_exact::kMaha:
+      return finalize_run<vrs_exact::kMaha>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
+                                            force_full, assign_out, dist, s);
+    case vrs_exact::kDot:
+      return finalize_run<vrs_exact::kDot>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
+                                           force_full, assign_out, dist, s);
+    case vrs_exact::kCos:
+      return finalize_run<vrs_exact::kCos>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
+                                           force_full, assign_out, dist, s);
+  }
+  set_error(VRS_ERR_INVALID_CONFIG, "k-means tensor-core finalize: unsupported metric");
+  return VRS_ERR_INVALID_CONFIG;
+}
+
+}  // namespace kmtc
+}  // namespace vrs

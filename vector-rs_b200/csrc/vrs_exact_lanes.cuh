@@ -10,17 +10,19 @@
 namespace vrs_exact {
 namespace lanes {
 
-__device__ __forceinline__ float hsum16(float v) {
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8, 16));
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4, 16));
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2, 16));
-  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1, 16));
+// `mask` names the lanes taking part: the full warp, or one half-warp when
+// the two halves run independently.
+__device__ __forceinline__ float hsum16(float v, unsigned mask = 0xffffffffu) {
+  v = __fadd_rn(v, __shfl_xor_sync(mask, v, 8, 16));
+  v = __fadd_rn(v, __shfl_xor_sync(mask, v, 4, 16));
+  v = __fadd_rn(v, __shfl_xor_sync(mask, v, 2, 16));
+  v = __fadd_rn(v, __shfl_xor_sync(mask, v, 1, 16));
   return v;
 }
 
 // avx512::dot_product (avx512.rs:23-76)
 __device__ __forceinline__ float dot(const float* __restrict__ a, const float* __restrict__ b, int n,
-                                     int l) {
+                                     int l, unsigned mask = 0xffffffffu) {
   float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
   const int chunks = n / 64;
   for (int c = 0; c < chunks; c++) {
@@ -33,14 +35,14 @@ __device__ __forceinline__ float dot(const float* __restrict__ a, const float* _
   }
   int i = chunks * 64;
   for (; i + 16 <= n; i += 16) s0 = __fmaf_rn(a[i + l], b[i + l], s0);
-  float r = hsum16(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
+  float r = hsum16(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), mask);
   for (; i < n; i++) r = __fadd_rn(r, __fmul_rn(a[i], b[i]));
   return r;
 }
 
 // avx512::l2_squared (avx512.rs:87-148)
 __device__ __forceinline__ float l2(const float* __restrict__ a, const float* __restrict__ b, int n,
-                                    int l) {
+                                    int l, unsigned mask = 0xffffffffu) {
   float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
   const int chunks = n / 64;
   for (int c = 0; c < chunks; c++) {
@@ -58,7 +60,7 @@ __device__ __forceinline__ float l2(const float* __restrict__ a, const float* __
     float d = __fsub_rn(a[i + l], b[i + l]);
     s0 = __fmaf_rn(d, d, s0);
   }
-  float r = hsum16(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)));
+  float r = hsum16(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), mask);
   for (; i < n; i++) {
     float d = __fsub_rn(a[i], b[i]);
     r = __fadd_rn(r, __fmul_rn(d, d));
@@ -68,7 +70,7 @@ __device__ __forceinline__ float l2(const float* __restrict__ a, const float* __
 
 // Dot product in the cosine kernel's order (avx512.rs:161-223).
 __device__ __forceinline__ float cos_dot(const float* __restrict__ a, const float* __restrict__ b,
-                                         int n, int l) {
+                                         int n, int l, unsigned mask = 0xffffffffu) {
   float s0 = 0.0f, s1 = 0.0f;
   const int chunks = n / 32;
   for (int c = 0; c < chunks; c++) {
@@ -79,19 +81,19 @@ __device__ __forceinline__ float cos_dot(const float* __restrict__ a, const floa
   }
   int i = chunks * 32;
   for (; i + 16 <= n; i += 16) s0 = __fmaf_rn(a[i + l], b[i + l], s0);
-  float r = hsum16(__fadd_rn(s0, s1));
+  float r = hsum16(__fadd_rn(s0, s1), mask);
   for (; i < n; i++) r = __fadd_rn(r, __fmul_rn(a[i], b[i]));
   return r;
 }
 
 // Rank key for the metrics re-ranked by lanes (others are scanned exactly).
 __device__ __forceinline__ float rank_key(int metric, const float* a, const float* b, int n, float na,
-                                          float nb, int l) {
+                                          float nb, int l, unsigned mask = 0xffffffffu) {
   switch (metric) {
     case kL2:
-    case kMaha: return l2(a, b, n, l);
-    case kDot: return dot(a, b, n, l);
-    case kCos: return cos_finish(cos_dot(a, b, n, l), na, nb);
+    case kMaha: return l2(a, b, n, l, mask);
+    case kDot: return dot(a, b, n, l, mask);
+    case kCos: return cos_finish(cos_dot(a, b, n, l, mask), na, nb);
   }
   return 0.0f;
 }

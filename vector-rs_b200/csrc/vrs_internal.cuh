@@ -150,6 +150,12 @@ int launch_kmeans_assign_exact(const float* x, int64_t n, int d, int dp, const f
 int launch_kmeans_accumulate(const float* x, int64_t n, int d, int dp, const int32_t* assign,
                              int k, int scale_exp, unsigned long long* sums,
                              unsigned long long* counts, cudaStream_t s);
+// Deterministic per-cluster fixed-point sums through a counting sort (d <= 256;
+// larger d falls back to per-element integer atomics). ws: kmeans_segsum_ws_bytes.
+int launch_kmeans_segsum(const float* x, int64_t n, int d, int dp, const int32_t* assign, int k,
+                         int scale_exp, unsigned long long* sums, unsigned long long* counts, int* ws,
+                         cudaStream_t s);
+size_t kmeans_segsum_ws_bytes(int64_t n, int k);
 int launch_kmeans_update(const unsigned long long* sums, const unsigned long long* counts,
                          int k, int d, int dp, int scale_exp, float* cent, float* shift,
                          float* max_shift, cudaStream_t s);

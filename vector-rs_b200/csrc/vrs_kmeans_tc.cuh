@@ -1,0 +1,31 @@
+// vrs_kmeans_tc.cuh -- host-side interface of the tensor-core k-means
+// assignment (kmeans_tc.cu).
+#pragma once
+#include "vrs_internal.cuh"
+
+namespace vrs {
+namespace kmtc {
+
+// Per (point, column half) result of the tensor-core pass: approximate best
+// score and centroid, candidate count within the margin, overflow flag.
+struct Res {
+  float best;
+  uint32_t bi;
+  int cnt;
+  int ovf;
+};
+
+bool supported(int metric, int d);
+// bf16 operand rows, |row|^2 (sq, nullable), |row| (nrm, nullable), max |row|
+// (maxn, nullable), near-zero cosine flags (nullable).
+int prep_rows(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* sq, float* nrm,
+              unsigned int* maxn, int* tiny_flag, int* any_tiny, cudaStream_t s);
+int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
+           const unsigned int* cmax, int metric, Res* res, Cand* cands, int* err, int num_sms,
+           cudaStream_t s);
+int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
+             const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
+             const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, cudaStream_t s);
+
+}  // namespace kmtc
+}  // namespace vrs
