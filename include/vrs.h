@@ -153,6 +153,23 @@ VRS_API int vrs_kmeans_fit_rank(vrs_comm* comm, const float* x_local, int64_t n_
                         int32_t metric, int32_t mem, float* out_centroids, int32_t* out_assign,
                         int32_t* out_k, int32_t* out_iters, double* out_inertia);
 
+/* No counterpart in the reference. Exact kNN for callers that cannot
+ * allocate device memory during a search (inside a captured or
+ * allocation-free region, behind a plugin host or caching pool that owns
+ * all device memory, or in latency-critical loops): nothing is allocated;
+ * base (n x d), queries (nq x d), out_dist and out_id (nq x k', k' =
+ * min(k, n), packed) are caller-provided device pointers on the current
+ * device, and work is queued on cuda_stream (NULL = default stream); the
+ * call returns without waiting. Scratch is one fixed 8 MiB device array per
+ * device, held until exit; a batch whose candidate lists do not fit is
+ * rejected with VRS_ERR_INVALID_CONFIG (split it). The first call on a
+ * device looks up that array's address, so make it before any stream
+ * capture. Calls that overlap on the GPU share the array and race.
+ * Cosine and Hellinger are rejected (they need per-row norms or roots). */
+VRS_API int vrs_knn_search_noalloc(const float* base, int64_t n, int32_t d, const float* queries,
+                                   int64_t nq, int32_t k, int32_t metric, float* out_dist,
+                                   uint32_t* out_id, int32_t* out_k, void* cuda_stream);
+
 /* ------------------------------------------------------ streams, profiling */
 /* Makes a single-GPU or rank-mode handle issue its work on `cuda_stream`
  * (a cudaStream_t of the handle's device; NULL restores the handle's own).
