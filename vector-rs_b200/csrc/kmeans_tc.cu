@@ -205,7 +205,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float absm = vp ? point_margin(a.metric, a.d, a.xq[p], X) : 0.0f;
       float best = INFINITY;
       float bound = INFINITY;
-      int cnt = 0, ovf = 0;
+      float lost = INFINITY;  // smallest score pushed out of a full buffer
+      int cnt = 0;
       for (int j = 0; j < kt; j++, g++) {
         const int b = g & 1;
         const bool w = mbar_wait(&tfull[b], (g >> 1) & 1, s_abort, a.err, 16, WAIT_NS);
@@ -281,10 +282,21 @@ __global__ void __launch_bounds__(THREADS, 1)
               for (int jj = 0; jj < 4; jj++) {
                 const float sc = jj == 0 ? w0 : jj == 1 ? w1 : jj == 2 ? w2 : w3;
                 if (4 * i + jj < cb && sc <= bound) {
-                  if (cnt < NCAND)
-                    buf[cnt++] = Cand{sc, (uint32_t)(c0 + c * 32 + 4 * i + jj)};
-                  else
-                    ovf = 1;
+                  const Cand cn = Cand{sc, (uint32_t)(c0 + c * 32 + 4 * i + jj)};
+                  if (cnt < NCAND) {
+                    buf[cnt++] = cn;
+                  } else {
+                    // Keep the NCAND best; remember the best score dropped.
+                    int wi = 0;
+                    for (int e = 1; e < NCAND; e++)
+                      if (buf[e].hs > buf[wi].hs) wi = e;
+                    if (sc < buf[wi].hs) {
+                      lost = fminf(lost, buf[wi].hs);
+                      buf[wi] = cn;
+                    } else {
+                      lost = fminf(lost, sc);
+                    }
+                  }
                 }
               }
             }
@@ -300,10 +312,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         r.best = best;
         r.bi = cnt > 0 ? buf[0].id : 0xffffffffu;
         r.cnt = cnt;
-        r.ovf = ovf;
+        r.lost = lost;
         a.res[p * 2 + ch] = r;
-        if (!ovf)
-          for (int e = 0; e < cnt; e++) a.cands[(p * 2 + ch) * NCAND + e] = buf[e];
+        for (int e = 0; e < cnt; e++) a.cands[(p * 2 + ch) * NCAND + e] = buf[e];
       }
     }
   }
@@ -346,12 +357,14 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
       best = (int)c;
     }
   };
-  if (r0.ovf || r1.ovf || (force_full && force_full[i])) {
+  const float bapprox = fminf(r0.best, r1.best);
+  const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax));
+  const float bound = __fadd_ru(bapprox, absm);
+  // A candidate that was pushed out of a full buffer only matters if it is
+  // still within the final bound; then every centroid is checked exactly.
+  if (r0.lost <= bound || r1.lost <= bound || (force_full && force_full[i])) {
     for (int c = 0; c < k; c++) consider((uint32_t)c);
   } else {
-    const float bapprox = fminf(r0.best, r1.best);
-    const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax));
-    const float bound = __fadd_ru(bapprox, absm);
     for (int h = 0; h < 2; h++) {
       const Res r = h ? r1 : r0;
       for (int e = 0; e < r.cnt; e++) {
@@ -368,19 +381,22 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
 
 // Operand rows (bf16; cosine rows unit-normalised), |row|^2 and |row| for
 // points or centroids; max |row| into *maxn; near-zero cosine rows flagged.
-__global__ void km_prep_rows_kernel(const float* __restrict__ x, int64_t n, int d, int dp, int metric,
-                                    __nv_bfloat16* __restrict__ xb, float* __restrict__ sq,
-                                    float* __restrict__ nrm, unsigned int* __restrict__ maxn,
-                                    int* __restrict__ tiny_flag, int* __restrict__ any_tiny) {
-  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+// One half-warp per row.
+__global__ void __launch_bounds__(128) km_prep_rows_kernel(
+    const float* __restrict__ x, int64_t n, int d, int dp, int metric, __nv_bfloat16* __restrict__ xb,
+    float* __restrict__ sq, float* __restrict__ nrm, unsigned int* __restrict__ maxn,
+    int* __restrict__ tiny_flag, int* __restrict__ any_tiny) {
+  const int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
   if (r >= n) return;
+  const int hl = threadIdx.x & 15;
+  const unsigned mask = 0xffffu << (threadIdx.x & 16);
   const int d16 = (d + 15) / 16 * 16;
   const float* v = x + r * dp;
   __nv_bfloat16* o = xb + r * d16;
   float scale = 1.0f;
   int tiny = 0;
   if (metric == vrs_exact::kCos) {
-    const float s = sqrtf(vrs_exact::cos_norm_sq(v, d));
+    const float s = sqrtf(vrs_exact::lanes::cos_dot(v, v, d, hl, mask));
     if (!(s >= 1e-4f)) {
       tiny = 1;
       scale = 0.0f;
@@ -389,17 +405,21 @@ __global__ void km_prep_rows_kernel(const float* __restrict__ x, int64_t n, int 
     }
   }
   double ss = 0.0;
-  for (int j = 0; j < d16; j++) {
+  for (int j = hl; j < d16; j += 16) {
     const float e = j < d ? v[j] : 0.0f;
     ss += (double)e * (double)e;
     o[j] = __float2bfloat16_rn(metric == vrs_exact::kCos ? e * scale : e);
   }
-  if (sq) sq[r] = (float)ss;
-  const float nr = (float)sqrt(ss);
-  if (nrm) nrm[r] = nr;
-  if (maxn) atomicMax(maxn, __float_as_uint(nr));
-  if (tiny_flag) tiny_flag[r] = tiny;
-  if (tiny && any_tiny) atomicOr(any_tiny, 1);
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(mask, ss, off, 16);
+  if (hl == 0) {
+    if (sq) sq[r] = (float)ss;
+    const float nr = (float)sqrt(ss);
+    if (nrm) nrm[r] = nr;
+    if (maxn) atomicMax(maxn, __float_as_uint(nr));
+    if (tiny_flag) tiny_flag[r] = tiny;
+    if (tiny && any_tiny) atomicOr(any_tiny, 1);
+  }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -456,8 +476,8 @@ bool supported(int metric, int d) {
 int prep_rows(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* sq, float* nrm,
               unsigned int* maxn, int* tiny_flag, int* any_tiny, cudaStream_t s) {
   if (n == 0) return VRS_OK;
-  km_prep_rows_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(x, n, d, dp, metric, (__nv_bfloat16*)xb, sq,
-                                                                 nrm, maxn, tiny_flag, any_tiny);
+  km_prep_rows_kernel<<<(unsigned)((n * 16 + 127) / 128), 128, 0, s>>>(x, n, d, dp, metric, (__nv_bfloat16*)xb,
+                                                                      sq, nrm, maxn, tiny_flag, any_tiny);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;

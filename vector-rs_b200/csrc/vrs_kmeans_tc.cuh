@@ -7,12 +7,13 @@ namespace vrs {
 namespace kmtc {
 
 // Per (point, column half) result of the tensor-core pass: approximate best
-// score and centroid, candidate count within the margin, overflow flag.
+// score and centroid, number of kept candidates (at most 4, the best within
+// the margin), and the smallest score that did not fit (+inf if none).
 struct Res {
   float best;
   uint32_t bi;
   int cnt;
-  int ovf;
+  float lost;
 };
 
 bool supported(int metric, int d);
