@@ -49,7 +49,6 @@ def parse():
     ap.add_argument("--n-query", type=int, default=N_QUERY)
     ap.add_argument("--km-n", type=int, default=KM_N, help="k-means points (C3: 1,000,000)")
     ap.add_argument("--km-iters", type=int, default=KM_ITERS)
-    ap.add_argument("--no-knn", action="store_true", help="skip the kNN measurement")
     return ap.parse_args()
 
 
@@ -216,8 +215,7 @@ def main():
     # ---------------------------------------------------------------- data
     n_base, n_q = args.n_base, args.n_query
     seed = vc.config_seed(1)
-    chunk = -(-n_base // world)
-    r0, r1 = min(n_base, rank * chunk), min(n_base, (rank + 1) * chunk)
+    r0, r1 = vc.shard_rows(n_base, world, rank)
     shard = torch.empty((max(r1 - r0, 1), DIM), dtype=torch.float32, device=dev)
     vc.gen_rows_device(vc.GEN_NORMAL_UNIT, seed, 0, r0, r1 - r0, DIM, shard.data_ptr())
     q_dev = torch.empty((n_q, DIM), dtype=torch.float32, device=dev)
@@ -334,8 +332,7 @@ def main():
     if not args.no_kmeans:
         km_seed = vc.config_seed(2)
         KMN = args.km_n
-        kchunk = -(-KMN // world)
-        k0, k1 = min(KMN, rank * kchunk), min(KMN, (rank + 1) * kchunk)
+        k0, k1 = vc.shard_rows(KMN, world, rank)
         cent = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)
         vc.gen_rows_device(vc.GEN_NORMAL, km_seed, 2, 0, KM_K, KM_D, cent.data_ptr())
         xs = torch.empty((max(k1 - k0, 1), KM_D), dtype=torch.float32, device=dev)

@@ -58,6 +58,14 @@ def lib():
                                      ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, _f32p, ctypes.c_void_p,
                                      ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double)]
+        L.orc_kmeans_local.restype = None
+        L.orc_kmeans_local.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _f32p,
+                                       ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.POINTER(ctypes.c_double)]
+        L.orc_kmeans_update.restype = ctypes.c_float
+        L.orc_kmeans_update.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                        _f32p]
         _lib = L
     return _lib
 
@@ -122,3 +130,30 @@ def kmeans_fit(x, k: int, init, max_iters: int, tol: float, metric: int,
                               int(nthreads or os.cpu_count() or 1), use_simd, cent,
                               assign.ctypes.data, ctypes.byref(it), ctypes.byref(inertia))
     return cent[:kk * d].reshape(kk, d), assign[:n], it.value, inertia.value
+
+
+def kmeans_local(x, centroids, metric: int, nthreads: int | None = None, use_simd: int = -1):
+    """One rank's share of a Lloyd iteration on its rows x.
+    Returns (assign[n], sums[k,d] f64, counts[k] i64, inertia f64)."""
+    x = _f32(x).reshape(-1, np.asarray(centroids).shape[1])
+    cent = _f32(centroids)
+    n, d = x.shape
+    kk = cent.shape[0]
+    assign = np.zeros(max(n, 1), np.int32)
+    sums = np.zeros((kk, d), np.float64)
+    counts = np.zeros(kk, np.int64)
+    inertia = ctypes.c_double(0.0)
+    lib().orc_kmeans_local(x, n, d, kk, cent, int(metric), int(nthreads or os.cpu_count() or 1),
+                           use_simd, assign.ctypes.data, sums.ctypes.data, counts.ctypes.data,
+                           ctypes.byref(inertia))
+    return assign[:n], sums, counts, inertia.value
+
+
+def kmeans_update(sums, counts, centroids):
+    """In-place centroid update from global sums/counts; returns the largest
+    squared shift."""
+    sums = np.ascontiguousarray(sums, np.float64)
+    counts = np.ascontiguousarray(counts, np.int64)
+    assert centroids.dtype == np.float32 and centroids.flags.c_contiguous
+    kk, d = centroids.shape
+    return float(lib().orc_kmeans_update(sums.ctypes.data, counts.ctypes.data, kk, d, centroids))

@@ -736,6 +736,52 @@ static void assign_all(const float* x, int64_t n, int d, int k, int metric, int 
     for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
 }
 
+/* One rank's share of a Lloyd iteration: assign the rank's rows to their
+ * nearest centroid, then per-cluster f64 sums of the rows (row order),
+ * counts and the summed distances (distributed_kmeans.rs:377-409, with f64
+ * sums in place of the reference's f32 ones). The sums of all ranks are
+ * added by an all-reduce before orc_kmeans_update. */
+void orc_kmeans_local(const float* x, int64_t n, int d, int kk, const float* cent, int metric,
+                      int nthreads, int use_simd, int32_t* out_assign, double* out_sums,
+                      int64_t* out_counts, double* out_inertia) {
+    int simd = pick_simd(use_simd);
+    float* dist = malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    memset(out_sums, 0, sizeof(double) * (size_t)kk * d);
+    memset(out_counts, 0, sizeof(int64_t) * (size_t)kk);
+    double inertia = 0.0;
+    if (n > 0) assign_all(x, n, d, kk, metric, simd, nthreads, cent, out_assign, dist);
+    for (int64_t i = 0; i < n; i++) {
+        int c = out_assign[i];
+        out_counts[c]++;
+        const float* v = x + i * d;
+        double* s = out_sums + (int64_t)c * d;
+        for (int e = 0; e < d; e++) s[e] += (double)v[e];
+        inertia += (double)dist[i];
+    }
+    *out_inertia = inertia;
+    free(dist);
+}
+
+/* Centroid update from the global sums and counts: mean = (float)(sum /
+ * count), squared shift accumulated in f32 per cluster, the largest shift
+ * returned; an empty cluster keeps its centroid (distributed_kmeans.rs:433-461
+ * reseeds it from a random row instead). */
+float orc_kmeans_update(const double* sums, const int64_t* counts, int kk, int d, float* cent) {
+    float max_shift = 0.0f;
+    for (int c = 0; c < kk; c++) {
+        if (counts[c] == 0) continue;
+        float shift = 0.0f;
+        for (int e = 0; e < d; e++) {
+            float val = (float)(sums[(int64_t)c * d + e] / (double)counts[c]);
+            float diff = val - cent[(int64_t)c * d + e];
+            shift += diff * diff;
+            cent[(int64_t)c * d + e] = val;
+        }
+        if (shift > max_shift) max_shift = shift;
+    }
+    return max_shift;
+}
+
 /* Returns the effective k (min(k, n); 0 when n == 0 or k == 0).
  * init: k_eff x d initial centroids (required). out_assign may be NULL.
  * out_inertia: f64 sum, in point order, of the last assignment step's
@@ -748,47 +794,23 @@ int orc_kmeans_fit(const float* x, int64_t n, int d, int k, const float* init,
     *out_inertia = 0.0;
     if (n <= 0 || k <= 0) return 0;
     int kk = (int)(k < n ? k : n);
-    int simd = pick_simd(use_simd);
     float* cent = malloc(sizeof(float) * (size_t)kk * d);
     memcpy(cent, init, sizeof(float) * (size_t)kk * d);
     int32_t* assign = malloc(sizeof(int32_t) * (size_t)n);
-    float* dist = malloc(sizeof(float) * (size_t)n);
     double* sums = malloc(sizeof(double) * (size_t)kk * d);
     int64_t* counts = malloc(sizeof(int64_t) * (size_t)kk);
     double inertia = 0.0;
     int iters = 0;
     for (int it = 0; it < max_iters; it++) {
         iters = it + 1;
-        assign_all(x, n, d, kk, metric, simd, nthreads, cent, assign, dist);
-        memset(sums, 0, sizeof(double) * (size_t)kk * d);
-        memset(counts, 0, sizeof(int64_t) * (size_t)kk);
-        inertia = 0.0;
-        for (int64_t i = 0; i < n; i++) {
-            int c = assign[i];
-            counts[c]++;
-            const float* v = x + i * d;
-            double* s = sums + (int64_t)c * d;
-            for (int e = 0; e < d; e++) s[e] += (double)v[e];
-            inertia += (double)dist[i];
-        }
-        float max_shift = 0.0f;
-        for (int c = 0; c < kk; c++) {
-            if (counts[c] == 0) continue;
-            float shift = 0.0f;
-            for (int e = 0; e < d; e++) {
-                float val = (float)(sums[(int64_t)c * d + e] / (double)counts[c]);
-                float diff = val - cent[(int64_t)c * d + e];
-                shift += diff * diff;
-                cent[(int64_t)c * d + e] = val;
-            }
-            if (shift > max_shift) max_shift = shift;
-        }
-        if (max_shift <= tol) break;
+        orc_kmeans_local(x, n, d, kk, cent, metric, nthreads, use_simd, assign, sums, counts,
+                         &inertia);
+        if (orc_kmeans_update(sums, counts, kk, d, cent) <= tol) break;
     }
     memcpy(out_centroids, cent, sizeof(float) * (size_t)kk * d);
     if (out_assign) memcpy(out_assign, assign, sizeof(int32_t) * (size_t)n);
     *out_iters = iters;
     *out_inertia = inertia;
-    free(cent); free(assign); free(dist); free(sums); free(counts);
+    free(cent); free(assign); free(sums); free(counts);
     return kk;
 }

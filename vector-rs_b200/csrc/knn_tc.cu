@@ -24,6 +24,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "tc_common.cuh"
 #include "vrs_exact.cuh"
@@ -66,17 +67,21 @@ struct TcScanArgs {
   int* overflow;     // [nq]
   int cap;
   int k;
-  int mode;          // 0: score = |x|^2 - 2 acc; 1: score = -acc
   const float* absm; // [nq]
   int* err;          // global error word (0 = ok)
   // Pivot pass: instead of appending, write each half tile's minimum score
-  // per query to tmin[2 * tile + half][query] (tile = global 128-row index).
-  int tilemin;
+  // per query to tmin[query][2 * tile + half] (tile = global 128-row index).
   float* tmin;
+  int64_t tmin_stride;  // entries per query row of tmin (2 * tiles)
   // Starting acceptance bound per query (null: +inf).
   const float* init_bound;
 };
 
+// MODE 0: heap score = |x|^2 - 2 acc (squared L2, Mahalanobis);
+// MODE 1: heap score = -acc (dot, cosine on unit rows). The epilogue works on
+// a per-mode "key" whose best end is the minimum (MODE 0: the score) or the
+// maximum (MODE 1: acc). TILEMIN selects the pivot pass.
+template <int MODE, bool TILEMIN>
 __global__ void __launch_bounds__(THREADS, 1)
     knn_scan_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        TcScanArgs a) {
@@ -193,7 +198,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int64_t list_id = ((int64_t)blockIdx.y * 2 + ch) * a.nq + (vq ? q : 0);
     Cand* list = a.cand + list_id * a.cap;
     int count = 0;
-    float bound = (vq && a.init_bound) ? a.init_bound[q] : INFINITY;
+    // Acceptance bound on the heap score; -inf for padding queries, so that
+    // nothing passes for them.
+    float bound = vq ? (a.init_bound ? a.init_bound[q] : INFINITY) : -INFINITY;
     const float absm = vq ? a.absm[q] : 0.0f;
     int* hist = s_hist + ew * 256;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
@@ -205,16 +212,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int64_t n0 = row_begin + (int64_t)t * BN + ch * HALF_COLS;
       const int64_t rem_cols = row_end - n0;
       const int valid_cols = rem_cols < HALF_COLS ? (int)(rem_cols > 0 ? rem_cols : 0) : HALF_COLS;
-      // Similarity mode keeps raw dot products and tests them against
-      // -bound (score = -acc); L2 mode forms the score |x|^2 - 2 acc.
-      const float nbound = -bound;
-      float tile_min = INFINITY;
+      // Key threshold: MODE 0 passes key <= bound, MODE 1 passes key >= -bound.
+      const float thr = MODE == 0 ? bound : -bound;
+      float tile_best = MODE == 0 ? INFINITY : -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < HALF_COLS / 32; c++) {
         float v[32];
         tmem_ld32(tmem + lane_base + acc * 256 + b * BN + ch * HALF_COLS + c * 32, v);
-        const int cb = valid_cols - c * 32;
-        if (a.mode == 0) {
+        if (MODE == 0) {
           const float4* xp = reinterpret_cast<const float4*>(a.xn + n0 + c * 32);
 #pragma unroll
           for (int j4 = 0; j4 < 8; j4++) {
@@ -224,55 +229,41 @@ __global__ void __launch_bounds__(THREADS, 1)
             v[4 * j4 + 2] = fmaf(-2.0f, v[4 * j4 + 2], x4.z);
             v[4 * j4 + 3] = fmaf(-2.0f, v[4 * j4 + 3], x4.w);
           }
-          if (cb < 32) {
-#pragma unroll
-            for (int j = 0; j < 32; j++)
-              if (j >= cb) v[j] = INFINITY;
-          }
-        } else if (cb < 32) {
+        }
+        const int cb = valid_cols - c * 32;
+        if (cb < 32) {
+          // Columns past the segment end: the worst key for the pivot
+          // minima; NaN for the append path, which fails every comparison
+          // (min/max ignore a NaN operand) even when the bound is infinite.
+          const float pad = TILEMIN ? (MODE == 0 ? INFINITY : -INFINITY) : __int_as_float(0x7fffffff);
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            if (j >= cb) v[j] = -INFINITY;
+            if (j >= cb) v[j] = pad;
         }
-        // Extremum (score-wise best) of each group of 4 columns.
+        // Best key of each group of 4 columns.
         float g[8];
-        if (a.mode == 0) {
-#pragma unroll
-          for (int i = 0; i < 8; i++)
-            g[i] = fminf(fminf(v[4 * i], v[4 * i + 1]), fminf(v[4 * i + 2], v[4 * i + 3]));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; i++)
-            g[i] = fmaxf(fmaxf(v[4 * i], v[4 * i + 1]), fmaxf(v[4 * i + 2], v[4 * i + 3]));
-        }
-        if (a.tilemin) {
-          float hm = g[0];
-          if (a.mode == 0) {
-#pragma unroll
-            for (int i = 1; i < 8; i++) hm = fminf(hm, g[i]);
-            tile_min = fminf(tile_min, hm);
-          } else {
-#pragma unroll
-            for (int i = 1; i < 8; i++) hm = fmaxf(hm, g[i]);
-            tile_min = fminf(tile_min, -hm);
-          }
-          continue;
-        }
-        // One ballot per group (independent); only groups where some lane
-        // passes take the append path.
-        unsigned gb[8];
 #pragma unroll
         for (int i = 0; i < 8; i++)
-          gb[i] = __ballot_sync(sel::kFull, vq && (a.mode == 0 ? g[i] <= bound : g[i] >= nbound));
+          g[i] = MODE == 0 ? fmin3(v[4 * i], v[4 * i + 1], fminf(v[4 * i + 2], v[4 * i + 3]))
+                           : fmax3(v[4 * i], v[4 * i + 1], fmaxf(v[4 * i + 2], v[4 * i + 3]));
+        if (TILEMIN) {
+          tile_best = MODE == 0 ? fmin3(fmin3(tile_best, g[0], g[1]), fmin3(g[2], g[3], g[4]), fmin3(g[5], g[6], g[7]))
+                                : fmax3(fmax3(tile_best, g[0], g[1]), fmax3(g[2], g[3], g[4]), fmax3(g[5], g[6], g[7]));
+          continue;
+        }
+        unsigned m = 0;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-          if (gb[i]) {
-            const bool gp = (gb[i] >> lane) & 1u;
+        for (int i = 0; i < 8; i++) m |= (MODE == 0 ? g[i] <= thr : g[i] >= thr) ? (1u << i) : 0u;
+        // One vote per chunk; most chunks have no passing group in any lane.
+        if (__any_sync(sel::kFull, m != 0)) {
 #pragma unroll
-            for (int jj = 0; jj < 4; jj++) {
-              const int j = 4 * i + jj;
-              const float sc = a.mode == 0 ? v[j] : -v[j];
-              if (gp && j < cb && sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + c * 32 + j)};
+          for (int i = 0; i < 8; i++) {
+            if ((m >> i) & 1u) {
+#pragma unroll
+              for (int jj = 0; jj < 4; jj++) {
+                const float sc = MODE == 0 ? v[4 * i + jj] : -v[4 * i + jj];
+                if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + c * 32 + 4 * i + jj)};
+              }
             }
           }
         }
@@ -280,8 +271,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
-      if (a.tilemin) {
-        if (vq) a.tmin[((row_begin / BN + t) * 2 + ch) * (int64_t)a.nq + q] = tile_min;
+      if (TILEMIN) {
+        if (vq)
+          a.tmin[(int64_t)q * a.tmin_stride + (row_begin / BN + t) * 2 + ch] =
+              MODE == 0 ? tile_best : -tile_best;
         continue;
       }
       // Shrink lists that could overflow on the next tile.
@@ -309,7 +302,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-    if (vq && !a.tilemin) a.cnt[list_id] = count;
+    if (vq && !TILEMIN) a.cnt[list_id] = count;
     if (vq && *s_abort) a.overflow[q] = 1;
   }
   tc_fence_before();
@@ -410,7 +403,8 @@ __global__ void __launch_bounds__(256) tc_tau_kernel(const float* __restrict__ t
     if (threadIdx.x == 0) init_bound[q] = INFINITY;
     return;
   }
-  for (int t = threadIdx.x; t < ntile; t += blockDim.x) buf[t] = Cand{tmin[(int64_t)t * nq + q], 0u};
+  const float* row = tmin + (int64_t)q * ntile;
+  for (int t = threadIdx.x; t < ntile; t += blockDim.x) buf[t] = Cand{row[t], 0u};
   __syncthreads();
   const uint32_t kth = sel::block_select(buf, ntile, k, s_hist, s_res);
   if (threadIdx.x == 0) {
@@ -564,22 +558,35 @@ int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d,
   a.overflow = overflow;
   a.cap = p.cap;
   a.k = kk;
-  a.mode = (metric == vrs_exact::kL2 || metric == vrs_exact::kMaha) ? 0 : 1;
   a.absm = absm;
   a.err = err;
-  a.tilemin = tmin != nullptr;
   a.tmin = tmin;
+  a.tmin_stride = 2 * ((n + BN - 1) / BN);
   a.init_bound = init_bound;
-  static bool attr_set[64] = {false};
+  const bool l2 = metric == vrs_exact::kL2 || metric == vrs_exact::kMaha;
+  auto kern = l2 ? (tmin ? knn_scan_tc_kernel<0, true> : knn_scan_tc_kernel<0, false>)
+                 : (tmin ? knn_scan_tc_kernel<1, true> : knn_scan_tc_kernel<1, false>);
+  static std::once_flag attr_once[64];
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    VRS_CUDA(cudaFuncSetAttribute(knn_scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)SMEM_TOTAL));
-    attr_set[dev] = true;
+  VRS_CUDA(cudaGetDevice(&dev));
+  int attr_err = 0;
+  if (dev < 64) {
+    std::call_once(attr_once[dev], [&] {
+      for (auto f : {knn_scan_tc_kernel<0, true>, knn_scan_tc_kernel<0, false>, knn_scan_tc_kernel<1, true>,
+                     knn_scan_tc_kernel<1, false>})
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL) !=
+            cudaSuccess)
+          attr_err = 1;
+    });
+  } else {
+    VRS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL));
+  }
+  if (attr_err) {
+    set_error(VRS_ERR_DRIVER, "cudaFuncSetAttribute(knn_scan_tc_kernel) failed");
+    return VRS_ERR_DRIVER;
   }
   dim3 grid(p.qtiles, p.nseg);
-  knn_scan_tc_kernel<<<grid, THREADS, SMEM_TOTAL, s>>>(tmA, tmB, a);
+  kern<<<grid, THREADS, SMEM_TOTAL, s>>>(tmA, tmB, a);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;

@@ -14,7 +14,7 @@ import enum
 import importlib.util
 import os
 from dataclasses import dataclass, field
-from typing import List, Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -485,6 +485,22 @@ GEN_NORMAL, GEN_NORMAL_UNIT, GEN_UNIFORM, GEN_UNIFORM_SUM1, GEN_MIXTURE = range(
 SEED_BASE = 0x5652535F42303031  # "VRS_B001"
 
 
+def shard_rows(n: int, world: int, rank: int) -> Tuple[int, int]:
+    """Rows [r0, r1) held by `rank` of `world` under GpuShardMode::Sharded:
+    contiguous chunks of ceil(n / world), the last ones possibly short or
+    empty (ddp/distributed_knn.rs:106-111, ddp/distributed_kmeans.rs:137-142).
+    Global row ids are r0 + local id."""
+    chunk = -(-n // world) if world > 0 else 0
+    r0 = min(n, rank * chunk)
+    return r0, min(n, r0 + chunk)
+
+
+def query_chunk(nq: int, world: int, rank: int) -> Tuple[int, int]:
+    """Queries [q0, q1) answered by `rank` under GpuShardMode::Replicated:
+    chunks of ceil(nq / world) in query order (ddp/distributed_knn.rs:203-229)."""
+    return shard_rows(nq, world, rank)
+
+
 def config_seed(index: int) -> int:
     return (SEED_BASE + index) & 0xFFFFFFFFFFFFFFFF
 
@@ -512,5 +528,5 @@ __all__ = [
     "DistanceMetric", "GpuShardMode", "CudaError", "SearchResult", "CudaDeviceContext",
     "DistributedKnnEngine", "CudaKnnEngine", "CudaKMeansResult", "CudaKMeansEngine",
     "DistributedKMeansEngine", "Comm", "kmeans_fit_rank", "gen_rows_host", "gen_rows_device",
-    "config_seed", "lib", "LIB_PATH", "profile_enable", "profile_reset", "profile_read",
+    "config_seed", "shard_rows", "query_chunk", "lib", "LIB_PATH", "profile_enable", "profile_reset", "profile_read",
 ]
