@@ -153,6 +153,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16(BM, BN);
+      // Descriptors differ only in the start-address field: the constant
+      // part is formed once, the field per MMA from an offset.
+      const DescSw128 a_desc(sA), b_desc(sB);
+      const int ksteps = a.ksteps;
       uint32_t g = 0;
       int lp = 0;
       bool ok = true;
@@ -168,13 +172,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
+          const uint32_t b_off = (uint32_t)(s * MAX_KBLK * BLK) >> 4;
+#pragma unroll
           for (int acc = 0; acc < NACC; acc++) {
             const uint32_t d = tmem + acc * 256 + b * BN;
-            for (int ks = 0; ks < a.ksteps; ks++) {
-              const int kb = ks >> 2, koff = (ks & 3) * 32;
-              const uint64_t ad = smem_desc_sw128(sA + (acc * MAX_KBLK + kb) * BLK + koff);
-              const uint64_t bd = smem_desc_sw128(sB + (s * MAX_KBLK + kb) * BLK + koff);
-              mma_bf16(d, ad, bd, idesc, ks > 0 ? 1u : 0u);
+            const uint32_t a_off = (uint32_t)(acc * MAX_KBLK * BLK) >> 4;
+#pragma unroll
+            for (int ks = 0; ks < MAX_KBLK * 4; ks++) {
+              if (ks < ksteps) {
+                const uint32_t off = (uint32_t)((ks >> 2) * BLK + (ks & 3) * 32) >> 4;
+                mma_bf16(d, a_desc.at(a_off + off), b_desc.at(b_off + off), idesc, ks > 0 ? 1u : 0u);
+              }
             }
           }
           mma_commit(&empty[s]);

@@ -158,6 +158,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------------- MMA issuer
     if (lane == 0 && ntiles > 0) {
       const uint32_t idesc = idesc_bf16(BM, BN);
+      // Descriptors differ only in the start-address field: the constant
+      // part is formed once, the field per MMA from an offset.
+      const DescSw128 a_desc(sA), b_desc(sB);
+      const int ksteps = a.ksteps;
       bool ok = mbar_wait(afull, 0, s_abort, a.err, 2, WAIT_NS);
       tc_fence_after();
       int last = -1;
@@ -166,13 +170,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(&full[s], (t / STAGES) & 1, s_abort, a.err, 3, WAIT_NS)) break;
         if (!mbar_wait(&tempty[b], ((t >> 1) & 1) ^ 1, s_abort, a.err, 4, WAIT_NS)) break;
         tc_fence_after();
+        const uint32_t b_off = (uint32_t)(s * MAX_KBLK * BLK_B) >> 4;
+#pragma unroll
         for (int acc = 0; acc < NACC; acc++) {
           const uint32_t d = tmem + acc * 256 + b * BN;
-          for (int ks = 0; ks < a.ksteps; ks++) {
-            const int kb = ks >> 2, koff = (ks & 3) * 32;
-            const uint64_t ad = smem_desc_sw128(sA + (acc * MAX_KBLK + kb) * BLK_A + koff);
-            const uint64_t bd = smem_desc_sw128(sB + (s * MAX_KBLK + kb) * BLK_B + koff);
-            mma_bf16(d, ad, bd, idesc, ks > 0 ? 1u : 0u);
+          const uint32_t a_off = (uint32_t)(acc * MAX_KBLK * BLK_A) >> 4;
+#pragma unroll
+          for (int ks = 0; ks < MAX_KBLK * 4; ks++) {
+            if (ks < ksteps) {
+              static_assert(BLK_A == BLK_B, "one K-step offset for both operands");
+              const uint32_t off = (uint32_t)((ks >> 2) * BLK_A + (ks & 3) * 32) >> 4;
+              mma_bf16(d, a_desc.at(a_off + off), b_desc.at(b_off + off), idesc, ks > 0 ? 1u : 0u);
+            }
           }
         }
         mma_commit(&empty[s]);

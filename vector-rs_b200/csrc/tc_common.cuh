@@ -180,6 +180,21 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
   return d;
 }
 
+// A descriptor stream for one operand region: the constant fields plus the
+// region's shared address >> 4. at(off16) gives the descriptor of the region
+// advanced by off16 * 16 bytes, masked to the 14-bit start-address field
+// exactly as smem_desc_sw128 masks it (a carry must not reach the reserved
+// bits above the field).
+struct DescSw128 {
+  uint64_t hi;    // every field except the start address
+  uint32_t base;  // shared address >> 4, unmasked
+  __device__ __forceinline__ explicit DescSw128(const void* p)
+      : hi(smem_desc_sw128(p) & ~0x3FFFull), base(smem_u32(p) >> 4) {}
+  __device__ __forceinline__ uint64_t at(uint32_t off16) const {
+    return hi | (uint64_t)((base + off16) & 0x3FFFu);
+  }
+};
+
 // Instruction descriptor, kind::f16: bf16 A and B (both K-major), f32 D.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4)                  // D format f32
