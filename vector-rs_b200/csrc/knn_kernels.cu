@@ -238,24 +238,65 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
   const int qrow = a.q_index ? a.q_index[slot] : slot;
   Cand* buf = s_buf[warp];
   int* hist = s_hist[warp];
+  // Lane l owns list l: its count and the exclusive prefix of the counts,
+  // so the lists read as one flattened array of `total` entries.
   const int cnt_l = lane < a.nseg ? a.cnt[(int64_t)lane * a.nq + slot] : 0;
-  int total = cnt_l;
+  const int pre_l = warp_incl_scan(cnt_l) - cnt_l;
+  const int total = __shfl_sync(kFull, pre_l + cnt_l, 31);
+  // Entry j of the flattened lists (all lanes call together; j may be out
+  // of range, in which case nothing is read).
+  auto entry = [&](int j, bool* valid) -> Cand {
+    int lo = 0;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFull, total, o);
+    for (int step = 16; step > 0; step >>= 1) {
+      const int pm = __shfl_sync(kFull, pre_l, lo + step);
+      if (lo + step < a.nseg && pm <= j) lo += step;
+    }
+    const int p0 = __shfl_sync(kFull, pre_l, lo);
+    *valid = j < total;
+    Cand e{INFINITY, 0xffffffffu};
+    if (*valid) e = a.cand[((int64_t)lo * a.nq + slot) * a.cap + (j - p0)];
+    return e;
+  };
+  constexpr int kBatch = 4;  // entries per lane in flight
 
   float bound = INFINITY;
   if (total > a.k) {
     uint32_t prefix = 0, pmask = 0;
     int kk = a.k;
+    // Up to kSelRmax * 2 keys are staged in shared memory (the candidate
+    // buffer, free until the compaction below), so the radix passes read
+    // global memory once; longer lists are read once per pass.
+    uint32_t* keys = reinterpret_cast<uint32_t*>(buf);
+    const bool staged = total <= 2 * kSelRmax;
+    if (staged) {
+      for (int j0 = 0; j0 < total; j0 += 32 * kBatch) {
+        Cand e[kBatch];
+        bool v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; u++) e[u] = entry(j0 + u * 32 + lane, &v[u]);
+#pragma unroll
+        for (int u = 0; u < kBatch; u++)
+          if (v[u]) keys[j0 + u * 32 + lane] = ord_key(e[u].hs);
+      }
+      __syncwarp();
+    }
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int b = lane; b < 256; b += 32) hist[b] = 0;
       __syncwarp();
-      for (int sgm = 0; sgm < a.nseg; sgm++) {
-        const int cs = __shfl_sync(kFull, cnt_l, sgm);
-        const Cand* l = a.cand + ((int64_t)sgm * a.nq + slot) * a.cap;
-        for (int i = lane; i < cs; i += 32) {
-          const uint32_t v = ord_key(l[i].hs);
+      if (staged) {
+        for (int i = lane; i < total; i += 32) {
+          const uint32_t v = keys[i];
           if ((v & pmask) == prefix) atomicAdd(&hist[(v >> shift) & 255], 1);
+        }
+      } else {
+        for (int sgm = 0; sgm < a.nseg; sgm++) {
+          const int cs = __shfl_sync(kFull, cnt_l, sgm);
+          const Cand* l = a.cand + ((int64_t)sgm * a.nq + slot) * a.cap;
+          for (int i = lane; i < cs; i += 32) {
+            const uint32_t v = ord_key(l[i].hs);
+            if ((v & pmask) == prefix) atomicAdd(&hist[(v >> shift) & 255], 1);
+          }
         }
       }
       __syncwarp();
@@ -269,22 +310,19 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
     const float absm = a.kind == kAbsMargin ? a.absm[qrow] : 0.0f;
     bound = accept_bound(a.kind, ord_inv(prefix), a.rho, absm);
   }
-  // Survivors -> shared memory.
+  // Survivors -> shared memory (batched reads of the flattened lists).
   int R = 0;
-  for (int sgm = 0; sgm < a.nseg; sgm++) {
-    const int cs = __shfl_sync(kFull, cnt_l, sgm);
-    const Cand* l = a.cand + ((int64_t)sgm * a.nq + slot) * a.cap;
-    for (int base = 0; base < cs; base += 32) {
-      const int i = base + lane;
-      Cand e;
-      bool keep = false;
-      if (i < cs) {
-        e = l[i];
-        keep = e.hs <= bound;
-      }
+  for (int j0 = 0; j0 < total; j0 += 32 * kBatch) {
+    Cand e[kBatch];
+    bool v[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; u++) e[u] = entry(j0 + u * 32 + lane, &v[u]);
+#pragma unroll
+    for (int u = 0; u < kBatch; u++) {
+      const bool keep = v[u] && e[u].hs <= bound;
       const unsigned m = __ballot_sync(kFull, keep);
       const int pos = R + __popc(m & ((1u << lane) - 1));
-      if (keep && pos < kSelRmax) buf[pos] = e;
+      if (keep && pos < kSelRmax) buf[pos] = e[u];
       R += __popc(m);
     }
   }
@@ -293,21 +331,29 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
     return;
   }
   __syncwarp();
-  // Exact re-rank, two candidates per warp step (one per half-warp); rows
-  // without an error bound (near-zero cosine rows) are scored here too.
+  // Exact re-rank, four candidates per warp step (two per half-warp, both
+  // rows' loads in flight); rows without an error bound (near-zero cosine
+  // rows) are scored here too.
   const float* qp = a.q + (int64_t)qrow * a.dp;
   const float qa = METRIC == vrs_exact::kCos ? a.q_aux[qrow] : 0.0f;
   const int half = lane >> 4, hl = lane & 15;
   const int RT = R + a.n_tiny;
-  for (int it = 0; 2 * it < RT; it++) {
-    const int i = 2 * it + half;
-    const bool act = i < RT;
-    const int ii = act ? i : 2 * it;
-    const uint32_t row = ii < R ? buf[ii].id : a.tiny[ii - R];
-    const float xa = METRIC == vrs_exact::kCos ? a.base_aux[row] : 0.0f;
-    const float key = vrs_exact::lanes::rank_key(METRIC, qp, a.base + (int64_t)row * a.dp, a.d, qa, xa, hl);
+  for (int it = 0; 4 * it < RT; it++) {
+    const int i0 = 4 * it + half, i1 = 4 * it + 2 + half;
+    const bool act0 = i0 < RT, act1 = i1 < RT;
+    const int ii0 = act0 ? i0 : 4 * it, ii1 = act1 ? i1 : 4 * it;
+    const uint32_t row0 = ii0 < R ? buf[ii0].id : a.tiny[ii0 - R];
+    const uint32_t row1 = ii1 < R ? buf[ii1].id : a.tiny[ii1 - R];
+    const float xa0 = METRIC == vrs_exact::kCos ? a.base_aux[row0] : 0.0f;
+    const float xa1 = METRIC == vrs_exact::kCos ? a.base_aux[row1] : 0.0f;
+    float key0, key1;
+    vrs_exact::lanes::rank_key2(METRIC, qp, a.base + (int64_t)row0 * a.dp, a.base + (int64_t)row1 * a.dp,
+                                a.d, qa, xa0, xa1, hl, kFull, &key0, &key1);
     __syncwarp();
-    if (act && hl == 0) buf[i] = Cand{vrs_exact::heap_score(METRIC, key), row};
+    if (hl == 0) {
+      if (act0) buf[i0] = Cand{vrs_exact::heap_score(METRIC, key0), row0};
+      if (act1) buf[i1] = Cand{vrs_exact::heap_score(METRIC, key1), row1};
+    }
   }
   __syncwarp();
   int P = 32;

@@ -158,31 +158,36 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------------- MMA issuer
     if (lane == 0 && ntiles > 0) {
       const uint32_t idesc = idesc_bf16(BM, BN);
-      // Descriptors differ only in the start-address field: the constant
-      // part is formed once, the field per MMA from an offset.
+      // This thread shares its scheduler with four epilogue warps, so each
+      // MMA should cost it about one instruction: the A descriptors (fixed
+      // for the CTA) are formed once into registers, the B descriptors once
+      // per tile. Descriptors differ only in the masked start-address field.
       const DescSw128 a_desc(sA), b_desc(sB);
       const int ksteps = a.ksteps;
+      uint64_t ad[NACC][MAX_KBLK * 4];
+#pragma unroll
+      for (int acc = 0; acc < NACC; acc++)
+#pragma unroll
+        for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+          ad[acc][ks] = a_desc.at((uint32_t)(acc * MAX_KBLK * BLK_A + (ks >> 2) * BLK_A + (ks & 3) * 32) >> 4);
       bool ok = mbar_wait(afull, 0, s_abort, a.err, 2, WAIT_NS);
       tc_fence_after();
       int last = -1;
       for (int t = 0; ok && t < ntiles; t++) {
         const int s = t % STAGES, b = t & 1;
+        uint64_t bd[MAX_KBLK * 4];
+#pragma unroll
+        for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+          bd[ks] = b_desc.at((uint32_t)(s * MAX_KBLK * BLK_B + (ks >> 2) * BLK_B + (ks & 3) * 32) >> 4);
         if (!mbar_wait(&full[s], (t / STAGES) & 1, s_abort, a.err, 3, WAIT_NS)) break;
         if (!mbar_wait(&tempty[b], ((t >> 1) & 1) ^ 1, s_abort, a.err, 4, WAIT_NS)) break;
         tc_fence_after();
-        const uint32_t b_off = (uint32_t)(s * MAX_KBLK * BLK_B) >> 4;
 #pragma unroll
         for (int acc = 0; acc < NACC; acc++) {
           const uint32_t d = tmem + acc * 256 + b * BN;
-          const uint32_t a_off = (uint32_t)(acc * MAX_KBLK * BLK_A) >> 4;
 #pragma unroll
-          for (int ks = 0; ks < MAX_KBLK * 4; ks++) {
-            if (ks < ksteps) {
-              static_assert(BLK_A == BLK_B, "one K-step offset for both operands");
-              const uint32_t off = (uint32_t)((ks >> 2) * BLK_A + (ks & 3) * 32) >> 4;
-              mma_bf16(d, a_desc.at(a_off + off), b_desc.at(b_off + off), idesc, ks > 0 ? 1u : 0u);
-            }
-          }
+          for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+            if (ks < ksteps) mma_bf16(d, ad[acc][ks], bd[ks], idesc, ks > 0 ? 1u : 0u);
         }
         mma_commit(&empty[s]);
         mma_commit(&tfull[b]);
@@ -219,6 +224,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!__all_sync(sel::kFull, ok)) break;
       tc_fence_after();
       const int64_t n0 = row_begin + (int64_t)t * BN + ch * HALF_COLS;
+      if (MODE == 0 && t + 1 < ntiles && lane < 2) {
+        // |x|^2 of this warp's columns of the next tile -> L1 (2 lines).
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(a.xn + n0 + BN + lane * 32));
+      }
       const int64_t rem_cols = row_end - n0;
       const int valid_cols = rem_cols < HALF_COLS ? (int)(rem_cols > 0 ? rem_cols : 0) : HALF_COLS;
       // Key threshold: MODE 0 passes key <= bound, MODE 1 passes key >= -bound.

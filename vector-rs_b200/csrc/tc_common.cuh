@@ -51,21 +51,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread in hardware for up to `hint_ns`
+// while the phase is incomplete (instead of spinning on issue slots).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: gives up after `limit_ns` or as soon as *abort is set, and
-// then records `code` in *abort and in the global error word.
+// then records `code` in *abort and in the global error word. Each try
+// suspends for at most 100 us, so the limit and the abort flag are checked
+// at least that often.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           int* gerr, int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; i++) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > limit_ns) {
-        *abort = code;
-        atomicCAS(gerr, 0, code);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      *abort = code;
+      atomicCAS(gerr, 0, code);
+      return false;
     }
   }
 }
