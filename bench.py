@@ -35,6 +35,11 @@ N_BASE, DIM, N_QUERY, K = 1_000_000, 128, 10_000, 100
 COS = 2
 CPU_SAMPLE_QUERIES = 1000
 KM_N, KM_D, KM_K, KM_ITERS, KM_SIGMA = 1_000_000, 128, 1024, 20, 0.1
+# DRAM bytes (read + write) of one main-scan launch over the full C2 base,
+# from the ncu capture summarised in profiles/knn_scan_tc_C2.txt; other base
+# sizes scale it by the rows scanned (the traffic is the base re-stream plus
+# the candidate lists, both proportional to the rows).
+SCAN_DRAM_BYTES_C2 = 324.854016e6 + 76.066816e6
 
 
 def parse():
@@ -77,10 +82,14 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # The timed region is short: start it only once samples flow.
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
@@ -301,7 +310,10 @@ def main():
                 "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"{pk_kind} bf16 dense (sustained)",
                 "per_launch_ms": per_launch_ms, "launches": scan_n,
-                "flops_per_launch": flops_per_launch, "traffic": None,
+                "flops_per_launch": flops_per_launch,
+                "traffic": SCAN_DRAM_BYTES_C2 * (r1 - r0) / N_BASE if n_q == N_QUERY else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size "
+                                  "C2 launch, scaled by rows scanned per GPU",
                 "breakdown_ms_per_step": {"pivot": piv_ms / max(piv_n, 1),
                                           "scan": per_launch_ms,
                                           "select": sel_ms / max(sel_n, 1),
