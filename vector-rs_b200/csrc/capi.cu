@@ -179,6 +179,7 @@ struct KnnShard {
   DBuf pb, pn;                  // pivot rows (every pivot_stride-th row)
   int64_t pivot_m = 0, pivot_stride = 1;
   DBuf tmin, ibound;            // per-search pivot-pass outputs
+  DBuf ptop, ptop_all;          // k smallest pivot minima per query: own, all shards
   // per-search scratch
   DBuf q_in, q, q_aux, cand, cnt, overflow, pairs, gathered, out_dist, out_id;
   DBuf qb, absm, err, qindex;
@@ -190,6 +191,11 @@ struct KnnShard {
 struct vrs_knn {
   int64_t n_global = 0;
   int d = 0, dp = 0, metric = 0, mode = 0, g = 1;
+  // Shards that split one base (row-sharded ranks or clique GPUs). With
+  // parts > 1 on the tensor-core path, the shards pool their pivot minima
+  // (an all-gather between the pivot pass and the main scan).
+  int parts = 1;
+  bool pooled_pivot = false;
   std::vector<std::unique_ptr<KnnShard>> shards;
   bool rank_mode = false;
   vrs_comm* comm = nullptr;  // rank mode
@@ -201,7 +207,7 @@ struct vrs_knn {
       for (DBuf* b : {&s->base, &s->base_aux, &s->q_in, &s->q, &s->q_aux, &s->cand, &s->cnt,
                       &s->overflow, &s->pairs, &s->gathered, &s->out_dist, &s->out_id, &s->xb,
                       &s->xn, &s->xmax, &s->tiny, &s->ntiny, &s->qb, &s->absm, &s->err, &s->qindex, &s->pb,
-                      &s->pn, &s->tmin, &s->ibound})
+                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all})
         b->release();
       if (s->own_stream) cudaStreamDestroy(s->own_stream);
     }
@@ -264,7 +270,7 @@ int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
     if (!s->use_tc) {
       s->xb.release();
     } else {
-      s->pivot_m = tc::tc_pivot_rows(s->n_local, &s->pivot_stride);
+      s->pivot_m = tc::tc_pivot_rows(s->n_local, h->parts, &s->pivot_stride);
       if (s->pivot_stride > 1) {
         const int64_t ppad = (s->pivot_m + 127) / 128 * 128 + 128;
         VRS_TRY(s->pb.reserve((size_t)s->pivot_m * d16 * 2));
@@ -370,12 +376,21 @@ int launch_exact_search(vrs_knn* h, KnnShard* s, int nq, int kk, const int* q_in
   return VRS_OK;
 }
 
+// Search phases. kPhaseAll runs everything on this shard. With pooled pivot
+// minima the search splits at the all-gather: kPhasePivot (query prep, pivot
+// pass, this shard's k smallest minima into ptop) and kPhaseMain (bound from
+// the gathered minima, main scan, select).
+enum { kPhaseAll = 0, kPhasePivot = 1, kPhaseMain = 2 };
+
 // Launches the tensor-core scan + exact re-rank select for all nq queries.
 int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
-                     Cand* out_pairs) {
+                     Cand* out_pairs, int phase) {
   cudaStream_t st = s->stream;
   const int d16 = tc::tc_d16(h->d);
   const int nq_alloc = (nq + 255) / 256 * 256;
+  tc::TcPlan p = tc::tc_plan(s->n_local, nq, kk, s->num_sms);
+  const int nlists = 2 * p.nseg;
+  if (phase == kPhaseMain) goto main_phase;
   VRS_TRY(s->qb.reserve((size_t)nq_alloc * d16 * 2));
   VRS_TRY(s->absm.reserve((size_t)nq * sizeof(float)));
   VRS_TRY(s->err.reserve(sizeof(int)));
@@ -384,15 +399,10 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   VRS_CUDA(cudaMemsetAsync(s->err.p, 0, sizeof(int), st));
   VRS_TRY(tc::tc_query_prep(s->q.as<float>(), nq, h->d, h->dp, h->metric, s->xmax.as<unsigned int>(),
                             s->qb.p, s->absm.as<float>(), s->overflow.as<int>(), st));
-  tc::TcPlan p = tc::tc_plan(s->n_local, nq, kk, s->num_sms);
-  const int nlists = 2 * p.nseg;
-  VRS_TRY(s->cand.reserve((size_t)nlists * nq * p.cap * sizeof(Cand)));
-  VRS_TRY(s->cnt.reserve((size_t)nlists * nq * sizeof(int)));
   VRS_TRY(s->ibound.reserve((size_t)nq * sizeof(float)));
-  VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)nlists * nq * sizeof(int), st));
+  if (phase == kPhasePivot) VRS_TRY(s->ptop.reserve((size_t)nq * kk * sizeof(float)));
   if (s->n_local > 0) {
-    // Pivot pass: per-query starting bound from the k-th smallest tile
-    // minimum over every pivot_stride-th row.
+    // Pivot pass: half-tile minima over every pivot_stride-th row.
     const void* pb = s->pivot_stride > 1 ? s->pb.p : s->xb.p;
     const float* pn = s->pivot_stride > 1 ? s->pn.as<float>() : s->xn.as<float>();
     const int ntile = 2 * (int)((s->pivot_m + 127) / 128);  // half-tile minima
@@ -402,8 +412,29 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
     VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, pb, s->pivot_m, h->d, pn, h->metric, nq, kk, pp, nullptr,
                         nullptr, s->overflow.as<int>(), s->absm.as<float>(), s->err.as<int>(),
                         s->tmin.as<float>(), nullptr, st));
-    VRS_TRY(tc::tc_tau(s->tmin.as<float>(), ntile, nq, kk, s->absm.as<float>(), s->ibound.as<float>(), st));
+    if (phase == kPhasePivot)
+      VRS_TRY(tc::tc_pivot_topk(s->tmin.as<float>(), ntile, nq, kk, s->ptop.as<float>(), st));
+    else
+      VRS_TRY(tc::tc_tau(s->tmin.as<float>(), 1, 0, ntile, nq, kk, s->absm.as<float>(),
+                         s->ibound.as<float>(), st));
     prof_end(t0, st);
+  } else if (phase == kPhasePivot) {
+    VRS_CUDA(cudaMemsetAsync(s->ptop.p, 0x7f, (size_t)nq * kk * sizeof(float), st));  // ~3.4e38
+  }
+  if (phase == kPhasePivot) return VRS_OK;
+main_phase:
+  if (phase == kPhaseMain && s->n_local > 0) {
+    // Bound from every shard's k smallest pivot minima (ptop_all, gathered).
+    const int parts = h->rank_mode ? h->comm->nranks : h->g;
+    ProfToken t0 = prof_begin("knn_pivot", st);
+    VRS_TRY(tc::tc_tau(s->ptop_all.as<float>(), parts, (int64_t)nq * kk, kk, nq, kk, s->absm.as<float>(),
+                       s->ibound.as<float>(), st));
+    prof_end(t0, st);
+  }
+  VRS_TRY(s->cand.reserve((size_t)nlists * nq * p.cap * sizeof(Cand)));
+  VRS_TRY(s->cnt.reserve((size_t)nlists * nq * sizeof(int)));
+  VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)nlists * nq * sizeof(int), st));
+  if (s->n_local > 0) {
     ProfToken t = prof_begin("knn_scan", st);
     VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, s->xb.p, s->n_local, h->d, s->xn.as<float>(), h->metric, nq, kk,
                         p, s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(),
@@ -447,9 +478,15 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
 
 // Phase 1 (asynchronous): local top-k' of the queries in s->q_in ([nq][d],
 // device). Writes final results (out_dist/out_id) or merge pairs (out_pairs).
+// `phase` splits a pooled-pivot search at its all-gather (see kPhaseAll).
 int shard_search_launch(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
-                        Cand* out_pairs) {
+                        Cand* out_pairs, int phase = kPhaseAll) {
   cudaStream_t st = s->stream;
+  if (phase == kPhaseMain) {
+    if (s->use_tc) return launch_tc_search(h, s, nq, kk, out_dist, out_id, out_pairs, phase);
+    // A shard without rows in a pooled search: padding results only.
+    return launch_exact_search(h, s, nq, kk, nullptr, s->overflow.as<int>(), out_dist, out_id, out_pairs);
+  }
   VRS_TRY(s->q.reserve((size_t)nq * h->dp * sizeof(float)));
   VRS_TRY(s->q_aux.reserve((size_t)nq * sizeof(float)));
   VRS_TRY(s->overflow.reserve((size_t)(2 * nq + 1) * sizeof(int)));
@@ -460,7 +497,13 @@ int shard_search_launch(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist
     VRS_TRY(launch_cos_norms(s->q.as<float>(), nq, h->d, h->dp, s->q_aux.as<float>(), st));
   s->last_nq = nq;
   s->last_kk = kk;
-  if (s->use_tc) return launch_tc_search(h, s, nq, kk, out_dist, out_id, out_pairs);
+  if (phase == kPhasePivot && !s->use_tc) {
+    // A shard without rows contributes no pivot minima (~3.4e38 fillers).
+    VRS_TRY(s->ptop.reserve((size_t)nq * kk * sizeof(float)));
+    VRS_CUDA(cudaMemsetAsync(s->ptop.p, 0x7f, (size_t)nq * kk * sizeof(float), st));
+    return VRS_OK;
+  }
+  if (s->use_tc) return launch_tc_search(h, s, nq, kk, out_dist, out_id, out_pairs, phase);
   return launch_exact_search(h, s, nq, kk, nullptr, s->overflow.as<int>(), out_dist, out_id, out_pairs);
 }
 
@@ -496,6 +539,69 @@ int shard_search_finish(vrs_knn* h, KnnShard* s, float* out_dist, uint32_t* out_
   return VRS_OK;
 }
 
+// Pooled pivot minima need every shard with rows on the tensor-core path and
+// one margin for all shards: the margins use the largest |x| of the whole
+// base, since a pooled bound comes from another shard's rows. Single-process
+// version: the shards' values are combined on the host.
+int agree_pooled_clique(vrs_knn* h) {
+  if (h->mode != VRS_SHARDED || h->g < 2 || !tc::tc_supported(h->metric, h->d) || getenv("VRS_DISABLE_TC"))
+    return VRS_OK;
+  unsigned int xm = 0;
+  bool all = true, any = false;
+  for (auto& sp : h->shards) {
+    KnnShard* s = sp.get();
+    if (s->n_local == 0) continue;
+    if (!s->use_tc) {
+      all = false;
+      continue;
+    }
+    any = true;
+    unsigned int v = 0;
+    VRS_CUDA(cudaSetDevice(s->device));
+    VRS_CUDA(cudaMemcpy(&v, s->xmax.p, sizeof(v), cudaMemcpyDeviceToHost));
+    xm = std::max(xm, v);  // bits of a non-negative float order like the float
+  }
+  if (!all || !any) return VRS_OK;
+  for (auto& sp : h->shards) {
+    KnnShard* s = sp.get();
+    if (!s->use_tc) continue;
+    VRS_CUDA(cudaSetDevice(s->device));
+    VRS_CUDA(cudaMemcpy(s->xmax.p, &xm, sizeof(xm), cudaMemcpyHostToDevice));
+  }
+  h->pooled_pivot = true;
+  return VRS_OK;
+}
+
+// Rank-mode version: every rank of a row-sharded handle calls this from
+// vrs_knn_create_rank (a collective: an all-reduce of the TC vote and of the
+// largest |x|).
+int agree_pooled_rank(vrs_knn* h) {
+  if (h->mode != VRS_SHARDED || h->comm->nranks < 2 || !tc::tc_supported(h->metric, h->d) ||
+      getenv("VRS_DISABLE_TC"))
+    return VRS_OK;
+  KnnShard* s = h->shards[0].get();
+  VRS_CUDA(cudaSetDevice(s->device));
+  DBuf v;
+  VRS_TRY(v.reserve(2 * sizeof(unsigned int)));
+  unsigned int host[2] = {(s->n_local == 0 || s->use_tc) ? 1u : 0u, 0u};
+  if (s->use_tc) VRS_CUDA(cudaMemcpy(&host[1], s->xmax.p, sizeof(unsigned int), cudaMemcpyDeviceToHost));
+  VRS_CUDA(cudaMemcpy(v.p, host, sizeof(host), cudaMemcpyHostToDevice));
+  unsigned int* d = v.as<unsigned int>();
+  const double tmo = env_timeout();
+  VRS_NCCL(ncclGroupStart());
+  VRS_NCCL(ncclAllReduce(d, d, 1, ncclUint32, ncclMin, s->comm, s->stream));
+  VRS_NCCL(ncclAllReduce(d + 1, d + 1, 1, ncclUint32, ncclMax, s->comm, s->stream));
+  VRS_NCCL(ncclGroupEnd());
+  VRS_TRY(nccl_ready(s->comm, tmo));
+  VRS_TRY(stream_wait(s->stream, s->comm, tmo));
+  VRS_CUDA(cudaMemcpy(host, d, sizeof(host), cudaMemcpyDeviceToHost));
+  v.release();
+  if (!host[0] || !host[1]) return VRS_OK;  // a shard off the TC path, or no rows anywhere
+  if (s->use_tc) VRS_CUDA(cudaMemcpy(s->xmax.p, &host[1], sizeof(unsigned int), cudaMemcpyHostToDevice));
+  h->pooled_pivot = true;
+  return VRS_OK;
+}
+
 int64_t query_batch(int kk) {
   (void)kk;
   return 16384;
@@ -527,7 +633,10 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
     uint32_t* oid = out_id + q0 * kk;
     if (h->mode == VRS_SHARDED) {
       // Every shard scores all queries; per-shard top-k' lists meet in an
-      // all-gather and a G-way merge.
+      // all-gather and a G-way merge. With pooled pivot minima the shards
+      // first exchange their k smallest pivot minima per query, so every
+      // shard starts its main scan from the bound of the whole base.
+      const bool pooled = h->pooled_pivot && nranks > 1;
       for (int r = 0; r < G; r++) {
         KnnShard* s = h->shards[r].get();
         VRS_CUDA(cudaSetDevice(s->device));
@@ -540,7 +649,27 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         } else {
           VRS_TRY(s->pairs.reserve((size_t)nb * kk * sizeof(Cand)));
           VRS_TRY(s->gathered.reserve((size_t)nranks * nb * kk * sizeof(Cand)));
-          VRS_TRY(shard_search_launch(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>()));
+          VRS_TRY(shard_search_launch(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>(),
+                                      pooled ? kPhasePivot : kPhaseAll));
+        }
+      }
+      if (pooled) {
+        for (int r = 0; r < G; r++) {
+          KnnShard* s = h->shards[r].get();
+          VRS_CUDA(cudaSetDevice(s->device));
+          VRS_TRY(s->ptop_all.reserve((size_t)nranks * nb * kk * sizeof(float)));
+        }
+        VRS_NCCL(ncclGroupStart());
+        for (int r = 0; r < G; r++) {
+          KnnShard* s = h->shards[r].get();
+          VRS_NCCL(ncclAllGather(s->ptop.p, s->ptop_all.p, (size_t)nb * kk, ncclFloat32, s->comm, s->stream));
+        }
+        VRS_NCCL(ncclGroupEnd());
+        for (int r = 0; r < G; r++) VRS_TRY(nccl_ready(h->shards[r]->comm, tmo));
+        for (int r = 0; r < G; r++) {
+          KnnShard* s = h->shards[r].get();
+          VRS_CUDA(cudaSetDevice(s->device));
+          VRS_TRY(shard_search_launch(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>(), kPhaseMain));
         }
       }
       for (int r = 0; r < G; r++) {
@@ -689,6 +818,7 @@ int vrs_knn_create(const float* base, int64_t n, int32_t d, int32_t num_gpus, in
   h->mode = mode;
   const int g = (int)std::max<int64_t>(1, std::min<int64_t>(num_gpus, std::max<int64_t>(n, 1)));
   h->g = g;
+  h->parts = mode == VRS_SHARDED ? g : 1;
   const int64_t chunk = (n + g - 1) / g;
   for (int r = 0; r < g; r++) {
     auto s = std::make_unique<KnnShard>();
@@ -714,6 +844,7 @@ int vrs_knn_create(const float* base, int64_t n, int32_t d, int32_t num_gpus, in
     for (int r = 0; r < g; r++) devs[r] = r;
     VRS_NCCL(ncclCommInitAll(h->clique.data(), g, devs.data()));
     for (int r = 0; r < g; r++) h->shards[r]->comm = h->clique[r];
+    VRS_TRY(agree_pooled_clique(h.get()));
   }
   *out = h.release();
   return VRS_OK;
@@ -830,6 +961,7 @@ int vrs_knn_create_rank(vrs_comm* comm, const float* shard, int64_t n_local, int
   h->g = 1;
   h->rank_mode = true;
   h->comm = comm;
+  h->parts = mode == VRS_SHARDED ? comm->nranks : 1;
   auto s = std::make_unique<KnnShard>();
   s->device = comm->device;
   s->comm = comm->comm;
@@ -840,6 +972,7 @@ int vrs_knn_create_rank(vrs_comm* comm, const float* shard, int64_t n_local, int
   s->stream = s->own_stream;
   h->shards.push_back(std::move(s));
   VRS_TRY(shard_upload(h.get(), h->shards[0].get(), shard, mem));
+  VRS_TRY(agree_pooled_rank(h.get()));
   *out = h.release();
   return VRS_OK;
 }

@@ -409,26 +409,61 @@ __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d,
 // Starting bound per query: the k-th smallest pivot-tile minimum. Each tile
 // minimum is the score of a distinct pivot row, so at least k rows score
 // <= tau and the exact k-th best is <= tau; anything in the exact top-k thus
-// has approximate score <= tau + absm.
-__global__ void __launch_bounds__(256) tc_tau_kernel(const float* __restrict__ tmin, int ntile, int nq,
-                                                     int k, const float* __restrict__ absm,
+// has approximate score <= tau + absm. With several shards the minima are
+// each shard's k smallest, all-gathered: the k-th smallest of the union is
+// the k-th smallest over every shard's pivot tiles.
+__global__ void __launch_bounds__(256) tc_tau_kernel(const float* __restrict__ vals, int nparts,
+                                                     int64_t part_stride, int len, int nq, int k,
+                                                     const float* __restrict__ absm,
                                                      float* __restrict__ init_bound) {
   extern __shared__ Cand buf[];
   __shared__ int s_hist[256];
   __shared__ int s_res[4];
   const int q = blockIdx.x;
-  if (ntile < k) {
+  const int total = nparts * len;
+  if (total < k) {
     if (threadIdx.x == 0) init_bound[q] = INFINITY;
     return;
   }
-  const float* row = tmin + (int64_t)q * ntile;
-  for (int t = threadIdx.x; t < ntile; t += blockDim.x) buf[t] = Cand{row[t], 0u};
+  for (int p = 0; p < nparts; p++) {
+    const float* row = vals + p * part_stride + (int64_t)q * len;
+    for (int t = threadIdx.x; t < len; t += blockDim.x) buf[p * len + t] = Cand{row[t], 0u};
+  }
   __syncthreads();
-  const uint32_t kth = sel::block_select(buf, ntile, k, s_hist, s_res);
+  const uint32_t kth = sel::block_select(buf, total, k, s_hist, s_res);
   if (threadIdx.x == 0) {
     const float tau = ord_inv(kth);
     init_bound[q] = isfinite(tau) ? __fadd_ru(tau, absm[q]) : INFINITY;
   }
+}
+
+// The k smallest pivot minima of each query (exactly k values: all below the
+// k-th smallest, then copies of it; +inf padding when ntile < k).
+__global__ void __launch_bounds__(256) tc_pivot_topk_kernel(const float* __restrict__ tmin, int ntile,
+                                                            int nq, int k, float* __restrict__ out) {
+  extern __shared__ Cand buf[];
+  __shared__ int s_hist[256];
+  __shared__ int s_res[4];
+  __shared__ int s_pos;
+  const int q = blockIdx.x;
+  const float* row = tmin + (int64_t)q * ntile;
+  float* dst = out + (int64_t)q * k;
+  if (ntile <= k) {
+    for (int j = threadIdx.x; j < k; j += blockDim.x) dst[j] = j < ntile ? row[j] : INFINITY;
+    return;
+  }
+  for (int t = threadIdx.x; t < ntile; t += blockDim.x) buf[t] = Cand{row[t], 0u};
+  if (threadIdx.x == 0) s_pos = 0;
+  __syncthreads();
+  const uint32_t kth = sel::block_select(buf, ntile, k, s_hist, s_res);
+  __syncthreads();
+  for (int t = threadIdx.x; t < ntile; t += blockDim.x) {
+    const float v = buf[t].hs;
+    if (ord_key(v) < kth) dst[atomicAdd(&s_pos, 1)] = v;
+  }
+  __syncthreads();
+  const float kv = ord_inv(kth);
+  for (int j = s_pos + threadIdx.x; j < k; j += blockDim.x) dst[j] = kv;
 }
 
 // Gathers every `stride`-th bf16 operand row (and |x|^2) into the pivot set.
@@ -518,16 +553,30 @@ int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, 
   return VRS_OK;
 }
 
-int tc_tau(const float* tmin, int ntile, int nq, int k, const float* absm, float* init_bound,
-           cudaStream_t s) {
+int tc_tau(const float* vals, int nparts, int64_t part_stride, int len, int nq, int k, const float* absm,
+           float* init_bound, cudaStream_t s) {
+  if (nq == 0) return VRS_OK;
+  const size_t smem = (size_t)std::max(nparts * len, 1) * sizeof(Cand);
+  if (smem > 200 * 1024) {
+    set_error(VRS_ERR_INVALID_CONFIG, "pivot tile count too large");
+    return VRS_ERR_INVALID_CONFIG;
+  }
+  VRS_CUDA(cudaFuncSetAttribute(tc_tau_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  tc_tau_kernel<<<nq, 256, smem, s>>>(vals, nparts, part_stride, len, nq, k, absm, init_bound);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+int tc_pivot_topk(const float* tmin, int ntile, int nq, int k, float* out, cudaStream_t s) {
   if (nq == 0) return VRS_OK;
   const size_t smem = (size_t)std::max(ntile, 1) * sizeof(Cand);
   if (smem > 200 * 1024) {
     set_error(VRS_ERR_INVALID_CONFIG, "pivot tile count too large");
     return VRS_ERR_INVALID_CONFIG;
   }
-  VRS_CUDA(cudaFuncSetAttribute(tc_tau_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  tc_tau_kernel<<<nq, 256, smem, s>>>(tmin, ntile, nq, k, absm, init_bound);
+  VRS_CUDA(cudaFuncSetAttribute(tc_pivot_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  tc_pivot_topk_kernel<<<nq, 256, smem, s>>>(tmin, ntile, nq, k, out);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;

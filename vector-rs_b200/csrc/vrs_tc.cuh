@@ -35,12 +35,22 @@ int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d,
             const float* absm, int* err, float* tmin, const float* init_bound, cudaStream_t s);
 int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, int d, void* pb,
                     float* pn, cudaStream_t s);
-int tc_tau(const float* tmin, int ntile, int nq, int k, const float* absm, float* init_bound,
-           cudaStream_t s);
-// Rows in the pivot set (every stride-th row) for a shard of n rows.
-inline int64_t tc_pivot_rows(int64_t n, int64_t* stride) {
+// Starting bound per query from pivot minima: query q's values are
+// vals[p * part_stride + q * len + j] for p < nparts, j < len (one part per
+// shard after an all-gather, or nparts = 1 for a single shard's minima); the
+// bound is the k-th smallest of them plus absm[q].
+int tc_tau(const float* vals, int nparts, int64_t part_stride, int len, int nq, int k, const float* absm,
+           float* init_bound, cudaStream_t s);
+// The k smallest of each query's ntile pivot minima (query-major rows) into
+// out[q * k + j], padded with +inf when there are fewer than k.
+int tc_pivot_topk(const float* tmin, int ntile, int nq, int k, float* out, cudaStream_t s);
+// Rows in the pivot set (every stride-th row) of a shard of n rows when
+// `parts` shards share one base and pool their pivot minima: the pooled
+// pivot set is about 1/6 of the base and at least 65,536 rows.
+inline int64_t tc_pivot_rows(int64_t n, int parts, int64_t* stride) {
   int64_t m = n / 6;
-  if (m < 65536) m = 65536;
+  const int64_t lo = (65536 + parts - 1) / parts;
+  if (m < lo) m = lo;
   if (m > 1600000) m = 1600000;
   if (m >= n) {
     *stride = 1;
