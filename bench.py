@@ -1,8 +1,9 @@
 #!/usr/bin/env python
-"""bench.py -- flat kNN queries/s (C2: 1M x 128 cosine, k=100) and k-means
-iterations/s (C3) on B200, through libvrs's C ABI.
+"""bench.py -- flat kNN queries/s (default C2: 1M x 128 cosine, k=100) and
+k-means iterations/s (default C3) on B200, through libvrs's C ABI.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1|c2|c4-l1|c4-linf|c4-hell|c5a] [--km-workload c3|c5b]
 
 N > 1 is launched by torchrun (one process per GPU); each rank holds a row
 shard of the base (GpuShardMode::Sharded) and the ranks meet in an NCCL
@@ -31,10 +32,45 @@ sys.path.insert(0, os.path.join(ROOT, "vector-rs_b200", "python"))
 
 import numpy as np  # noqa: E402
 
-N_BASE, DIM, N_QUERY, K = 1_000_000, 128, 10_000, 100
-COS = 2
-CPU_SAMPLE_QUERIES = 1000
-KM_N, KM_D, KM_K, KM_ITERS, KM_SIGMA = 1_000_000, 128, 1024, 20, 0.1
+L2, DOT, COS, L1, CHEB, HELL = 0, 1, 2, 3, 5, 9
+
+# kNN workloads (the default is the headline C2).
+# seed index = config index (C1 0, C2 1, C3 2, C4 3, C5 4).
+WORKLOADS = {
+    "c2": dict(metric=COS, n=1_000_000, d=128, nq=10_000, k=100, gen="GEN_NORMAL_UNIT", seed=1,
+               cpu_sample=1000,
+               name="C2 cosine flat kNN: base 1,000,000 x 128, 10,000 queries, k=100, "
+                    "GpuShardMode::Sharded over N GPUs",
+               data="synthetic: Philox4x32-10 N(0,1) rows L2-normalised (f64), generated on device"),
+    "c1": dict(metric=L2, n=10_000, d=128, nq=1_000, k=10, gen="GEN_NORMAL", seed=0, cpu_sample=1000,
+               name="C1 squared-L2 flat kNN: base 10,000 x 128, 1,000 queries, k=10",
+               data="synthetic: Philox4x32-10 N(0,1), generated on device"),
+    "c4-l1": dict(metric=L1, n=1_000_000, d=96, nq=10_000, k=10, gen="GEN_UNIFORM", seed=3, cpu_sample=200,
+                  name="C4 Manhattan flat kNN: base 1,000,000 x 96 U[0,1), 10,000 queries, k=10",
+                  data="synthetic: Philox4x32-10 U[0,1), generated on device"),
+    "c4-linf": dict(metric=CHEB, n=1_000_000, d=96, nq=10_000, k=10, gen="GEN_UNIFORM", seed=3, cpu_sample=200,
+                    name="C4 Chebyshev flat kNN: base 1,000,000 x 96 U[0,1), 10,000 queries, k=10",
+                    data="synthetic: Philox4x32-10 U[0,1), generated on device"),
+    "c4-hell": dict(metric=HELL, n=1_000_000, d=96, nq=10_000, k=10, gen="GEN_UNIFORM_SUM1", seed=3,
+                    cpu_sample=200,
+                    name="C4 Hellinger flat kNN: base 1,000,000 x 96 U[0,1) rows scaled to sum 1, "
+                         "10,000 queries, k=10",
+                    data="synthetic: Philox4x32-10 U[0,1) rows scaled to sum 1 (f64), generated on device"),
+    "c5a": dict(metric=L2, n=100_000_000, d=96, nq=10_000, k=100, gen="GEN_NORMAL", seed=4, cpu_sample=20,
+                name="C5a squared-L2 flat kNN: base 100,000,000 x 96 N(0,1) (38.4 GB), 10,000 queries, "
+                     "k=100, row-sharded",
+                data="synthetic: Philox4x32-10 N(0,1), generated on device shard by shard"),
+}
+# k-means workloads (the default is C3).
+KM_WORKLOADS = {
+    "c3": dict(n=1_000_000, d=128, K=1024, iters=20, sigma=0.1, seed=2, stream_c=2, stream_x=0,
+               name="C3: 1M x 128, K=1024, 20 iterations"),
+    "c5b": dict(n=10_000_000, d=96, K=16_384, iters=10, sigma=0.05, seed=4, stream_c=5, stream_x=6,
+                name="C5b: 10M x 96, K=16384, 10 iterations"),
+}
+METRIC_NAMES = {L2: "squared-L2", DOT: "dot", COS: "cosine", L1: "Manhattan", CHEB: "Chebyshev",
+                HELL: "Hellinger"}
+TC_METRICS = (L2, DOT, COS, 7)
 # DRAM bytes (read + write) of one main-scan launch over the full C2 base,
 # from the ncu capture summarised in profiles/knn_scan_tc_C2.txt; other base
 # sizes scale it by the rows scanned (the traffic is the base re-stream plus
@@ -48,12 +84,15 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--km-workload", choices=sorted(KM_WORKLOADS), default="c3")
     ap.add_argument("--no-kmeans", action="store_true")
+    ap.add_argument("--no-knn", action="store_true", help="k-means only (its line becomes the output)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--n-base", type=int, default=N_BASE)
-    ap.add_argument("--n-query", type=int, default=N_QUERY)
-    ap.add_argument("--km-n", type=int, default=KM_N, help="k-means points (C3: 1,000,000)")
-    ap.add_argument("--km-iters", type=int, default=KM_ITERS)
+    ap.add_argument("--n-base", type=int, default=None, help="override the workload's base rows")
+    ap.add_argument("--n-query", type=int, default=None, help="override the workload's query count")
+    ap.add_argument("--km-n", type=int, default=None, help="override the k-means point count")
+    ap.add_argument("--km-iters", type=int, default=None)
     return ap.parse_args()
 
 
@@ -144,7 +183,7 @@ def host_gen(vc, kind, seed, stream, rows, d, threads=None):
     return out
 
 
-def cpu_leg(base, queries, k, sample):
+def cpu_leg(w, base, queries, sample):
     """Timed oracle (restated reference CPU path) on a query sample."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
@@ -152,42 +191,75 @@ def cpu_leg(base, queries, k, sample):
     cores = os.cpu_count() or 1
     qs = queries[:sample]
     t0 = time.perf_counter()
-    d, i = oracle.knn_search(base, qs, k, COS, nthreads=cores)
+    d, i = oracle.knn_search(base, qs, w["k"], w["metric"], nthreads=cores)
     dt = time.perf_counter() - t0
     return {"value": sample / dt, "unit": "queries/s", "cores": cores, "kind": "port",
-            "sample": f"{sample} of the {N_QUERY} C2 queries against the full {len(base)}-row base "
+            "sample": f"{sample} of the {w['nq']} queries against the full {len(base)}-row base "
                       f"(AVX-512 restatement of search_batch_cpu, {cores} threads)",
             "seconds": dt}, (d, i)
 
 
+def workload(args):
+    w = dict(WORKLOADS[args.workload])
+    if args.n_base:
+        w["n"] = args.n_base
+    if args.n_query:
+        w["nq"] = args.n_query
+    return w
+
+
+def km_workload(args):
+    w = dict(KM_WORKLOADS[args.km_workload])
+    if args.km_n:
+        w["n"] = args.km_n
+    if args.km_iters:
+        w["iters"] = args.km_iters
+    return w
+
+
+def fmt_count(n):
+    if n % 1_000_000 == 0:
+        return f"{n // 1_000_000}M"
+    if n % 1000 == 0:
+        return f"{n // 1000}k"
+    return str(n)
+
+
+def metric_label(w):
+    return f"flat kNN queries/s ({fmt_count(w['n'])} x {w['d']} {METRIC_NAMES[w['metric']]}, k={w['k']})"
+
+
 def reference_arm(args):
+    """The reference's CPU path (oracle restatement of search_batch_cpu, all
+    host threads) on the same workload, a bounded query sample per step."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     import vector_cuda as vc
-    seed = vc.config_seed(1)
-    base = host_gen(vc, vc.GEN_NORMAL_UNIT, seed, 0, args.n_base, DIM)
-    queries = host_gen(vc, vc.GEN_NORMAL_UNIT, seed, 1, min(args.n_query, 2000), DIM)
+    w = workload(args)
+    seed = vc.config_seed(w["seed"])
+    kind = getattr(vc, w["gen"])
+    base = host_gen(vc, kind, seed, 0, w["n"], w["d"])
+    queries = host_gen(vc, kind, seed, 1, min(w["nq"], 2000), w["d"])
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     oracle.build()
     cores = os.cpu_count() or 1
-    per_step = 100
-    for w in range(args.warmup):
-        oracle.knn_search(base, queries[:16], K, COS, nthreads=cores)
+    per_step = max(1, min(100, w["cpu_sample"]))
+    for _ in range(args.warmup):
+        oracle.knn_search(base, queries[:16], w["k"], w["metric"], nthreads=cores)
     t0 = time.perf_counter()
     for s in range(args.steps):
         q0 = (s * per_step) % (len(queries) - per_step + 1)
-        oracle.knn_search(base, queries[q0:q0 + per_step], K, COS, nthreads=cores)
+        oracle.knn_search(base, queries[q0:q0 + per_step], w["k"], w["metric"], nthreads=cores)
     dt = time.perf_counter() - t0
     v = per_step * args.steps / dt
     line = {
-        "impl": "reference", "metric": "flat kNN queries/s (1M x 128 cosine, k=100)", "value": v,
+        "impl": "reference", "metric": metric_label(w), "value": v,
         "unit": "queries/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (Philox4x32-10, C2 distribution)",
-        "config": {"workload": "C2 cosine flat kNN, base 1,000,000 x 128 unit rows, k=100",
-                   "n_base": args.n_base, "queries_per_step": per_step, "k": K},
+        "vs_baseline": None, "dtype": "f32", "data": w["data"].replace("generated on device", "host"),
+        "config": {"workload": w["name"], "n_base": w["n"], "queries_per_step": per_step, "k": w["k"]},
         "cpu_baseline": {"value": v, "unit": "queries/s", "cores": cores, "kind": "port",
                          "sample": f"{per_step} queries per step against the full base, "
                                    f"{cores} threads (reference Rust cannot build here: "
@@ -220,26 +292,7 @@ def main():
     if dist:
         dist.broadcast_object_list(uid, src=0)
     comm = vc.Comm.init(uid[0], world, rank, local)
-
-    # ---------------------------------------------------------------- data
-    n_base, n_q = args.n_base, args.n_query
-    seed = vc.config_seed(1)
-    r0, r1 = vc.shard_rows(n_base, world, rank)
-    shard = torch.empty((max(r1 - r0, 1), DIM), dtype=torch.float32, device=dev)
-    vc.gen_rows_device(vc.GEN_NORMAL_UNIT, seed, 0, r0, r1 - r0, DIM, shard.data_ptr())
-    q_dev = torch.empty((n_q, DIM), dtype=torch.float32, device=dev)
-    vc.gen_rows_device(vc.GEN_NORMAL_UNIT, seed, 1, 0, n_q, DIM, q_dev.data_ptr())
-    torch.cuda.synchronize()
-    eng = vc.DistributedKnnEngine.create_rank(comm, None, DIM, r0, n_base, vc.GpuShardMode.Sharded,
-                                              vc.DistanceMetric.CosineSimilarity,
-                                              device_ptr=shard.data_ptr(), n_local=r1 - r0)
     stream = torch.cuda.current_stream(dev)
-    eng.set_stream(stream.cuda_stream)
-    out_d = torch.empty((n_q, K), dtype=torch.float32, device=dev)
-    out_i = torch.empty((n_q, K), dtype=torch.int32, device=dev)
-
-    def step_dev():
-        return eng.search_device(q_dev.data_ptr(), n_q, K, out_d.data_ptr(), out_i.data_ptr())
 
     def barrier():
         if dist:
@@ -252,6 +305,48 @@ def main():
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    pk, pk_kind = peaks()
+    peak_tc = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    line = None
+    if not args.no_knn:
+        line = knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, max_over_ranks,
+                         pk, pk_kind, peak_tc)
+    if not args.no_kmeans:
+        km = kmeans_bench(args, vc, torch, comm, dev, world, rank, barrier, max_over_ranks, peak_tc)
+        if line is None:
+            line = km
+        else:
+            line["kmeans"] = km
+    comm.close()
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, max_over_ranks,
+              pk, pk_kind, peak_tc):
+    w = workload(args)
+    n_base, n_q, D, K, metric = w["n"], w["nq"], w["d"], w["k"], w["metric"]
+    seed = vc.config_seed(w["seed"])
+    kind = getattr(vc, w["gen"])
+    r0, r1 = vc.shard_rows(n_base, world, rank)
+    shard = torch.empty((max(r1 - r0, 1), D), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(kind, seed, 0, r0, r1 - r0, D, shard.data_ptr())
+    q_dev = torch.empty((n_q, D), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(kind, seed, 1, 0, n_q, D, q_dev.data_ptr())
+    torch.cuda.synchronize()
+    eng = vc.DistributedKnnEngine.create_rank(comm, None, D, r0, n_base, vc.GpuShardMode.Sharded,
+                                              vc.DistanceMetric(metric),
+                                              device_ptr=shard.data_ptr(), n_local=r1 - r0)
+    eng.set_stream(stream.cuda_stream)
+    out_d = torch.empty((n_q, K), dtype=torch.float32, device=dev)
+    out_i = torch.empty((n_q, K), dtype=torch.int32, device=dev)
+
+    def step_dev():
+        return eng.search_device(q_dev.data_ptr(), n_q, K, out_d.data_ptr(), out_i.data_ptr())
 
     for _ in range(args.warmup):
         step_dev()
@@ -276,7 +371,7 @@ def main():
     value = n_q * args.steps / (ms / 1e3)
 
     # ----------------------------------------------------------- e2e (host)
-    q_host = torch.empty((n_q, DIM), dtype=torch.float32, pin_memory=True)
+    q_host = torch.empty((n_q, D), dtype=torch.float32, pin_memory=True)
     q_host.copy_(q_dev.cpu())
     hd = torch.empty((n_q, K), dtype=torch.float32, pin_memory=True)
     hi = torch.empty((n_q, K), dtype=torch.int32, pin_memory=True)
@@ -301,111 +396,130 @@ def main():
     e2e = n_q * args.steps / (ms_e2e / 1e3)
 
     # ------------------------------------------------------------ roofline
-    pk, pk_kind = peaks()
-    flops_per_launch = 2.0 * (r1 - r0) * DIM * n_q  # algorithmic: 2*N_local*D per query
+    n_loc = r1 - r0
     per_launch_ms = scan_ms / max(scan_n, 1)
-    achieved = flops_per_launch / (per_launch_ms / 1e3) / 1e12
-    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
-    roofline = {"bound": "tensor", "kernel": "knn_scan", "achieved": achieved, "peak": peak,
-                "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_source": f"{pk_kind} bf16 dense (sustained)",
-                "per_launch_ms": per_launch_ms, "launches": scan_n,
-                "flops_per_launch": flops_per_launch,
-                "traffic": SCAN_DRAM_BYTES_C2 * (r1 - r0) / N_BASE if n_q == N_QUERY else None,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size "
-                                  "C2 launch, scaled by rows scanned per GPU",
-                "breakdown_ms_per_step": {"pivot": piv_ms / max(piv_n, 1),
-                                          "scan": per_launch_ms,
-                                          "select": sel_ms / max(sel_n, 1),
-                                          "merge": merge_ms / max(merge_n, 1)},
-                "note": "knn_scan = tcgen05 bf16 distance GEMM fused with thresholded candidate "
-                        "lists (pivot-seeded bound); survivors re-ranked exactly in f32"}
-
+    breakdown = {"pivot": piv_ms / max(piv_n, 1), "scan": per_launch_ms,
+                 "select": sel_ms / max(sel_n, 1), "merge": merge_ms / max(merge_n, 1)}
+    if metric in TC_METRICS and D <= 128:
+        flops_per_launch = 2.0 * n_loc * D * n_q  # algorithmic: 2*N_local*D per query
+        achieved = flops_per_launch / (per_launch_ms / 1e3) / 1e12
+        is_c2 = args.workload == "c2" and n_base == WORKLOADS["c2"]["n"] and n_q == WORKLOADS["c2"]["nq"]
+        roofline = {"bound": "tensor", "kernel": "knn_scan", "achieved": achieved, "peak": peak_tc,
+                    "unit": "TFLOP/s", "frac": achieved / peak_tc,
+                    "peak_source": f"{pk_kind} bf16 dense (sustained)",
+                    "per_launch_ms": per_launch_ms, "launches": scan_n,
+                    "flops_per_launch": flops_per_launch,
+                    "traffic": SCAN_DRAM_BYTES_C2 * n_loc / n_base if is_c2 else None,
+                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size "
+                                      "C2 launch, scaled by rows scanned per GPU",
+                    "breakdown_ms_per_step": breakdown,
+                    "note": "knn_scan = tcgen05 bf16 distance GEMM fused with thresholded candidate "
+                            "lists (pivot-seeded bound); survivors re-ranked exactly in f32"}
+        dtype = "bf16 tensor-core scan + f32 exact re-rank"
+    else:
+        bytes_per_launch = n_loc * D * 4.0 + n_q * D * 4.0 + n_q * K * 8.0
+        gbs = bytes_per_launch / (per_launch_ms / 1e3) / 1e9
+        ops = 2.0 * n_loc * D * n_q
+        clock_mhz = clk.summary().get("sm_mhz") or 1965.0
+        fp32_peak = 148 * 128 * clock_mhz * 1e6 / 1e12  # FP32 lanes x clock, T ops/s
+        ach_ops = ops / (per_launch_ms / 1e3) / 1e12
+        roofline = {"bound": "hbm", "kernel": "knn_scan", "achieved": gbs, "peak": pk["hbm_gbs"],
+                    "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": f"{pk_kind} HBM copy",
+                    "per_launch_ms": per_launch_ms, "launches": scan_n,
+                    "bytes_per_launch": bytes_per_launch, "traffic": None,
+                    "binding": {"pipe": "fp32 CUDA cores", "achieved": ach_ops, "unit": "T ops/s",
+                                "peak": fp32_peak, "frac": ach_ops / fp32_peak,
+                                "ops_per_launch": ops,
+                                "peak_source": "148 SMs x 128 FP32 lanes x median SM clock in the timed region"},
+                    "breakdown_ms_per_step": breakdown,
+                    "note": "knn_scan = register-blocked CUDA-core scan (2 FP32 ops per element pair) "
+                            "with pivot-seeded bounds; survivors re-ranked exactly"}
+        dtype = "f32 CUDA-core scan + f32 exact re-rank"
+    big = n_loc * D * 4 > 126e6
     line = {
-        "metric": "flat kNN queries/s (1M x 128 cosine, k=100)", "value": value,
+        "metric": metric_label(w), "value": value,
         "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16 tensor-core scan + f32 exact re-rank",
-        "data": "synthetic: Philox4x32-10 N(0,1) rows L2-normalised (f64), generated on device",
-        "config": {"workload": "C2 cosine flat kNN: base 1,000,000 x 128, 10,000 queries, k=100, "
-                               "GpuShardMode::Sharded over N GPUs",
-                   "n_base": n_base, "queries_per_step": n_q, "k": K, "dim": DIM,
+        "vs_baseline": None, "dtype": dtype, "data": w["data"],
+        "config": {"workload": w["name"], "n_base": n_base, "queries_per_step": n_q, "k": K, "dim": D,
                    "parallelism": f"row-sharded x{world} + NCCL all-gather merge",
-                   "l2": "inputs larger than L2 (512 MB f32 base), no flush"},
+                   "l2": ("inputs larger than L2 (f32 base shard %.0f MB), no flush" % (n_loc * D * 4 / 1e6))
+                         if big else "base shard smaller than L2: steps see a warm L2"},
         "roofline": roofline,
-        "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": n_q * DIM * 4,
+        "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": n_q * D * 4,
                 "d2h_bytes_per_step": n_q * K * 8, "ms_per_step": ms_e2e / args.steps},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
         "clocks_e2e": clk2.summary(),
     }
-
-    # ------------------------------------------------------- k-means (C3)
-    if not args.no_kmeans:
-        km_seed = vc.config_seed(2)
-        KMN = args.km_n
-        k0, k1 = vc.shard_rows(KMN, world, rank)
-        cent = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)
-        vc.gen_rows_device(vc.GEN_NORMAL, km_seed, 2, 0, KM_K, KM_D, cent.data_ptr())
-        xs = torch.empty((max(k1 - k0, 1), KM_D), dtype=torch.float32, device=dev)
-        vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, 0, k0, k1 - k0, KM_D, xs.data_ptr(),
-                           cent.data_ptr(), KM_K, KM_SIGMA)
-        init = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)
-        vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, 0, 0, KM_K, KM_D, init.data_ptr(),
-                           cent.data_ptr(), KM_K, KM_SIGMA)
-        init_h = init.cpu().numpy()
-        torch.cuda.synchronize()
-        vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, 2, 0.0,
-                           vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(), n_local=k1 - k0)
-        barrier()
-        vc.profile_reset()
-        vc.profile_enable(True)
-        t0 = time.perf_counter()
-        res = vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, args.km_iters, 0.0,
-                                 vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(),
-                                 n_local=k1 - k0)
-        barrier()
-        km_s = max_over_ranks(time.perf_counter() - t0)
-        vc.profile_enable(False)
-        a_ms, a_n = vc.profile_read("kmeans_assign")
-        u_ms, u_n = vc.profile_read("kmeans_update")
-        f_ms, f_n = vc.profile_read("kmeans_finalize")
-        s_ms, s_n = vc.profile_read("kmeans_sums")
-        a_flops = 2.0 * (k1 - k0) * KM_K * KM_D
-        a_ach = a_flops / (a_ms / max(a_n, 1) / 1e3) / 1e12
-        line["kmeans"] = {
-            "metric": "k-means iterations/s (C3: 1M x 128, K=1024, 20 iterations)",
-            "value": res.iterations / km_s, "unit": "iterations/s", "iterations": res.iterations,
-            "inertia": res.inertia, "seconds": km_s,
-            "timing": "host wall clock around vrs_kmeans_fit_rank (data resident in HBM, "
-                      "includes per-iteration convergence readback), max over ranks",
-            "assign_roofline": {"bound": "tensor", "achieved": a_ach, "peak": peak,
-                                "unit": "TFLOP/s", "frac": a_ach / peak,
-                                "per_launch_ms": a_ms / max(a_n, 1), "launches": a_n},
-            "update_ms_per_launch": u_ms / max(u_n, 1),
-            "finalize_ms_per_launch": f_ms / max(f_n, 1),
-            "sums_ms_per_launch": s_ms / max(s_n, 1)}
-
     # ------------------------------------------------------- CPU baseline
     if rank == 0 and world == 1 and not args.no_cpu:
-        base_h = shard[: r1 - r0].cpu().numpy()
-        q_h = q_dev[:CPU_SAMPLE_QUERIES].cpu().numpy()
-        cb, (do, io) = cpu_leg(base_h, q_h, K, CPU_SAMPLE_QUERIES)
+        sample = min(w["cpu_sample"], n_q)
+        base_h = shard[:n_loc].cpu().numpy()
+        q_h = q_dev[:sample].cpu().numpy()
+        cb, (do, io) = cpu_leg(w, base_h, q_h, sample)
         line["cpu_baseline"] = cb
-        gi = out_i[:CPU_SAMPLE_QUERIES].cpu().numpy().view(np.uint32)
-        gd = out_d[:CPU_SAMPLE_QUERIES].cpu().numpy()
+        gi = out_i[:sample].cpu().numpy().view(np.uint32)
+        gd = out_d[:sample].cpu().numpy()
         line["parity_sample"] = {
-            "queries": CPU_SAMPLE_QUERIES,
+            "queries": sample,
             "ids_equal_frac": float((gi == io).mean()),
             "dist_bit_equal_frac": float((gd.view(np.uint32) == do.view(np.uint32)).mean())}
-
     eng.close()
-    comm.close()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist:
-        dist.destroy_process_group()
-    return 0
+    del shard, q_dev
+    torch.cuda.empty_cache()
+    return line
+
+
+def kmeans_bench(args, vc, torch, comm, dev, world, rank, barrier, max_over_ranks, peak_tc):
+    w = km_workload(args)
+    KMN, KM_D, KM_K = w["n"], w["d"], w["K"]
+    km_seed = vc.config_seed(w["seed"])
+    k0, k1 = vc.shard_rows(KMN, world, rank)
+    cent = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(vc.GEN_NORMAL, km_seed, w["stream_c"], 0, KM_K, KM_D, cent.data_ptr())
+    xs = torch.empty((max(k1 - k0, 1), KM_D), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, w["stream_x"], k0, k1 - k0, KM_D, xs.data_ptr(),
+                       cent.data_ptr(), KM_K, w["sigma"])
+    init = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)  # the first K points
+    vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, w["stream_x"], 0, KM_K, KM_D, init.data_ptr(),
+                       cent.data_ptr(), KM_K, w["sigma"])
+    init_h = init.cpu().numpy()
+    torch.cuda.synchronize()
+    vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, 2, 0.0,
+                       vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(), n_local=k1 - k0)
+    barrier()
+    vc.profile_reset()
+    vc.profile_enable(True)
+    t0 = time.perf_counter()
+    res = vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, w["iters"], 0.0,
+                             vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(), n_local=k1 - k0)
+    barrier()
+    km_s = max_over_ranks(time.perf_counter() - t0)
+    vc.profile_enable(False)
+    a_ms, a_n = vc.profile_read("kmeans_assign")
+    u_ms, u_n = vc.profile_read("kmeans_update")
+    f_ms, f_n = vc.profile_read("kmeans_finalize")
+    s_ms, s_n = vc.profile_read("kmeans_sums")
+    a_flops = 2.0 * (k1 - k0) * KM_K * KM_D
+    a_ach = a_flops / (a_ms / max(a_n, 1) / 1e3) / 1e12
+    out = {
+        "metric": f"k-means iterations/s ({w['name']})",
+        "value": res.iterations / km_s, "unit": "iterations/s", "higher_is_better": True,
+        "n_gpus": world, "iterations": res.iterations, "inertia": res.inertia, "seconds": km_s,
+        "config": {"workload": w["name"], "n": KMN, "dim": KM_D, "K": KM_K, "sigma": w["sigma"],
+                   "init": "the first K points", "tol": 0.0},
+        "timing": "host wall clock around vrs_kmeans_fit_rank (data resident in HBM, "
+                  "includes per-iteration convergence readback), max over ranks",
+        "assign_roofline": {"bound": "tensor", "achieved": a_ach, "peak": peak_tc,
+                            "unit": "TFLOP/s", "frac": a_ach / peak_tc,
+                            "per_launch_ms": a_ms / max(a_n, 1), "launches": a_n},
+        "update_ms_per_launch": u_ms / max(u_n, 1),
+        "finalize_ms_per_launch": f_ms / max(f_n, 1),
+        "sums_ms_per_launch": s_ms / max(s_n, 1)}
+    del xs, cent, init
+    torch.cuda.empty_cache()
+    return out
 
 
 if __name__ == "__main__":

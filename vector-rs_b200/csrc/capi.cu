@@ -17,6 +17,7 @@
 #include "vrs_exact.cuh"
 #include "vrs_internal.cuh"
 #include "vrs_kmeans_tc.cuh"
+#include "vrs_simt.cuh"
 #include "vrs_tc.cuh"
 
 namespace vrs {
@@ -180,6 +181,7 @@ struct KnnShard {
   int64_t pivot_m = 0, pivot_stride = 1;
   DBuf tmin, ibound;            // per-search pivot-pass outputs
   DBuf ptop, ptop_all;          // k smallest pivot minima per query: own, all shards
+  bool use_simt = false;        // CUDA-core scan (Manhattan, Chebyshev, Hellinger)
   // per-search scratch
   DBuf q_in, q, q_aux, cand, cnt, overflow, pairs, gathered, out_dist, out_id;
   DBuf qb, absm, err, qindex;
@@ -250,6 +252,7 @@ int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
                              s->stream));
   VRS_CUDA(cudaStreamSynchronize(s->stream));
   VRS_CUDA(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, s->device));
+  if (simt::simt_supported(h->metric, h->dp) && !getenv("VRS_DISABLE_SIMT")) s->use_simt = true;
   if (tc::tc_supported(h->metric, h->d) && !getenv("VRS_DISABLE_TC")) {
     const int d16 = tc::tc_d16(h->d);
     const int64_t npad = (s->n_local + 127) / 128 * 128 + 128;
@@ -476,6 +479,69 @@ main_phase:
   return VRS_OK;
 }
 
+// CUDA-core scan (Manhattan, Chebyshev, Hellinger): pivot pass for the
+// starting bounds, main scan, then the block select's exact re-rank.
+int launch_simt_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
+                       Cand* out_pairs) {
+  cudaStream_t st = s->stream;
+  const float rho = simt::simt_rho(h->metric, h->d);
+  simt::SimtPlan p = simt::simt_plan(s->n_local, nq, s->num_sms);
+  const int cap = next_pow2(std::max(256, 2 * kk + 64));
+  VRS_TRY(s->ibound.reserve((size_t)nq * sizeof(float)));
+  VRS_TRY(s->cand.reserve((size_t)p.nseg * nq * cap * sizeof(Cand)));
+  VRS_TRY(s->cnt.reserve((size_t)p.nseg * nq * sizeof(int)));
+  VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)p.nseg * nq * sizeof(int), st));
+  if (s->n_local > 0) {
+    // Pivot pass over every pstride-th row, read in place.
+    int64_t pstride = 1;
+    const int64_t pm = simt::simt_pivot_rows(s->n_local, kk, 1, &pstride);
+    const int64_t tr = simt::simt_tile_rows();
+    const int ntile = (int)((pm + tr - 1) / tr);
+    simt::SimtPlan pp = simt::simt_plan(pm, nq, s->num_sms);
+    VRS_TRY(s->tmin.reserve((size_t)ntile * nq * sizeof(float)));
+    ProfToken t0 = prof_begin("knn_pivot", st);
+    VRS_TRY(simt::simt_scan(s->base.as<float>(), pm, pstride, h->dp, s->q.as<float>(), nq, h->metric, pp, nullptr,
+                            nullptr, nullptr, 0, nullptr, s->tmin.as<float>(), ntile, st));
+    VRS_TRY(simt::simt_tau(s->tmin.as<float>(), ntile, nq, kk, rho, s->ibound.as<float>(), st));
+    prof_end(t0, st);
+    ProfToken t = prof_begin("knn_scan", st);
+    VRS_TRY(simt::simt_scan(s->base.as<float>(), s->n_local, 1, h->dp, s->q.as<float>(), nq, h->metric, p,
+                            s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(), cap,
+                            s->ibound.as<float>(), nullptr, 0, st));
+    prof_end(t, st);
+  }
+  KnnSelectArgs sa{};
+  sa.base = s->base.as<float>();
+  sa.base_aux = s->base_aux.as<float>();
+  sa.d = h->d;
+  sa.dp = h->dp;
+  sa.q = s->q.as<float>();
+  sa.q_aux = s->q_aux.as<float>();
+  sa.q_index = nullptr;
+  sa.nq = nq;
+  sa.k = kk;
+  sa.nseg = s->n_local > 0 ? p.nseg : 0;
+  sa.cand = s->cand.as<Cand>();
+  sa.cnt = s->cnt.as<int>();
+  sa.overflow = s->overflow.as<int>();
+  sa.cap = cap;
+  sa.metric = h->metric;
+  sa.kind = kRelMargin;
+  sa.rho = rho;
+  sa.absm = nullptr;
+  sa.id_offset = (uint32_t)s->offset;
+  sa.out_dist = out_dist;
+  sa.out_id = out_id;
+  sa.out_pairs = out_pairs;
+  sa.max_sort = std::min(16384, next_pow2(std::max(1024, 8 * kk + 256)));
+  sa.tiny = nullptr;
+  sa.n_tiny = 0;
+  ProfToken t = prof_begin("knn_select", st);
+  VRS_TRY(launch_knn_select(sa, st));
+  prof_end(t, st);
+  return VRS_OK;
+}
+
 // Phase 1 (asynchronous): local top-k' of the queries in s->q_in ([nq][d],
 // device). Writes final results (out_dist/out_id) or merge pairs (out_pairs).
 // `phase` splits a pooled-pivot search at its all-gather (see kPhaseAll).
@@ -504,6 +570,7 @@ int shard_search_launch(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist
     return VRS_OK;
   }
   if (s->use_tc) return launch_tc_search(h, s, nq, kk, out_dist, out_id, out_pairs, phase);
+  if (s->use_simt) return launch_simt_search(h, s, nq, kk, out_dist, out_id, out_pairs);
   return launch_exact_search(h, s, nq, kk, nullptr, s->overflow.as<int>(), out_dist, out_id, out_pairs);
 }
 
