@@ -1061,12 +1061,13 @@ struct KmShard {
   // tensor-core assignment operands
   bool use_tc = false;
   DBuf xb, xq, xtiny, cb, cn, cmax, res, cands, err, ctiny;
+  DBuf flags;  // points for the full exact scan: [count, indices...]
   DBuf segws;  // counting-sort workspace of the centroid sums
   ~KmShard() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     for (DBuf* b : {&x, &xr, &x_aux, &assign, &dist, &acc, &cent, &cent_r, &cent_aux, &shift, &scal, &red, &xb,
-                    &xq, &xtiny, &cb, &cn, &cmax, &res, &cands, &err, &ctiny, &segws})
+                    &xq, &xtiny, &cb, &cn, &cmax, &res, &cands, &err, &ctiny, &segws, &flags})
       b->release();
     if (stream) cudaStreamDestroy(stream);
   }
@@ -1125,7 +1126,8 @@ int km_prepare_shard(const KmParams& P, KmShard* s, const float* rows, int mem) 
     VRS_TRY(s->cmax.reserve(2 * sizeof(unsigned int)));
     VRS_TRY(s->ctiny.reserve(sizeof(int)));
     VRS_TRY(s->res.reserve(nx * 2 * sizeof(kmtc::Res)));
-    VRS_TRY(s->cands.reserve(nx * 2 * 4 * sizeof(Cand)));
+    VRS_TRY(s->cands.reserve(nx * 2 * 8 * sizeof(Cand)));
+    VRS_TRY(s->flags.reserve((nx + 1) * sizeof(int)));
     VRS_TRY(s->err.reserve(sizeof(int)));
     VRS_CUDA(cudaMemsetAsync(s->cn.p, 0, (size_t)kpad * sizeof(float), s->stream));
     VRS_TRY(kmtc::prep_rows(s->x.as<float>(), s->n_local, P.d, P.dp, P.metric, s->xb.p, nullptr,
@@ -1180,6 +1182,10 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
   }
   const size_t acc_elems = (size_t)P.k * P.dp + P.k;
   int iters = 0;
+  // The Lloyd loop proper (upload, operand prep and initial centroids are
+  // outside it), timed on shard 0's stream as profile name "kmeans_loop".
+  VRS_CUDA(cudaSetDevice(shards[0]->device));
+  ProfToken tloop = prof_begin("kmeans_loop", shards[0]->stream);
   for (int it = 0; it < P.max_iters; it++) {
     iters = it + 1;
     for (KmShard* s : shards) {
@@ -1221,7 +1227,8 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
                                  s->cmax.as<unsigned int>(), P.metric, s->res.as<kmtc::Res>(),
                                  s->cands.as<Cand>(),
                                  P.metric == vrs_exact::kCos ? s->xtiny.as<int>() : nullptr,
-                                 s->assign.as<int32_t>(), s->dist.as<float>(), s->stream));
+                                 s->assign.as<int32_t>(), s->dist.as<float>(), s->flags.as<int>(), s->num_sms,
+                                 s->stream));
           prof_end(t2, s->stream);
           tc_done = true;
         }
@@ -1275,6 +1282,8 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
     VRS_CUDA(cudaMemcpy(&max_shift, shards[0]->scal.as<float>() + 1, sizeof(float), cudaMemcpyDeviceToHost));
     if (max_shift <= P.tol) break;
   }
+  VRS_CUDA(cudaSetDevice(shards[0]->device));
+  prof_end(tloop, shards[0]->stream);
   // Inertia of the last assignment step: deterministic per-shard f64 sums,
   // added in rank order.
   double inertia = 0.0;

@@ -36,7 +36,7 @@ constexpr int BM = 128, NACC = 2, BN = 128, KBW = 64, MAX_KBLK = 2, STAGES = 4;
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + EPI_WARPS * 32;
 constexpr int HALF_COLS = BN / 2;
-constexpr int NCAND = 4;
+constexpr int NCAND = 8;
 constexpr uint32_t BLK = BM * 128;
 constexpr size_t SMEM_A = (size_t)NACC * MAX_KBLK * BLK;
 constexpr size_t SMEM_B = (size_t)STAGES * MAX_KBLK * BLK;
@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
     const float* __restrict__ cent_aux, const float* __restrict__ x_aux, int k,
     const float* __restrict__ xq, const unsigned int* __restrict__ cmax, const Res* __restrict__ res,
     const Cand* __restrict__ cands, const int* __restrict__ force_full, int32_t* __restrict__ assign,
-    float* __restrict__ dist) {
+    float* __restrict__ dist, int* __restrict__ flags) {
   const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
   if (i >= n) return;  // whole half-warps leave together
   const int hl = threadIdx.x & 15;
@@ -369,9 +369,12 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
   const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax));
   const float bound = __fadd_ru(bapprox, absm);
   // A candidate that was pushed out of a full buffer only matters if it is
-  // still within the final bound; then every centroid is checked exactly.
+  // still within the final bound; then every centroid must be checked
+  // exactly: the point goes to the flagged list (flags[0] = count), which
+  // kmeans_flagged_kernel scans with a whole CTA per point.
   if (r0.lost <= bound || r1.lost <= bound || (force_full && force_full[i])) {
-    for (int c = 0; c < k; c++) consider((uint32_t)c);
+    if (hl == 0) flags[1 + atomicAdd(&flags[0], 1)] = (int)i;
+    return;
   } else {
     for (int h = 0; h < 2; h++) {
       const Res r = h ? r1 : r0;
@@ -384,6 +387,60 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
   if (hl == 0) {
     assign[i] = best;
     dist[i] = vrs_exact::finish(METRIC, best_key);
+  }
+}
+
+// Exact assignment of the flagged points (flags[0] of them, indices in
+// flags[1..]): one CTA per point, its 16 half-warps split the centroids
+// (half-warp h takes c = h, h + 16, ...), then the CTA keeps the best key,
+// lowest centroid index on ties (kmeans.rs:361-407).
+template <int METRIC>
+__global__ void __launch_bounds__(256) kmeans_flagged_kernel(
+    const float* __restrict__ x, int d, int dp, const float* __restrict__ cent,
+    const float* __restrict__ cent_aux, const float* __restrict__ x_aux, int k, const int* __restrict__ flags,
+    int32_t* __restrict__ assign, float* __restrict__ dist) {
+  __shared__ float s_key[16];
+  __shared__ int s_idx[16];
+  const int hw = threadIdx.x >> 4, hl = threadIdx.x & 15;
+  const unsigned mask = 0xffffu << (threadIdx.x & 16);
+  const bool hib = vrs_exact::higher_is_better(METRIC);
+  const int count = flags[0];
+  for (int f = blockIdx.x; f < count; f += gridDim.x) {
+    const int64_t i = flags[1 + f];
+    const float* v = x + i * dp;
+    const float va = METRIC == vrs_exact::kCos ? x_aux[i] : 0.0f;
+    int best = 0x7fffffff;
+    float best_key = hib ? -INFINITY : INFINITY;
+    for (int c = hw; c < k; c += 16) {
+      const float ca = METRIC == vrs_exact::kCos ? cent_aux[c] : 0.0f;
+      const float key = vrs_exact::lanes::rank_key(METRIC, v, cent + (int64_t)c * dp, d, va, ca, hl, mask);
+      const bool better = hib ? (key > best_key) : (key < best_key);  // c increases: ties keep the lower
+      if (better) {
+        best_key = key;
+        best = c;
+      }
+    }
+    if (hl == 0) {
+      s_key[hw] = best_key;
+      s_idx[hw] = best;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float bk = s_key[0];
+      int bi = s_idx[0];
+      for (int h = 1; h < 16; h++) {
+        const float kk = s_key[h];
+        const int ii = s_idx[h];
+        const bool better = hib ? (kk > bk || (kk == bk && ii < bi)) : (kk < bk || (kk == bk && ii < bi));
+        if (better) {
+          bk = kk;
+          bi = ii;
+        }
+      }
+      assign[i] = bi;
+      dist[i] = vrs_exact::finish(METRIC, bk);
+    }
+    __syncthreads();
   }
 }
 
@@ -465,11 +522,16 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16) {
 template <int M>
 int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
                  const float* x_aux, int k, const float* xq, const unsigned int* cmax, const Res* res,
-                 const Cand* cands, const int* force_full, int32_t* assign, float* dist, cudaStream_t s) {
+                 const Cand* cands, const int* force_full, int32_t* assign, float* dist, int* flags,
+                 int num_sms, cudaStream_t s) {
+  VRS_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), s));
   kmeans_finalize_kernel<M><<<(unsigned)((n * 16 + 127) / 128), 128, 0, s>>>(
-      x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full, assign, dist);
+      x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full, assign, dist, flags);
   VRS_CUDA(cudaGetLastError());
-  count_launch();
+  kmeans_flagged_kernel<M><<<(unsigned)(num_sms * 8), 256, 0, s>>>(x, d, dp, cent, cent_aux, x_aux, k, flags,
+                                                                   assign, dist);
+  VRS_CUDA(cudaGetLastError());
+  count_launch(2);
   return VRS_OK;
 }
 
@@ -531,21 +593,22 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
 
 int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
              const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
-             const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, cudaStream_t s) {
+             const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
+             cudaStream_t s) {
   if (n == 0) return VRS_OK;
   switch (metric) {
     case vrs_exact::kL2:
       return finalize_run<vrs_exact::kL2>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full,
-                                          assign_out, dist, s);
+                                          assign_out, dist, flags, num_sms, s);
     case vrs_exact::kMaha:
       return finalize_run<vrs_exact::kMaha>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                            force_full, assign_out, dist, s);
+                                            force_full, assign_out, dist, flags, num_sms, s);
     case vrs_exact::kDot:
       return finalize_run<vrs_exact::kDot>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                           force_full, assign_out, dist, s);
+                                           force_full, assign_out, dist, flags, num_sms, s);
     case vrs_exact::kCos:
       return finalize_run<vrs_exact::kCos>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                           force_full, assign_out, dist, s);
+                                           force_full, assign_out, dist, flags, num_sms, s);
   }
   set_error(VRS_ERR_INVALID_CONFIG, "k-means tensor-core finalize: unsupported metric");
   return VRS_ERR_INVALID_CONFIG;

@@ -7,7 +7,7 @@ namespace vrs {
 namespace kmtc {
 
 // Per (point, column half) result of the tensor-core pass: approximate best
-// score and centroid, number of kept candidates (at most 4, the best within
+// score and centroid, number of kept candidates (at most 8, the best within
 // the margin), and the smallest score that did not fit (+inf if none).
 struct Res {
   float best;
@@ -24,9 +24,13 @@ int prep_rows(const float* x, int64_t n, int d, int dp, int metric, void* xb, fl
 int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
            const unsigned int* cmax, int metric, Res* res, Cand* cands, int* err, int num_sms,
            cudaStream_t s);
+// Exact assignment from the candidates; points whose candidates may be
+// incomplete go to `flags` (flags[0] = count, then indices; n + 1 ints) and
+// are assigned by a full exact scan, one CTA per point.
 int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
              const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
-             const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, cudaStream_t s);
+             const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
+             cudaStream_t s);
 
 }  // namespace kmtc
 }  // namespace vrs
