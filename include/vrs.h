@@ -139,7 +139,10 @@ VRS_API void vrs_comm_destroy(vrs_comm* c);
 
 /* Rank-local shard of a Sharded (or full copy of a Replicated) index.
  * shard: n_local x d, host or device (mem). global_offset: global id of
- * shard row 0; n_global: rows over all ranks. */
+ * shard row 0; n_global: rows over all ranks. For a Sharded handle over more
+ * than one rank this is a collective (all ranks call it): the ranks agree on
+ * the search path and the largest row norm, which the pooled pivot bounds
+ * of vrs_knn_search need. */
 VRS_API int vrs_knn_create_rank(vrs_comm* comm, const float* shard, int64_t n_local,
                         int64_t global_offset, int64_t n_global, int32_t d, int32_t mode,
                         int32_t metric, int32_t mem, vrs_knn** out);

@@ -105,11 +105,13 @@ static int nccl_ready(ncclComm_t comm, double timeout_s) {
       ncclCommAbort(comm);
       return fail(VRS_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(ar));
     }
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
+    const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (waited > timeout_s) {
       ncclCommAbort(comm);
       return fail(VRS_ERR_TIMEOUT, "NCCL call not enqueued within " + std::to_string(timeout_s) + " s");
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(20));
+    // Spin for the first 200 us (the usual case), then poll every 20 us.
+    if (waited > 200e-6) std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
 }
 
@@ -142,7 +144,9 @@ static int stream_wait(cudaStream_t s, ncclComm_t comm, double timeout_s) {
       if (comm) ncclCommAbort(comm);
       return fail(VRS_ERR_TIMEOUT, "device wait exceeded " + std::to_string(timeout_s) + " s");
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(comm ? 50 : 5));
+    // Poll tightly for the first millisecond (most waits end there), then
+    // back off so a long wait does not spin a core.
+    if (el > 1e-3) std::this_thread::sleep_for(std::chrono::microseconds(comm ? 50 : 5));
   }
 }
 
@@ -254,7 +258,7 @@ int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
   VRS_CUDA(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, s->device));
   if (simt::simt_supported(h->metric, h->dp) && !getenv("VRS_DISABLE_SIMT")) s->use_simt = true;
   if (tc::tc_supported(h->metric, h->d) && !getenv("VRS_DISABLE_TC")) {
-    const int d16 = tc::tc_d16(h->d);
+    const int d16 = tc::tc_d16(h->metric, h->d);
     const int64_t npad = (s->n_local + 127) / 128 * 128 + 128;
     VRS_TRY(s->xb.reserve((size_t)s->n_local * d16 * 2));
     VRS_TRY(s->xn.reserve((size_t)npad * sizeof(float)));
@@ -279,7 +283,7 @@ int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
         VRS_TRY(s->pb.reserve((size_t)s->pivot_m * d16 * 2));
         VRS_TRY(s->pn.reserve((size_t)ppad * sizeof(float)));
         VRS_CUDA(cudaMemsetAsync(s->pn.p, 0, (size_t)ppad * sizeof(float), s->stream));
-        VRS_TRY(tc::tc_pivot_gather(s->xb.p, s->xn.as<float>(), s->pivot_m, s->pivot_stride, h->d, s->pb.p,
+        VRS_TRY(tc::tc_pivot_gather(s->xb.p, s->xn.as<float>(), s->pivot_m, s->pivot_stride, d16, s->pb.p,
                                     s->pn.as<float>(), s->stream));
         VRS_CUDA(cudaStreamSynchronize(s->stream));
       }
@@ -389,7 +393,7 @@ enum { kPhaseAll = 0, kPhasePivot = 1, kPhaseMain = 2 };
 int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
                      Cand* out_pairs, int phase) {
   cudaStream_t st = s->stream;
-  const int d16 = tc::tc_d16(h->d);
+  const int d16 = tc::tc_d16(h->metric, h->d);
   const int nq_alloc = (nq + 255) / 256 * 256;
   tc::TcPlan p = tc::tc_plan(s->n_local, nq, kk, s->num_sms);
   const int nlists = 2 * p.nseg;
@@ -471,10 +475,14 @@ main_phase:
   sa.tiny = s->tiny.as<uint32_t>();
   sa.n_tiny = h->metric == vrs_exact::kCos ? s->n_tiny : 0;
   ProfToken t = prof_begin("knn_select", st);
-  if (nlists <= 32 && kk <= 256 && sa.n_tiny <= 256)
+  if (nlists <= 32 && kk <= 256 && sa.n_tiny <= 256) {
     VRS_TRY(launch_knn_select_warp(sa, st));
-  else
+    // Queries with more survivors than a warp holds: block select.
+    sa.retry = 1;
     VRS_TRY(launch_knn_select(sa, st));
+  } else {
+    VRS_TRY(launch_knn_select(sa, st));
+  }
   prof_end(t, st);
   return VRS_OK;
 }
@@ -764,16 +772,17 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
                                    s0->out_dist.as<float>(), s0->out_id.as<uint32_t>(), s0->stream));
         prof_end(t, s0->stream);
       }
+      // Results leave shard 0 behind the merge; one bounded wait per shard
+      // covers the collective and the copies.
+      KnnShard* s0 = h->shards[0].get();
+      VRS_CUDA(cudaSetDevice(s0->device));
+      VRS_CUDA(cudaMemcpyAsync(odst, s0->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s0->stream));
+      VRS_CUDA(cudaMemcpyAsync(oid, s0->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s0->stream));
       for (int r = 0; r < G; r++) {
         KnnShard* s = h->shards[r].get();
         VRS_CUDA(cudaSetDevice(s->device));
         VRS_TRY(stream_wait(s->stream, nranks > 1 ? s->comm : nullptr, tmo));
       }
-      KnnShard* s0 = h->shards[0].get();
-      VRS_CUDA(cudaSetDevice(s0->device));
-      VRS_CUDA(cudaMemcpyAsync(odst, s0->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s0->stream));
-      VRS_CUDA(cudaMemcpyAsync(oid, s0->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s0->stream));
-      VRS_CUDA(cudaStreamSynchronize(s0->stream));
     } else {
       // Replicated: query chunks of ceil(nb / ranks) (distributed_knn.rs:201-229).
       const int chunk = (nb + nranks - 1) / nranks;

@@ -66,7 +66,11 @@ struct AssignArgs {
 __device__ __forceinline__ float point_margin(int metric, int d, float Q, float X) {
   const double u = 0x1p-24;
   const int d16 = (d + 15) / 16 * 16;
-  const double c_tc = 0x1p-8 + 0x1p-17 + (double)(d16 + 2) * 0x1p-22;
+  // bf16 keeps 8 significant bits: each rounded operand is within 2^-8
+  // (relative) of its value, so a dot product of rounded operands is within
+  // (2^-7 + 2^-16) |q| |x| of the exact one (Cauchy-Schwarz), plus the f32
+  // accumulation of d16 + 2 terms (4 ulps each, allowing truncation).
+  const double c_tc = 0x1p-7 + 0x1p-16 + (double)(d16 + 2) * 0x1p-22;
   const double g = (double)(d + 4) * u * 1.01;
   double e;
   if (metric == vrs_exact::kCos) {

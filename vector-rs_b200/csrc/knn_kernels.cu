@@ -136,7 +136,14 @@ __global__ void __launch_bounds__(256) knn_select_kernel(KnnSelectArgs a) {
   __shared__ int s_off[65];
   const int slot = blockIdx.x;
   const int tid = threadIdx.x;
-  if (a.overflow[slot]) return;
+  if (a.retry) {
+    // Second chance for queries the warp select could not hold (flag 2).
+    if (a.overflow[slot] != 2) return;
+    __syncthreads();
+    if (tid == 0) a.overflow[slot] = 0;
+  } else if (a.overflow[slot]) {
+    return;
+  }
   const int qrow = a.q_index ? a.q_index[slot] : slot;
   if (tid == 0) {
     int tot = 0;
@@ -224,8 +231,8 @@ __global__ void __launch_bounds__(256) knn_select_kernel(KnnSelectArgs a) {
 // are copied to shared memory, re-ranked exactly by half-warps (the 16 lanes
 // are the reference's 16 SIMD lanes, loads coalesced), sorted by
 // (score, id) with a warp bitonic sort, and written out.
-constexpr int kSelWarps = 8;
-constexpr int kSelRmax = 512;
+constexpr int kSelWarps = 4;
+constexpr int kSelRmax = 1024;
 
 template <int METRIC>
 __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSelectArgs a) {
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
     }
   }
   if (R + a.n_tiny > kSelRmax) {
-    if (lane == 0) a.overflow[slot] = 1;
+    if (lane == 0) a.overflow[slot] = 2;  // retried by the block select (knn_select_kernel, retry)
     return;
   }
   __syncwarp();

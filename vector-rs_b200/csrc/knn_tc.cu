@@ -21,6 +21,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cmath>
@@ -75,12 +76,16 @@ struct TcScanArgs {
   int64_t tmin_stride;  // entries per query row of tmin (2 * tiles)
   // Starting acceptance bound per query (null: +inf).
   const float* init_bound;
+  uint32_t idesc;    // MMA instruction descriptor (fp16 or bf16 operands)
 };
 
 // MODE 0: heap score = |x|^2 - 2 acc (squared L2, Mahalanobis);
-// MODE 1: heap score = -acc (dot, cosine on unit rows). The epilogue works on
-// a per-mode "key" whose best end is the minimum (MODE 0: the score) or the
-// maximum (MODE 1: acc). TILEMIN selects the pivot pass.
+// MODE 1: heap score = -acc (dot, cosine on unit rows);
+// MODE 2: heap score = -2 acc, where the operands carry -|x|^2 / 2 in two
+//         extra K columns (squared L2 and Mahalanobis with d <= 126).
+// The epilogue works on a per-mode "key" whose best end is the minimum
+// (MODE 0: the score) or the maximum (MODE 1 and 2: acc). TILEMIN selects
+// the pivot pass.
 template <int MODE, bool TILEMIN>
 __global__ void __launch_bounds__(THREADS, 1)
     knn_scan_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -157,7 +162,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------- MMA issuer
     if (lane == 0 && ntiles > 0) {
-      const uint32_t idesc = idesc_bf16(BM, BN);
+      const uint32_t idesc = a.idesc;
       // This thread shares its scheduler with four epilogue warps, so each
       // MMA should cost it about one instruction: the A descriptors (fixed
       // for the CTA) are formed once into registers, the B descriptors once
@@ -230,8 +235,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const int64_t rem_cols = row_end - n0;
       const int valid_cols = rem_cols < HALF_COLS ? (int)(rem_cols > 0 ? rem_cols : 0) : HALF_COLS;
-      // Key threshold: MODE 0 passes key <= bound, MODE 1 passes key >= -bound.
-      const float thr = MODE == 0 ? bound : -bound;
+      // Key threshold: MODE 0 passes key <= bound, MODE 1 key >= -bound,
+      // MODE 2 key >= -bound / 2 (halving and doubling are exact).
+      const float thr = MODE == 0 ? bound : MODE == 1 ? -bound : -0.5f * bound;
       float tile_best = MODE == 0 ? INFINITY : -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < HALF_COLS / 32; c++) {
@@ -279,7 +285,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if ((m >> i) & 1u) {
 #pragma unroll
               for (int jj = 0; jj < 4; jj++) {
-                const float sc = MODE == 0 ? v[4 * i + jj] : -v[4 * i + jj];
+                const float sc = MODE == 0 ? v[4 * i + jj] : MODE == 1 ? -v[4 * i + jj] : -2.0f * v[4 * i + jj];
                 if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + c * 32 + 4 * i + jj)};
               }
             }
@@ -292,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (TILEMIN) {
         if (vq)
           a.tmin[(int64_t)q * a.tmin_stride + (row_begin / BN + t) * 2 + ch] =
-              MODE == 0 ? tile_best : -tile_best;
+              MODE == 0 ? tile_best : MODE == 1 ? -tile_best : -2.0f * tile_best;
         continue;
       }
       // Shrink lists that could overflow on the next tile.
@@ -334,15 +340,21 @@ __global__ void __launch_bounds__(THREADS, 1)
 // ------------------------------------------------------------------ prep
 // Base rows -> bf16 operand rows (cosine: unit-normalised), |x|^2 for the L2
 // epilogue, max |x| for the margins, and the list of near-zero cosine rows.
+// One 2-byte tensor-core operand: fp16 for cosine, bf16 otherwise.
+__device__ __forceinline__ uint16_t to_operand(float v, bool f16) {
+  return f16 ? __half_as_ushort(__float2half_rn(v)) : __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
 __global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int d, int dp, int d16,
-                                    int metric, __nv_bfloat16* __restrict__ xb,
+                                    int metric, uint16_t* __restrict__ xb,
                                     float* __restrict__ xn, unsigned int* __restrict__ xmax_bits,
                                     uint32_t* __restrict__ tiny, int* __restrict__ n_tiny,
                                     int tiny_cap) {
   int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (r >= n) return;
   const float* v = x + r * dp;
-  __nv_bfloat16* o = xb + r * d16;
+  uint16_t* o = xb + r * d16;
+  const bool f16 = tc_fp16(metric);
   float scale = 1.0f;
   if (metric == vrs_exact::kCos) {
     const float sx = sqrtf(vrs_exact::cos_norm_sq(v, d));
@@ -358,7 +370,15 @@ __global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int 
   for (int j = 0; j < d16; j++) {
     float e = j < d ? v[j] : 0.0f;
     ss += (double)e * (double)e;
-    o[j] = __float2bfloat16_rn(metric == vrs_exact::kCos ? e * scale : e);
+    o[j] = to_operand(metric == vrs_exact::kCos ? e * scale : e, f16);
+  }
+  if (tc_fold(metric, d)) {
+    // -|x|^2 / 2 as hi + lo bf16 in columns d and d + 1 (queries put 1.0
+    // there): within 2^-16 |x|^2 / 2 of the value.
+    const double t = -0.5 * ss;
+    const __nv_bfloat16 hi = __float2bfloat16_rn((float)t);
+    o[d] = __bfloat16_as_ushort(hi);
+    o[d + 1] = __bfloat16_as_ushort(__float2bfloat16_rn((float)(t - (double)__bfloat162float(hi))));
   }
   if (xn) xn[r] = (float)ss;
   atomicMax(xmax_bits, __float_as_uint((float)sqrt(ss)));
@@ -368,12 +388,13 @@ __global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int 
 // units). Near-zero cosine queries are routed to the exact fallback.
 __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d, int dp, int d16,
                                      int metric, const unsigned int* __restrict__ xmax_bits,
-                                     __nv_bfloat16* __restrict__ qb, float* __restrict__ absm,
+                                     uint16_t* __restrict__ qb, float* __restrict__ absm,
                                      int* __restrict__ overflow) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nq) return;
   const float* v = q + (int64_t)i * dp;
-  __nv_bfloat16* o = qb + (int64_t)i * d16;
+  uint16_t* o = qb + (int64_t)i * d16;
+  const bool f16 = tc_fp16(metric);
   float scale = 1.0f;
   if (metric == vrs_exact::kCos) {
     const float sq = sqrtf(vrs_exact::cos_norm_sq(v, d));
@@ -388,12 +409,25 @@ __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d,
   for (int j = 0; j < d16; j++) {
     float e = j < d ? v[j] : 0.0f;
     ss += (double)e * (double)e;
-    o[j] = __float2bfloat16_rn(metric == vrs_exact::kCos ? e * scale : e);
+    o[j] = to_operand(metric == vrs_exact::kCos ? e * scale : e, f16);
+  }
+  const bool fold = tc_fold(metric, d);
+  if (fold) {
+    o[d] = __bfloat16_as_ushort(__float2bfloat16_rn(1.0f));
+    o[d + 1] = __bfloat16_as_ushort(__float2bfloat16_rn(1.0f));
   }
   const double X = (double)__uint_as_float(*xmax_bits);
   const double Q = sqrt(ss);
   const double u = 0x1p-24;
-  const double c_tc = 0x1p-8 + 0x1p-17 + (double)(d16 + 2) * 0x1p-22;
+  // bf16 keeps 8 significant bits: each rounded operand is within 2^-8
+  // (relative) of its value, so a dot product of rounded operands is within
+  // (2^-7 + 2^-16) |q| |x| of the exact one (Cauchy-Schwarz), plus the f32
+  // accumulation of d16 + 2 terms (4 ulps each, allowing truncation). fp16
+  // (cosine: unit vectors) keeps 11: 2^-10 + 2^-22, plus 2^-20 for elements
+  // below fp16's normal range (absolute error <= 2^-25 each, at most
+  // 2^-25 sqrt(d) |other| per side).
+  const double c_tc = f16 ? 0x1p-10 + 0x1p-22 + 0x1p-20 + (double)(d16 + 2) * 0x1p-22
+                          : 0x1p-7 + 0x1p-16 + (double)(d16 + 2) * 0x1p-22;
   const double g = (double)(d + 4) * u * 1.01;
   double e;
   if (metric == vrs_exact::kCos) {
@@ -402,6 +436,9 @@ __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d,
     e = (c_tc + 2.0 * g) * Q * X;
   } else {  // squared L2 / Mahalanobis scores |x|^2 - 2 q.x
     e = 2.0 * c_tc * Q * X + 8.0 * g * (Q + X) * (Q + X);
+    // Folded |x|^2: its hi + lo split (2^-16 |x|^2 / 2) and its share of the
+    // accumulation, doubled by the score's factor -2.
+    if (fold) e += (0x1p-16 + (double)(d16 + 2) * 0x1p-22) * X * X;
   }
   absm[i] = (float)(2.0 * e * 1.25) * (1.0f + 0x1p-20f);
 }
@@ -467,9 +504,9 @@ __global__ void __launch_bounds__(256) tc_pivot_topk_kernel(const float* __restr
 }
 
 // Gathers every `stride`-th bf16 operand row (and |x|^2) into the pivot set.
-__global__ void tc_pivot_gather_kernel(const __nv_bfloat16* __restrict__ xb, const float* __restrict__ xn,
+__global__ void tc_pivot_gather_kernel(const uint16_t* __restrict__ xb, const float* __restrict__ xn,
                                        int64_t m, int64_t stride, int d16,
-                                       __nv_bfloat16* __restrict__ pb, float* __restrict__ pn) {
+                                       uint16_t* __restrict__ pb, float* __restrict__ pn) {
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= m * d16) return;
   int64_t r = i / d16;
@@ -491,7 +528,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // bf16 [rows][d16] row-major, box 64 x 128, 128-byte swizzle, zero OOB fill.
-int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16) {
+int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16, bool f16) {
   auto fn = encode_fn();
   if (!fn) {
     set_error(VRS_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
@@ -501,7 +538,8 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16) {
   cuuint64_t strides[1] = {(cuuint64_t)d16 * 2};
   cuuint32_t box[2] = {(cuuint32_t)KBW, (cuuint32_t)BM};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+  CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box,
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -519,13 +557,13 @@ bool tc_supported(int metric, int d) {
           metric == vrs_exact::kCos);
 }
 
-int tc_d16(int d) { return (d + 15) / 16 * 16; }
+int tc_d16(int metric, int d) { return (tc_fold(metric, d) ? d + 2 + 15 : d + 15) / 16 * 16; }
 
 int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* xn,
                  unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s) {
   if (n == 0) return VRS_OK;
   tc_base_prep_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(
-      x, n, d, dp, tc_d16(d), metric, (__nv_bfloat16*)xb, xn, xmax_bits, tiny, n_tiny, tiny_cap);
+      x, n, d, dp, tc_d16(metric, d), metric, (uint16_t*)xb, xn, xmax_bits, tiny, n_tiny, tiny_cap);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;
@@ -534,20 +572,19 @@ int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, void* xb,
 int tc_query_prep(const float* q, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
                   void* qb, float* absm, int* overflow, cudaStream_t s) {
   if (nq == 0) return VRS_OK;
-  tc_query_prep_kernel<<<(nq + 127) / 128, 128, 0, s>>>(q, nq, d, dp, tc_d16(d), metric, xmax_bits,
-                                                         (__nv_bfloat16*)qb, absm, overflow);
+  tc_query_prep_kernel<<<(nq + 127) / 128, 128, 0, s>>>(q, nq, d, dp, tc_d16(metric, d), metric, xmax_bits,
+                                                         (uint16_t*)qb, absm, overflow);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;
 }
 
-int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, int d, void* pb,
+int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, int d16, void* pb,
                     float* pn, cudaStream_t s) {
   if (m == 0) return VRS_OK;
-  const int d16 = tc_d16(d);
   const int64_t total = m * d16;
   tc_pivot_gather_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
-      (const __nv_bfloat16*)xb, xn, m, stride, d16, (__nv_bfloat16*)pb, pn);
+      (const uint16_t*)xb, xn, m, stride, d16, (uint16_t*)pb, pn);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;
@@ -609,15 +646,16 @@ int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d,
             int metric, int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow,
             const float* absm, int* err, float* tmin, const float* init_bound, cudaStream_t s) {
   if (n == 0 || nq == 0) return VRS_OK;
-  const int d16 = tc_d16(d);
+  const int d16 = tc_d16(metric, d);
   CUtensorMap tmA, tmB;
-  VRS_TRY(make_tmap(&tmA, qb, nq_rows_alloc, d16));
-  VRS_TRY(make_tmap(&tmB, xb, n, d16));
+  const bool f16 = tc_fp16(metric);
+  VRS_TRY(make_tmap(&tmA, qb, nq_rows_alloc, d16, f16));
+  VRS_TRY(make_tmap(&tmB, xb, n, d16, f16));
   TcScanArgs a;
   a.xn = xn;
   a.n = n;
   a.nq = nq;
-  a.ksteps = (d + 15) / 16;
+  a.ksteps = d16 / 16;
   a.kblk = (d16 + KBW - 1) / KBW;
   a.seg_len = p.seg_len;
   a.cand = cand;
@@ -629,10 +667,12 @@ int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d,
   a.err = err;
   a.tmin = tmin;
   a.tmin_stride = 2 * ((n + BN - 1) / BN);
+  a.idesc = f16 ? idesc_f16(BM, BN) : idesc_bf16(BM, BN);
   a.init_bound = init_bound;
   const bool l2 = metric == vrs_exact::kL2 || metric == vrs_exact::kMaha;
-  auto kern = l2 ? (tmin ? knn_scan_tc_kernel<0, true> : knn_scan_tc_kernel<0, false>)
-                 : (tmin ? knn_scan_tc_kernel<1, true> : knn_scan_tc_kernel<1, false>);
+  auto kern = tc_fold(metric, d) ? (tmin ? knn_scan_tc_kernel<2, true> : knn_scan_tc_kernel<2, false>)
+              : l2               ? (tmin ? knn_scan_tc_kernel<0, true> : knn_scan_tc_kernel<0, false>)
+                                 : (tmin ? knn_scan_tc_kernel<1, true> : knn_scan_tc_kernel<1, false>);
   static std::once_flag attr_once[64];
   int dev = 0;
   VRS_CUDA(cudaGetDevice(&dev));
@@ -640,7 +680,7 @@ int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d,
   if (dev < 64) {
     std::call_once(attr_once[dev], [&] {
       for (auto f : {knn_scan_tc_kernel<0, true>, knn_scan_tc_kernel<0, false>, knn_scan_tc_kernel<1, true>,
-                     knn_scan_tc_kernel<1, false>})
+                     knn_scan_tc_kernel<1, false>, knn_scan_tc_kernel<2, true>, knn_scan_tc_kernel<2, false>})
         if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL) !=
             cudaSuccess)
           attr_err = 1;

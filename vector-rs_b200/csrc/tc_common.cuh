@@ -218,6 +218,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor, kind::f16: fp16 A and B (both K-major), f32 D.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4)                  // D format f32 (A/B format 0 = f16)
+         | ((uint32_t)(N >> 3) << 17)
+         | ((uint32_t)(M >> 4) << 24);
+}
+
 // Three-input minimum / maximum (PTX ISA 8.8, sm_100+).
 __device__ __forceinline__ float fmin3(float a, float b, float c) {
   float r;

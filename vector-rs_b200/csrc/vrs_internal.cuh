@@ -127,6 +127,7 @@ struct KnnSelectArgs {
   int max_sort;          // shared-memory sort capacity (power of two)
   const uint32_t* tiny;  // rows always re-ranked exactly (cosine near-zero rows)
   int n_tiny;
+  int retry;             // block select: only the slots the warp select flagged (2)
 };
 
 // Launchers (knn_kernels.cu).

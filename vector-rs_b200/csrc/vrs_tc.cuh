@@ -22,7 +22,17 @@ struct TcPlan {
 };
 
 bool tc_supported(int metric, int d);
-int tc_d16(int d);
+// Squared L2 / Mahalanobis with d <= 126 fold -|x|^2 / 2 into the GEMM as two
+// extra K columns (hi + lo bf16; the query side holds 1.0 there).
+__host__ __device__ inline bool tc_fold(int metric, int d) {
+  return (metric == 0 || metric == 7) && d + 2 <= 128;  // kL2, kMaha
+}
+// Cosine operands are unit vectors (elements in [-1, 1]) and go to the
+// tensor cores as fp16 (11 significant bits; bf16's 8 would make the error
+// margin 8x wider); the other metrics use bf16 for its range.
+__host__ __device__ inline bool tc_fp16(int metric) { return metric == 2; }  // kCos
+// Operand row length (multiple of 16): d, plus the folded columns.
+int tc_d16(int metric, int d);
 int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* xn,
                  unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s);
 int tc_query_prep(const float* q, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
@@ -33,7 +43,7 @@ TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms);
 int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn,
             int metric, int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow,
             const float* absm, int* err, float* tmin, const float* init_bound, cudaStream_t s);
-int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, int d, void* pb,
+int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, int d16, void* pb,
                     float* pn, cudaStream_t s);
 // Starting bound per query from pivot minima: query q's values are
 // vals[p * part_stride + q * len + j] for p < nparts, j < len (one part per
