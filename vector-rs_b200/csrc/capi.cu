@@ -110,8 +110,12 @@ static int nccl_ready(ncclComm_t comm, double timeout_s) {
       ncclCommAbort(comm);
       return fail(VRS_ERR_TIMEOUT, "NCCL call not enqueued within " + std::to_string(timeout_s) + " s");
     }
-    // Spin for the first 200 us (the usual case), then poll every 20 us.
-    if (waited > 200e-6) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    // Poll (yielding the core) for the first 200 us, the usual case, then
+    // every 20 us.
+    if (waited > 200e-6)
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    else
+      std::this_thread::yield();
   }
 }
 
@@ -144,9 +148,12 @@ static int stream_wait(cudaStream_t s, ncclComm_t comm, double timeout_s) {
       if (comm) ncclCommAbort(comm);
       return fail(VRS_ERR_TIMEOUT, "device wait exceeded " + std::to_string(timeout_s) + " s");
     }
-    // Poll tightly for the first millisecond (most waits end there), then
-    // back off so a long wait does not spin a core.
-    if (el > 1e-3) std::this_thread::sleep_for(std::chrono::microseconds(comm ? 50 : 5));
+    // Poll (yielding the core) for the first millisecond, where most waits
+    // end, then back off so a long wait does not occupy a core.
+    if (el > 1e-3)
+      std::this_thread::sleep_for(std::chrono::microseconds(comm ? 50 : 5));
+    else
+      std::this_thread::yield();
   }
 }
 

@@ -422,6 +422,48 @@ __global__ void __launch_bounds__(256) merge_pairs_kernel(const Cand* g, int nli
   }
 }
 
+// G-way merge of lists that are each sorted by (score, id) (every rank's
+// select writes its top-k' sorted): an element's output position is its
+// index in its own list plus, for every other list, the number of elements
+// ordered before it, found by binary search. The order is (score, id, list),
+// so padding entries (+inf, 0xffffffff) of different lists stay distinct and
+// exactly k' elements land below k'. No sort.
+template <int METRIC>
+__global__ void __launch_bounds__(256) merge_sorted_kernel(const Cand* g, int nlists, int nq, int k,
+                                                           float* out_dist, uint32_t* out_id) {
+  extern __shared__ Cand sl[];  // [nlists][k]
+  const int q = blockIdx.x;
+  const int T = nlists * k;
+  for (int i = threadIdx.x; i < T; i += blockDim.x) {
+    const int l = i / k, r = i - l * k;
+    sl[i] = g[((int64_t)l * nq + q) * k + r];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < T; i += blockDim.x) {
+    const int l = i / k, j = i - l * k;
+    const Cand e = sl[i];
+    int rank = j;
+    for (int m = 0; m < nlists && rank < k; m++) {
+      if (m == l) continue;
+      const Cand* lm = sl + m * k;
+      int lo = 0, hi = k;  // first position of list m not ordered before e
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        const Cand c = lm[mid];
+        const bool before = cand_less(c, e) || (!cand_less(e, c) && m < l);
+        if (before) lo = mid + 1;
+        else hi = mid;
+      }
+      rank += lo;
+    }
+    if (rank < k) {
+      const float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
+      out_dist[(int64_t)q * k + rank] = e.id == 0xffffffffu ? NAN : vrs_exact::finish(METRIC, key);
+      out_id[(int64_t)q * k + rank] = e.id;
+    }
+  }
+}
+
 template <int METRIC>
 __global__ void finish_pairs_kernel(const Cand* p, int64_t count, float* out_dist, uint32_t* out_id) {
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -515,6 +557,14 @@ struct SelectWarpL {
 template <int M>
 struct MergeL {
   static int run(const Cand* g, int nlists, int nq, int k, float* od, uint32_t* oi, cudaStream_t s) {
+    const size_t lsm = (size_t)nlists * k * sizeof(Cand);
+    if (lsm <= 200 * 1024) {
+      VRS_CUDA(cudaFuncSetAttribute(merge_sorted_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm));
+      merge_sorted_kernel<M><<<nq, 256, lsm, s>>>(g, nlists, nq, k, od, oi);
+      VRS_CUDA(cudaGetLastError());
+      count_launch();
+      return VRS_OK;
+    }
     int P = 1;
     while (P < nlists * k) P <<= 1;
     size_t smem = (size_t)P * sizeof(Cand);
