@@ -1146,9 +1146,7 @@ int km_prepare_shard(const KmParams& P, KmShard* s, const float* rows, int mem) 
     VRS_TRY(s->flags.reserve((nx + 1) * sizeof(int)));
     VRS_TRY(s->err.reserve(sizeof(int)));
     VRS_CUDA(cudaMemsetAsync(s->cn.p, 0, (size_t)kpad * sizeof(float), s->stream));
-    VRS_TRY(kmtc::prep_rows(s->x.as<float>(), s->n_local, P.d, P.dp, P.metric, s->xb.p, nullptr,
-                            s->xq.as<float>(), nullptr, s->xtiny.as<int>(), nullptr, s->stream));
-    s->use_tc = true;
+    s->use_tc = true;  // point operands are prepared in km_run, once the global max |x| is known
   }
   return VRS_OK;
 }
@@ -1196,6 +1194,22 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
     scale_exp = (int)std::floor(lim);
     scale_exp = std::max(-200, std::min(100, scale_exp));
   }
+  // Tensor-core operands: fp16 of value * op_scale, a power of two putting
+  // the largest element in [2^13, 2^14) (centroids are means of points, so
+  // they fit too); cosine rows are normalised and use 1.
+  // Empty clusters keep their initial centroid, so the initial centroids
+  // count too.
+  float omax = gmax;
+  for (size_t i = 0; i < (size_t)P.k * P.d; i++) omax = std::max(omax, std::fabs(init_host[i]));
+  float op_scale = 1.0f;
+  if (P.metric != vrs_exact::kCos && omax > 0.0f && std::isfinite(omax))
+    op_scale = std::ldexp(1.0f, std::max(-100, std::min(100, 13 - std::ilogb(omax))));
+  for (KmShard* s : shards) {
+    if (!s->use_tc) continue;
+    VRS_CUDA(cudaSetDevice(s->device));
+    VRS_TRY(kmtc::prep_rows(s->x.as<float>(), s->n_local, P.d, P.dp, P.metric, op_scale, s->xb.p, nullptr,
+                            s->xq.as<float>(), nullptr, s->xtiny.as<int>(), nullptr, s->stream));
+  }
   const size_t acc_elems = (size_t)P.k * P.dp + P.k;
   int iters = 0;
   // The Lloyd loop proper (upload, operand prep and initial centroids are
@@ -1222,7 +1236,7 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
         int any_tiny = 0;
         VRS_CUDA(cudaMemsetAsync(s->cmax.p, 0, 2 * sizeof(unsigned int), s->stream));
         VRS_CUDA(cudaMemsetAsync(s->ctiny.p, 0, sizeof(int), s->stream));
-        VRS_TRY(kmtc::prep_rows(s->cent.as<float>(), P.k, P.d, P.dp, P.metric, s->cb.p,
+        VRS_TRY(kmtc::prep_rows(s->cent.as<float>(), P.k, P.d, P.dp, P.metric, op_scale, s->cb.p,
                                 (P.metric == vrs_exact::kL2 || P.metric == vrs_exact::kMaha) ? s->cn.as<float>()
                                                                                               : nullptr,
                                 nullptr, s->cmax.as<unsigned int>(), nullptr, s->ctiny.as<int>(), s->stream));
@@ -1234,7 +1248,8 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
           VRS_CUDA(cudaMemsetAsync(s->err.p, 0, sizeof(int), s->stream));
           ProfToken t = prof_begin("kmeans_assign", s->stream);
           VRS_TRY(kmtc::assign(s->xb.p, s->n_local, s->cb.p, P.k, P.d, s->cn.as<float>(), s->xq.as<float>(),
-                               s->cmax.as<unsigned int>(), P.metric, s->res.as<kmtc::Res>(), s->cands.as<Cand>(),
+                               s->cmax.as<unsigned int>(), P.metric, op_scale, s->res.as<kmtc::Res>(),
+                               s->cands.as<Cand>(),
                                s->err.as<int>(), s->num_sms, s->stream));
           prof_end(t, s->stream);
           ProfToken t2 = prof_begin("kmeans_finalize", s->stream);
@@ -1244,7 +1259,7 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
                                  s->cands.as<Cand>(),
                                  P.metric == vrs_exact::kCos ? s->xtiny.as<int>() : nullptr,
                                  s->assign.as<int32_t>(), s->dist.as<float>(), s->flags.as<int>(), s->num_sms,
-                                 s->stream));
+                                 op_scale, s->stream));
           prof_end(t2, s->stream);
           tc_done = true;
         }

@@ -15,6 +15,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cmath>
@@ -56,29 +57,34 @@ struct AssignArgs {
   int ksteps, kblk;
   int mode;                 // 0: score |c|^2 - 2 x.c ; 1: score -x.c
   int metric;
+  float acc_scale;          // 1 / (operand scale)^2: unscales the accumulator
+  float inv_scale;          // 1 / operand scale (margins)
   Res* res;                 // [n][2] per (point, column half)
   Cand* cands;              // [n][2][NCAND]
   int* err;
 };
 
 // Acceptance margin of one point in score units (same bound as the kNN
-// path, with the centroids as the "base").
-__device__ __forceinline__ float point_margin(int metric, int d, float Q, float X) {
+// path, with the centroids as the "base"). Operands are fp16 of the values
+// times a power-of-two scale s (largest element in [2^13, 2^14)): fp16 keeps
+// 11 significant bits, so each product of rounded operands is within
+// 2^-10 + 2^-22 (relative) of the exact one; elements below fp16's normal
+// range add at most 2^-25 each in scaled units, i.e. 2^-25 sqrt(d) |other| / s
+// per side after unscaling; plus the f32 accumulation of d16 + 2 terms
+// (4 ulps each, allowing truncation).
+__device__ __forceinline__ float point_margin(int metric, int d, float Q, float X, float inv_s) {
   const double u = 0x1p-24;
   const int d16 = (d + 15) / 16 * 16;
-  // bf16 keeps 8 significant bits: each rounded operand is within 2^-8
-  // (relative) of its value, so a dot product of rounded operands is within
-  // (2^-7 + 2^-16) |q| |x| of the exact one (Cauchy-Schwarz), plus the f32
-  // accumulation of d16 + 2 terms (4 ulps each, allowing truncation).
-  const double c_tc = 0x1p-7 + 0x1p-16 + (double)(d16 + 2) * 0x1p-22;
+  const double c_tc = 0x1p-10 + 0x1p-22 + (double)(d16 + 2) * 0x1p-22;
+  const double sub = 0x1p-25 * sqrt((double)d) * ((double)Q + X) * (double)inv_s;
   const double g = (double)(d + 4) * u * 1.01;
   double e;
-  if (metric == vrs_exact::kCos) {
-    e = c_tc + 8.0 * u + 4.0 * g;
+  if (metric == vrs_exact::kCos) {  // unit vectors, s = 1
+    e = c_tc + 0x1p-25 * sqrt((double)d) * 2.0 + 8.0 * u + 4.0 * g;
   } else if (metric == vrs_exact::kDot) {
-    e = (c_tc + 2.0 * g) * (double)Q * (double)X;
+    e = (c_tc + 2.0 * g) * (double)Q * (double)X + sub;
   } else {
-    e = 2.0 * c_tc * (double)Q * (double)X + 8.0 * g * ((double)Q + X) * ((double)Q + X);
+    e = 2.0 * (c_tc * (double)Q * (double)X + sub) + 8.0 * g * ((double)Q + X) * ((double)Q + X);
   }
   return (float)(2.0 * e * 1.25) * (1.0f + 0x1p-20f);
 }
@@ -156,7 +162,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(BM, BN);
+      const uint32_t idesc = idesc_f16(BM, BN);
       // Descriptors differ only in the start-address field: the constant
       // part is formed once, the field per MMA from an offset.
       const DescSw128 a_desc(sA), b_desc(sB);
@@ -214,7 +220,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x) {
       const int64_t p = (int64_t)pt * BM * NACC + acc * BM + quad * 32 + lane;
       const bool vp = p < a.n;
-      const float absm = vp ? point_margin(a.metric, a.d, a.xq[p], X) : 0.0f;
+      const float absm = vp ? point_margin(a.metric, a.d, a.xq[p], X, a.inv_scale) : 0.0f;
+      const float f2 = -2.0f * a.acc_scale, f1 = -a.acc_scale;
       float best = INFINITY;
       float bound = INFINITY;
       float lost = INFINITY;  // smallest score pushed out of a full buffer
@@ -241,14 +248,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j4 = 0; j4 < 8; j4++) {
               const float4 x4 = __ldg(cp + j4);
-              v[4 * j4 + 0] = fmaf(-2.0f, v[4 * j4 + 0], x4.x);
-              v[4 * j4 + 1] = fmaf(-2.0f, v[4 * j4 + 1], x4.y);
-              v[4 * j4 + 2] = fmaf(-2.0f, v[4 * j4 + 2], x4.z);
-              v[4 * j4 + 3] = fmaf(-2.0f, v[4 * j4 + 3], x4.w);
+              v[4 * j4 + 0] = fmaf(f2, v[4 * j4 + 0], x4.x);
+              v[4 * j4 + 1] = fmaf(f2, v[4 * j4 + 1], x4.y);
+              v[4 * j4 + 2] = fmaf(f2, v[4 * j4 + 2], x4.z);
+              v[4 * j4 + 3] = fmaf(f2, v[4 * j4 + 3], x4.w);
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = -v[i];
+            for (int i = 0; i < 32; i++) v[i] = f1 * v[i];
           }
           if (cb < 32) {
 #pragma unroll
@@ -347,7 +354,7 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
     const float* __restrict__ cent_aux, const float* __restrict__ x_aux, int k,
     const float* __restrict__ xq, const unsigned int* __restrict__ cmax, const Res* __restrict__ res,
     const Cand* __restrict__ cands, const int* __restrict__ force_full, int32_t* __restrict__ assign,
-    float* __restrict__ dist, int* __restrict__ flags) {
+    float* __restrict__ dist, int* __restrict__ flags, float inv_scale) {
   const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
   if (i >= n) return;  // whole half-warps leave together
   const int hl = threadIdx.x & 15;
@@ -370,7 +377,7 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
     }
   };
   const float bapprox = fminf(r0.best, r1.best);
-  const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax));
+  const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax), inv_scale);
   const float bound = __fadd_ru(bapprox, absm);
   // A candidate that was pushed out of a full buffer only matters if it is
   // still within the final bound; then every centroid must be checked
@@ -452,7 +459,7 @@ __global__ void __launch_bounds__(256) kmeans_flagged_kernel(
 // points or centroids; max |row| into *maxn; near-zero cosine rows flagged.
 // One half-warp per row.
 __global__ void __launch_bounds__(128) km_prep_rows_kernel(
-    const float* __restrict__ x, int64_t n, int d, int dp, int metric, __nv_bfloat16* __restrict__ xb,
+    const float* __restrict__ x, int64_t n, int d, int dp, int metric, float op_scale, uint16_t* __restrict__ xb,
     float* __restrict__ sq, float* __restrict__ nrm, unsigned int* __restrict__ maxn,
     int* __restrict__ tiny_flag, int* __restrict__ any_tiny) {
   const int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
@@ -461,7 +468,7 @@ __global__ void __launch_bounds__(128) km_prep_rows_kernel(
   const unsigned mask = 0xffffu << (threadIdx.x & 16);
   const int d16 = (d + 15) / 16 * 16;
   const float* v = x + r * dp;
-  __nv_bfloat16* o = xb + r * d16;
+  uint16_t* o = xb + r * d16;
   float scale = 1.0f;
   int tiny = 0;
   if (metric == vrs_exact::kCos) {
@@ -477,7 +484,7 @@ __global__ void __launch_bounds__(128) km_prep_rows_kernel(
   for (int j = hl; j < d16; j += 16) {
     const float e = j < d ? v[j] : 0.0f;
     ss += (double)e * (double)e;
-    o[j] = __float2bfloat16_rn(metric == vrs_exact::kCos ? e * scale : e);
+    o[j] = __half_as_ushort(__float2half_rn(metric == vrs_exact::kCos ? e * scale : e * op_scale));
   }
 #pragma unroll
   for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(mask, ss, off, 16);
@@ -513,7 +520,7 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16) {
   cuuint64_t strides[1] = {(cuuint64_t)d16 * 2};
   cuuint32_t box[2] = {(cuuint32_t)KBW, (cuuint32_t)BM};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -527,10 +534,10 @@ template <int M>
 int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
                  const float* x_aux, int k, const float* xq, const unsigned int* cmax, const Res* res,
                  const Cand* cands, const int* force_full, int32_t* assign, float* dist, int* flags,
-                 int num_sms, cudaStream_t s) {
+                 int num_sms, float inv_scale, cudaStream_t s) {
   VRS_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), s));
   kmeans_finalize_kernel<M><<<(unsigned)((n * 16 + 127) / 128), 128, 0, s>>>(
-      x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full, assign, dist, flags);
+      x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full, assign, dist, flags, inv_scale);
   VRS_CUDA(cudaGetLastError());
   kmeans_flagged_kernel<M><<<(unsigned)(num_sms * 8), 256, 0, s>>>(x, d, dp, cent, cent_aux, x_aux, k, flags,
                                                                    assign, dist);
@@ -547,10 +554,10 @@ bool supported(int metric, int d) {
           metric == vrs_exact::kCos);
 }
 
-int prep_rows(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* sq, float* nrm,
-              unsigned int* maxn, int* tiny_flag, int* any_tiny, cudaStream_t s) {
+int prep_rows(const float* x, int64_t n, int d, int dp, int metric, float op_scale, void* xb, float* sq,
+              float* nrm, unsigned int* maxn, int* tiny_flag, int* any_tiny, cudaStream_t s) {
   if (n == 0) return VRS_OK;
-  km_prep_rows_kernel<<<(unsigned)((n * 16 + 127) / 128), 128, 0, s>>>(x, n, d, dp, metric, (__nv_bfloat16*)xb,
+  km_prep_rows_kernel<<<(unsigned)((n * 16 + 127) / 128), 128, 0, s>>>(x, n, d, dp, metric, op_scale, (uint16_t*)xb,
                                                                       sq, nrm, maxn, tiny_flag, any_tiny);
   VRS_CUDA(cudaGetLastError());
   count_launch();
@@ -558,7 +565,7 @@ int prep_rows(const float* x, int64_t n, int d, int dp, int metric, void* xb, fl
 }
 
 int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
-           const unsigned int* cmax, int metric, Res* res, Cand* cands, int* err, int num_sms,
+           const unsigned int* cmax, int metric, float op_scale, Res* res, Cand* cands, int* err, int num_sms,
            cudaStream_t s) {
   if (n == 0) return VRS_OK;
   const int d16 = (d + 15) / 16 * 16;
@@ -575,6 +582,8 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
   a.ksteps = (d + 15) / 16;
   a.kblk = (d16 + KBW - 1) / KBW;
   a.mode = (metric == vrs_exact::kL2 || metric == vrs_exact::kMaha) ? 0 : 1;
+  a.acc_scale = 1.0f / (op_scale * op_scale);
+  a.inv_scale = 1.0f / op_scale;
   a.metric = metric;
   a.res = res;
   a.cands = cands;
@@ -598,21 +607,21 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
 int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
              const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
              const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
-             cudaStream_t s) {
+             float op_scale, cudaStream_t s) {
   if (n == 0) return VRS_OK;
   switch (metric) {
     case vrs_exact::kL2:
       return finalize_run<vrs_exact::kL2>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full,
-                                          assign_out, dist, flags, num_sms, s);
+                                          assign_out, dist, flags, num_sms, 1.0f / op_scale, s);
     case vrs_exact::kMaha:
       return finalize_run<vrs_exact::kMaha>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                            force_full, assign_out, dist, flags, num_sms, s);
+                                            force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, s);
     case vrs_exact::kDot:
       return finalize_run<vrs_exact::kDot>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                           force_full, assign_out, dist, flags, num_sms, s);
+                                           force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, s);
     case vrs_exact::kCos:
       return finalize_run<vrs_exact::kCos>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                           force_full, assign_out, dist, flags, num_sms, s);
+                                           force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, s);
   }
   set_error(VRS_ERR_INVALID_CONFIG, "k-means tensor-core finalize: unsupported metric");
   return VRS_ERR_INVALID_CONFIG;

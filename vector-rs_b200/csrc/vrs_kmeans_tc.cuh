@@ -19,10 +19,13 @@ struct Res {
 bool supported(int metric, int d);
 // bf16 operand rows, |row|^2 (sq, nullable), |row| (nrm, nullable), max |row|
 // (maxn, nullable), near-zero cosine flags (nullable).
-int prep_rows(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* sq, float* nrm,
-              unsigned int* maxn, int* tiny_flag, int* any_tiny, cudaStream_t s);
+// Operands are fp16 of value * op_scale (a power of two putting the largest
+// element of points and centroids in [2^13, 2^14); 1 for cosine, whose rows
+// are normalised). sq / nrm / maxn are unscaled.
+int prep_rows(const float* x, int64_t n, int d, int dp, int metric, float op_scale, void* xb, float* sq,
+              float* nrm, unsigned int* maxn, int* tiny_flag, int* any_tiny, cudaStream_t s);
 int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
-           const unsigned int* cmax, int metric, Res* res, Cand* cands, int* err, int num_sms,
+           const unsigned int* cmax, int metric, float op_scale, Res* res, Cand* cands, int* err, int num_sms,
            cudaStream_t s);
 // Exact assignment from the candidates; points whose candidates may be
 // incomplete go to `flags` (flags[0] = count, then indices; n + 1 ints) and
@@ -30,7 +33,7 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
 int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
              const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
              const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
-             cudaStream_t s);
+             float op_scale, cudaStream_t s);
 
 }  // namespace kmtc
 }  // namespace vrs
