@@ -42,8 +42,9 @@ constexpr uint32_t BLK = BM * 128;
 constexpr size_t SMEM_A = (size_t)NACC * MAX_KBLK * BLK;
 constexpr size_t SMEM_B = (size_t)STAGES * MAX_KBLK * BLK;
 constexpr size_t SMEM_CAND = (size_t)EPI_WARPS * 32 * NCAND * sizeof(Cand);
+constexpr size_t SMEM_CN = 2 * BN * sizeof(float);  // |c|^2 of the tile in each TMEM buffer
 constexpr size_t SMEM_BAR = 256;
-constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_CAND + SMEM_BAR;
+constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_CAND + SMEM_CN + SMEM_BAR;
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -89,6 +90,9 @@ __device__ __forceinline__ float point_margin(int metric, int d, float Q, float 
   return (float)(2.0 * e * 1.25) * (1.0f + 0x1p-20f);
 }
 
+// MODE 0: score = |c|^2 - 2 x.c (squared L2, Mahalanobis); MODE 1: score =
+// -x.c (dot, cosine on unit rows).
+template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     kmeans_assign_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             AssignArgs a) {
@@ -97,7 +101,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + SMEM_A;
   Cand* s_cand = (Cand*)(sB + SMEM_B);
-  uint64_t* bars = (uint64_t*)((uint8_t*)s_cand + SMEM_CAND);
+  float* s_cn = (float*)((uint8_t*)s_cand + SMEM_CAND);  // [2][BN]
+  uint64_t* bars = (uint64_t*)((uint8_t*)s_cn + SMEM_CN);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -163,10 +168,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(BM, BN);
-      // Descriptors differ only in the start-address field: the constant
-      // part is formed once, the field per MMA from an offset.
+      // The A descriptors are fixed for the CTA (registers); the B ones are
+      // formed per tile before the waits. Descriptors differ only in the
+      // masked start-address field.
       const DescSw128 a_desc(sA), b_desc(sB);
       const int ksteps = a.ksteps;
+      uint64_t ad[NACC][MAX_KBLK * 4];
+#pragma unroll
+      for (int acc = 0; acc < NACC; acc++)
+#pragma unroll
+        for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+          ad[acc][ks] = a_desc.at((uint32_t)(acc * MAX_KBLK * BLK + (ks >> 2) * BLK + (ks & 3) * 32) >> 4);
       uint32_t g = 0;
       int lp = 0;
       bool ok = true;
@@ -176,24 +188,28 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         for (int j = 0; j < kt; j++, g++) {
           const int s = g % STAGES, b = g & 1;
+          uint64_t bd[MAX_KBLK * 4];
+#pragma unroll
+          for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+            bd[ks] = b_desc.at((uint32_t)(s * MAX_KBLK * BLK + (ks >> 2) * BLK + (ks & 3) * 32) >> 4);
           if (!mbar_wait(&full[s], (g / STAGES) & 1, s_abort, a.err, 14, WAIT_NS) ||
               !mbar_wait(&tempty[b], ((g >> 1) & 1) ^ 1, s_abort, a.err, 15, WAIT_NS)) {
             ok = false;
             break;
           }
+          if (MODE == 0) {
+            // |c|^2 of this tile's centroids rides on the same barrier as
+            // the accumulator (cn is zero padded to whole tiles + 128).
+            mbar_expect_tx_only(&tfull[b], BN * sizeof(float));
+            bulk_copy_g2s(s_cn + b * BN, a.cn + (int64_t)j * BN, BN * sizeof(float), &tfull[b]);
+          }
           tc_fence_after();
-          const uint32_t b_off = (uint32_t)(s * MAX_KBLK * BLK) >> 4;
 #pragma unroll
           for (int acc = 0; acc < NACC; acc++) {
             const uint32_t d = tmem + acc * 256 + b * BN;
-            const uint32_t a_off = (uint32_t)(acc * MAX_KBLK * BLK) >> 4;
 #pragma unroll
-            for (int ks = 0; ks < MAX_KBLK * 4; ks++) {
-              if (ks < ksteps) {
-                const uint32_t off = (uint32_t)((ks >> 2) * BLK + (ks & 3) * 32) >> 4;
-                mma_bf16(d, a_desc.at(a_off + off), b_desc.at(b_off + off), idesc, ks > 0 ? 1u : 0u);
-              }
-            }
+            for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+              if (ks < ksteps) mma_bf16(d, ad[acc][ks], bd[ks], idesc, ks > 0 ? 1u : 0u);
           }
           mma_commit(&empty[s]);
           mma_commit(&tfull[b]);
@@ -223,9 +239,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float absm = vp ? point_margin(a.metric, a.d, a.xq[p], X, a.inv_scale) : 0.0f;
       const float f2 = -2.0f * a.acc_scale, f1 = -a.acc_scale;
       float best = INFINITY;
-      float bound = INFINITY;
+      float bound = vp ? INFINITY : -INFINITY;  // padding points keep nothing
       float lost = INFINITY;  // smallest score pushed out of a full buffer
       int cnt = 0;
+      // Keeps the NCAND best candidates; remembers the best score dropped.
+      auto insert = [&](float sc, uint32_t id) {
+        if (cnt < NCAND) {
+          buf[cnt++] = Cand{sc, id};
+          return;
+        }
+        int wi = 0;
+        for (int e = 1; e < NCAND; e++)
+          if (buf[e].hs > buf[wi].hs) wi = e;
+        if (sc < buf[wi].hs) {
+          lost = fminf(lost, buf[wi].hs);
+          buf[wi] = Cand{sc, id};
+        } else {
+          lost = fminf(lost, sc);
+        }
+      };
       for (int j = 0; j < kt; j++, g++) {
         const int b = g & 1;
         const bool w = mbar_wait(&tfull[b], (g >> 1) & 1, s_abort, a.err, 16, WAIT_NS);
@@ -243,11 +275,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(tmem + lane_base + acc * 256 + b * BN + ch * HALF_COLS + c * 32, v);
           const int cb = valid - c * 32;
           // scores, smaller is better
-          if (a.mode == 0) {
-            const float4* cp = reinterpret_cast<const float4*>(a.cn + c0 + c * 32);
+          if (MODE == 0) {
+            const float4* cp = reinterpret_cast<const float4*>(s_cn + b * BN + ch * HALF_COLS + c * 32);
 #pragma unroll
             for (int j4 = 0; j4 < 8; j4++) {
-              const float4 x4 = __ldg(cp + j4);
+              const float4 x4 = cp[j4];
               v[4 * j4 + 0] = fmaf(f2, v[4 * j4 + 0], x4.x);
               v[4 * j4 + 1] = fmaf(f2, v[4 * j4 + 1], x4.y);
               v[4 * j4 + 2] = fmaf(f2, v[4 * j4 + 2], x4.z);
@@ -264,9 +296,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           float gm[8];
 #pragma unroll
-          for (int i = 0; i < 8; i++) gm[i] = fminf(fminf(v[4 * i], v[4 * i + 1]), fminf(v[4 * i + 2], v[4 * i + 3]));
-          const float cmn = fminf(fminf(fminf(gm[0], gm[1]), fminf(gm[2], gm[3])),
-                                  fminf(fminf(gm[4], gm[5]), fminf(gm[6], gm[7])));
+          for (int i = 0; i < 8; i++) gm[i] = fmin3(v[4 * i], v[4 * i + 1], fminf(v[4 * i + 2], v[4 * i + 3]));
+          const float cmn = fmin3(fmin3(gm[0], gm[1], gm[2]), fmin3(gm[3], gm[4], gm[5]), fminf(gm[6], gm[7]));
           // A better chunk minimum tightens the bound; drop candidates that
           // fall outside it.
           if (vp && cmn < best) {
@@ -281,41 +312,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           unsigned m = 0;
 #pragma unroll
-          for (int i = 0; i < 8; i++) m |= (vp && gm[i] <= bound) ? (1u << i) : 0u;
-          unsigned um = __reduce_or_sync(sel::kFull, m);
-          while (um) {
-            const int i = __ffs(um) - 1;
-            um &= um - 1;
-            if ((m >> i) & 1u) {
-              float w0 = v[0], w1 = v[1], w2 = v[2], w3 = v[3];
+          for (int i = 0; i < 8; i++) m |= gm[i] <= bound ? (1u << i) : 0u;
+          // One vote per chunk; static register indices for the groups.
+          if (__any_sync(sel::kFull, m != 0)) {
 #pragma unroll
-              for (int t = 1; t < 8; t++) {
-                if (i == t) {
-                  w0 = v[4 * t];
-                  w1 = v[4 * t + 1];
-                  w2 = v[4 * t + 2];
-                  w3 = v[4 * t + 3];
-                }
-              }
+            for (int i = 0; i < 8; i++) {
+              if ((m >> i) & 1u) {
+                float w0 = v[4 * i], w1 = v[4 * i + 1], w2 = v[4 * i + 2], w3 = v[4 * i + 3];
 #pragma unroll 1
-              for (int jj = 0; jj < 4; jj++) {
-                const float sc = jj == 0 ? w0 : jj == 1 ? w1 : jj == 2 ? w2 : w3;
-                if (4 * i + jj < cb && sc <= bound) {
-                  const Cand cn = Cand{sc, (uint32_t)(c0 + c * 32 + 4 * i + jj)};
-                  if (cnt < NCAND) {
-                    buf[cnt++] = cn;
-                  } else {
-                    // Keep the NCAND best; remember the best score dropped.
-                    int wi = 0;
-                    for (int e = 1; e < NCAND; e++)
-                      if (buf[e].hs > buf[wi].hs) wi = e;
-                    if (sc < buf[wi].hs) {
-                      lost = fminf(lost, buf[wi].hs);
-                      buf[wi] = cn;
-                    } else {
-                      lost = fminf(lost, sc);
-                    }
-                  }
+                for (int jj = 0; jj < 4; jj++) {
+                  const float sc = w0;
+                  w0 = w1;
+                  w1 = w2;
+                  w2 = w3;
+                  if (4 * i + jj < cb && sc <= bound) insert(sc, (uint32_t)(c0 + c * 32 + 4 * i + jj));
                 }
               }
             }
@@ -588,17 +598,11 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
   a.res = res;
   a.cands = cands;
   a.err = err;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    VRS_CUDA(cudaFuncSetAttribute(kmeans_assign_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)SMEM_TOTAL));
-    attr_set[dev] = true;
-  }
+  auto kern = a.mode == 0 ? kmeans_assign_tc_kernel<0> : kmeans_assign_tc_kernel<1>;
+  VRS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL));
   const int nptiles = (int)((n + BM * NACC - 1) / (BM * NACC));
   const int grid = std::max(1, std::min(nptiles, num_sms));
-  kmeans_assign_tc_kernel<<<grid, THREADS, SMEM_TOTAL, s>>>(tmA, tmB, a);
+  kern<<<grid, THREADS, SMEM_TOTAL, s>>>(tmA, tmB, a);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;
