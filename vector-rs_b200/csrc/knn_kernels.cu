@@ -128,22 +128,9 @@ __global__ void __launch_bounds__(kScanThreads) knn_scan_exact_kernel(KnnScanArg
 
 // ------------------------------------------------------------------ select
 template <int METRIC>
-__global__ void __launch_bounds__(256) knn_select_kernel(KnnSelectArgs a) {
-  extern __shared__ Cand sbuf[];
-  __shared__ int s_hist[256];
-  __shared__ int s_res[4];
-  __shared__ int s_wt[32];
-  __shared__ int s_off[65];
-  const int slot = blockIdx.x;
+__device__ void select_one(const KnnSelectArgs& a, int slot, Cand* sbuf, int* s_hist, int* s_res, int* s_wt,
+                           int* s_off) {
   const int tid = threadIdx.x;
-  if (a.retry) {
-    // Second chance for queries the warp select could not hold (flag 2).
-    if (a.overflow[slot] != 2) return;
-    __syncthreads();
-    if (tid == 0) a.overflow[slot] = 0;
-  } else if (a.overflow[slot]) {
-    return;
-  }
   const int qrow = a.q_index ? a.q_index[slot] : slot;
   if (tid == 0) {
     int tot = 0;
@@ -221,6 +208,30 @@ __global__ void __launch_bounds__(256) knn_select_kernel(KnnSelectArgs a) {
       a.out_dist[(int64_t)qrow * a.k + r] = e.id == 0xffffffffu ? NAN : vrs_exact::finish(METRIC, key);
       a.out_id[(int64_t)qrow * a.k + r] = gid;
     }
+  }
+}
+
+// Block per query (grid = nq), or, with a.retry, a small grid striding over
+// the queries and taking only those the warp select flagged (2).
+template <int METRIC>
+__global__ void __launch_bounds__(256) knn_select_kernel(KnnSelectArgs a) {
+  extern __shared__ Cand sbuf[];
+  __shared__ int s_hist[256];
+  __shared__ int s_res[4];
+  __shared__ int s_wt[32];
+  __shared__ int s_off[65];
+  if (!a.retry) {
+    if (a.overflow[blockIdx.x]) return;
+    select_one<METRIC>(a, blockIdx.x, sbuf, s_hist, s_res, s_wt, s_off);
+    return;
+  }
+  for (int slot = blockIdx.x; slot < a.nq; slot += gridDim.x) {
+    if (a.overflow[slot] != 2) continue;  // uniform over the block
+    __syncthreads();
+    if (threadIdx.x == 0) a.overflow[slot] = 0;
+    __syncthreads();
+    select_one<METRIC>(a, slot, sbuf, s_hist, s_res, s_wt, s_off);
+    __syncthreads();
   }
 }
 
@@ -529,7 +540,8 @@ struct SelectL {
     size_t smem = (size_t)a.max_sort * sizeof(Cand);
     VRS_CUDA(cudaFuncSetAttribute(knn_select_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem));
-    knn_select_kernel<M><<<a.nq, 256, smem, s>>>(a);
+    const unsigned grid = a.retry ? (unsigned)std::min(a.nq, 148 * 2) : (unsigned)a.nq;
+    knn_select_kernel<M><<<grid, 256, smem, s>>>(a);
     VRS_CUDA(cudaGetLastError());
     count_launch();
     return VRS_OK;
