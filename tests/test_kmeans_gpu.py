@@ -90,3 +90,18 @@ def test_tolerance_stop_and_determinism(vc, orc, gpu):
     assert r1.inertia == r2.inertia
     c_o, a_o, it_o, in_o = orc.kmeans_fit(x, 8, init, 50, 1e-6, 0)
     _check(r1, c_o, a_o, it_o, in_o)
+
+
+@pytest.mark.parametrize("scale", [1e4, 1e-4, 1e-12])
+@pytest.mark.parametrize("metric", [L2, DOT])
+def test_operand_scale_extremes(vc, orc, gpu, metric, scale):
+    """The tensor-core assignment scales points and centroids by one power of
+    two into fp16's range: data far from unit magnitude (and initial
+    centroids larger than the data) must give the oracle's result."""
+    x = (_mixture(vc, 20000, 24, 32, 0.1, 11) * scale).astype(np.float32)
+    K = 32
+    init = x[:K].copy()
+    init[0] *= 4.0  # an initial centroid outside the data's range
+    res = vc.CudaKMeansEngine.new().fit(x, 24, K, 5, 0.0, vc.DistanceMetric(metric), init=init)
+    c_o, a_o, it_o, in_o = orc.kmeans_fit(x, K, init, 5, 0.0, metric)
+    _check(res, c_o, a_o, it_o, in_o)

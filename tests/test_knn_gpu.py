@@ -168,3 +168,31 @@ def test_full_size_c4_sample(vc, orc, gpu, metric):
     assert (np.diff(dg, axis=1) >= 0).all()
     do, io = orc.knn_search(base, qs, 10, metric)
     _assert_parity(metric, dg, ig, do, io)
+
+
+@pytest.mark.parametrize("d", [125, 126, 127])
+def test_l2_fold_boundary(vc, orc, gpu, d):
+    """Squared L2 folds -|x|^2/2 into two extra K columns while d + 2 <= 128;
+    d = 127 keeps |x|^2 in the epilogue. Both sides of the boundary, with a
+    wide value range."""
+    base, qs = _data(vc, L2, 5000, 40, d, 900 + d)
+    base[::7] *= 30.0
+    eng = _engine(vc, base, L2)
+    for k in (1, 64):
+        dg, ig = eng.search_arrays(qs, k)
+        do, io = orc.knn_search(base, qs, k, L2)
+        _assert_parity(L2, dg, ig, do, io, f"d={d} k={k}")
+
+
+def test_cosine_fp16_tiny_norms(vc, orc, gpu):
+    """Cosine runs on fp16 unit rows; rows and queries with near-zero norms
+    (where the reference's zero guard can fire) bypass the bound."""
+    base, qs = _data(vc, COS, 4000, 30, 64, 77)
+    base[5] *= 1e-6
+    base[17] = 0.0
+    qs[3] *= 1e-7
+    qs[4] = 0.0
+    eng = _engine(vc, base, COS)
+    dg, ig = eng.search_arrays(qs, 20)
+    do, io = orc.knn_search(base, qs, 20, COS)
+    _assert_parity(COS, dg, ig, do, io)
