@@ -55,6 +55,7 @@ constexpr size_t SMEM_BAR = 256;
 constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_HIST + SMEM_BAR;
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait, then abort
 constexpr uint32_t TMEM_COLS = 512;
+constexpr int kTauCap = 24576;  // pivot minima per query held in shared memory (192 KB)
 
 struct TcScanArgs {
   const float* xn;   // |x|^2 per row (L2 mode), zero padded to a multiple of BN
@@ -457,14 +458,22 @@ __global__ void __launch_bounds__(256) tc_tau_kernel(const float* __restrict__ v
   __shared__ int s_hist[256];
   __shared__ int s_res[4];
   const int q = blockIdx.x;
-  const int total = nparts * len;
+  // More minima than shared memory holds: groups of `grp` consecutive
+  // minima enter as their minimum (still one distinct row each).
+  const int grp = (len + kTauCap / nparts - 1) / (kTauCap / nparts);
+  const int glen = (len + grp - 1) / grp;
+  const int total = nparts * glen;
   if (total < k) {
     if (threadIdx.x == 0) init_bound[q] = INFINITY;
     return;
   }
   for (int p = 0; p < nparts; p++) {
     const float* row = vals + p * part_stride + (int64_t)q * len;
-    for (int t = threadIdx.x; t < len; t += blockDim.x) buf[p * len + t] = Cand{row[t], 0u};
+    for (int t = threadIdx.x; t < glen; t += blockDim.x) {
+      float m = INFINITY;
+      for (int e = t * grp; e < min(len, t * grp + grp); e++) m = fminf(m, row[e]);
+      buf[p * glen + t] = Cand{m, 0u};
+    }
   }
   __syncthreads();
   const uint32_t kth = sel::block_select(buf, total, k, s_hist, s_res);
@@ -485,16 +494,28 @@ __global__ void __launch_bounds__(256) tc_pivot_topk_kernel(const float* __restr
   const int q = blockIdx.x;
   const float* row = tmin + (int64_t)q * ntile;
   float* dst = out + (int64_t)q * k;
-  if (ntile <= k) {
-    for (int j = threadIdx.x; j < k; j += blockDim.x) dst[j] = j < ntile ? row[j] : INFINITY;
+  // Groups of consecutive minima beyond the shared capacity (see tc_tau_kernel).
+  const int grp = (ntile + kTauCap - 1) / kTauCap;
+  const int glen = (ntile + grp - 1) / grp;
+  if (glen <= k) {
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+      float m = INFINITY;
+      if (j < glen)
+        for (int e = j * grp; e < min(ntile, j * grp + grp); e++) m = fminf(m, row[e]);
+      dst[j] = m;
+    }
     return;
   }
-  for (int t = threadIdx.x; t < ntile; t += blockDim.x) buf[t] = Cand{row[t], 0u};
+  for (int t = threadIdx.x; t < glen; t += blockDim.x) {
+    float m = INFINITY;
+    for (int e = t * grp; e < min(ntile, t * grp + grp); e++) m = fminf(m, row[e]);
+    buf[t] = Cand{m, 0u};
+  }
   if (threadIdx.x == 0) s_pos = 0;
   __syncthreads();
-  const uint32_t kth = sel::block_select(buf, ntile, k, s_hist, s_res);
+  const uint32_t kth = sel::block_select(buf, glen, k, s_hist, s_res);
   __syncthreads();
-  for (int t = threadIdx.x; t < ntile; t += blockDim.x) {
+  for (int t = threadIdx.x; t < glen; t += blockDim.x) {
     const float v = buf[t].hs;
     if (ord_key(v) < kth) dst[atomicAdd(&s_pos, 1)] = v;
   }
@@ -593,11 +614,12 @@ int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, 
 int tc_tau(const float* vals, int nparts, int64_t part_stride, int len, int nq, int k, const float* absm,
            float* init_bound, cudaStream_t s) {
   if (nq == 0) return VRS_OK;
-  const size_t smem = (size_t)std::max(nparts * len, 1) * sizeof(Cand);
-  if (smem > 200 * 1024) {
-    set_error(VRS_ERR_INVALID_CONFIG, "pivot tile count too large");
+  if (nparts > kTauCap) {
+    set_error(VRS_ERR_INVALID_CONFIG, "too many shards for the pooled pivot");
     return VRS_ERR_INVALID_CONFIG;
   }
+  const int grp = (len + kTauCap / nparts - 1) / (kTauCap / nparts);
+  const size_t smem = (size_t)std::max(nparts * ((len + grp - 1) / grp), 1) * sizeof(Cand);
   VRS_CUDA(cudaFuncSetAttribute(tc_tau_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   tc_tau_kernel<<<nq, 256, smem, s>>>(vals, nparts, part_stride, len, nq, k, absm, init_bound);
   VRS_CUDA(cudaGetLastError());
@@ -607,11 +629,8 @@ int tc_tau(const float* vals, int nparts, int64_t part_stride, int len, int nq, 
 
 int tc_pivot_topk(const float* tmin, int ntile, int nq, int k, float* out, cudaStream_t s) {
   if (nq == 0) return VRS_OK;
-  const size_t smem = (size_t)std::max(ntile, 1) * sizeof(Cand);
-  if (smem > 200 * 1024) {
-    set_error(VRS_ERR_INVALID_CONFIG, "pivot tile count too large");
-    return VRS_ERR_INVALID_CONFIG;
-  }
+  const int grp = (ntile + kTauCap - 1) / kTauCap;
+  const size_t smem = (size_t)std::max((ntile + grp - 1) / grp, 1) * sizeof(Cand);
   VRS_CUDA(cudaFuncSetAttribute(tc_pivot_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   tc_pivot_topk_kernel<<<nq, 256, smem, s>>>(tmin, ntile, nq, k, out);
   VRS_CUDA(cudaGetLastError());

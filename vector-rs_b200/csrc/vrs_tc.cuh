@@ -56,12 +56,15 @@ int tc_tau(const float* vals, int nparts, int64_t part_stride, int len, int nq, 
 int tc_pivot_topk(const float* tmin, int ntile, int nq, int k, float* out, cudaStream_t s);
 // Rows in the pivot set (every stride-th row) of a shard of n rows when
 // `parts` shards share one base and pool their pivot minima: the pooled
-// pivot set is about 1/6 of the base and at least 65,536 rows.
+// pivot set is about 1/6 of the base and at least 65,536 rows; beyond
+// 1.6M pivot rows, 1/16 of the shard (the pivot pass's epilogue is cheap, and
+// a denser pivot keeps the candidate band of huge bases small).
 inline int64_t tc_pivot_rows(int64_t n, int parts, int64_t* stride) {
   int64_t m = n / 6;
   const int64_t lo = (65536 + parts - 1) / parts;
   if (m < lo) m = lo;
-  if (m > 1600000) m = 1600000;
+  const int64_t hi = n / 16 > 1600000 ? n / 16 : 1600000;
+  if (m > hi) m = hi;
   if (m >= n) {
     *stride = 1;
     return n;
