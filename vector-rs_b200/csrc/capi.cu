@@ -192,6 +192,9 @@ struct KnnShard {
   int64_t pivot_m = 0, pivot_stride = 1;
   DBuf tmin, ibound;            // per-search pivot-pass outputs
   DBuf ptop, ptop_all;          // k smallest pivot minima per query: own, all shards
+  float xscale = 1.0f;          // tensor-core operand scale of the base rows
+  int fold_m = 0;               // exponent of the folded -|x|^2 column
+  DBuf qscale;                  // per-search operand scale of each query
   bool use_simt = false;        // CUDA-core scan (Manhattan, Chebyshev, Hellinger)
   // per-search scratch
   DBuf q_in, q, q_aux, cand, cnt, overflow, pairs, gathered, out_dist, out_id;
@@ -220,7 +223,7 @@ struct vrs_knn {
       for (DBuf* b : {&s->base, &s->base_aux, &s->q_in, &s->q, &s->q_aux, &s->cand, &s->cnt,
                       &s->overflow, &s->pairs, &s->gathered, &s->out_dist, &s->out_id, &s->xb,
                       &s->xn, &s->xmax, &s->tiny, &s->ntiny, &s->qb, &s->absm, &s->err, &s->qindex, &s->pb,
-                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all})
+                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all, &s->qscale})
         b->release();
       if (s->own_stream) cudaStreamDestroy(s->own_stream);
     }
@@ -275,8 +278,20 @@ int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
     VRS_CUDA(cudaMemsetAsync(s->xn.p, 0, (size_t)npad * sizeof(float), s->stream));
     VRS_CUDA(cudaMemsetAsync(s->xmax.p, 0, sizeof(unsigned int), s->stream));
     VRS_CUDA(cudaMemsetAsync(s->ntiny.p, 0, sizeof(int), s->stream));
-    VRS_TRY(tc::tc_base_prep(s->base.as<float>(), s->n_local, h->d, h->dp, h->metric, s->xb.p,
-                             s->xn.as<float>(), s->xmax.as<unsigned int>(), s->tiny.as<uint32_t>(),
+    // Operand scale from the largest |element| of the shard.
+    {
+      DBuf mx;
+      VRS_TRY(mx.reserve(sizeof(float)));
+      VRS_CUDA(cudaMemsetAsync(mx.p, 0, sizeof(float), s->stream));
+      VRS_TRY(launch_abs_max(s->base.as<float>(), s->n_local, h->d, h->dp, mx.as<float>(), s->stream));
+      float maxabs = 0.0f;
+      VRS_CUDA(cudaMemcpyAsync(&maxabs, mx.p, sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+      VRS_CUDA(cudaStreamSynchronize(s->stream));
+      s->xscale = tc::tc_base_scale(h->metric, maxabs);
+      s->fold_m = tc::tc_fold_exponent(h->d, s->xscale, maxabs);
+    }
+    VRS_TRY(tc::tc_base_prep(s->base.as<float>(), s->n_local, h->d, h->dp, h->metric, s->xscale, s->fold_m,
+                             s->xb.p, s->xn.as<float>(), s->xmax.as<unsigned int>(), s->tiny.as<uint32_t>(),
                              s->ntiny.as<int>(), tc::kTinyCap, s->stream));
     VRS_CUDA(cudaMemcpyAsync(&s->n_tiny, s->ntiny.p, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
     VRS_CUDA(cudaStreamSynchronize(s->stream));
@@ -411,8 +426,10 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   if (nq_alloc > nq)
     VRS_CUDA(cudaMemsetAsync((char*)s->qb.p + (size_t)nq * d16 * 2, 0, (size_t)(nq_alloc - nq) * d16 * 2, st));
   VRS_CUDA(cudaMemsetAsync(s->err.p, 0, sizeof(int), st));
-  VRS_TRY(tc::tc_query_prep(s->q.as<float>(), nq, h->d, h->dp, h->metric, s->xmax.as<unsigned int>(),
-                            s->qb.p, s->absm.as<float>(), s->overflow.as<int>(), st));
+  VRS_TRY(s->qscale.reserve((size_t)nq * sizeof(float)));
+  VRS_TRY(tc::tc_query_prep(s->q.as<float>(), nq, h->d, h->dp, h->metric, s->xmax.as<unsigned int>(), s->xscale,
+                            s->fold_m, s->qb.p, s->qscale.as<float>(), s->absm.as<float>(), s->overflow.as<int>(),
+                            st));
   VRS_TRY(s->ibound.reserve((size_t)nq * sizeof(float)));
   if (phase == kPhasePivot) VRS_TRY(s->ptop.reserve((size_t)nq * kk * sizeof(float)));
   if (s->n_local > 0) {
@@ -425,7 +442,7 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
     ProfToken t0 = prof_begin("knn_pivot", st);
     VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, pb, s->pivot_m, h->d, pn, h->metric, nq, kk, pp, nullptr,
                         nullptr, s->overflow.as<int>(), s->absm.as<float>(), s->err.as<int>(),
-                        s->tmin.as<float>(), nullptr, st));
+                        s->tmin.as<float>(), nullptr, s->qscale.as<float>(), s->xscale, st));
     if (phase == kPhasePivot)
       VRS_TRY(tc::tc_pivot_topk(s->tmin.as<float>(), ntile, nq, kk, s->ptop.as<float>(), st));
     else
@@ -452,7 +469,8 @@ main_phase:
     ProfToken t = prof_begin("knn_scan", st);
     VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, s->xb.p, s->n_local, h->d, s->xn.as<float>(), h->metric, nq, kk,
                         p, s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(),
-                        s->absm.as<float>(), s->err.as<int>(), nullptr, s->ibound.as<float>(), st));
+                        s->absm.as<float>(), s->err.as<int>(), nullptr, s->ibound.as<float>(), s->qscale.as<float>(),
+                        s->xscale, st));
     prof_end(t, st);
   }
   KnnSelectArgs sa{};

@@ -77,7 +77,11 @@ struct TcScanArgs {
   int64_t tmin_stride;  // entries per query row of tmin (2 * tiles)
   // Starting acceptance bound per query (null: +inf).
   const float* init_bound;
-  uint32_t idesc;    // MMA instruction descriptor (fp16 or bf16 operands)
+  uint32_t idesc;    // MMA instruction descriptor
+  // Operand scales (powers of two): accumulators are qscale[q] * xscale
+  // times the unscaled products.
+  const float* qscale;
+  float xscale;
 };
 
 // MODE 0: heap score = |x|^2 - 2 acc (squared L2, Mahalanobis);
@@ -221,6 +225,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     // Acceptance bound on the heap score; -inf for padding queries, so that
     // nothing passes for them.
     float bound = vq ? (a.init_bound ? a.init_bound[q] : INFINITY) : -INFINITY;
+    // Accumulator scale of this query and its inverse (both exact powers of two).
+    const float ks = vq ? a.qscale[q] * a.xscale : 1.0f;
+    const float inv_ks = 1.0f / ks;
+    const float f2 = -2.0f * inv_ks;
     const float absm = vq ? a.absm[q] : 0.0f;
     int* hist = s_hist + ew * 256;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
@@ -236,9 +244,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const int64_t rem_cols = row_end - n0;
       const int valid_cols = rem_cols < HALF_COLS ? (int)(rem_cols > 0 ? rem_cols : 0) : HALF_COLS;
-      // Key threshold: MODE 0 passes key <= bound, MODE 1 key >= -bound,
-      // MODE 2 key >= -bound / 2 (halving and doubling are exact).
-      const float thr = MODE == 0 ? bound : MODE == 1 ? -bound : -0.5f * bound;
+      // Key threshold: MODE 0 passes key <= bound, MODE 1 key >= -bound ks,
+      // MODE 2 key >= -bound ks / 2 (all factors are exact powers of two).
+      const float thr = MODE == 0 ? bound : MODE == 1 ? -bound * ks : -0.5f * bound * ks;
       float tile_best = MODE == 0 ? INFINITY : -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < HALF_COLS / 32; c++) {
@@ -249,10 +257,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int j4 = 0; j4 < 8; j4++) {
             const float4 x4 = __ldg(xp + j4);
-            v[4 * j4 + 0] = fmaf(-2.0f, v[4 * j4 + 0], x4.x);
-            v[4 * j4 + 1] = fmaf(-2.0f, v[4 * j4 + 1], x4.y);
-            v[4 * j4 + 2] = fmaf(-2.0f, v[4 * j4 + 2], x4.z);
-            v[4 * j4 + 3] = fmaf(-2.0f, v[4 * j4 + 3], x4.w);
+            v[4 * j4 + 0] = fmaf(f2, v[4 * j4 + 0], x4.x);
+            v[4 * j4 + 1] = fmaf(f2, v[4 * j4 + 1], x4.y);
+            v[4 * j4 + 2] = fmaf(f2, v[4 * j4 + 2], x4.z);
+            v[4 * j4 + 3] = fmaf(f2, v[4 * j4 + 3], x4.w);
           }
         }
         const int cb = valid_cols - c * 32;
@@ -286,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if ((m >> i) & 1u) {
 #pragma unroll
               for (int jj = 0; jj < 4; jj++) {
-                const float sc = MODE == 0 ? v[4 * i + jj] : MODE == 1 ? -v[4 * i + jj] : -2.0f * v[4 * i + jj];
+                const float sc = MODE == 0 ? v[4 * i + jj] : MODE == 1 ? -inv_ks * v[4 * i + jj] : f2 * v[4 * i + jj];
                 if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + c * 32 + 4 * i + jj)};
               }
             }
@@ -299,7 +307,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (TILEMIN) {
         if (vq)
           a.tmin[(int64_t)q * a.tmin_stride + (row_begin / BN + t) * 2 + ch] =
-              MODE == 0 ? tile_best : MODE == 1 ? -tile_best : -2.0f * tile_best;
+              MODE == 0 ? tile_best : MODE == 1 ? -inv_ks * tile_best : f2 * tile_best;
         continue;
       }
       // Shrink lists that could overflow on the next tile.
@@ -347,7 +355,7 @@ __device__ __forceinline__ uint16_t to_operand(float v, bool f16) {
 }
 
 __global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int d, int dp, int d16,
-                                    int metric, uint16_t* __restrict__ xb,
+                                    int metric, float xscale, int fold_m, uint16_t* __restrict__ xb,
                                     float* __restrict__ xn, unsigned int* __restrict__ xmax_bits,
                                     uint32_t* __restrict__ tiny, int* __restrict__ n_tiny,
                                     int tiny_cap) {
@@ -371,15 +379,16 @@ __global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int 
   for (int j = 0; j < d16; j++) {
     float e = j < d ? v[j] : 0.0f;
     ss += (double)e * (double)e;
-    o[j] = to_operand(metric == vrs_exact::kCos ? e * scale : e, f16);
+    o[j] = to_operand(metric == vrs_exact::kCos ? e * scale : e * xscale, f16);
   }
   if (tc_fold(metric, d)) {
-    // -|x|^2 / 2 as hi + lo bf16 in columns d and d + 1 (queries put 1.0
-    // there): within 2^-16 |x|^2 / 2 of the value.
-    const double t = -0.5 * ss;
-    const __nv_bfloat16 hi = __float2bfloat16_rn((float)t);
-    o[d] = __bfloat16_as_ushort(hi);
-    o[d + 1] = __bfloat16_as_ushort(__float2bfloat16_rn((float)(t - (double)__bfloat162float(hi))));
+    // F = -xscale |x|^2 / 2^(fold_m + 1) as hi + lo fp16 in columns d and
+    // d + 1 (|F| <= 2^14 by the choice of fold_m); queries put
+    // qscale * 2^fold_m there, so the accumulator gains -qscale xscale |x|^2 / 2.
+    const double t = -(double)xscale * ss * ldexp(1.0, -(fold_m + 1));
+    const __half hi = __double2half(t);
+    o[d] = __half_as_ushort(hi);
+    o[d + 1] = __half_as_ushort(__double2half(t - (double)__half2float(hi)));
   }
   if (xn) xn[r] = (float)ss;
   atomicMax(xmax_bits, __float_as_uint((float)sqrt(ss)));
@@ -388,9 +397,9 @@ __global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int 
 // Queries -> bf16 operand rows and per-query acceptance margins (heap-score
 // units). Near-zero cosine queries are routed to the exact fallback.
 __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d, int dp, int d16,
-                                     int metric, const unsigned int* __restrict__ xmax_bits,
-                                     uint16_t* __restrict__ qb, float* __restrict__ absm,
-                                     int* __restrict__ overflow) {
+                                     int metric, const unsigned int* __restrict__ xmax_bits, float xscale,
+                                     int fold_m, uint16_t* __restrict__ qb, float* __restrict__ qscale,
+                                     float* __restrict__ absm, int* __restrict__ overflow) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nq) return;
   const float* v = q + (int64_t)i * dp;
@@ -406,40 +415,60 @@ __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d,
       scale = 1.0f / sq;
     }
   }
+  // Query scale: largest element into [2^7, 2^8) (unit cosine rows: 1);
+  // with the folded |x|^2 the fold column qs 2^fold_m must stay a normal
+  // fp16 (<= 2^15, >= 2^-14); a query that cannot meet both goes to the
+  // exact scan.
+  const bool fold = tc_fold(metric, d);
+  float qs = 1.0f;
+  if (metric != vrs_exact::kCos) {
+    float mx = 0.0f;
+    for (int j = 0; j < d; j++) mx = fmaxf(mx, fabsf(v[j]));
+    int ex = mx > 0.0f ? 7 - ilogbf(mx) : 0;
+    ex = max(-60, min(60, ex));
+    if (fold) {
+      ex = min(ex, 15 - fold_m);
+      if (ex < -14 - fold_m || (mx > 0.0f && ldexpf(mx, ex) > 32768.0f)) overflow[i] = 1;
+    }
+    qs = ldexpf(1.0f, ex);
+  }
+  qscale[i] = qs;
   double ss = 0.0;
   for (int j = 0; j < d16; j++) {
     float e = j < d ? v[j] : 0.0f;
     ss += (double)e * (double)e;
-    o[j] = to_operand(metric == vrs_exact::kCos ? e * scale : e, f16);
+    o[j] = to_operand(metric == vrs_exact::kCos ? e * scale : e * qs, f16);
   }
-  const bool fold = tc_fold(metric, d);
   if (fold) {
-    o[d] = __bfloat16_as_ushort(__float2bfloat16_rn(1.0f));
-    o[d + 1] = __bfloat16_as_ushort(__float2bfloat16_rn(1.0f));
+    const __half c = __float2half_rn(ldexpf(qs, fold_m));
+    o[d] = __half_as_ushort(c);
+    o[d + 1] = __half_as_ushort(c);
   }
   const double X = (double)__uint_as_float(*xmax_bits);
   const double Q = sqrt(ss);
   const double u = 0x1p-24;
-  // bf16 keeps 8 significant bits: each rounded operand is within 2^-8
-  // (relative) of its value, so a dot product of rounded operands is within
-  // (2^-7 + 2^-16) |q| |x| of the exact one (Cauchy-Schwarz), plus the f32
-  // accumulation of d16 + 2 terms (4 ulps each, allowing truncation). fp16
-  // (cosine: unit vectors) keeps 11: 2^-10 + 2^-22, plus 2^-20 for elements
-  // below fp16's normal range (absolute error <= 2^-25 each, at most
-  // 2^-25 sqrt(d) |other| per side).
-  const double c_tc = f16 ? 0x1p-10 + 0x1p-22 + 0x1p-20 + (double)(d16 + 2) * 0x1p-22
-                          : 0x1p-7 + 0x1p-16 + (double)(d16 + 2) * 0x1p-22;
+  // fp16 keeps 11 significant bits: each rounded (scaled) operand is within
+  // 2^-11 (relative) of its value, so a dot product of rounded operands is
+  // within (2^-10 + 2^-22) |q| |x| of the exact one (Cauchy-Schwarz), plus
+  // the f32 accumulation of d16 + 2 terms (4 ulps each, allowing
+  // truncation). Elements below fp16's normal range (2^-14, scaled) err by at
+  // most 2^-25 (scaled) each: 2^-25 sqrt(d) (X / qscale + Q / xscale)
+  // unscaled (cosine: unit vectors, scale 1).
+  const double c_tc = 0x1p-10 + 0x1p-22 + (double)(d16 + 2) * 0x1p-22;
+  const double sub = metric == vrs_exact::kCos ? 0x1p-25 * sqrt((double)d) * 2.0
+                                               : 0x1p-25 * sqrt((double)d) * (X / qs + Q / xscale);
   const double g = (double)(d + 4) * u * 1.01;
   double e;
   if (metric == vrs_exact::kCos) {
-    e = c_tc + 8.0 * u + 4.0 * g;
+    e = c_tc + sub + 8.0 * u + 4.0 * g;
   } else if (metric == vrs_exact::kDot) {
-    e = (c_tc + 2.0 * g) * Q * X;
+    e = (c_tc + 2.0 * g) * Q * X + sub;
   } else {  // squared L2 / Mahalanobis scores |x|^2 - 2 q.x
-    e = 2.0 * c_tc * Q * X + 8.0 * g * (Q + X) * (Q + X);
-    // Folded |x|^2: its hi + lo split (2^-16 |x|^2 / 2) and its share of the
-    // accumulation, doubled by the score's factor -2.
-    if (fold) e += (0x1p-16 + (double)(d16 + 2) * 0x1p-22) * X * X;
+    e = 2.0 * (c_tc * Q * X + sub) + 8.0 * g * (Q + X) * (Q + X);
+    // Folded |x|^2: its hi + lo split (2^-22 relative, or 2^-25 absolute in
+    // fp16 units when lo is subnormal) and its share of the accumulation,
+    // doubled by the score's factor -2.
+    if (fold) e += (0x1p-22 + (double)(d16 + 2) * 0x1p-22) * X * X + 0x1p-24 * ldexp(1.0, fold_m) / xscale;
   }
   absm[i] = (float)(2.0 * e * 1.25) * (1.0f + 0x1p-20f);
 }
@@ -580,21 +609,22 @@ bool tc_supported(int metric, int d) {
 
 int tc_d16(int metric, int d) { return (tc_fold(metric, d) ? d + 2 + 15 : d + 15) / 16 * 16; }
 
-int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* xn,
-                 unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s) {
+int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, float xscale, int fold_m, void* xb,
+                 float* xn, unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s) {
   if (n == 0) return VRS_OK;
   tc_base_prep_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(
-      x, n, d, dp, tc_d16(metric, d), metric, (uint16_t*)xb, xn, xmax_bits, tiny, n_tiny, tiny_cap);
+      x, n, d, dp, tc_d16(metric, d), metric, xscale, fold_m, (uint16_t*)xb, xn, xmax_bits, tiny, n_tiny,
+      tiny_cap);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;
 }
 
 int tc_query_prep(const float* q, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
-                  void* qb, float* absm, int* overflow, cudaStream_t s) {
+                  float xscale, int fold_m, void* qb, float* qscale, float* absm, int* overflow, cudaStream_t s) {
   if (nq == 0) return VRS_OK;
   tc_query_prep_kernel<<<(nq + 127) / 128, 128, 0, s>>>(q, nq, d, dp, tc_d16(metric, d), metric, xmax_bits,
-                                                         (uint16_t*)qb, absm, overflow);
+                                                         xscale, fold_m, (uint16_t*)qb, qscale, absm, overflow);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;
@@ -663,7 +693,8 @@ TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms) {
 
 int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn,
             int metric, int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow,
-            const float* absm, int* err, float* tmin, const float* init_bound, cudaStream_t s) {
+            const float* absm, int* err, float* tmin, const float* init_bound, const float* qscale, float xscale,
+            cudaStream_t s) {
   if (n == 0 || nq == 0) return VRS_OK;
   const int d16 = tc_d16(metric, d);
   CUtensorMap tmA, tmB;
@@ -687,6 +718,8 @@ int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d,
   a.tmin = tmin;
   a.tmin_stride = 2 * ((n + BN - 1) / BN);
   a.idesc = f16 ? idesc_f16(BM, BN) : idesc_bf16(BM, BN);
+  a.qscale = qscale;
+  a.xscale = xscale;
   a.init_bound = init_bound;
   const bool l2 = metric == vrs_exact::kL2 || metric == vrs_exact::kMaha;
   auto kern = tc_fold(metric, d) ? (tmin ? knn_scan_tc_kernel<2, true> : knn_scan_tc_kernel<2, false>)

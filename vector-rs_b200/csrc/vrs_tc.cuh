@@ -1,5 +1,7 @@
 // vrs_tc.cuh -- host-side interface of the tensor-core scan (knn_tc.cu).
 #pragma once
+#include <cmath>
+
 #include "vrs_internal.cuh"
 
 namespace vrs {
@@ -23,26 +25,47 @@ struct TcPlan {
 
 bool tc_supported(int metric, int d);
 // Squared L2 / Mahalanobis with d <= 126 fold -|x|^2 / 2 into the GEMM as two
-// extra K columns (hi + lo bf16; the query side holds 1.0 there).
+// extra K columns (hi + lo fp16 of -xscale |x|^2 / 2^(m+1); the query side
+// holds qscale * 2^m in both).
 __host__ __device__ inline bool tc_fold(int metric, int d) {
   return (metric == 0 || metric == 7) && d + 2 <= 128;  // kL2, kMaha
 }
-// Cosine operands are unit vectors (elements in [-1, 1]) and go to the
-// tensor cores as fp16 (11 significant bits; bf16's 8 would make the error
-// margin 8x wider); the other metrics use bf16 for its range.
-__host__ __device__ inline bool tc_fp16(int metric) { return metric == 2; }  // kCos
+// Operands go to the tensor cores as fp16 (11 significant bits; bf16's 8
+// would make the error margin 8x wider): cosine rows unit-normalised, the
+// other metrics scaled by powers of two (base: largest element in [2^7, 2^8);
+// each query likewise), undone exactly in the epilogue.
+__host__ __device__ inline bool tc_fp16(int) { return true; }
 // Operand row length (multiple of 16): d, plus the folded columns.
 int tc_d16(int metric, int d);
-int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, void* xb, float* xn,
-                 unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s);
+// xscale: the base's operand scale; fold_m: exponent of the folded -|x|^2
+// column (tc_fold_exponent).
+int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, float xscale, int fold_m, void* xb,
+                 float* xn, unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s);
+// Writes each query's operand scale to qscale[nq]; queries whose scale
+// cannot fit the folded column are flagged for the exact scan.
 int tc_query_prep(const float* q, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
-                  void* qb, float* absm, int* overflow, cudaStream_t s);
+                  float xscale, int fold_m, void* qb, float* qscale, float* absm, int* overflow, cudaStream_t s);
+// Base operand scale for a base whose largest |element| is maxabs, and the
+// folded column's exponent (|F| = xscale |x|^2 / 2^(m+1) <= 2^14 with
+// |x|^2 <= d maxabs^2).
+inline float tc_base_scale(int metric, float maxabs) {
+  if (metric == 2 || !(maxabs > 0.0f) || !std::isfinite(maxabs)) return 1.0f;  // kCos: unit rows
+  int ex = 7 - std::ilogb(maxabs);
+  ex = ex < -60 ? -60 : (ex > 60 ? 60 : ex);
+  return std::ldexp(1.0f, ex);
+}
+inline int tc_fold_exponent(int d, float xscale, float maxabs) {
+  if (!(maxabs > 0.0f)) return 0;
+  const double top = (double)xscale * d * (double)maxabs * (double)maxabs;
+  return (int)std::ceil(std::log2(top)) - 15;
+}
 TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms);
 // With tmin != null this is the pivot pass (per-tile minima, no appends);
 // init_bound (nullable) seeds each query's acceptance bound.
 int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn,
             int metric, int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow,
-            const float* absm, int* err, float* tmin, const float* init_bound, cudaStream_t s);
+            const float* absm, int* err, float* tmin, const float* init_bound, const float* qscale, float xscale,
+            cudaStream_t s);
 int tc_pivot_gather(const void* xb, const float* xn, int64_t m, int64_t stride, int d16, void* pb,
                     float* pn, cudaStream_t s);
 // Starting bound per query from pivot minima: query q's values are
