@@ -340,8 +340,9 @@ ScanPlan plan_scan(int64_t n_local, int nq, int kk) {
 // Launches the exact-order CUDA-core scan + select for `nq` query slots.
 // q_index (device, nullable) maps slots to query rows of s->q; results land
 // in the rows the slots name. `ovf` receives per-slot overflow flags.
+// `fallback` files the launches under the knn_fallback profiling token.
 int launch_exact_search(vrs_knn* h, KnnShard* s, int nq, int kk, const int* q_index, int* ovf,
-                        float* out_dist, uint32_t* out_id, Cand* out_pairs) {
+                        float* out_dist, uint32_t* out_id, Cand* out_pairs, bool fallback = false) {
   cudaStream_t st = s->stream;
   ScanPlan p = plan_scan(s->n_local, nq, kk);
   VRS_TRY(s->cand.reserve((size_t)p.nseg * nq * p.cap * sizeof(Cand)));
@@ -369,7 +370,7 @@ int launch_exact_search(vrs_knn* h, KnnShard* s, int nq, int kk, const int* q_in
   a.rho = 1.0f;
   a.absm = nullptr;
   if (s->n_local > 0) {
-    ProfToken t = prof_begin("knn_scan", st);
+    ProfToken t = prof_begin(fallback ? "knn_fallback" : "knn_scan", st);
     VRS_TRY(launch_knn_scan_exact(a, st));
     prof_end(t, st);
   }
@@ -399,7 +400,7 @@ int launch_exact_search(vrs_knn* h, KnnShard* s, int nq, int kk, const int* q_in
   sa.max_sort = p.max_sort;
   sa.tiny = nullptr;
   sa.n_tiny = 0;
-  ProfToken t = prof_begin("knn_select", st);
+  ProfToken t = prof_begin(fallback ? "knn_fallback" : "knn_select", st);
   VRS_TRY(launch_knn_select(sa, st));
   prof_end(t, st);
   return VRS_OK;
@@ -419,6 +420,9 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   const int nq_alloc = (nq + 255) / 256 * 256;
   tc::TcPlan p = tc::tc_plan(s->n_local, nq, kk, s->num_sms);
   const int nlists = 2 * p.nseg;
+  // A single shard's bound comes from a lower pivot rank and is verified by
+  // the select; pooled bounds stay proven (rank k).
+  const int tau_rank = phase == kPhaseAll ? tc::tc_optimistic_rank(kk, s->pivot_stride) : kk;
   if (phase == kPhaseMain) goto main_phase;
   VRS_TRY(s->qb.reserve((size_t)nq_alloc * d16 * 2));
   VRS_TRY(s->absm.reserve((size_t)nq * sizeof(float)));
@@ -446,7 +450,7 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
     if (phase == kPhasePivot)
       VRS_TRY(tc::tc_pivot_topk(s->tmin.as<float>(), ntile, nq, kk, s->ptop.as<float>(), st));
     else
-      VRS_TRY(tc::tc_tau(s->tmin.as<float>(), 1, 0, ntile, nq, kk, s->absm.as<float>(),
+      VRS_TRY(tc::tc_tau(s->tmin.as<float>(), 1, 0, ntile, nq, tau_rank, s->absm.as<float>(),
                          s->ibound.as<float>(), st));
     prof_end(t0, st);
   } else if (phase == kPhasePivot) {
@@ -499,6 +503,7 @@ main_phase:
   sa.max_sort = std::min(16384, next_pow2(std::max(512, nlists * (kk + 160) + s->n_tiny)));
   sa.tiny = s->tiny.as<uint32_t>();
   sa.n_tiny = h->metric == vrs_exact::kCos ? s->n_tiny : 0;
+  sa.init_bound = tau_rank < kk ? s->ibound.as<float>() : nullptr;
   ProfToken t = prof_begin("knn_select", st);
   if (nlists <= 32 && kk <= 256 && sa.n_tiny <= 256) {
     VRS_TRY(launch_knn_select_warp(sa, st));
@@ -630,7 +635,7 @@ int shard_search_finish(vrs_knn* h, KnnShard* s, float* out_dist, uint32_t* out_
   VRS_CUDA(cudaMemcpyAsync(s->qindex.p, idx.data(), (size_t)nf * sizeof(int), cudaMemcpyHostToDevice,
                            s->stream));
   int* ovf2 = s->overflow.as<int>() + nq;
-  VRS_TRY(launch_exact_search(h, s, nf, kk, s->qindex.as<int>(), ovf2, out_dist, out_id, out_pairs));
+  VRS_TRY(launch_exact_search(h, s, nf, kk, s->qindex.as<int>(), ovf2, out_dist, out_id, out_pairs, true));
   std::vector<int> f2(nf);
   VRS_CUDA(cudaMemcpyAsync(f2.data(), ovf2, (size_t)nf * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
   VRS_TRY(stream_wait(s->stream, nullptr, tmo));

@@ -154,12 +154,20 @@ __device__ void select_one(const KnnSelectArgs& a, int slot, Cand* sbuf, int* s_
   __syncthreads();
   // k-th best scan score over all segments -> acceptance bound -> survivors.
   int R = total;
-  if (total > a.k) {
+  const float sb = a.init_bound ? a.init_bound[slot] : INFINITY;
+  if (total > a.k || (total == a.k && sb < INFINITY)) {
     uint32_t kth = block_select(sbuf, total, a.k, s_hist, s_res);
     float tau = ord_inv(kth);
     float absm = a.kind == kAbsMargin ? a.absm[qrow] : 0.0f;
     float b = accept_bound(a.kind, tau, a.rho, absm);
+    if (!(b <= sb)) {
+      if (tid == 0) a.overflow[slot] = 1;
+      return;
+    }
     R = block_filter(sbuf, total, KeepBound{b}, s_wt);
+  } else if (total < a.k && sb < INFINITY) {
+    if (tid == 0) a.overflow[slot] = 1;
+    return;
   }
   // Exact re-rank of approximate survivors in the reference's order.
   if (a.kind != kExactScores) {
@@ -279,7 +287,12 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
   constexpr int kBatch = 4;  // entries per lane in flight
 
   float bound = INFINITY;
-  if (total > a.k) {
+  const float sb = a.init_bound ? a.init_bound[slot] : INFINITY;
+  if (total < a.k && sb < INFINITY) {
+    if (lane == 0) a.overflow[slot] = 1;  // fewer than k rows within an unproven bound
+    return;
+  }
+  if (total > a.k || (total == a.k && sb < INFINITY)) {
     uint32_t prefix = 0, pmask = 0;
     int kk = a.k;
     // Up to kSelRmax * 2 keys are staged in shared memory (the candidate
@@ -327,6 +340,10 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
     }
     const float absm = a.kind == kAbsMargin ? a.absm[qrow] : 0.0f;
     bound = accept_bound(a.kind, ord_inv(prefix), a.rho, absm);
+    if (!(bound <= sb)) {
+      if (lane == 0) a.overflow[slot] = 1;  // the scan's bound may have cut a top-k row
+      return;
+    }
   }
   // Survivors -> shared memory (batched reads of the flattened lists).
   int R = 0;

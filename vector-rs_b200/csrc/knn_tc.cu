@@ -1,17 +1,18 @@
 // knn_tc.cu -- tensor-core (tcgen05) fused distance + candidate scan for the
 // GEMM-form metrics (squared L2, Mahalanobis = sqrt L2, dot, cosine).
 //
-// Each CTA owns 256 queries (two M=128 bf16 operand tiles, loaded once by
-// TMA) and streams 128-row bf16 tiles of one base segment through a 4-stage
+// Each CTA owns 256 queries (two M=128 fp16 operand tiles, loaded once by
+// TMA) and streams 128-row fp16 tiles of one base segment through a 4-stage
 // TMA ring. One thread issues tcgen05.mma into two 128x128 f32 accumulators
-// per tile, double-buffered in TMEM (4 x 128 = 512 columns). Eight epilogue
-// warps read their lanes with tcgen05.ld (one thread = one query), form the
-// approximate heap score (L2: |x|^2 - 2 q.x, similarity: -q.x), and append
-// (score, row) to the query's segment list only when the score is within the
-// query's acceptance bound; lists are shrunk in place by a warp radix select
-// when nearly full. The Q x N score matrix never reaches HBM.
+// per tile, double-buffered in TMEM (4 x 128 = 512 columns). Sixteen
+// epilogue warps (one per TMEM lane quadrant, accumulator and column half)
+// read their lanes with tcgen05.ld (one thread = one query), reduce each
+// 64-column half to its best key, and only where that passes the query's
+// acceptance bound append (score, row) to the query's segment list; lists
+// are shrunk in place by a warp radix select when nearly full. The Q x N
+// score matrix never reaches HBM.
 //
-// Correctness: bf16 products carry a bounded error; a row can belong to the
+// Correctness: fp16 products carry a bounded error; a row can belong to the
 // exact top-k only if its approximate score is within `absm[q]` of the k-th
 // best approximate score, so every such row is kept and later re-ranked in
 // the reference's exact f32 arithmetic (knn_select in knn_kernels.cu).
@@ -40,7 +41,7 @@ namespace {
 constexpr int BM = 128;        // queries per accumulator
 constexpr int NACC = 2;        // accumulators per CTA (256 queries)
 constexpr int BN = 128;        // base rows per tile
-constexpr int KBW = 64;        // bf16 elements per K-block (one 128-byte swizzle row)
+constexpr int KBW = 64;        // 16-bit elements per K-block (one 128-byte swizzle row)
 constexpr int MAX_KBLK = 2;    // D <= 128 on this path
 constexpr int STAGES = 4;
 constexpr int EPI_WARPS = 16;   // 2 per (TMEM lane quadrant, accumulator): column halves
@@ -247,56 +248,53 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Key threshold: MODE 0 passes key <= bound, MODE 1 key >= -bound ks,
       // MODE 2 key >= -bound ks / 2 (all factors are exact powers of two).
       const float thr = MODE == 0 ? bound : MODE == 1 ? -bound * ks : -0.5f * bound * ks;
-      float tile_best = MODE == 0 ? INFINITY : -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < HALF_COLS / 32; c++) {
-        float v[32];
-        tmem_ld32(tmem + lane_base + acc * 256 + b * BN + ch * HALF_COLS + c * 32, v);
-        if (MODE == 0) {
-          const float4* xp = reinterpret_cast<const float4*>(a.xn + n0 + c * 32);
+      // The warp's whole column half: 64 accumulators per thread, one wait.
+      float v[HALF_COLS];
+      tmem_ld64(tmem + lane_base + acc * 256 + b * BN + ch * HALF_COLS, v);
+      if (MODE == 0) {
+        const float4* xp = reinterpret_cast<const float4*>(a.xn + n0);
 #pragma unroll
-          for (int j4 = 0; j4 < 8; j4++) {
-            const float4 x4 = __ldg(xp + j4);
-            v[4 * j4 + 0] = fmaf(f2, v[4 * j4 + 0], x4.x);
-            v[4 * j4 + 1] = fmaf(f2, v[4 * j4 + 1], x4.y);
-            v[4 * j4 + 2] = fmaf(f2, v[4 * j4 + 2], x4.z);
-            v[4 * j4 + 3] = fmaf(f2, v[4 * j4 + 3], x4.w);
-          }
+        for (int j4 = 0; j4 < HALF_COLS / 4; j4++) {
+          // Four loads in flight at a time keep the register count under
+          // the 96 that 18 warps per SM allow.
+          if (j4 % 4 == 0) asm volatile("" ::: "memory");
+          const float4 x4 = __ldg(xp + j4);
+          v[4 * j4 + 0] = fmaf(f2, v[4 * j4 + 0], x4.x);
+          v[4 * j4 + 1] = fmaf(f2, v[4 * j4 + 1], x4.y);
+          v[4 * j4 + 2] = fmaf(f2, v[4 * j4 + 2], x4.z);
+          v[4 * j4 + 3] = fmaf(f2, v[4 * j4 + 3], x4.w);
         }
-        const int cb = valid_cols - c * 32;
-        if (cb < 32) {
-          // Columns past the segment end: the worst key for the pivot
-          // minima; NaN for the append path, which fails every comparison
-          // (min/max ignore a NaN operand) even when the bound is infinite.
-          const float pad = TILEMIN ? (MODE == 0 ? INFINITY : -INFINITY) : __int_as_float(0x7fffffff);
+      }
+      if (valid_cols < HALF_COLS) {
+        // Columns past the segment end (the segment's last tile only): the
+        // worst key for the pivot minima; NaN for the append path, which
+        // fails every comparison (min/max ignore a NaN operand) even when
+        // the bound is infinite.
+        const float pad = TILEMIN ? (MODE == 0 ? INFINITY : -INFINITY) : __int_as_float(0x7fffffff);
 #pragma unroll
-          for (int j = 0; j < 32; j++)
-            if (j >= cb) v[j] = pad;
-        }
-        // Best key of each group of 4 columns.
-        float g[8];
+        for (int j = 0; j < HALF_COLS; j++)
+          if (j >= valid_cols) v[j] = pad;
+      }
+      // Best key of each group of 8 columns, then of the half: 36 three-input
+      // min/max for 64 keys. The per-group tests run only in lanes whose
+      // half passes.
+      float g[8];
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-          g[i] = MODE == 0 ? fmin3(v[4 * i], v[4 * i + 1], fminf(v[4 * i + 2], v[4 * i + 3]))
-                           : fmax3(v[4 * i], v[4 * i + 1], fmaxf(v[4 * i + 2], v[4 * i + 3]));
-        if (TILEMIN) {
-          tile_best = MODE == 0 ? fmin3(fmin3(tile_best, g[0], g[1]), fmin3(g[2], g[3], g[4]), fmin3(g[5], g[6], g[7]))
-                                : fmax3(fmax3(tile_best, g[0], g[1]), fmax3(g[2], g[3], g[4]), fmax3(g[5], g[6], g[7]));
-          continue;
-        }
-        unsigned m = 0;
+      for (int i = 0; i < 8; i++) {
+        const float* w = v + 8 * i;
+        g[i] = MODE == 0 ? fmin3(fmin3(w[0], w[1], w[2]), fmin3(w[3], w[4], w[5]), fminf(w[6], w[7]))
+                         : fmax3(fmax3(w[0], w[1], w[2]), fmax3(w[3], w[4], w[5]), fmaxf(w[6], w[7]));
+      }
+      const float best = MODE == 0 ? fmin3(fmin3(g[0], g[1], g[2]), fmin3(g[3], g[4], g[5]), fminf(g[6], g[7]))
+                                   : fmax3(fmax3(g[0], g[1], g[2]), fmax3(g[3], g[4], g[5]), fmaxf(g[6], g[7]));
+      if (!TILEMIN && (MODE == 0 ? best <= thr : best >= thr)) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) m |= (MODE == 0 ? g[i] <= thr : g[i] >= thr) ? (1u << i) : 0u;
-        // One vote per chunk; most chunks have no passing group in any lane.
-        if (__any_sync(sel::kFull, m != 0)) {
+        for (int i = 0; i < 8; i++) {
+          if (MODE == 0 ? g[i] <= thr : g[i] >= thr) {
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
-            if ((m >> i) & 1u) {
-#pragma unroll
-              for (int jj = 0; jj < 4; jj++) {
-                const float sc = MODE == 0 ? v[4 * i + jj] : MODE == 1 ? -inv_ks * v[4 * i + jj] : f2 * v[4 * i + jj];
-                if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + c * 32 + 4 * i + jj)};
-              }
+            for (int jj = 0; jj < 8; jj++) {
+              const float sc = MODE == 0 ? v[8 * i + jj] : MODE == 1 ? -inv_ks * v[8 * i + jj] : f2 * v[8 * i + jj];
+              if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + 8 * i + jj)};
             }
           }
         }
@@ -307,7 +305,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (TILEMIN) {
         if (vq)
           a.tmin[(int64_t)q * a.tmin_stride + (row_begin / BN + t) * 2 + ch] =
-              MODE == 0 ? tile_best : MODE == 1 ? -inv_ks * tile_best : f2 * tile_best;
+              MODE == 0 ? best : MODE == 1 ? -inv_ks * best : f2 * best;
         continue;
       }
       // Shrink lists that could overflow on the next tile.
@@ -347,7 +345,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ------------------------------------------------------------------ prep
-// Base rows -> bf16 operand rows (cosine: unit-normalised), |x|^2 for the L2
+// Base rows -> fp16 operand rows (cosine: unit-normalised), |x|^2 for the L2
 // epilogue, max |x| for the margins, and the list of near-zero cosine rows.
 // One 2-byte tensor-core operand: fp16 for cosine, bf16 otherwise.
 __device__ __forceinline__ uint16_t to_operand(float v, bool f16) {
@@ -394,7 +392,7 @@ __global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int 
   atomicMax(xmax_bits, __float_as_uint((float)sqrt(ss)));
 }
 
-// Queries -> bf16 operand rows and per-query acceptance margins (heap-score
+// Queries -> fp16 operand rows and per-query acceptance margins (heap-score
 // units). Near-zero cosine queries are routed to the exact fallback.
 __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d, int dp, int d16,
                                      int metric, const unsigned int* __restrict__ xmax_bits, float xscale,
@@ -553,7 +551,7 @@ __global__ void __launch_bounds__(256) tc_pivot_topk_kernel(const float* __restr
   for (int j = s_pos + threadIdx.x; j < k; j += blockDim.x) dst[j] = kv;
 }
 
-// Gathers every `stride`-th bf16 operand row (and |x|^2) into the pivot set.
+// Gathers every `stride`-th operand row (and |x|^2) into the pivot set.
 __global__ void tc_pivot_gather_kernel(const uint16_t* __restrict__ xb, const float* __restrict__ xn,
                                        int64_t m, int64_t stride, int d16,
                                        uint16_t* __restrict__ pb, float* __restrict__ pn) {
@@ -577,7 +575,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// bf16 [rows][d16] row-major, box 64 x 128, 128-byte swizzle, zero OOB fill.
+// 16-bit [rows][d16] row-major, box 64 x 128, 128-byte swizzle, zero OOB fill.
 int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16, bool f16) {
   auto fn = encode_fn();
   if (!fn) {

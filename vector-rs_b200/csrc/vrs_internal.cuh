@@ -128,6 +128,11 @@ struct KnnSelectArgs {
   const uint32_t* tiny;  // rows always re-ranked exactly (cosine near-zero rows)
   int n_tiny;
   int retry;             // block select: only the slots the warp select flagged (2)
+  // Starting acceptance bound of the scan per slot when it was not proven to
+  // cover k rows (null otherwise). The select then checks that the scan kept
+  // at least k rows and that the k-th best kept score plus the margin stays
+  // within it; a slot that fails goes to the exact fallback (overflow 1).
+  const float* init_bound;
 };
 
 // Launchers (knn_kernels.cu).

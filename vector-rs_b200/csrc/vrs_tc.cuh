@@ -77,6 +77,22 @@ int tc_tau(const float* vals, int nparts, int64_t part_stride, int len, int nq, 
 // The k smallest of each query's ntile pivot minima (query-major rows) into
 // out[q * k + j], padded with +inf when there are fewer than k.
 int tc_pivot_topk(const float* tmin, int ntile, int nq, int k, float* out, cudaStream_t s);
+// Rank of the pivot minimum that seeds an unproven starting bound (one
+// shard, pivot set = every stride-th row, so a row is a pivot row with
+// probability p = 1/stride). Below the j-th pivot minimum lie about j/p base
+// rows, with standard deviation sqrt(j (1 - p))/p; j is the smallest rank
+// whose count stays at k or more 4.5 standard deviations below the mean. The
+// select verifies the bound per query (k rows kept, k-th kept score plus
+// margin within it) and sends a query that fails to the exact fallback. Never
+// above k, where the bound is proven.
+inline int tc_optimistic_rank(int k, int64_t stride) {
+  if (stride <= 1) return k;
+  const double p = 1.0 / (double)stride, z = 4.5;
+  for (int j = 1; j < k; j++)
+    if (j - z * std::sqrt(j * (1.0 - p)) >= k * p) return j;
+  return k;
+}
+
 // Rows in the pivot set (every stride-th row) of a shard of n rows when
 // `parts` shards share one base and pool their pivot minima: the pooled
 // pivot set is about 1/6 of the base and at least 65,536 rows; beyond
