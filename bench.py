@@ -386,8 +386,10 @@ def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, m
 
     for _ in range(max(1, args.warmup // 2)):
         step_host()
-    barrier()
     with ClockSampler(local) as clk2:
+        # Ranks meet after their samplers start, so no rank's first
+        # collective waits out another rank's sampler start-up.
+        barrier()
         ev0.record(stream)
         for _ in range(args.steps):
             step_host()
@@ -399,8 +401,8 @@ def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, m
     # ------------------------------------------------------------ roofline
     n_loc = r1 - r0
     per_launch_ms = scan_ms / max(scan_n, 1)
-    breakdown = {"pivot": piv_ms / max(piv_n, 1), "scan": per_launch_ms,
-                 "select": sel_ms / max(sel_n, 1), "merge": merge_ms / max(merge_n, 1),
+    breakdown = {"pivot": piv_ms / args.steps, "scan": scan_ms / args.steps,
+                 "select": sel_ms / args.steps, "merge": merge_ms / args.steps,
                  # exact re-search of queries whose scan bound failed verification
                  "fallback": fb_ms / args.steps, "fallback_launches": fb_n}
     if metric in TC_METRICS and D <= 128:

@@ -196,3 +196,29 @@ def test_cosine_fp16_tiny_norms(vc, orc, gpu):
     dg, ig = eng.search_arrays(qs, 20)
     do, io = orc.knn_search(base, qs, 20, COS)
     _assert_parity(COS, dg, ig, do, io)
+
+
+def test_unproven_bound_fallback(vc, orc, gpu):
+    """A single shard's starting bound comes from a low rank of the pivot
+    minima (pivot rows: every 6th row at this size) and the select verifies
+    it per query. Near rows placed only on pivot rows, fewer than k of them,
+    make that bound cut true neighbours: the select must flag the queries and
+    the exact fallback must return the oracle's answer."""
+    n, d, k = 396_000, 32, 100
+    rng = np.random.default_rng(11)
+    qs = rng.standard_normal((3, d)).astype(np.float32)
+    base = (rng.standard_normal((n, d)) * 3 + 20).astype(np.float32)
+    for i in range(3):
+        near = 384 * (i * 60 + np.arange(60))            # pivot rows, one per pivot tile half
+        base[near] = qs[i] + 0.05 * rng.standard_normal((60, d)).astype(np.float32)
+        mid = 6 * (20_000 + i * 300 + np.arange(200)) + 1  # rows outside the pivot set
+        base[mid] = qs[i] + 0.5 * rng.standard_normal((200, d)).astype(np.float32)
+    eng = _engine(vc, base, L2)
+    vc.profile_reset()
+    vc.profile_enable(True)
+    dg, ig = eng.search_arrays(qs, k)
+    vc.profile_enable(False)
+    _, n_fb = vc.profile_read("knn_fallback")
+    do, io = orc.knn_search(base, qs, k, L2)
+    _assert_parity(L2, dg, ig, do, io)
+    assert n_fb > 0

@@ -51,6 +51,37 @@ static int fail(int st, const std::string& m) {
       return ::vrs::fail(VRS_ERR_NCCL, std::string(#call) + ": " + ncclGetErrorString(_r)); \
   } while (0)
 
+// Pinned host staging (portable across the handle's devices), grown on demand.
+struct HBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  HBuf() = default;
+  HBuf(const HBuf&) = delete;
+  HBuf& operator=(const HBuf&) = delete;
+  ~HBuf() { release(); }
+  int reserve(size_t bytes) {
+    if (bytes <= cap && p) return VRS_OK;
+    release();
+    bytes = std::max<size_t>(bytes, 256);
+    cudaError_t e = cudaHostAlloc(&p, bytes, cudaHostAllocPortable);
+    if (e != cudaSuccess) {
+      p = nullptr;
+      return fail(cuda_status(e), "cudaHostAlloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    }
+    cap = bytes;
+    return VRS_OK;
+  }
+  void release() {
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+  }
+  template <class T>
+  T* as() const {
+    return reinterpret_cast<T*>(p);
+  }
+};
+
 // Growable device buffer bound to one device.
 struct DBuf {
   void* p = nullptr;
@@ -199,6 +230,8 @@ struct KnnShard {
   // per-search scratch
   DBuf q_in, q, q_aux, cand, cnt, overflow, pairs, gathered, out_dist, out_id;
   DBuf qb, absm, err, qindex;
+  DBuf mflags;                  // [nq] queries whose merged top-k' holds a sentinel
+  HBuf hstat;                   // pinned: [nq] flags, then the scan's error word
   int last_nq = 0, last_kk = 0, last_nseg = 0, last_cap = 0;
 };
 
@@ -223,8 +256,9 @@ struct vrs_knn {
       for (DBuf* b : {&s->base, &s->base_aux, &s->q_in, &s->q, &s->q_aux, &s->cand, &s->cnt,
                       &s->overflow, &s->pairs, &s->gathered, &s->out_dist, &s->out_id, &s->xb,
                       &s->xn, &s->xmax, &s->tiny, &s->ntiny, &s->qb, &s->absm, &s->err, &s->qindex, &s->pb,
-                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all, &s->qscale})
+                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all, &s->qscale, &s->mflags})
         b->release();
+      s->hstat.release();
       if (s->own_stream) cudaStreamDestroy(s->own_stream);
     }
     for (ncclComm_t c : clique) ncclCommDestroy(c);
@@ -420,9 +454,11 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   const int nq_alloc = (nq + 255) / 256 * 256;
   tc::TcPlan p = tc::tc_plan(s->n_local, nq, kk, s->num_sms);
   const int nlists = 2 * p.nseg;
-  // A single shard's bound comes from a lower pivot rank and is verified by
-  // the select; pooled bounds stay proven (rank k).
-  const int tau_rank = phase == kPhaseAll ? tc::tc_optimistic_rank(kk, s->pivot_stride) : kk;
+  // The starting bound comes from a pivot rank below k (tc_optimistic_rank)
+  // and is checked by the select: a single shard's failures are flagged for
+  // the exact re-search; merge pairs carry a sentinel instead and the merge
+  // decides (a pooled bound is global, so no shard can check it alone).
+  const int tau_rank = tc::tc_optimistic_rank(kk, s->pivot_stride);
   if (phase == kPhaseMain) goto main_phase;
   VRS_TRY(s->qb.reserve((size_t)nq_alloc * d16 * 2));
   VRS_TRY(s->absm.reserve((size_t)nq * sizeof(float)));
@@ -462,7 +498,7 @@ main_phase:
     // Bound from every shard's k smallest pivot minima (ptop_all, gathered).
     const int parts = h->rank_mode ? h->comm->nranks : h->g;
     ProfToken t0 = prof_begin("knn_pivot", st);
-    VRS_TRY(tc::tc_tau(s->ptop_all.as<float>(), parts, (int64_t)nq * kk, kk, nq, kk, s->absm.as<float>(),
+    VRS_TRY(tc::tc_tau(s->ptop_all.as<float>(), parts, (int64_t)nq * kk, kk, nq, tau_rank, s->absm.as<float>(),
                        s->ibound.as<float>(), st));
     prof_end(t0, st);
   }
@@ -504,6 +540,7 @@ main_phase:
   sa.tiny = s->tiny.as<uint32_t>();
   sa.n_tiny = h->metric == vrs_exact::kCos ? s->n_tiny : 0;
   sa.init_bound = tau_rank < kk ? s->ibound.as<float>() : nullptr;
+  sa.certify = out_pairs != nullptr;
   ProfToken t = prof_begin("knn_select", st);
   if (nlists <= 32 && kk <= 256 && sa.n_tiny <= 256) {
     VRS_TRY(launch_knn_select_warp(sa, st));
@@ -712,6 +749,104 @@ int64_t query_batch(int kk) {
   return 16384;
 }
 
+// Row-sharded merge: slots a shard flagged become sentinel pairs, every
+// shard's pairs are all-gathered, and the merge (GPU 0 of a clique, every
+// rank in rank mode, so every rank sees the same flags) marks the queries
+// whose top-k' holds a sentinel.
+int sharded_merge(vrs_knn* h, int nb, int kk, double tmo) {
+  const int G = (int)h->shards.size();
+  const int nranks = h->rank_mode ? h->comm->nranks : G;
+  for (int r = 0; r < G; r++) {
+    KnnShard* s = h->shards[r].get();
+    VRS_CUDA(cudaSetDevice(s->device));
+    VRS_TRY(launch_flag_pairs(s->overflow.as<int>(), nb, kk, s->pairs.as<Cand>(), s->stream));
+  }
+  VRS_NCCL(ncclGroupStart());
+  for (int r = 0; r < G; r++) {
+    KnnShard* s = h->shards[r].get();
+    VRS_NCCL(ncclAllGather(s->pairs.p, s->gathered.p, (size_t)nb * kk, ncclUint64, s->comm, s->stream));
+  }
+  VRS_NCCL(ncclGroupEnd());
+  for (int r = 0; r < G; r++) VRS_TRY(nccl_ready(h->shards[r]->comm, tmo));
+  KnnShard* s0 = h->shards[0].get();
+  VRS_CUDA(cudaSetDevice(s0->device));
+  VRS_TRY(s0->mflags.reserve((size_t)nb * sizeof(int)));
+  VRS_CUDA(cudaMemsetAsync(s0->mflags.p, 0, (size_t)nb * sizeof(int), s0->stream));
+  ProfToken t = prof_begin("knn_merge", s0->stream);
+  VRS_TRY(launch_merge_pairs(s0->gathered.as<Cand>(), nranks, nb, kk, h->metric, s0->out_dist.as<float>(),
+                             s0->out_id.as<uint32_t>(), s0->mflags.as<int>(), s0->stream));
+  prof_end(t, s0->stream);
+  return VRS_OK;
+}
+
+// After every shard's search is enqueued: merge (row shards), then results,
+// per-query flags and the scans' error words leave the devices behind one
+// bounded wait per shard. Flagged queries (a list overflowed, a bound failed
+// its check, a near-zero cosine query) are searched again with the exact
+// scan on every shard and merged again; that second pass must come out
+// clean. No host round trip sits between the scan and the merge.
+int sharded_finish(vrs_knn* h, int nb, int kk, float* odst, uint32_t* oid, cudaMemcpyKind d2h, double tmo) {
+  const int G = (int)h->shards.size();
+  const int nranks = h->rank_mode ? h->comm->nranks : G;
+  KnnShard* s0 = h->shards[0].get();
+  for (int pass = 0; pass < 2; pass++) {
+    if (nranks > 1) VRS_TRY(sharded_merge(h, nb, kk, tmo));
+    for (int r = 0; r < G; r++) {
+      KnnShard* s = h->shards[r].get();
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_TRY(s->hstat.reserve((size_t)(nb + 1) * sizeof(int)));
+      int* hs = s->hstat.as<int>();
+      hs[nb] = 0;
+      if (s->use_tc && s->last_nq > 0)
+        VRS_CUDA(cudaMemcpyAsync(hs + nb, s->err.p, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+      if (r == 0) {
+        const int* dflags = nranks > 1 ? s0->mflags.as<int>() : s0->overflow.as<int>();
+        VRS_CUDA(cudaMemcpyAsync(hs, dflags, (size_t)nb * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+        VRS_CUDA(cudaMemcpyAsync(odst, s0->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s->stream));
+        VRS_CUDA(cudaMemcpyAsync(oid, s0->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s->stream));
+      }
+    }
+    for (int r = 0; r < G; r++) {
+      KnnShard* s = h->shards[r].get();
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_TRY(stream_wait(s->stream, nranks > 1 ? s->comm : nullptr, tmo));
+    }
+    for (int r = 0; r < G; r++) {
+      const int e = h->shards[r]->hstat.as<int>()[nb];
+      if (e) return fail(VRS_ERR_TIMEOUT, "tensor-core scan gave up waiting (stage code " + std::to_string(e) + ")");
+    }
+    std::vector<int> idx;
+    const int* hf = s0->hstat.as<int>();
+    for (int i = 0; i < nb; i++)
+      if (hf[i]) idx.push_back(i);
+    if (idx.empty()) return VRS_OK;
+    if (pass == 1)
+      return fail(VRS_ERR_DRIVER, "exact re-search left query " + std::to_string(idx[0]) + " unresolved");
+    // Exact re-search of the flagged queries on every shard; results land in
+    // their rows (final results for one shard, merge pairs otherwise).
+    const int nf = (int)idx.size();
+    for (int r = 0; r < G; r++) {
+      KnnShard* s = h->shards[r].get();
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_TRY(s->qindex.reserve((size_t)nf * sizeof(int)));
+      VRS_CUDA(cudaMemcpyAsync(s->qindex.p, idx.data(), (size_t)nf * sizeof(int), cudaMemcpyHostToDevice,
+                               s->stream));
+      int* ovf = s->overflow.as<int>();
+      VRS_CUDA(cudaMemsetAsync(ovf, 0, (size_t)(nb + nf) * sizeof(int), s->stream));
+      if (nranks == 1)
+        VRS_TRY(launch_exact_search(h, s, nf, kk, s->qindex.as<int>(), ovf + nb, s->out_dist.as<float>(),
+                                    s->out_id.as<uint32_t>(), nullptr, true));
+      else
+        VRS_TRY(launch_exact_search(h, s, nf, kk, s->qindex.as<int>(), ovf + nb, nullptr, nullptr,
+                                    s->pairs.as<Cand>(), true));
+      // The exact scan's own overflow flags (per flagged slot) feed the
+      // second pass through the query rows they name.
+      VRS_TRY(launch_scatter_flags(ovf + nb, s->qindex.as<int>(), nf, ovf, s->stream));
+    }
+  }
+  return VRS_OK;
+}
+
 int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, float* out_dist,
                     uint32_t* out_id, int32_t* out_k, int mem) {
   if (!h || !out_k) return fail(VRS_ERR_INVALID_CONFIG, "null handle or out_k");
@@ -777,42 +912,7 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
           VRS_TRY(shard_search_launch(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>(), kPhaseMain));
         }
       }
-      for (int r = 0; r < G; r++) {
-        KnnShard* s = h->shards[r].get();
-        VRS_CUDA(cudaSetDevice(s->device));
-        if (nranks == 1)
-          VRS_TRY(shard_search_finish(h, s, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr, tmo));
-        else
-          VRS_TRY(shard_search_finish(h, s, nullptr, nullptr, s->pairs.as<Cand>(), tmo));
-      }
-      if (nranks > 1) {
-        VRS_NCCL(ncclGroupStart());
-        for (int r = 0; r < G; r++) {
-          KnnShard* s = h->shards[r].get();
-          VRS_NCCL(ncclAllGather(s->pairs.p, s->gathered.p, (size_t)nb * kk, ncclUint64, s->comm,
-                                 s->stream));
-        }
-        VRS_NCCL(ncclGroupEnd());
-        for (int r = 0; r < G; r++) VRS_TRY(nccl_ready(h->shards[r]->comm, tmo));
-        // Rank mode: every rank merges. Clique: GPU 0 merges.
-        KnnShard* s0 = h->shards[0].get();
-        VRS_CUDA(cudaSetDevice(s0->device));
-        ProfToken t = prof_begin("knn_merge", s0->stream);
-        VRS_TRY(launch_merge_pairs(s0->gathered.as<Cand>(), nranks, nb, kk, h->metric,
-                                   s0->out_dist.as<float>(), s0->out_id.as<uint32_t>(), s0->stream));
-        prof_end(t, s0->stream);
-      }
-      // Results leave shard 0 behind the merge; one bounded wait per shard
-      // covers the collective and the copies.
-      KnnShard* s0 = h->shards[0].get();
-      VRS_CUDA(cudaSetDevice(s0->device));
-      VRS_CUDA(cudaMemcpyAsync(odst, s0->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s0->stream));
-      VRS_CUDA(cudaMemcpyAsync(oid, s0->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s0->stream));
-      for (int r = 0; r < G; r++) {
-        KnnShard* s = h->shards[r].get();
-        VRS_CUDA(cudaSetDevice(s->device));
-        VRS_TRY(stream_wait(s->stream, nranks > 1 ? s->comm : nullptr, tmo));
-      }
+      VRS_TRY(sharded_finish(h, nb, kk, odst, oid, d2h, tmo));
     } else {
       // Replicated: query chunks of ceil(nb / ranks) (distributed_knn.rs:201-229).
       const int chunk = (nb + nranks - 1) / nranks;

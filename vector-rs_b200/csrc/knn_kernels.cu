@@ -155,20 +155,28 @@ __device__ void select_one(const KnnSelectArgs& a, int slot, Cand* sbuf, int* s_
   // k-th best scan score over all segments -> acceptance bound -> survivors.
   int R = total;
   const float sb = a.init_bound ? a.init_bound[slot] : INFINITY;
+  bool cut = false;  // unverified bound, merge pairs cut at `lim`
   if (total > a.k || (total == a.k && sb < INFINITY)) {
     uint32_t kth = block_select(sbuf, total, a.k, s_hist, s_res);
     float tau = ord_inv(kth);
     float absm = a.kind == kAbsMargin ? a.absm[qrow] : 0.0f;
     float b = accept_bound(a.kind, tau, a.rho, absm);
     if (!(b <= sb)) {
-      if (tid == 0) a.overflow[slot] = 1;
-      return;
+      if (!a.certify) {
+        if (tid == 0) a.overflow[slot] = 1;
+        return;
+      }
+      cut = true;  // b > sb keeps every stored row
     }
     R = block_filter(sbuf, total, KeepBound{b}, s_wt);
   } else if (total < a.k && sb < INFINITY) {
-    if (tid == 0) a.overflow[slot] = 1;
-    return;
+    if (!a.certify) {
+      if (tid == 0) a.overflow[slot] = 1;
+      return;
+    }
+    cut = true;
   }
+  const float lim = cut ? __fsub_rd(sb, 0.5f * a.absm[qrow]) : INFINITY;
   // Exact re-rank of approximate survivors in the reference's order.
   if (a.kind != kExactScores) {
     const float* qp = a.q + (int64_t)qrow * a.dp;
@@ -210,6 +218,12 @@ __device__ void select_one(const KnnSelectArgs& a, int slot, Cand* sbuf, int* s_
   for (int r = tid; r < a.k; r += blockDim.x) {
     Cand e = r < R ? sbuf[r] : Cand{INFINITY, 0xffffffffu};
     uint32_t gid = e.id == 0xffffffffu ? 0xffffffffu : e.id + a.id_offset;
+    if (cut && !(e.hs < lim)) {
+      // Sorted: rows below lim form a prefix; the sentinel follows it.
+      const bool first = r == 0 || (r - 1 < R && sbuf[r - 1].hs < lim);
+      e = first ? Cand{lim, kSentinelId} : Cand{INFINITY, 0xffffffffu};
+      gid = e.id;
+    }
     if (a.out_pairs) a.out_pairs[(int64_t)qrow * a.k + r] = Cand{e.hs, gid};
     if (a.out_dist) {
       float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
@@ -288,9 +302,14 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
 
   float bound = INFINITY;
   const float sb = a.init_bound ? a.init_bound[slot] : INFINITY;
+  bool cut = false;  // unverified bound, merge pairs cut at `lim`
   if (total < a.k && sb < INFINITY) {
-    if (lane == 0) a.overflow[slot] = 1;  // fewer than k rows within an unproven bound
-    return;
+    // Fewer than k rows within an unproven bound.
+    if (!a.certify) {
+      if (lane == 0) a.overflow[slot] = 1;
+      return;
+    }
+    cut = true;
   }
   if (total > a.k || (total == a.k && sb < INFINITY)) {
     uint32_t prefix = 0, pmask = 0;
@@ -341,10 +360,16 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
     const float absm = a.kind == kAbsMargin ? a.absm[qrow] : 0.0f;
     bound = accept_bound(a.kind, ord_inv(prefix), a.rho, absm);
     if (!(bound <= sb)) {
-      if (lane == 0) a.overflow[slot] = 1;  // the scan's bound may have cut a top-k row
-      return;
+      // The scan's bound may have cut a top-k row (bound > sb keeps every
+      // stored row).
+      if (!a.certify) {
+        if (lane == 0) a.overflow[slot] = 1;
+        return;
+      }
+      cut = true;
     }
   }
+  const float lim = cut ? __fsub_rd(sb, 0.5f * a.absm[qrow]) : INFINITY;
   // Survivors -> shared memory (batched reads of the flattened lists).
   int R = 0;
   for (int j0 = 0; j0 < total; j0 += 32 * kBatch) {
@@ -412,8 +437,14 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
     }
   }
   for (int r = lane; r < a.k; r += 32) {
-    const Cand e = r < RT ? buf[r] : Cand{INFINITY, 0xffffffffu};
-    const uint32_t gid = e.id == 0xffffffffu ? 0xffffffffu : e.id + a.id_offset;
+    Cand e = r < RT ? buf[r] : Cand{INFINITY, 0xffffffffu};
+    uint32_t gid = e.id == 0xffffffffu ? 0xffffffffu : e.id + a.id_offset;
+    if (cut && !(e.hs < lim)) {
+      // Sorted: rows below lim form a prefix; the sentinel follows it.
+      const bool first = r == 0 || (r - 1 < RT && buf[r - 1].hs < lim);
+      e = first ? Cand{lim, kSentinelId} : Cand{INFINITY, 0xffffffffu};
+      gid = e.id;
+    }
     if (a.out_pairs) a.out_pairs[(int64_t)qrow * a.k + r] = Cand{e.hs, gid};
     if (a.out_dist) {
       const float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
@@ -426,7 +457,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
 // --------------------------------------------------------------- merge
 template <int METRIC>
 __global__ void __launch_bounds__(256) merge_pairs_kernel(const Cand* g, int nlists, int nq, int k,
-                                                           float* out_dist, uint32_t* out_id) {
+                                                           float* out_dist, uint32_t* out_id, int* flags) {
   extern __shared__ Cand sbuf[];
   const int q = blockIdx.x;
   const int T = nlists * k;
@@ -444,6 +475,7 @@ __global__ void __launch_bounds__(256) merge_pairs_kernel(const Cand* g, int nli
   block_bitonic_sort(sbuf, P);
   for (int r = threadIdx.x; r < k; r += blockDim.x) {
     Cand e = sbuf[r];
+    if (flags && e.id == kSentinelId) flags[q] = 1;
     float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
     out_dist[(int64_t)q * k + r] = e.id == 0xffffffffu ? NAN : vrs_exact::finish(METRIC, key);
     out_id[(int64_t)q * k + r] = e.id;
@@ -458,7 +490,7 @@ __global__ void __launch_bounds__(256) merge_pairs_kernel(const Cand* g, int nli
 // exactly k' elements land below k'. No sort.
 template <int METRIC>
 __global__ void __launch_bounds__(256) merge_sorted_kernel(const Cand* g, int nlists, int nq, int k,
-                                                           float* out_dist, uint32_t* out_id) {
+                                                           float* out_dist, uint32_t* out_id, int* flags) {
   extern __shared__ Cand sl[];  // [nlists][k]
   const int q = blockIdx.x;
   const int T = nlists * k;
@@ -485,11 +517,25 @@ __global__ void __launch_bounds__(256) merge_sorted_kernel(const Cand* g, int nl
       rank += lo;
     }
     if (rank < k) {
+      if (flags && e.id == kSentinelId) flags[q] = 1;
       const float key = vrs_exact::higher_is_better(METRIC) ? -e.hs : e.hs;
       out_dist[(int64_t)q * k + rank] = e.id == 0xffffffffu ? NAN : vrs_exact::finish(METRIC, key);
       out_id[(int64_t)q * k + rank] = e.id;
     }
   }
+}
+
+__global__ void flag_pairs_kernel(const int* __restrict__ overflow, int nq, int k, Cand* __restrict__ pairs) {
+  const int q = blockIdx.x;
+  if (q >= nq || !overflow[q]) return;
+  for (int r = threadIdx.x; r < k; r += blockDim.x)
+    pairs[(int64_t)q * k + r] = r == 0 ? Cand{-INFINITY, kSentinelId} : Cand{INFINITY, 0xffffffffu};
+}
+
+__global__ void scatter_flags_kernel(const int* __restrict__ src, const int* __restrict__ idx, int n,
+                                     int* __restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[idx[i]] = src[i];
 }
 
 template <int METRIC>
@@ -585,11 +631,11 @@ struct SelectWarpL {
 
 template <int M>
 struct MergeL {
-  static int run(const Cand* g, int nlists, int nq, int k, float* od, uint32_t* oi, cudaStream_t s) {
+  static int run(const Cand* g, int nlists, int nq, int k, float* od, uint32_t* oi, int* flags, cudaStream_t s) {
     const size_t lsm = (size_t)nlists * k * sizeof(Cand);
     if (lsm <= 200 * 1024) {
       VRS_CUDA(cudaFuncSetAttribute(merge_sorted_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsm));
-      merge_sorted_kernel<M><<<nq, 256, lsm, s>>>(g, nlists, nq, k, od, oi);
+      merge_sorted_kernel<M><<<nq, 256, lsm, s>>>(g, nlists, nq, k, od, oi, flags);
       VRS_CUDA(cudaGetLastError());
       count_launch();
       return VRS_OK;
@@ -599,7 +645,7 @@ struct MergeL {
     size_t smem = (size_t)P * sizeof(Cand);
     VRS_CUDA(cudaFuncSetAttribute(merge_pairs_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem));
-    merge_pairs_kernel<M><<<nq, 256, smem, s>>>(g, nlists, nq, k, od, oi);
+    merge_pairs_kernel<M><<<nq, 256, smem, s>>>(g, nlists, nq, k, od, oi, flags);
     VRS_CUDA(cudaGetLastError());
     count_launch();
     return VRS_OK;
@@ -635,9 +681,25 @@ int launch_knn_select_warp(const KnnSelectArgs& a, cudaStream_t s) {
 }
 
 int launch_merge_pairs(const Cand* gathered, int nlists, int nq, int k, int metric, float* out_dist,
-                       uint32_t* out_id, cudaStream_t s) {
+                       uint32_t* out_id, int* flags, cudaStream_t s) {
   if (nq == 0 || k == 0) return VRS_OK;
-  return dispatch_metric<MergeL>(metric, gathered, nlists, nq, k, out_dist, out_id, s);
+  return dispatch_metric<MergeL>(metric, gathered, nlists, nq, k, out_dist, out_id, flags, s);
+}
+
+int launch_scatter_flags(const int* src, const int* idx, int n, int* dst, cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  scatter_flags_kernel<<<(n + 255) / 256, 256, 0, s>>>(src, idx, n, dst);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
+
+int launch_flag_pairs(const int* overflow, int nq, int k, Cand* pairs, cudaStream_t s) {
+  if (nq == 0 || k == 0) return VRS_OK;
+  flag_pairs_kernel<<<nq, 128, 0, s>>>(overflow, nq, k, pairs);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
 }
 
 int launch_finish_pairs(const Cand* pairs, int64_t count, int metric, float* out_dist,

@@ -51,6 +51,11 @@ struct Cand {
   uint32_t id;
 };
 
+// Merge-pair id that marks "rows of this shard at or beyond this score may
+// be missing" (ids are below 2^32 - 2; 0xffffffff is padding). A query whose
+// merged top-k' holds one is searched again exactly.
+constexpr uint32_t kSentinelId = 0xfffffffeu;
+
 // Monotone map float -> uint32 (total order of non-NaN floats).
 __host__ __device__ __forceinline__ uint32_t ord_key(float f) {
   uint32_t u;
@@ -133,6 +138,11 @@ struct KnnSelectArgs {
   // at least k rows and that the k-th best kept score plus the margin stays
   // within it; a slot that fails goes to the exact fallback (overflow 1).
   const float* init_bound;
+  // With init_bound and merge pairs: a slot whose bound fails the check is
+  // not flagged; its pairs keep the rows scored below init_bound - absm / 2
+  // (no unkept row of this shard can score below that) followed by a
+  // kSentinelId pair at that score, and the merge decides.
+  int certify;
 };
 
 // Launchers (knn_kernels.cu).
@@ -141,8 +151,15 @@ int launch_knn_select(const KnnSelectArgs& a, cudaStream_t s);
 // Warp-per-query select with half-warp exact re-rank (approximate scans of
 // L2 / Mahalanobis / dot / cosine; nseg <= 32, k <= 512).
 int launch_knn_select_warp(const KnnSelectArgs& a, cudaStream_t s);
+// flags (nullable, [nq]) is set to 1 for queries whose merged top-k' holds
+// a kSentinelId pair.
 int launch_merge_pairs(const Cand* gathered, int nlists, int nq, int k, int metric,
-                       float* out_dist, uint32_t* out_id, cudaStream_t s);
+                       float* out_dist, uint32_t* out_id, int* flags, cudaStream_t s);
+// Slots with overflow != 0 get pairs (-inf, kSentinelId), then padding, so
+// that the merge flags them.
+int launch_flag_pairs(const int* overflow, int nq, int k, Cand* pairs, cudaStream_t s);
+// dst[idx[i]] = src[i] for i < n.
+int launch_scatter_flags(const int* src, const int* idx, int n, int* dst, cudaStream_t s);
 int launch_pad_rows(const float* src, int64_t rows, int d, int dp, float* dst, int transform,
                     cudaStream_t s);
 int launch_cos_norms(const float* x, int64_t rows, int d, int dp, float* out, cudaStream_t s);
