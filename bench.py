@@ -351,8 +351,7 @@ def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, m
     for _ in range(args.warmup):
         step_dev()
     barrier()
-    vc.profile_reset()
-    vc.profile_enable(True)
+    vc.profile_reset()  # the launch counter covers the timed steps
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
@@ -361,14 +360,24 @@ def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, m
             step_dev()
         ev1.record(stream)
         barrier()
-    vc.profile_enable(False)
     ms = max_over_ranks(ev0.elapsed_time(ev1))
+    launches = vc.profile_read("*")[1]
+    # Per-kernel breakdown from the same steps run again with the library's
+    # CUDA-event profiling on (its events cost host time per launch, so the
+    # timed loop above runs without it).
+    vc.profile_reset()
+    vc.profile_enable(True)
+    for _ in range(args.steps):
+        step_dev()
+    barrier()
+    vc.profile_enable(False)
     scan_ms, scan_n = vc.profile_read("knn_scan")
     sel_ms, sel_n = vc.profile_read("knn_select")
     merge_ms, merge_n = vc.profile_read("knn_merge")
     piv_ms, piv_n = vc.profile_read("knn_pivot")
     fb_ms, fb_n = vc.profile_read("knn_fallback")
-    launches = vc.profile_read("*")[1]
+    prep_ms, _ = vc.profile_read("knn_prep")
+    gath_ms, _ = vc.profile_read("knn_gather")
     value = n_q * args.steps / (ms / 1e3)
 
     # ----------------------------------------------------------- e2e (host)
@@ -403,6 +412,7 @@ def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, m
     per_launch_ms = scan_ms / max(scan_n, 1)
     breakdown = {"pivot": piv_ms / args.steps, "scan": scan_ms / args.steps,
                  "select": sel_ms / args.steps, "merge": merge_ms / args.steps,
+                 "query_prep": prep_ms / args.steps, "all_gathers": gath_ms / args.steps,
                  # exact re-search of queries whose scan bound failed verification
                  "fallback": fb_ms / args.steps, "fallback_launches": fb_n}
     if metric in TC_METRICS and D <= 128:

@@ -204,12 +204,12 @@ def test_unproven_bound_fallback(vc, orc, gpu):
     it per query. Near rows placed only on pivot rows, fewer than k of them,
     make that bound cut true neighbours: the select must flag the queries and
     the exact fallback must return the oracle's answer."""
-    n, d, k = 396_000, 32, 100
+    n, d, k = 1_200_000, 32, 100
     rng = np.random.default_rng(11)
     qs = rng.standard_normal((3, d)).astype(np.float32)
     base = (rng.standard_normal((n, d)) * 3 + 20).astype(np.float32)
     for i in range(3):
-        near = 384 * (i * 60 + np.arange(60))            # pivot rows, one per pivot tile half
+        near = 6144 * (i * 60 + np.arange(60))  # pivot rows, 1024 pivot rows apart
         base[near] = qs[i] + 0.05 * rng.standard_normal((60, d)).astype(np.float32)
         mid = 6 * (20_000 + i * 300 + np.arange(200)) + 1  # rows outside the pivot set
         base[mid] = qs[i] + 0.5 * rng.standard_normal((200, d)).astype(np.float32)

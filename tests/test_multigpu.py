@@ -158,3 +158,30 @@ def test_rank_mode_knn_and_kmeans(vc, orc, two):
         assert got[r][5] == it_o
         np.testing.assert_allclose(got[r][3], c_o, rtol=1e-6, atol=1e-6)
         assert abs(got[r][6] - in_o) <= 1e-6 * abs(in_o)
+
+
+def test_pooled_bound_sentinel_redo(vc, orc, two):
+    """Row shards pool their pivot minima into one starting bound taken at a
+    rank below k; no shard can check it alone, so each cuts its merge pairs
+    where its unkept rows could start (a sentinel pair). Near rows only on
+    pivot rows, fewer than k of them, put a sentinel inside the merged
+    top-k: the query must be searched again exactly and match the oracle."""
+    n, d, k = 1_200_000, 32, 100
+    rng = np.random.default_rng(12)
+    qs = rng.standard_normal((3, d)).astype(np.float32)
+    base = (rng.standard_normal((n, d)) * 3 + 20).astype(np.float32)
+    for i in range(3):
+        near = 6144 * (i * 60 + np.arange(60))  # pivot rows, 1024 pivot rows apart
+        base[near] = qs[i] + 0.05 * rng.standard_normal((60, d)).astype(np.float32)
+        mid = 6 * (20_000 + i * 300 + np.arange(200)) + 1
+        base[mid] = qs[i] + 0.5 * rng.standard_normal((200, d)).astype(np.float32)
+    eng = vc.DistributedKnnEngine.try_new(base, d, 2, vc.GpuShardMode.Sharded, vc.DistanceMetric.L2Squared)
+    vc.profile_reset()
+    vc.profile_enable(True)
+    dg, ig = eng.search_arrays(qs, k)
+    vc.profile_enable(False)
+    _, n_fb = vc.profile_read("knn_fallback")
+    do, io = orc.knn_search(base, qs, k, L2)
+    _same(dg, ig, do, io)
+    assert n_fb > 0
+    eng.close()

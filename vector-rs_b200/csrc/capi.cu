@@ -222,7 +222,7 @@ struct KnnShard {
   DBuf pb, pn;                  // pivot rows (every pivot_stride-th row)
   int64_t pivot_m = 0, pivot_stride = 1;
   DBuf tmin, ibound;            // per-search pivot-pass outputs
-  DBuf ptop, ptop_all;          // k smallest pivot minima per query: own, all shards
+  DBuf ptop, ptop_all;          // smallest pivot minima per query (pool_len each): own, all shards
   float xscale = 1.0f;          // tensor-core operand scale of the base rows
   int fold_m = 0;               // exponent of the folded -|x|^2 column
   DBuf qscale;                  // per-search operand scale of each query
@@ -245,6 +245,9 @@ struct vrs_knn {
   // (an all-gather between the pivot pass and the main scan).
   int parts = 1;
   bool pooled_pivot = false;
+  // Smallest pivot stride over the pooling shards (agreed at create time);
+  // fixes the pooled bound's pivot rank, and so the all-gather's length.
+  int64_t pool_stride = 1;
   std::vector<std::unique_ptr<KnnShard>> shards;
   bool rank_mode = false;
   vrs_comm* comm = nullptr;  // rank mode
@@ -446,6 +449,13 @@ int launch_exact_search(vrs_knn* h, KnnShard* s, int nq, int kk, const int* q_in
 // the gathered minima, main scan, select).
 enum { kPhaseAll = 0, kPhasePivot = 1, kPhaseMain = 2 };
 
+// Pivot rank of the starting bound (tc_optimistic_rank): from this shard's
+// own pivot stride for a search on its own, from the agreed pool stride for
+// pooled minima (the same on every shard: it is also the all-gather length).
+int pool_len(const vrs_knn* h, const KnnShard* s, int kk, int phase) {
+  return tc::tc_optimistic_rank(kk, phase == kPhaseAll ? s->pivot_stride : h->pool_stride);
+}
+
 // Launches the tensor-core scan + exact re-rank select for all nq queries.
 int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, uint32_t* out_id,
                      Cand* out_pairs, int phase) {
@@ -458,7 +468,7 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   // and is checked by the select: a single shard's failures are flagged for
   // the exact re-search; merge pairs carry a sentinel instead and the merge
   // decides (a pooled bound is global, so no shard can check it alone).
-  const int tau_rank = tc::tc_optimistic_rank(kk, s->pivot_stride);
+  const int tau_rank = pool_len(h, s, kk, phase);
   if (phase == kPhaseMain) goto main_phase;
   VRS_TRY(s->qb.reserve((size_t)nq_alloc * d16 * 2));
   VRS_TRY(s->absm.reserve((size_t)nq * sizeof(float)));
@@ -467,38 +477,44 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
     VRS_CUDA(cudaMemsetAsync((char*)s->qb.p + (size_t)nq * d16 * 2, 0, (size_t)(nq_alloc - nq) * d16 * 2, st));
   VRS_CUDA(cudaMemsetAsync(s->err.p, 0, sizeof(int), st));
   VRS_TRY(s->qscale.reserve((size_t)nq * sizeof(float)));
-  VRS_TRY(tc::tc_query_prep(s->q.as<float>(), nq, h->d, h->dp, h->metric, s->xmax.as<unsigned int>(), s->xscale,
-                            s->fold_m, s->qb.p, s->qscale.as<float>(), s->absm.as<float>(), s->overflow.as<int>(),
-                            st));
+  {
+    ProfToken t = prof_begin("knn_prep", st);
+    VRS_TRY(tc::tc_query_prep(s->q_in.as<float>(), nq, h->d, h->dp, h->metric, s->xmax.as<unsigned int>(),
+                              s->xscale, s->fold_m, s->q.as<float>(),
+                              h->metric == vrs_exact::kCos ? s->q_aux.as<float>() : nullptr, s->qb.p,
+                              s->qscale.as<float>(), s->absm.as<float>(), s->overflow.as<int>(), st));
+    prof_end(t, st);
+  }
   VRS_TRY(s->ibound.reserve((size_t)nq * sizeof(float)));
-  if (phase == kPhasePivot) VRS_TRY(s->ptop.reserve((size_t)nq * kk * sizeof(float)));
+  if (phase == kPhasePivot) VRS_TRY(s->ptop.reserve((size_t)nq * tau_rank * sizeof(float)));
   if (s->n_local > 0) {
-    // Pivot pass: half-tile minima over every pivot_stride-th row.
+    // Pivot pass: minima per column half of each tile group over every
+    // pivot_stride-th row.
     const void* pb = s->pivot_stride > 1 ? s->pb.p : s->xb.p;
     const float* pn = s->pivot_stride > 1 ? s->pn.as<float>() : s->xn.as<float>();
-    const int ntile = 2 * (int)((s->pivot_m + 127) / 128);  // half-tile minima
-    tc::TcPlan pp = tc::tc_plan(s->pivot_m, nq, kk, s->num_sms);
+    const int ntile = 2 * (int)tc::tc_pivot_groups(s->pivot_m);
+    tc::TcPlan pp = tc::tc_plan(s->pivot_m, nq, kk, s->num_sms, tc::kPivotGroup);
     VRS_TRY(s->tmin.reserve((size_t)ntile * nq * sizeof(float)));
     ProfToken t0 = prof_begin("knn_pivot", st);
     VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, pb, s->pivot_m, h->d, pn, h->metric, nq, kk, pp, nullptr,
                         nullptr, s->overflow.as<int>(), s->absm.as<float>(), s->err.as<int>(),
                         s->tmin.as<float>(), nullptr, s->qscale.as<float>(), s->xscale, st));
     if (phase == kPhasePivot)
-      VRS_TRY(tc::tc_pivot_topk(s->tmin.as<float>(), ntile, nq, kk, s->ptop.as<float>(), st));
+      VRS_TRY(tc::tc_pivot_topk(s->tmin.as<float>(), ntile, nq, tau_rank, s->ptop.as<float>(), st));
     else
       VRS_TRY(tc::tc_tau(s->tmin.as<float>(), 1, 0, ntile, nq, tau_rank, s->absm.as<float>(),
                          s->ibound.as<float>(), st));
     prof_end(t0, st);
   } else if (phase == kPhasePivot) {
-    VRS_CUDA(cudaMemsetAsync(s->ptop.p, 0x7f, (size_t)nq * kk * sizeof(float), st));  // ~3.4e38
+    VRS_CUDA(cudaMemsetAsync(s->ptop.p, 0x7f, (size_t)nq * tau_rank * sizeof(float), st));  // ~3.4e38
   }
   if (phase == kPhasePivot) return VRS_OK;
 main_phase:
   if (phase == kPhaseMain && s->n_local > 0) {
-    // Bound from every shard's k smallest pivot minima (ptop_all, gathered).
+    // Bound from every shard's smallest pivot minima (ptop_all, gathered).
     const int parts = h->rank_mode ? h->comm->nranks : h->g;
     ProfToken t0 = prof_begin("knn_pivot", st);
-    VRS_TRY(tc::tc_tau(s->ptop_all.as<float>(), parts, (int64_t)nq * kk, kk, nq, tau_rank, s->absm.as<float>(),
+    VRS_TRY(tc::tc_tau(s->ptop_all.as<float>(), parts, (int64_t)nq * tau_rank, tau_rank, nq, tau_rank, s->absm.as<float>(),
                        s->ibound.as<float>(), st));
     prof_end(t0, st);
   }
@@ -632,16 +648,21 @@ int shard_search_launch(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist
   VRS_TRY(s->q_aux.reserve((size_t)nq * sizeof(float)));
   VRS_TRY(s->overflow.reserve((size_t)(2 * nq + 1) * sizeof(int)));
   VRS_CUDA(cudaMemsetAsync(s->overflow.p, 0, (size_t)(2 * nq + 1) * sizeof(int), st));
-  VRS_TRY(launch_pad_rows(s->q_in.as<float>(), nq, h->d, h->dp, s->q.as<float>(),
-                          h->metric == vrs_exact::kHell ? 1 : 0, st));
-  if (h->metric == vrs_exact::kCos)
-    VRS_TRY(launch_cos_norms(s->q.as<float>(), nq, h->d, h->dp, s->q_aux.as<float>(), st));
+  if (!s->use_tc) {  // the tensor-core query prep writes these itself
+    ProfToken t = prof_begin("knn_prep", st);
+    VRS_TRY(launch_pad_rows(s->q_in.as<float>(), nq, h->d, h->dp, s->q.as<float>(),
+                            h->metric == vrs_exact::kHell ? 1 : 0, st));
+    if (h->metric == vrs_exact::kCos)
+      VRS_TRY(launch_cos_norms(s->q.as<float>(), nq, h->d, h->dp, s->q_aux.as<float>(), st));
+    prof_end(t, st);
+  }
   s->last_nq = nq;
   s->last_kk = kk;
   if (phase == kPhasePivot && !s->use_tc) {
     // A shard without rows contributes no pivot minima (~3.4e38 fillers).
-    VRS_TRY(s->ptop.reserve((size_t)nq * kk * sizeof(float)));
-    VRS_CUDA(cudaMemsetAsync(s->ptop.p, 0x7f, (size_t)nq * kk * sizeof(float), st));
+    const int plen = pool_len(h, s, kk, phase);
+    VRS_TRY(s->ptop.reserve((size_t)nq * plen * sizeof(float)));
+    VRS_CUDA(cudaMemsetAsync(s->ptop.p, 0x7f, (size_t)nq * plen * sizeof(float), st));
     return VRS_OK;
   }
   if (s->use_tc) return launch_tc_search(h, s, nq, kk, out_dist, out_id, out_pairs, phase);
@@ -690,6 +711,7 @@ int agree_pooled_clique(vrs_knn* h) {
     return VRS_OK;
   unsigned int xm = 0;
   bool all = true, any = false;
+  int64_t stride = INT64_MAX;
   for (auto& sp : h->shards) {
     KnnShard* s = sp.get();
     if (s->n_local == 0) continue;
@@ -698,6 +720,7 @@ int agree_pooled_clique(vrs_knn* h) {
       continue;
     }
     any = true;
+    stride = std::min(stride, s->pivot_stride);
     unsigned int v = 0;
     VRS_CUDA(cudaSetDevice(s->device));
     VRS_CUDA(cudaMemcpy(&v, s->xmax.p, sizeof(v), cudaMemcpyDeviceToHost));
@@ -710,6 +733,7 @@ int agree_pooled_clique(vrs_knn* h) {
     VRS_CUDA(cudaSetDevice(s->device));
     VRS_CUDA(cudaMemcpy(s->xmax.p, &xm, sizeof(xm), cudaMemcpyHostToDevice));
   }
+  h->pool_stride = stride;
   h->pooled_pivot = true;
   return VRS_OK;
 }
@@ -724,22 +748,26 @@ int agree_pooled_rank(vrs_knn* h) {
   KnnShard* s = h->shards[0].get();
   VRS_CUDA(cudaSetDevice(s->device));
   DBuf v;
-  VRS_TRY(v.reserve(2 * sizeof(unsigned int)));
-  unsigned int host[2] = {(s->n_local == 0 || s->use_tc) ? 1u : 0u, 0u};
-  if (s->use_tc) VRS_CUDA(cudaMemcpy(&host[1], s->xmax.p, sizeof(unsigned int), cudaMemcpyDeviceToHost));
+  VRS_TRY(v.reserve(3 * sizeof(unsigned int)));
+  // {TC vote (min), pivot stride (min; rows-less ranks are neutral), max |x| bits (max)}
+  unsigned int host[3] = {(s->n_local == 0 || s->use_tc) ? 1u : 0u,
+                          s->n_local > 0 ? (unsigned int)std::min<int64_t>(s->pivot_stride, 0xffffffffLL) : 0xffffffffu,
+                          0u};
+  if (s->use_tc) VRS_CUDA(cudaMemcpy(&host[2], s->xmax.p, sizeof(unsigned int), cudaMemcpyDeviceToHost));
   VRS_CUDA(cudaMemcpy(v.p, host, sizeof(host), cudaMemcpyHostToDevice));
   unsigned int* d = v.as<unsigned int>();
   const double tmo = env_timeout();
   VRS_NCCL(ncclGroupStart());
-  VRS_NCCL(ncclAllReduce(d, d, 1, ncclUint32, ncclMin, s->comm, s->stream));
-  VRS_NCCL(ncclAllReduce(d + 1, d + 1, 1, ncclUint32, ncclMax, s->comm, s->stream));
+  VRS_NCCL(ncclAllReduce(d, d, 2, ncclUint32, ncclMin, s->comm, s->stream));
+  VRS_NCCL(ncclAllReduce(d + 2, d + 2, 1, ncclUint32, ncclMax, s->comm, s->stream));
   VRS_NCCL(ncclGroupEnd());
   VRS_TRY(nccl_ready(s->comm, tmo));
   VRS_TRY(stream_wait(s->stream, s->comm, tmo));
   VRS_CUDA(cudaMemcpy(host, d, sizeof(host), cudaMemcpyDeviceToHost));
   v.release();
-  if (!host[0] || !host[1]) return VRS_OK;  // a shard off the TC path, or no rows anywhere
-  if (s->use_tc) VRS_CUDA(cudaMemcpy(s->xmax.p, &host[1], sizeof(unsigned int), cudaMemcpyHostToDevice));
+  if (!host[0] || !host[2]) return VRS_OK;  // a shard off the TC path, or no rows anywhere
+  if (s->use_tc) VRS_CUDA(cudaMemcpy(s->xmax.p, &host[2], sizeof(unsigned int), cudaMemcpyHostToDevice));
+  h->pool_stride = host[1] == 0xffffffffu ? 1 : host[1];
   h->pooled_pivot = true;
   return VRS_OK;
 }
@@ -761,12 +789,21 @@ int sharded_merge(vrs_knn* h, int nb, int kk, double tmo) {
     VRS_CUDA(cudaSetDevice(s->device));
     VRS_TRY(launch_flag_pairs(s->overflow.as<int>(), nb, kk, s->pairs.as<Cand>(), s->stream));
   }
+  std::vector<ProfToken> tg(G);
+  for (int r = 0; r < G; r++) {
+    VRS_CUDA(cudaSetDevice(h->shards[r]->device));
+    tg[r] = prof_begin("knn_gather", h->shards[r]->stream);
+  }
   VRS_NCCL(ncclGroupStart());
   for (int r = 0; r < G; r++) {
     KnnShard* s = h->shards[r].get();
     VRS_NCCL(ncclAllGather(s->pairs.p, s->gathered.p, (size_t)nb * kk, ncclUint64, s->comm, s->stream));
   }
   VRS_NCCL(ncclGroupEnd());
+  for (int r = 0; r < G; r++) {
+    VRS_CUDA(cudaSetDevice(h->shards[r]->device));
+    prof_end(tg[r], h->shards[r]->stream);
+  }
   for (int r = 0; r < G; r++) VRS_TRY(nccl_ready(h->shards[r]->comm, tmo));
   KnnShard* s0 = h->shards[0].get();
   VRS_CUDA(cudaSetDevice(s0->device));
@@ -894,17 +931,27 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         }
       }
       if (pooled) {
+        const int plen = pool_len(h, h->shards[0].get(), kk, kPhasePivot);
         for (int r = 0; r < G; r++) {
           KnnShard* s = h->shards[r].get();
           VRS_CUDA(cudaSetDevice(s->device));
-          VRS_TRY(s->ptop_all.reserve((size_t)nranks * nb * kk * sizeof(float)));
+          VRS_TRY(s->ptop_all.reserve((size_t)nranks * nb * plen * sizeof(float)));
+        }
+        std::vector<ProfToken> tg(G);
+        for (int r = 0; r < G; r++) {
+          VRS_CUDA(cudaSetDevice(h->shards[r]->device));
+          tg[r] = prof_begin("knn_gather", h->shards[r]->stream);
         }
         VRS_NCCL(ncclGroupStart());
         for (int r = 0; r < G; r++) {
           KnnShard* s = h->shards[r].get();
-          VRS_NCCL(ncclAllGather(s->ptop.p, s->ptop_all.p, (size_t)nb * kk, ncclFloat32, s->comm, s->stream));
+          VRS_NCCL(ncclAllGather(s->ptop.p, s->ptop_all.p, (size_t)nb * plen, ncclFloat32, s->comm, s->stream));
         }
         VRS_NCCL(ncclGroupEnd());
+        for (int r = 0; r < G; r++) {
+          VRS_CUDA(cudaSetDevice(h->shards[r]->device));
+          prof_end(tg[r], h->shards[r]->stream);
+        }
         for (int r = 0; r < G; r++) VRS_TRY(nccl_ready(h->shards[r]->comm, tmo));
         for (int r = 0; r < G; r++) {
           KnnShard* s = h->shards[r].get();

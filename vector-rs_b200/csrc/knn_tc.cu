@@ -30,6 +30,7 @@
 
 #include "tc_common.cuh"
 #include "vrs_exact.cuh"
+#include "vrs_exact_lanes.cuh"
 #include "vrs_internal.cuh"
 #include "vrs_select.cuh"
 #include "vrs_tc.cuh"
@@ -72,10 +73,12 @@ struct TcScanArgs {
   int k;
   const float* absm; // [nq]
   int* err;          // global error word (0 = ok)
-  // Pivot pass: instead of appending, write each half tile's minimum score
-  // per query to tmin[query][2 * tile + half] (tile = global 128-row index).
+  // Pivot pass: instead of appending, write the minimum score of each
+  // column half of every group of kPivotGroup tiles per query to
+  // tmin[query][2 * group + half] (group = global 128-row tile / kPivotGroup;
+  // segments start on group boundaries).
   float* tmin;
-  int64_t tmin_stride;  // entries per query row of tmin (2 * tiles)
+  int64_t tmin_stride;  // entries per query row of tmin (2 * groups)
   // Starting acceptance bound per query (null: +inf).
   const float* init_bound;
   uint32_t idesc;    // MMA instruction descriptor
@@ -233,6 +236,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float absm = vq ? a.absm[q] : 0.0f;
     int* hist = s_hist + ew * 256;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    float run = MODE == 0 ? INFINITY : -INFINITY;  // pivot pass: best key of the current group
     for (int t = 0; t < ntiles; t++) {
       const int b = t & 1;
       const bool ok = mbar_wait(&tfull[b], (t >> 1) & 1, s_abort, a.err, 5, WAIT_NS);
@@ -303,9 +307,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
       if (TILEMIN) {
-        if (vq)
-          a.tmin[(int64_t)q * a.tmin_stride + (row_begin / BN + t) * 2 + ch] =
-              MODE == 0 ? best : MODE == 1 ? -inv_ks * best : f2 * best;
+        run = MODE == 0 ? fminf(run, best) : fmaxf(run, best);
+        if ((t + 1) % kPivotGroup == 0 || t == ntiles - 1) {
+          if (vq)
+            a.tmin[(int64_t)q * a.tmin_stride + (row_begin / BN + t) / kPivotGroup * 2 + ch] =
+                MODE == 0 ? run : MODE == 1 ? -inv_ks * run : f2 * run;
+          run = MODE == 0 ? INFINITY : -INFINITY;
+        }
         continue;
       }
       // Shrink lists that could overflow on the next tile.
@@ -392,22 +400,58 @@ __global__ void tc_base_prep_kernel(const float* __restrict__ x, int64_t n, int 
   atomicMax(xmax_bits, __float_as_uint((float)sqrt(ss)));
 }
 
-// Queries -> fp16 operand rows and per-query acceptance margins (heap-score
-// units). Near-zero cosine queries are routed to the exact fallback.
-__global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d, int dp, int d16,
-                                     int metric, const unsigned int* __restrict__ xmax_bits, float xscale,
-                                     int fold_m, uint16_t* __restrict__ qb, float* __restrict__ qscale,
-                                     float* __restrict__ absm, int* __restrict__ overflow) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= nq) return;
-  const float* v = q + (int64_t)i * dp;
-  uint16_t* o = qb + (int64_t)i * d16;
+// Queries -> padded f32 rows for the exact re-rank (and, for cosine, their
+// norms in the reference's order), fp16 operand rows, per-query operand
+// scales and acceptance margins (heap-score units). One warp per query: lane
+// l holds columns l, l + 32, l + 64, l + 96 (d <= 128 on this path). Near-zero
+// cosine queries are routed to the exact fallback.
+constexpr int kPrepWarps = 8;
+
+__global__ void __launch_bounds__(kPrepWarps * 32)
+    tc_query_prep_kernel(const float* __restrict__ q_in, int nq, int d, int dp, int d16, int metric,
+                         const unsigned int* __restrict__ xmax_bits, float xscale, int fold_m,
+                         float* __restrict__ qpad, float* __restrict__ qaux, uint16_t* __restrict__ qb,
+                         float* __restrict__ qscale, float* __restrict__ absm, int* __restrict__ overflow) {
+  const int lane = threadIdx.x & 31;
+  const int i = blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
+  if (i >= nq) return;  // uniform per warp
+  const float* src = q_in + (int64_t)i * d;
+  float v[4];
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    const int c = lane + 32 * t;
+    v[t] = c < d ? src[c] : 0.0f;
+    if (c < dp) qpad[(int64_t)i * dp + c] = v[t];
+  }
   const bool f16 = tc_fp16(metric);
   float scale = 1.0f;
   if (metric == vrs_exact::kCos) {
-    const float sq = sqrtf(vrs_exact::cos_norm_sq(v, d));
+    // cos_norm_sq in the reference's order (vrs_exact.cuh): lane l < 16
+    // plays SIMD lane l of s0, lane l + 16 of s1; chunks of 32 in order,
+    // then one 16-wide step, the halving tree, and the tail in order.
+    const int chunks = d / 32;
+    float acc = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+      if (t < chunks) acc = __fmaf_rn(v[t], v[t], acc);
+    int e0 = chunks * 32;
+    if (e0 + 16 <= d) {
+      const float x = chunks == 0 ? v[0] : chunks == 1 ? v[1] : chunks == 2 ? v[2] : v[3];
+      if (lane < 16) acc = __fmaf_rn(x, x, acc);
+      e0 += 16;
+    }
+    const float s1 = __shfl_down_sync(0xffffffffu, acc, 16);
+    float r = vrs_exact::lanes::hsum16(__fadd_rn(acc, s1));
+    r = __shfl_sync(0xffffffffu, r, 0);
+    for (int e = e0; e < d; e++) {  // uniform
+      const int t = e >> 5;
+      const float x = __shfl_sync(0xffffffffu, t == 0 ? v[0] : t == 1 ? v[1] : t == 2 ? v[2] : v[3], e & 31);
+      r = __fadd_rn(r, __fmul_rn(x, x));
+    }
+    if (lane == 0 && qaux) qaux[i] = r;
+    const float sq = sqrtf(r);
     if (!(sq >= kTinyNorm)) {
-      overflow[i] = 1;
+      if (lane == 0) overflow[i] = 1;
       scale = 0.0f;
     } else {
       scale = 1.0f / sq;
@@ -420,28 +464,35 @@ __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d,
   const bool fold = tc_fold(metric, d);
   float qs = 1.0f;
   if (metric != vrs_exact::kCos) {
-    float mx = 0.0f;
-    for (int j = 0; j < d; j++) mx = fmaxf(mx, fabsf(v[j]));
+    float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     int ex = mx > 0.0f ? 7 - ilogbf(mx) : 0;
     ex = max(-60, min(60, ex));
     if (fold) {
       ex = min(ex, 15 - fold_m);
-      if (ex < -14 - fold_m || (mx > 0.0f && ldexpf(mx, ex) > 32768.0f)) overflow[i] = 1;
+      if ((ex < -14 - fold_m || (mx > 0.0f && ldexpf(mx, ex) > 32768.0f)) && lane == 0) overflow[i] = 1;
     }
     qs = ldexpf(1.0f, ex);
   }
-  qscale[i] = qs;
   double ss = 0.0;
-  for (int j = 0; j < d16; j++) {
-    float e = j < d ? v[j] : 0.0f;
-    ss += (double)e * (double)e;
-    o[j] = to_operand(metric == vrs_exact::kCos ? e * scale : e * qs, f16);
+#pragma unroll
+  for (int t = 0; t < 4; t++) ss += (double)v[t] * (double)v[t];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  uint16_t* o = qb + (int64_t)i * d16;
+  const uint16_t fc = __half_as_ushort(__float2half_rn(ldexpf(qs, fold_m)));
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    const int c = lane + 32 * t;
+    if (c < d16) {
+      uint16_t w = to_operand(metric == vrs_exact::kCos ? v[t] * scale : v[t] * qs, f16);
+      if (fold && (c == d || c == d + 1)) w = fc;
+      o[c] = w;
+    }
   }
-  if (fold) {
-    const __half c = __float2half_rn(ldexpf(qs, fold_m));
-    o[d] = __half_as_ushort(c);
-    o[d + 1] = __half_as_ushort(c);
-  }
+  if (lane != 0) return;
+  qscale[i] = qs;
   const double X = (double)__uint_as_float(*xmax_bits);
   const double Q = sqrt(ss);
   const double u = 0x1p-24;
@@ -471,12 +522,13 @@ __global__ void tc_query_prep_kernel(const float* __restrict__ q, int nq, int d,
   absm[i] = (float)(2.0 * e * 1.25) * (1.0f + 0x1p-20f);
 }
 
-// Starting bound per query: the k-th smallest pivot-tile minimum. Each tile
-// minimum is the score of a distinct pivot row, so at least k rows score
-// <= tau and the exact k-th best is <= tau; anything in the exact top-k thus
-// has approximate score <= tau + absm. With several shards the minima are
-// each shard's k smallest, all-gathered: the k-th smallest of the union is
-// the k-th smallest over every shard's pivot tiles.
+// Starting bound per query: the k-th smallest pivot-tile minimum plus absm.
+// Each tile minimum is the score of a distinct pivot row, so at least k rows
+// score <= tau; with k the pivot rank of the proven bound, anything in the
+// exact top-k then has approximate score <= tau + absm (a lower rank gives
+// the unproven bound that the select checks). With several shards the minima
+// are each shard's smallest, all-gathered: the k-th smallest of the union is
+// the k-th smallest over every shard's pivot tiles. One block per query.
 __global__ void __launch_bounds__(256) tc_tau_kernel(const float* __restrict__ vals, int nparts,
                                                      int64_t part_stride, int len, int nq, int k,
                                                      const float* __restrict__ absm,
@@ -618,11 +670,17 @@ int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, float xsc
   return VRS_OK;
 }
 
-int tc_query_prep(const float* q, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
-                  float xscale, int fold_m, void* qb, float* qscale, float* absm, int* overflow, cudaStream_t s) {
+int tc_query_prep(const float* q_in, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
+                  float xscale, int fold_m, float* qpad, float* qaux, void* qb, float* qscale, float* absm,
+                  int* overflow, cudaStream_t s) {
   if (nq == 0) return VRS_OK;
-  tc_query_prep_kernel<<<(nq + 127) / 128, 128, 0, s>>>(q, nq, d, dp, tc_d16(metric, d), metric, xmax_bits,
-                                                         xscale, fold_m, (uint16_t*)qb, qscale, absm, overflow);
+  if (d > 128) {
+    set_error(VRS_ERR_INVALID_CONFIG, "tensor-core query prep needs d <= 128");
+    return VRS_ERR_INVALID_CONFIG;
+  }
+  tc_query_prep_kernel<<<(nq + kPrepWarps - 1) / kPrepWarps, kPrepWarps * 32, 0, s>>>(
+      q_in, nq, d, dp, tc_d16(metric, d), metric, xmax_bits, xscale, fold_m, qpad, qaux, (uint16_t*)qb, qscale,
+      absm, overflow);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;
@@ -666,7 +724,7 @@ int tc_pivot_topk(const float* tmin, int ntile, int nq, int k, float* out, cudaS
   return VRS_OK;
 }
 
-TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms) {
+TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms, int align_tiles) {
   TcPlan p;
   p.qtiles = (nq + BM * NACC - 1) / (BM * NACC);
   p.cap = 1024;
@@ -683,7 +741,8 @@ TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms) {
       p.nseg = s;
     }
   }
-  const int64_t tiles_per_seg = (ntile_total + p.nseg - 1) / p.nseg;
+  int64_t tiles_per_seg = (ntile_total + p.nseg - 1) / p.nseg;
+  tiles_per_seg = (tiles_per_seg + align_tiles - 1) / align_tiles * align_tiles;
   p.seg_len = std::max<int64_t>(1, tiles_per_seg) * BN;
   p.nseg = (int)std::max<int64_t>(1, (n + p.seg_len - 1) / p.seg_len);
   return p;
@@ -714,7 +773,11 @@ int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d,
   a.absm = absm;
   a.err = err;
   a.tmin = tmin;
-  a.tmin_stride = 2 * ((n + BN - 1) / BN);
+  a.tmin_stride = 2 * tc_pivot_groups(n);
+  if (tmin && p.seg_len % ((int64_t)kPivotGroup * BN) != 0) {
+    set_error(VRS_ERR_INVALID_CONFIG, "pivot segments must start on pivot-group boundaries");
+    return VRS_ERR_INVALID_CONFIG;
+  }
   a.idesc = f16 ? idesc_f16(BM, BN) : idesc_bf16(BM, BN);
   a.qscale = qscale;
   a.xscale = xscale;

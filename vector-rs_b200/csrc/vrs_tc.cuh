@@ -41,10 +41,14 @@ int tc_d16(int metric, int d);
 // column (tc_fold_exponent).
 int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, float xscale, int fold_m, void* xb,
                  float* xn, unsigned int* xmax_bits, uint32_t* tiny, int* n_tiny, int tiny_cap, cudaStream_t s);
-// Writes each query's operand scale to qscale[nq]; queries whose scale
-// cannot fit the folded column are flagged for the exact scan.
-int tc_query_prep(const float* q, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
-                  float xscale, int fold_m, void* qb, float* qscale, float* absm, int* overflow, cudaStream_t s);
+// From the unpadded queries q_in ([nq][d]): the padded f32 rows qpad
+// ([nq][dp], for the exact re-rank), cosine norms in the reference's order
+// (qaux, cosine only), fp16 operand rows, each query's operand scale
+// (qscale) and margin (absm). Near-zero cosine queries and queries whose
+// scale cannot fit the folded column are flagged for the exact scan.
+int tc_query_prep(const float* q_in, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
+                  float xscale, int fold_m, float* qpad, float* qaux, void* qb, float* qscale, float* absm,
+                  int* overflow, cudaStream_t s);
 // Base operand scale for a base whose largest |element| is maxabs, and the
 // folded column's exponent (|F| = xscale |x|^2 / 2^(m+1) <= 2^14 with
 // |x|^2 <= d maxabs^2).
@@ -59,7 +63,14 @@ inline int tc_fold_exponent(int d, float xscale, float maxabs) {
   const double top = (double)xscale * d * (double)maxabs * (double)maxabs;
   return (int)std::ceil(std::log2(top)) - 15;
 }
-TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms);
+// align_tiles: segments hold a multiple of this many 128-row tiles (the
+// pivot pass passes kPivotGroup).
+TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms, int align_tiles = 1);
+// The pivot pass reports one minimum per column half of every group of
+// kPivotGroup 128-row tiles (256 pivot rows per value): fewer values to
+// store and to select from, each still the score of a distinct row.
+constexpr int kPivotGroup = 4;
+inline int64_t tc_pivot_groups(int64_t m) { return ((m + 127) / 128 + kPivotGroup - 1) / kPivotGroup; }
 // With tmin != null this is the pivot pass (per-tile minima, no appends);
 // init_bound (nullable) seeds each query's acceptance bound.
 int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn,
