@@ -15,6 +15,8 @@
 // Reference kernels replaced: kmeans_zero_accumulators,
 // kmeans_assign_and_accumulate, kmeans_update_centroids
 // (crates/vector-cuda/src/kernels/kmeans.cu:22-395).
+#include <mutex>
+
 #include "vrs_exact.cuh"
 #include "vrs_internal.cuh"
 
@@ -150,7 +152,7 @@ __global__ void abs_max_kernel(const float* __restrict__ x, int64_t n, int d, in
 // point and added to the cluster's sums with one integer atomic per
 // dimension. Integer addition is associative, so the result does not
 // depend on the order of points or blocks.
-constexpr int kChunk = 2048;
+constexpr int kChunk = 256;
 
 __global__ void km_count_kernel(const int32_t* __restrict__ assign, int64_t n, int* __restrict__ counts) {
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -199,6 +201,56 @@ __global__ void km_scan_kernel(const int* __restrict__ counts, int k, int* __res
   }
 }
 
+// Block-local variants for k <= kSmemBins: a shared-memory histogram per
+// block of kBinPts points, then one global atomic per non-empty bin (counts),
+// or one range reservation per non-empty bin and local ranks (scatter).
+constexpr int kSmemBins = 16384;
+constexpr int kBinThreads = 256;
+constexpr int kBinPer = 16;
+constexpr int kBinPts = kBinThreads * kBinPer;
+
+__global__ void __launch_bounds__(kBinThreads) km_count_smem_kernel(const int32_t* __restrict__ assign, int64_t n,
+                                                                    int k, int* __restrict__ counts) {
+  extern __shared__ int h[];
+  for (int c = threadIdx.x; c < k; c += kBinThreads) h[c] = 0;
+  __syncthreads();
+  const int64_t b0 = (int64_t)blockIdx.x * kBinPts;
+#pragma unroll
+  for (int u = 0; u < kBinPer; u++) {
+    const int64_t i = b0 + u * kBinThreads + threadIdx.x;
+    if (i < n) atomicAdd(&h[assign[i]], 1);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < k; c += kBinThreads)
+    if (h[c]) atomicAdd(&counts[c], h[c]);
+}
+
+__global__ void __launch_bounds__(kBinThreads) km_scatter_smem_kernel(const int32_t* __restrict__ assign, int64_t n,
+                                                                      int k, const int* __restrict__ off,
+                                                                      int* __restrict__ cursor,
+                                                                      int32_t* __restrict__ perm) {
+  extern __shared__ int h[];
+  for (int c = threadIdx.x; c < k; c += kBinThreads) h[c] = 0;
+  __syncthreads();
+  const int64_t b0 = (int64_t)blockIdx.x * kBinPts;
+  int cl[kBinPer], lr[kBinPer];
+#pragma unroll
+  for (int u = 0; u < kBinPer; u++) {
+    const int64_t i = b0 + u * kBinThreads + threadIdx.x;
+    cl[u] = i < n ? assign[i] : -1;
+    lr[u] = cl[u] >= 0 ? atomicAdd(&h[cl[u]], 1) : 0;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < k; c += kBinThreads) {
+    const int cnt = h[c];
+    h[c] = cnt ? off[c] + atomicAdd(&cursor[c], cnt) : 0;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kBinPer; u++)
+    if (cl[u] >= 0) perm[h[cl[u]] + lr[u]] = (int32_t)(b0 + u * kBinThreads + threadIdx.x);
+}
+
 __global__ void km_scatter_kernel(const int32_t* __restrict__ assign, int64_t n, const int* __restrict__ off,
                                   int* __restrict__ cursor, int32_t* __restrict__ perm) {
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -229,14 +281,30 @@ __global__ void __launch_bounds__(128) km_chunk_sum_kernel(
   long long acc[NJ];
 #pragma unroll
   for (int j = 0; j < NJ; j++) acc[j] = 0;
-  const double scale = ldexp(1.0, scale_exp);
-  for (int p = p0 + warp; p < p1; p += 4) {
-    const float* v = x + (int64_t)perm[p] * dp;
+  // v * 2^s is exact in f32 (|v| 2^s < 2^61; a product that underflows is
+  // below 1/2 and rounds to 0 either way), so f32 -> s64 rounding gives the
+  // same integer as the f64 path at a fraction of the cost.
+  const float scalef = ldexpf(1.0f, scale_exp);
+  // Four points per warp step (indices, then all their rows, in flight
+  // together): the rows are scattered, so memory-level parallelism is what
+  // sets the rate.
+  constexpr int U = 4;
+  for (int p = p0 + warp * U; p < p1; p += 4 * U) {
+    int64_t row[U];
 #pragma unroll
-    for (int j = 0; j < NJ; j++) {
-      const int e = lane + 32 * j;
-      if (e < d) acc[j] += __double2ll_rn((double)v[e] * scale);
-    }
+    for (int u = 0; u < U; u++) row[u] = p + u < p1 ? (int64_t)perm[p + u] : -1;
+    float val[U][NJ];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        const int e = lane + 32 * j;
+        val[u][j] = (row[u] >= 0 && e < d) ? x[row[u] * dp + e] : 0.0f;
+      }
+#pragma unroll
+    for (int u = 0; u < U; u++)
+#pragma unroll
+      for (int j = 0; j < NJ; j++) acc[j] += __float2ll_rn(val[u][j] * scalef);
   }
 #pragma unroll
   for (int j = 0; j < NJ; j++) s_part[warp][lane + 32 * j] = acc[j];
@@ -342,9 +410,31 @@ int launch_kmeans_segsum(const float* x, int64_t n, int d, int dp, const int32_t
   int32_t* perm = cursor + k;   // [n]
   VRS_CUDA(cudaMemsetAsync(cnt, 0, (size_t)k * sizeof(int), s));
   const unsigned nb = (unsigned)((n + 255) / 256);
-  km_count_kernel<<<nb, 256, 0, s>>>(assign, n, cnt);
+  const bool smem_bins = k <= kSmemBins;
+  if (smem_bins) {
+    static std::once_flag once[64];
+    int dev = 0;
+    VRS_CUDA(cudaGetDevice(&dev));
+    auto set = [] {
+      cudaFuncSetAttribute(km_count_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBins * 4);
+      cudaFuncSetAttribute(km_scatter_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBins * 4);
+    };
+    if (dev < 64)
+      std::call_once(once[dev], set);
+    else
+      set();
+  }
+  const unsigned nbb = (unsigned)((n + kBinPts - 1) / kBinPts);
+  const size_t hsm = (size_t)k * sizeof(int);
+  if (smem_bins)
+    km_count_smem_kernel<<<nbb, kBinThreads, hsm, s>>>(assign, n, k, cnt);
+  else
+    km_count_kernel<<<nb, 256, 0, s>>>(assign, n, cnt);
   km_scan_kernel<<<1, 1024, 0, s>>>(cnt, k, off, coff, cursor);
-  km_scatter_kernel<<<nb, 256, 0, s>>>(assign, n, off, cursor, perm);
+  if (smem_bins)
+    km_scatter_smem_kernel<<<nbb, kBinThreads, hsm, s>>>(assign, n, k, off, cursor, perm);
+  else
+    km_scatter_kernel<<<nb, 256, 0, s>>>(assign, n, off, cursor, perm);
   const unsigned nchunks = (unsigned)((n + kChunk - 1) / kChunk + k);
   if (d <= 128)
     km_chunk_sum_kernel<4><<<nchunks, 128, 0, s>>>(x, d, dp, k, off, coff, perm, scale_exp, sums);

@@ -370,9 +370,13 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
   const int hl = threadIdx.x & 15;
   const unsigned mask = 0xffffu << (threadIdx.x & 16);
   const float* v = x + i * dp;
+  // The point's row (HBM) is pulled into L1 while its records and first
+  // candidates load; the exact re-scoring below then reads it from L1.
+  if (hl * 32 < dp) asm volatile("prefetch.global.L1 [%0];" ::"l"(v + hl * 32));
   const float va = METRIC == vrs_exact::kCos ? x_aux[i] : 0.0f;
   const bool hib = vrs_exact::higher_is_better(METRIC);
   const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
+  const Cand first0 = cands[(i * 2) * NCAND], first1 = cands[(i * 2 + 1) * NCAND];
   int best = 0x7fffffff;
   float best_key = hib ? -INFINITY : INFINITY;
   auto consider = [&](uint32_t c) {
@@ -400,7 +404,7 @@ __global__ void __launch_bounds__(128) kmeans_finalize_kernel(
     for (int h = 0; h < 2; h++) {
       const Res r = h ? r1 : r0;
       for (int e = 0; e < r.cnt; e++) {
-        const Cand ce = cands[(i * 2 + h) * NCAND + e];
+        const Cand ce = e == 0 ? (h ? first1 : first0) : cands[(i * 2 + h) * NCAND + e];
         if (ce.hs <= bound) consider(ce.id);
       }
     }
