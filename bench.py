@@ -75,7 +75,7 @@ TC_METRICS = (L2, DOT, COS, 7)
 # from the ncu capture summarised in profiles/knn_scan_tc_C2.txt; other base
 # sizes scale it by the rows scanned (the traffic is the base re-stream plus
 # the candidate lists, both proportional to the rows).
-SCAN_DRAM_BYTES_C2 = 321.725696e6 + 55.456512e6
+SCAN_DRAM_BYTES_C2 = 318.847488e6 + 29.940224e6
 
 
 def parse():
