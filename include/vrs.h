@@ -179,10 +179,14 @@ VRS_API int vrs_knn_search_noalloc(const float* base, int64_t n, int32_t d, cons
  * Calls still return only after their results are ready. */
 VRS_API int vrs_knn_set_stream(vrs_knn* h, void* cuda_stream);
 
-/* Kernel timing with CUDA events (off by default). When on, every launch of
- * the named kernels below is bracketed by events on its stream and the
- * elapsed device time is accumulated per name: "knn_scan", "knn_select",
- * "knn_merge", "kmeans_assign", "kmeans_update". */
+/* Kernel timing with CUDA events (off by default). When on (1), every
+ * launch of the named stages below is bracketed by events on its stream and
+ * the elapsed device time is accumulated per name: "knn_prep", "knn_pivot",
+ * "knn_scan", "knn_select", "knn_gather", "knn_merge", "knn_fallback",
+ * "kmeans_assign", "kmeans_finalize", "kmeans_sums", "kmeans_update",
+ * "kmeans_loop" (a whole Lloyd loop). With on = 2 only the whole-loop stage
+ * ("kmeans_loop") is timed, so the per-iteration host work stays as with
+ * profiling off. "*" reads the count of kernel launches since the reset. */
 VRS_API int vrs_profile_enable(int32_t on);
 VRS_API int vrs_profile_reset(void);
 VRS_API int vrs_profile_read(const char* name, double* total_ms, int64_t* launches);

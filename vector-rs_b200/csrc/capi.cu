@@ -1249,12 +1249,14 @@ struct KmShard {
   DBuf xb, xq, xtiny, cb, cn, cmax, res, cands, err, ctiny;
   DBuf flags;  // points for the full exact scan: [count, indices...]
   DBuf segws;  // counting-sort workspace of the centroid sums
+  HBuf hstat;  // pinned: {assignment error word, max centroid shift} per iteration
   ~KmShard() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     for (DBuf* b : {&x, &xr, &x_aux, &assign, &dist, &acc, &cent, &cent_r, &cent_aux, &shift, &scal, &red, &xb,
                     &xq, &xtiny, &cb, &cn, &cmax, &res, &cands, &err, &ctiny, &segws, &flags})
       b->release();
+    hstat.release();
     if (stream) cudaStreamDestroy(stream);
   }
 };
@@ -1465,22 +1467,29 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
                                    s->stream));
       prof_end(t, s->stream);
     }
-    float max_shift = 0.0f;
+    // The error words and the convergence value ride the same bounded wait
+    // (pinned copies queued behind the update), one per shard.
+    for (KmShard* s : shards) {
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_TRY(s->hstat.reserve(2 * sizeof(int)));
+      int* hs = s->hstat.as<int>();
+      hs[0] = 0;
+      if (s->use_tc) VRS_CUDA(cudaMemcpyAsync(hs, s->err.p, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+      if (s == shards[0])
+        VRS_CUDA(cudaMemcpyAsync(hs + 1, s->scal.as<float>() + 1, sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    }
     for (KmShard* s : shards) {
       VRS_CUDA(cudaSetDevice(s->device));
       VRS_TRY(stream_wait(s->stream, coll ? s->comm : nullptr, tmo));
     }
     for (KmShard* s : shards) {
-      if (!s->use_tc) continue;
-      int err = 0;
-      VRS_CUDA(cudaSetDevice(s->device));
-      VRS_CUDA(cudaMemcpy(&err, s->err.p, sizeof(int), cudaMemcpyDeviceToHost));
+      const int err = s->hstat.as<int>()[0];
       if (err)
         return fail(VRS_ERR_TIMEOUT, "tensor-core k-means assignment gave up waiting (stage code " +
                                          std::to_string(err) + ")");
     }
-    VRS_CUDA(cudaSetDevice(shards[0]->device));
-    VRS_CUDA(cudaMemcpy(&max_shift, shards[0]->scal.as<float>() + 1, sizeof(float), cudaMemcpyDeviceToHost));
+    float max_shift = 0.0f;
+    std::memcpy(&max_shift, shards[0]->hstat.as<int>() + 1, sizeof(float));
     if (max_shift <= P.tol) break;
   }
   VRS_CUDA(cudaSetDevice(shards[0]->device));

@@ -2,6 +2,7 @@
 // (vrs_profile_* in include/vrs.h). Each timed launch records a start and a
 // stop event on its own stream; totals are gathered when read.
 #include <atomic>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
@@ -19,7 +20,7 @@ struct Pending {
 };
 
 std::mutex g_mu;
-bool g_on = false;
+int g_on = 0;  // 0 off, 1 every stage, 2 whole-loop stages only
 std::vector<Pending> g_pending;
 std::map<std::string, std::pair<double, int64_t>> g_acc;
 std::atomic<int64_t> g_launches{0};
@@ -52,6 +53,7 @@ ProfToken prof_begin(const char* name, cudaStream_t s) {
   {
     std::lock_guard<std::mutex> g(g_mu);
     if (!g_on) return t;
+    if (g_on == 2 && std::strcmp(name, "kmeans_loop") != 0) return t;
   }
   t.active = true;
   t.name = name;
@@ -74,7 +76,7 @@ void prof_end(ProfToken& t, cudaStream_t s) {
 
 extern "C" int vrs_profile_enable(int32_t on) {
   std::lock_guard<std::mutex> g(vrs::g_mu);
-  vrs::g_on = on != 0;
+  vrs::g_on = on;
   return VRS_OK;
 }
 

@@ -464,8 +464,10 @@ def kmeans_fit_rank(comm: Comm, x_local, n_global: int, dimension: int, k: int, 
 # ------------------------------------------------------------ profiling
 
 
-def profile_enable(on: bool = True):
-    _check(lib().vrs_profile_enable(1 if on else 0))
+def profile_enable(on=True):
+    """True/1: time every named stage; 2: only whole loops ("kmeans_loop");
+    False/0: off."""
+    _check(lib().vrs_profile_enable(int(on)))
 
 
 def profile_reset():
