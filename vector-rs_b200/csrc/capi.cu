@@ -1247,14 +1247,16 @@ struct KmShard {
   // tensor-core assignment operands
   bool use_tc = false;
   DBuf xb, xq, xtiny, cb, cn, cmax, res, cands, err, ctiny;
-  DBuf flags;  // points for the full exact scan: [count, indices...]
+  DBuf flags;  // finalize lists: [count F, count M, F indices (n), M indices (n)]
   DBuf segws;  // counting-sort workspace of the centroid sums
   HBuf hstat;  // pinned: {assignment error word, max centroid shift} per iteration
+  DBuf cent_prev;        // centroids the latest assignment was made against
+  bool last_tc = false;  // the latest assignment took the tensor-core path
   ~KmShard() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     for (DBuf* b : {&x, &xr, &x_aux, &assign, &dist, &acc, &cent, &cent_r, &cent_aux, &shift, &scal, &red, &xb,
-                    &xq, &xtiny, &cb, &cn, &cmax, &res, &cands, &err, &ctiny, &segws, &flags})
+                    &xq, &xtiny, &cb, &cn, &cmax, &res, &cands, &err, &ctiny, &segws, &flags, &cent_prev})
       b->release();
     hstat.release();
     if (stream) cudaStreamDestroy(stream);
@@ -1315,7 +1317,7 @@ int km_prepare_shard(const KmParams& P, KmShard* s, const float* rows, int mem) 
     VRS_TRY(s->ctiny.reserve(sizeof(int)));
     VRS_TRY(s->res.reserve(nx * 2 * sizeof(kmtc::Res)));
     VRS_TRY(s->cands.reserve(nx * 2 * 8 * sizeof(Cand)));
-    VRS_TRY(s->flags.reserve((nx + 1) * sizeof(int)));
+    VRS_TRY(s->flags.reserve((2 * nx + 2) * sizeof(int)));
     VRS_TRY(s->err.reserve(sizeof(int)));
     VRS_CUDA(cudaMemsetAsync(s->cn.p, 0, (size_t)kpad * sizeof(float), s->stream));
     s->use_tc = true;  // point operands are prepared in km_run, once the global max |x| is known
@@ -1387,6 +1389,11 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
   // The Lloyd loop proper (upload, operand prep and initial centroids are
   // outside it), timed on shard 0's stream as profile name "kmeans_loop".
   VRS_CUDA(cudaSetDevice(shards[0]->device));
+  for (KmShard* s : shards)
+    if (s->use_tc) {
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_TRY(s->cent_prev.reserve((size_t)P.k * P.dp * sizeof(float)));
+    }
   ProfToken tloop = prof_begin("kmeans_loop", shards[0]->stream);
   for (int it = 0; it < P.max_iters; it++) {
     iters = it + 1;
@@ -1436,6 +1443,7 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
           tc_done = true;
         }
       }
+      s->last_tc = tc_done;
       if (!tc_done) {
         ProfToken t = prof_begin("kmeans_assign", s->stream);
         VRS_TRY(launch_kmeans_assign_exact(x_ops, s->n_local, P.d, P.dp, cent_ops, s->cent_aux.as<float>(),
@@ -1461,6 +1469,13 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
     for (KmShard* s : shards) {
       VRS_CUDA(cudaSetDevice(s->device));
       unsigned long long* sums = s->acc.as<unsigned long long>();
+      if (s->last_tc) {
+        // The tensor-core finalize leaves single-candidate points without
+        // an exact distance; keep the centroids they were assigned against
+        // for the inertia pass after the loop.
+        VRS_CUDA(cudaMemcpyAsync(s->cent_prev.p, s->cent.p, (size_t)P.k * P.dp * sizeof(float),
+                                 cudaMemcpyDeviceToDevice, s->stream));
+      }
       ProfToken t = prof_begin("kmeans_update", s->stream);
       VRS_TRY(launch_kmeans_update(sums, sums + (size_t)P.k * P.dp, P.k, P.d, P.dp, scale_exp,
                                    s->cent.as<float>(), s->shift.as<float>(), s->scal.as<float>() + 1,
@@ -1501,6 +1516,10 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
     std::vector<double> parts;
     for (KmShard* s : shards) {
       VRS_CUDA(cudaSetDevice(s->device));
+      if (s->last_tc)
+        VRS_TRY(kmtc::fill_dist(s->x.as<float>(), s->n_local, P.d, P.dp, s->cent_prev.as<float>(),
+                                s->cent_aux.as<float>(), s->x_aux.as<float>(), P.metric, s->assign.as<int32_t>(),
+                                s->dist.as<float>(), s->stream));
       VRS_TRY(launch_sum_f64(s->dist.as<float>(), s->n_local, s->red.as<double>(), s->stream));
     }
     if (P.rank_mode && coll) {

@@ -355,68 +355,122 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-// Exact argmin among each point's candidates (all K centroids when flagged),
-// in the reference's pair arithmetic; writes assignment and exact distance.
-// One half-warp per point: its 16 lanes are the reference's 16 SIMD lanes.
+// Finalize, step 1 (one thread per point): the bound from the point's two
+// records. The exact nearest centroid c* is always within it: its
+// approximate score is at most exact(c*) + e <= exact(best approximate) + e
+// <= best approximate + 2e < bound, and it was kept unless a full buffer
+// pushed out something within the bound. So
+//  * a candidate pushed out within the bound (or a near-zero cosine point)
+//    -> list F (flags[0] = count, indices from flags + 2): all K centroids
+//    scored exactly;
+//  * exactly one candidate within the bound -> it is c*: assigned here, no
+//    exact distance (kmeans_dist_kernel fills distances in after the loop);
+//  * several -> list M (flags[1] = count, indices from flags + 2 + n):
+//    scored exactly by kmeans_multi_kernel.
 template <int METRIC>
-__global__ void __launch_bounds__(128) kmeans_finalize_kernel(
+__global__ void __launch_bounds__(256) kmeans_triage_kernel(
+    int64_t n, int d, const float* __restrict__ xq, const unsigned int* __restrict__ cmax,
+    const Res* __restrict__ res, const Cand* __restrict__ cands, const int* __restrict__ force_full,
+    int32_t* __restrict__ assign, int* __restrict__ flags, float inv_scale) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
+  const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax), inv_scale);
+  const float bound = __fadd_ru(fminf(r0.best, r1.best), absm);
+  if (r0.lost <= bound || r1.lost <= bound || (force_full && force_full[i])) {
+    flags[2 + atomicAdd(&flags[0], 1)] = (int)i;
+    return;
+  }
+  int nin = 0;
+  uint32_t only = 0;
+  for (int h = 0; h < 2; h++) {
+    const Res r = h ? r1 : r0;
+    for (int e = 0; e < r.cnt; e++) {
+      const Cand ce = cands[(i * 2 + h) * NCAND + e];
+      if (ce.hs <= bound) {
+        nin++;
+        only = ce.id;
+      }
+    }
+  }
+  if (nin == 1)
+    assign[i] = (int)only;
+  else
+    flags[2 + n + atomicAdd(&flags[1], 1)] = (int)i;
+}
+
+// Finalize, step 2: the points of list M, one half-warp per point (its 16
+// lanes are the reference's 16 SIMD lanes), striding over the list: exact
+// argmin among the candidates within the bound (lowest index on ties), with
+// the exact distance.
+template <int METRIC>
+__global__ void __launch_bounds__(128) kmeans_multi_kernel(
     const float* __restrict__ x, int64_t n, int d, int dp, const float* __restrict__ cent,
-    const float* __restrict__ cent_aux, const float* __restrict__ x_aux, int k,
-    const float* __restrict__ xq, const unsigned int* __restrict__ cmax, const Res* __restrict__ res,
-    const Cand* __restrict__ cands, const int* __restrict__ force_full, int32_t* __restrict__ assign,
-    float* __restrict__ dist, int* __restrict__ flags, float inv_scale) {
+    const float* __restrict__ cent_aux, const float* __restrict__ x_aux, const float* __restrict__ xq,
+    const unsigned int* __restrict__ cmax, const Res* __restrict__ res, const Cand* __restrict__ cands,
+    const int* __restrict__ flags, int32_t* __restrict__ assign, float* __restrict__ dist, float inv_scale) {
+  const int hl = threadIdx.x & 15;
+  const unsigned mask = 0xffffu << (threadIdx.x & 16);
+  const bool hib = vrs_exact::higher_is_better(METRIC);
+  const int count = flags[1];
+  const int* list = flags + 2 + n;
+  const int64_t nhw = ((int64_t)gridDim.x * blockDim.x) >> 4;
+  for (int64_t f = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4; f < count; f += nhw) {
+    const int64_t i = list[f];
+    const float* v = x + i * dp;
+    const float va = METRIC == vrs_exact::kCos ? x_aux[i] : 0.0f;
+    const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
+    const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax), inv_scale);
+    const float bound = __fadd_ru(fminf(r0.best, r1.best), absm);
+    int best = 0x7fffffff;
+    float best_key = hib ? -INFINITY : INFINITY;
+    for (int h = 0; h < 2; h++) {
+      const Res r = h ? r1 : r0;
+      for (int e = 0; e < r.cnt; e++) {
+        const Cand ce = cands[(i * 2 + h) * NCAND + e];
+        if (!(ce.hs <= bound)) continue;
+        const uint32_t c = ce.id;
+        const float ca = METRIC == vrs_exact::kCos ? cent_aux[c] : 0.0f;
+        const float key = vrs_exact::lanes::rank_key(METRIC, v, cent + (int64_t)c * dp, d, va, ca, hl, mask);
+        const bool better = hib ? (key > best_key || (key == best_key && (int)c < best))
+                                : (key < best_key || (key == best_key && (int)c < best));
+        if (better) {
+          best_key = key;
+          best = (int)c;
+        }
+      }
+    }
+    if (hl == 0) {
+      assign[i] = best;
+      dist[i] = vrs_exact::finish(METRIC, best_key);
+    }
+  }
+}
+
+// Exact distance of every point to its assigned centroid, in the reference's
+// pair arithmetic (one half-warp per point), for the inertia of the last
+// assignment step.
+template <int METRIC>
+__global__ void __launch_bounds__(128) kmeans_dist_kernel(const float* __restrict__ x, int64_t n, int d, int dp,
+                                                          const float* __restrict__ cent,
+                                                          const float* __restrict__ cent_aux,
+                                                          const float* __restrict__ x_aux,
+                                                          const int32_t* __restrict__ assign,
+                                                          float* __restrict__ dist) {
   const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 4;
   if (i >= n) return;  // whole half-warps leave together
   const int hl = threadIdx.x & 15;
   const unsigned mask = 0xffffu << (threadIdx.x & 16);
-  const float* v = x + i * dp;
-  // The point's row (HBM) is pulled into L1 while its records and first
-  // candidates load; the exact re-scoring below then reads it from L1.
-  if (hl * 32 < dp) asm volatile("prefetch.global.L1 [%0];" ::"l"(v + hl * 32));
+  const int c = assign[i];
   const float va = METRIC == vrs_exact::kCos ? x_aux[i] : 0.0f;
-  const bool hib = vrs_exact::higher_is_better(METRIC);
-  const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
-  const Cand first0 = cands[(i * 2) * NCAND], first1 = cands[(i * 2 + 1) * NCAND];
-  int best = 0x7fffffff;
-  float best_key = hib ? -INFINITY : INFINITY;
-  auto consider = [&](uint32_t c) {
-    const float ca = METRIC == vrs_exact::kCos ? cent_aux[c] : 0.0f;
-    const float key =
-        vrs_exact::lanes::rank_key(METRIC, v, cent + (int64_t)c * dp, d, va, ca, hl, mask);
-    const bool better = hib ? (key > best_key || (key == best_key && (int)c < best))
-                            : (key < best_key || (key == best_key && (int)c < best));
-    if (better) {
-      best_key = key;
-      best = (int)c;
-    }
-  };
-  const float bapprox = fminf(r0.best, r1.best);
-  const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax), inv_scale);
-  const float bound = __fadd_ru(bapprox, absm);
-  // A candidate that was pushed out of a full buffer only matters if it is
-  // still within the final bound; then every centroid must be checked
-  // exactly: the point goes to the flagged list (flags[0] = count), which
-  // kmeans_flagged_kernel scans with a whole CTA per point.
-  if (r0.lost <= bound || r1.lost <= bound || (force_full && force_full[i])) {
-    if (hl == 0) flags[1 + atomicAdd(&flags[0], 1)] = (int)i;
-    return;
-  } else {
-    for (int h = 0; h < 2; h++) {
-      const Res r = h ? r1 : r0;
-      for (int e = 0; e < r.cnt; e++) {
-        const Cand ce = e == 0 ? (h ? first1 : first0) : cands[(i * 2 + h) * NCAND + e];
-        if (ce.hs <= bound) consider(ce.id);
-      }
-    }
-  }
-  if (hl == 0) {
-    assign[i] = best;
-    dist[i] = vrs_exact::finish(METRIC, best_key);
-  }
+  const float ca = METRIC == vrs_exact::kCos ? cent_aux[c] : 0.0f;
+  const float key =
+      vrs_exact::lanes::rank_key(METRIC, x + i * dp, cent + (int64_t)c * dp, d, va, ca, hl, mask);
+  if (hl == 0) dist[i] = vrs_exact::finish(METRIC, key);
 }
 
-// Exact assignment of the flagged points (flags[0] of them, indices in
-// flags[1..]): one CTA per point, its 16 half-warps split the centroids
+// Exact assignment of the flagged points (list F: flags[0] of them, indices
+// from flags + 2): one CTA per point, its 16 half-warps split the centroids
 // (half-warp h takes c = h, h + 16, ...), then the CTA keeps the best key,
 // lowest centroid index on ties (kmeans.rs:361-407).
 template <int METRIC>
@@ -431,7 +485,7 @@ __global__ void __launch_bounds__(256) kmeans_flagged_kernel(
   const bool hib = vrs_exact::higher_is_better(METRIC);
   const int count = flags[0];
   for (int f = blockIdx.x; f < count; f += gridDim.x) {
-    const int64_t i = flags[1 + f];
+    const int64_t i = flags[2 + f];
     const float* v = x + i * dp;
     const float va = METRIC == vrs_exact::kCos ? x_aux[i] : 0.0f;
     int best = 0x7fffffff;
@@ -549,14 +603,17 @@ int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, co
                  const float* x_aux, int k, const float* xq, const unsigned int* cmax, const Res* res,
                  const Cand* cands, const int* force_full, int32_t* assign, float* dist, int* flags,
                  int num_sms, float inv_scale, cudaStream_t s) {
-  VRS_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), s));
-  kmeans_finalize_kernel<M><<<(unsigned)((n * 16 + 127) / 128), 128, 0, s>>>(
-      x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full, assign, dist, flags, inv_scale);
+  VRS_CUDA(cudaMemsetAsync(flags, 0, 2 * sizeof(int), s));
+  kmeans_triage_kernel<M><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, d, xq, cmax, res, cands, force_full,
+                                                                        assign, flags, inv_scale);
+  VRS_CUDA(cudaGetLastError());
+  kmeans_multi_kernel<M><<<(unsigned)(num_sms * 8), 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, xq, cmax,
+                                                                 res, cands, flags, assign, dist, inv_scale);
   VRS_CUDA(cudaGetLastError());
   kmeans_flagged_kernel<M><<<(unsigned)(num_sms * 8), 256, 0, s>>>(x, d, dp, cent, cent_aux, x_aux, k, flags,
                                                                    assign, dist);
   VRS_CUDA(cudaGetLastError());
-  count_launch(2);
+  count_launch(3);
   return VRS_OK;
 }
 
@@ -633,6 +690,32 @@ int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const 
   }
   set_error(VRS_ERR_INVALID_CONFIG, "k-means tensor-core finalize: unsupported metric");
   return VRS_ERR_INVALID_CONFIG;
+}
+
+int fill_dist(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
+              const float* x_aux, int metric, const int32_t* assign, float* dist, cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  const unsigned blocks = (unsigned)((n * 16 + 127) / 128);
+  switch (metric) {
+    case vrs_exact::kL2:
+      kmeans_dist_kernel<vrs_exact::kL2><<<blocks, 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, assign, dist);
+      break;
+    case vrs_exact::kMaha:
+      kmeans_dist_kernel<vrs_exact::kMaha><<<blocks, 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, assign, dist);
+      break;
+    case vrs_exact::kDot:
+      kmeans_dist_kernel<vrs_exact::kDot><<<blocks, 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, assign, dist);
+      break;
+    case vrs_exact::kCos:
+      kmeans_dist_kernel<vrs_exact::kCos><<<blocks, 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, assign, dist);
+      break;
+    default:
+      set_error(VRS_ERR_INVALID_CONFIG, "k-means distance fill: unsupported metric");
+      return VRS_ERR_INVALID_CONFIG;
+  }
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
 }
 
 }  // namespace kmtc

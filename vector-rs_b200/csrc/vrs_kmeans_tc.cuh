@@ -27,13 +27,19 @@ int prep_rows(const float* x, int64_t n, int d, int dp, int metric, float op_sca
 int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
            const unsigned int* cmax, int metric, float op_scale, Res* res, Cand* cands, int* err, int num_sms,
            cudaStream_t s);
-// Exact assignment from the candidates; points whose candidates may be
-// incomplete go to `flags` (flags[0] = count, then indices; n + 1 ints) and
-// are assigned by a full exact scan, one CTA per point.
+// Exact assignment from the candidates (flags: 2 n + 2 ints of scratch).
+// Points whose candidates may be incomplete are assigned by a full exact
+// scan, one CTA per point; points with several candidates within their
+// bound by exact scoring of those; a point with a single candidate within
+// its bound takes it and gets no exact distance here (fill_dist).
 int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
              const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
              const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
              float op_scale, cudaStream_t s);
+// dist[i] = exact distance of point i to centroid assign[i] (the centroids
+// the assignment was made against), in the reference's arithmetic.
+int fill_dist(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
+              const float* x_aux, int metric, const int32_t* assign, float* dist, cudaStream_t s);
 
 }  // namespace kmtc
 }  // namespace vrs
