@@ -105,3 +105,23 @@ def test_operand_scale_extremes(vc, orc, gpu, metric, scale):
     res = vc.CudaKMeansEngine.new().fit(x, 24, K, 5, 0.0, vc.DistanceMetric(metric), init=init)
     c_o, a_o, it_o, in_o = orc.kmeans_fit(x, K, init, 5, 0.0, metric)
     _check(res, c_o, a_o, it_o, in_o)
+
+
+@pytest.mark.parametrize("metric", [L2, COS, DOT])
+def test_duplicate_centroids_exact_ties(vc, orc, gpu, metric):
+    """Initial centroids with exact duplicates: every point near a duplicated
+    pair has two candidates with equal exact scores inside its bound, so the
+    multi-candidate exact pass must pick the lower index (kmeans.rs:361-407,
+    strict comparison); points with a single in-bound candidate are assigned
+    without being re-scored, and the inertia still comes from exact
+    distances."""
+    x = _mixture(vc, 30000, 48, 96, 0.1, 40 + metric)
+    K = 96
+    init = np.array(x[:K])
+    init[1::2] = init[0::2]  # pairs (0,1), (2,3), ... coincide
+    res = vc.CudaKMeansEngine.new().fit(x, 48, K, 6, 0.0, vc.DistanceMetric(metric), init=init)
+    c_o, a_o, it_o, in_o = orc.kmeans_fit(x, K, init, 6, 0.0, metric)
+    agree = _check(res, c_o, a_o, it_o, in_o)
+    if metric == L2:
+        assert agree == 1.0
+        assert abs(res.inertia - in_o) <= 1e-6 * abs(in_o)
