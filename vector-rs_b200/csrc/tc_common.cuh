@@ -1,8 +1,8 @@
 // tc_common.cuh -- thin wrappers over the sm_100a PTX used by the
 // tensor-core kernels: mbarriers (every wait bounded), TMA tile loads
 // without multicast, tcgen05 TMEM allocation / MMA / commit / load, and
-// the shared-memory matrix descriptor for K-major 128-byte-swizzled bf16
-// tiles (the layout a SWIZZLE_128B TMA box writes).
+// the shared-memory matrix descriptor for K-major 128-byte-swizzled 16-bit
+// (fp16 or bf16) tiles (the layout a SWIZZLE_128B TMA box writes).
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
@@ -137,7 +137,8 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (bf16 in, f32 acc).
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16: 16-bit operands
+// (fp16 or bf16, as the instruction descriptor says), f32 accumulate.
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
   asm volatile(

@@ -17,7 +17,7 @@ struct Res {
 };
 
 bool supported(int metric, int d);
-// bf16 operand rows, |row|^2 (sq, nullable), |row| (nrm, nullable), max |row|
+// fp16 operand rows, |row|^2 (sq, nullable), |row| (nrm, nullable), max |row|
 // (maxn, nullable), near-zero cosine flags (nullable).
 // Operands are fp16 of value * op_scale (a power of two putting the largest
 // element of points and centroids in [2^13, 2^14); 1 for cosine, whose rows
