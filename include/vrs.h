@@ -124,6 +124,32 @@ VRS_API int vrs_kmeans_fit(const float* x, int64_t n, int32_t d, int32_t k, cons
                    float* out_centroids, int32_t* out_assign, int32_t* out_k, int32_t* out_iters,
                    double* out_inertia);
 
+/* ------------------------------------------- IVF coarse quantiser probing */
+/* Both take a vrs_knn handle created over the K coarse centroids (K x d,
+ * vrs_knn_create with the index's metric) and run one batched kNN search;
+ * scores are the metric's raw values (similarities not negated) in the
+ * AVX-512 DistanceEngine's arithmetic, indices are centroid rows. */
+
+/* Replaces KMeans::find_top_centroids (crates/vector-index/src/ivf/kmeans.rs:312-356),
+ * batched over nq queries as IvfPqIndex::search calls it per query
+ * (crates/vector-index/src/ivf/mod.rs:277-284). Writes P = min(nprobe, K)
+ * entries per query, row stride P: out_score[nq*P], out_idx[nq*P], best
+ * first (ascending distance, descending similarity); exactly equal values
+ * keep index order, as the reference's stable sort does (kmeans.rs:345-350).
+ * nprobe == 0 or K == 0 -> *out_p = 0. P > 2048 is rejected. */
+VRS_API int vrs_ivf_find_top_centroids(vrs_knn* centroids, const float* queries, int64_t nq,
+                                       int32_t nprobe, float* out_score, int64_t* out_idx,
+                                       int32_t* out_p);
+
+/* Replaces KMeans::find_nearest_centroid (kmeans.rs:264-309) over n vectors,
+ * as IvfPqIndex::build calls it per base vector (mod.rs:119-125, 203-210):
+ * out_idx[n] the nearest centroid (lowest index among equal best values, the
+ * reference's strict comparison, kmeans.rs:297-305), out_score[n] (nullable)
+ * its value. K == 0 -> index 0 and +inf (-inf for dot/cosine), the initial
+ * values of the reference's loop (kmeans.rs:272-277). */
+VRS_API int vrs_ivf_assign(vrs_knn* centroids, const float* x, int64_t n, int64_t* out_idx,
+                           float* out_score);
+
 /* ---------------------------------------- one process per GPU (rank mode) */
 /* The multi-process form of the engines above: each process drives one GPU
  * and owns one row shard; the ranks exchange through NCCL. Replaces the

@@ -157,3 +157,61 @@ def kmeans_update(sums, counts, centroids):
     assert centroids.dtype == np.float32 and centroids.flags.c_contiguous
     kk, d = centroids.shape
     return float(lib().orc_kmeans_update(sums.ctypes.data, counts.ctypes.data, kk, d, centroids))
+
+
+# ---------------------------------------------------------------------------
+# IVF coarse quantiser: KMeans::find_nearest_centroid / find_top_centroids
+# (crates/vector-index/src/ivf/kmeans.rs:264-356), pair values from the same
+# AVX-512 restatement as everything above.
+# ---------------------------------------------------------------------------
+
+HIGHER_IS_BETTER = (1, 2)  # DotProduct, CosineSimilarity (crates/vector-index/src/lib.rs:89-94)
+
+
+def find_nearest_centroid(vector, centroids, metric: int):
+    """kmeans.rs:264-309, literally: start from (0, +inf) (-inf for
+    similarities), walk the centroids in order, replace on a strict
+    improvement only."""
+    centroids = _f32(centroids)
+    hib = metric in HIGHER_IS_BETTER
+    best_idx, best = 0, (-np.inf if hib else np.inf)
+    for c in range(centroids.shape[0]):
+        v = distance(metric, vector, centroids[c])
+        if (v > best) if hib else (v < best):
+            best_idx, best = c, v
+    return best_idx, np.float32(best)
+
+
+def find_top_centroids(query, centroids, nprobe: int, metric: int):
+    """kmeans.rs:312-356, literally: score every centroid in index order,
+    stable sort by score (descending for similarities), keep min(nprobe, K)."""
+    centroids = _f32(centroids)
+    target = min(nprobe, centroids.shape[0])
+    if target == 0:
+        return []
+    scored = [(c, distance(metric, query, centroids[c])) for c in range(centroids.shape[0])]
+    scored.sort(key=lambda t: t[1], reverse=metric in HIGHER_IS_BETTER)  # stable both ways
+    return [(c, np.float32(v)) for c, v in scored[:target]]
+
+
+def find_top_centroids_batch(queries, centroids, nprobe: int, metric: int,
+                             nthreads: int | None = None):
+    """The same result for many queries at once: every centroid scored by the
+    batch kNN restatement (k = K, all reported values), then each row
+    ordered by (value, index) -- the stable sort of kmeans.rs:345-350 -- and
+    cut to min(nprobe, K). Returns (scores[nq, P] f32, indices[nq, P] int64)."""
+    centroids, queries = _f32(centroids), _f32(queries)
+    K = centroids.shape[0]
+    nq = queries.shape[0]
+    p = min(nprobe, K)
+    if p == 0 or nq == 0:
+        return np.zeros((nq, 0), np.float32), np.zeros((nq, 0), np.int64)
+    dist, ids = knn_search(centroids, queries, K, metric, nthreads)
+    sign = -1.0 if metric in HIGHER_IS_BETTER else 1.0
+    out_s = np.empty((nq, p), np.float32)
+    out_i = np.empty((nq, p), np.int64)
+    for r in range(nq):
+        order = np.lexsort((ids[r].astype(np.int64), sign * dist[r].astype(np.float64)))[:p]
+        out_s[r] = dist[r][order]
+        out_i[r] = ids[r][order]
+    return out_s, out_i

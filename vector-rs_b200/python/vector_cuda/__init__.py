@@ -147,6 +147,9 @@ def lib() -> ctypes.CDLL:
                                           c.c_int32, c.c_void_p, c.c_int32, c.c_float, c.c_int32,
                                           c.c_int32, c.c_void_p, c.c_void_p, P(c.c_int32),
                                           P(c.c_int32), P(c.c_double)]
+        L.vrs_ivf_find_top_centroids.argtypes = [c.c_void_p, c.c_void_p, c.c_int64, c.c_int32,
+                                                 c.c_void_p, c.c_void_p, P(c.c_int32)]
+        L.vrs_ivf_assign.argtypes = [c.c_void_p, c.c_void_p, c.c_int64, c.c_void_p, c.c_void_p]
         L.vrs_knn_set_stream.argtypes = [c.c_void_p, c.c_void_p]
         L.vrs_profile_enable.argtypes = [c.c_int32]
         L.vrs_profile_read.argtypes = [c.c_char_p, P(c.c_double), P(c.c_int64)]
@@ -405,6 +408,88 @@ class CudaKMeansEngine(DistributedKMeansEngine):
     @classmethod
     def new(cls) -> "CudaKMeansEngine":
         return cls()
+
+
+# ------------------------------------------------ IVF coarse quantiser
+
+
+class CoarseQuantizer:
+    """The K coarse centroids of an IVF index held on the GPU, answering the
+    two questions the reference's IvfPqIndex asks its k-means quantiser:
+    `find_top_centroids` (crates/vector-index/src/ivf/kmeans.rs:312-356, per
+    query in IvfPqIndex::search, ivf/mod.rs:277-284) and `assign`
+    (kmeans.rs:264-309 per base vector in IvfPqIndex::build, mod.rs:119-125),
+    each as one batched GPU search over the centroids."""
+
+    def __init__(self, centroids, dimension: int, metric: DistanceMetric, num_gpus: int = 1):
+        self._engine = DistributedKnnEngine.try_new(centroids, dimension, num_gpus,
+                                                    GpuShardMode.Sharded, metric)
+        self._dim = dimension
+        self.metric = DistanceMetric(metric)
+
+    @property
+    def nlist(self) -> int:
+        return self._engine.num_vectors()
+
+    def close(self):
+        self._engine.close()
+
+    def _rows(self, x) -> Tuple[np.ndarray, int]:
+        q = _f32(x).reshape(-1)
+        if q.size % self._dim:
+            raise ValueError("input length must be a multiple of dimension")
+        return q, q.size // self._dim
+
+    def find_top_centroids(self, queries, nprobe: int) -> Tuple[np.ndarray, np.ndarray]:
+        """(scores[nq, P] f32, indices[nq, P] int64), P = min(nprobe, K),
+        best first; equal scores keep index order."""
+        q, nq = self._rows(queries)
+        if nprobe < 0:
+            raise ValueError("nprobe must be non-negative")
+        cap = max(nq * min(nprobe, self.nlist), 1)
+        sc = np.empty(cap, np.float32)
+        ix = np.empty(cap, np.int64)
+        p = ctypes.c_int32(0)
+        _check(lib().vrs_ivf_find_top_centroids(self._engine._h, _ptr(q), nq, int(nprobe),
+                                                _ptr(sc), _ptr(ix), ctypes.byref(p)))
+        p = p.value
+        return sc[:nq * p].reshape(nq, p), ix[:nq * p].reshape(nq, p)
+
+    def assign(self, x) -> Tuple[np.ndarray, np.ndarray]:
+        """(indices[n] int64, scores[n] f32): the nearest centroid of each row."""
+        q, n = self._rows(x)
+        ix = np.empty(max(n, 1), np.int64)
+        sc = np.empty(max(n, 1), np.float32)
+        _check(lib().vrs_ivf_assign(self._engine._h, _ptr(q), n, _ptr(ix), _ptr(sc)))
+        return ix[:n], sc[:n]
+
+
+class KMeans:
+    """The reference's single-vector helpers (crates/vector-index/src/ivf/kmeans.rs),
+    answered on the GPU. Each call uploads the centroids; hold a
+    CoarseQuantizer to probe or assign many vectors against the same ones."""
+
+    @staticmethod
+    def find_nearest_centroid(vector, centroids, dimension: int,
+                              metric: DistanceMetric) -> Tuple[int, float]:
+        """kmeans.rs:264-309."""
+        cq = CoarseQuantizer(centroids, dimension, metric)
+        try:
+            ix, sc = cq.assign(vector)
+            return int(ix[0]), float(sc[0])
+        finally:
+            cq.close()
+
+    @staticmethod
+    def find_top_centroids(query, centroids, dimension: int, nprobe: int,
+                           metric: DistanceMetric) -> List[Tuple[int, float]]:
+        """kmeans.rs:312-356."""
+        cq = CoarseQuantizer(centroids, dimension, metric)
+        try:
+            sc, ix = cq.find_top_centroids(query, nprobe)
+            return [(int(i), float(s)) for i, s in zip(ix[0], sc[0])] if len(sc) else []
+        finally:
+            cq.close()
 
 
 # ---------------------------------------------------- rank mode (NCCL)
