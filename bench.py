@@ -91,6 +91,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--ivf", action="store_true",
                     help="IVF coarse probe/assign line only (1 GPU; not part of the default run)")
+    ap.add_argument("--storage", action="store_true",
+                    help="VECRSTOR file -> GPU engine load line only (1 GPU; not part of the default run)")
     ap.add_argument("--n-base", type=int, default=None, help="override the workload's base rows")
     ap.add_argument("--n-query", type=int, default=None, help="override the workload's query count")
     ap.add_argument("--km-n", type=int, default=None, help="override the k-means point count")
@@ -313,6 +315,9 @@ def main():
     line = None
     if args.ivf:
         line = ivf_bench(args, vc, torch, dev, peak_tc) if rank == 0 else None
+        args.no_knn = args.no_kmeans = True
+    if args.storage:
+        line = storage_bench(args, vc, torch, dev, pk) if rank == 0 else None
         args.no_knn = args.no_kmeans = True
     if not args.no_knn:
         line = knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, max_over_ranks,
@@ -639,6 +644,45 @@ def ivf_bench(args, vc, torch, dev, peak_tc):
         "clocks": clk.summary(),
         "gpu_launches": sum(v["launches"] for v in stages.values()),
     }
+
+
+def storage_bench(args, vc, torch, dev, pk):
+    """Loading a base from a VECRSTOR file (crates/vector-index/src/storage/mmap.rs)
+    into a one-GPU engine: vrs_knn_create_from_file (validate, map, upload
+    from the mapping) against vrs_knn_create from the same rows already in
+    host memory. The file is written first, so it is read from the page cache."""
+    import tempfile
+    N, D = args.n_base or 5_000_000, 96
+    rows = host_gen(vc, vc.GEN_NORMAL, vc.config_seed(4), 0, N, D)
+    fd, path = tempfile.mkstemp(suffix=".vecrstor", dir=os.environ.get("TMPDIR", "/tmp"))
+    os.close(fd)
+    try:
+        vc.MmapStorage.create_from_flat(path, D, rows)
+        M = vc.DistanceMetric.L2Squared
+        vc.DistributedKnnEngine.from_file(path, 1, vc.GpuShardMode.Sharded, M).close()  # warm
+        t_file, t_mem = [], []
+        for _ in range(max(args.steps, 1)):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            e = vc.DistributedKnnEngine.from_file(path, 1, vc.GpuShardMode.Sharded, M)
+            t_file.append(time.perf_counter() - t0)
+            e.close()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            e = vc.DistributedKnnEngine.try_new(rows, D, 1, vc.GpuShardMode.Sharded, M)
+            t_mem.append(time.perf_counter() - t0)
+            e.close()
+    finally:
+        os.unlink(path)
+    gb = N * D * 4 / 1e9
+    tf, tm = float(np.median(t_file)), float(np.median(t_mem))
+    return {"metric": "VECRSTOR file -> GPU engine load GB/s (rows of f32)", "value": gb / tf,
+            "unit": "GB/s", "higher_is_better": True, "n_gpus": 1, "steps": len(t_file),
+            "seconds_file": tf, "seconds_from_host_array": tm, "gb": gb,
+            "from_host_array_gbs": gb / tm, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{N} x {D} N(0,1) rows in one VECRSTOR file (page cache)",
+                       "metric": "squared L2 (norms computed at upload)"},
+            "timing": "host clock around the synchronous create call, median of steps"}
 
 
 if __name__ == "__main__":

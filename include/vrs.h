@@ -37,7 +37,9 @@ typedef enum vrs_status {
   VRS_ERR_INVALID_CONFIG = 5,       /* CudaError::InvalidConfig (error.rs:27-29) */
   VRS_ERR_NCCL = 6,                 /* NCCL failure (no reference counterpart: it has no NCCL) */
   VRS_ERR_TIMEOUT = 7,              /* a bounded device or collective wait gave up */
-  VRS_ERR_OOM = 8                   /* device allocation failed */
+  VRS_ERR_OOM = 8,                  /* device allocation failed */
+  VRS_ERR_INVALID_FILE = 9          /* VECRSTOR file: VectorIndexError::{Io, InvalidHeader,
+                                       FileSizeMismatch}, crates/vector-index/src/types.rs:60-85 */
 } vrs_status;
 
 /* DistanceMetric codes: the reference's launch codes,
@@ -149,6 +151,27 @@ VRS_API int vrs_ivf_find_top_centroids(vrs_knn* centroids, const float* queries,
  * values of the reference's loop (kmeans.rs:272-277). */
 VRS_API int vrs_ivf_assign(vrs_knn* centroids, const float* x, int64_t n, int64_t* out_idx,
                            float* out_score);
+
+/* --------------------------------------------------- VECRSTOR vector files */
+/* Format of crates/vector-index/src/storage/mmap.rs:7-16: three little-endian
+ * u64 (magic 0x5645435253544F52 "VECRSTOR", N, D), then N x D f32 rows. */
+
+/* The header checks of MmapStorage::open (mmap.rs:171-223): shorter than 24
+ * bytes or another magic -> VRS_ERR_INVALID_FILE (InvalidHeader); shorter
+ * than 24 + N*D*4 bytes -> VRS_ERR_INVALID_FILE (FileSizeMismatch); longer
+ * files are accepted. Writes N and D. */
+VRS_API int vrs_vecrstor_info(const char* path, int64_t* num_vectors, int64_t* dimension);
+
+/* MmapStorage::create_from_flat (mmap.rs:131-160): header + n x d rows. */
+VRS_API int vrs_vecrstor_write(const char* path, const float* data, int64_t n, int64_t d);
+
+/* vrs_knn_create over the rows of a VECRSTOR file, in place of
+ * DistributedKnnEngine::try_new(storage.as_raw_slice(), ...) with an
+ * MmapStorage: the file is validated as vrs_vecrstor_info does, mapped
+ * read-only and each GPU's row range is uploaded from the mapping (no host
+ * copy of the base). D must be in 1..2^31-1. */
+VRS_API int vrs_knn_create_from_file(const char* path, int32_t num_gpus, int32_t mode,
+                                     int32_t metric, vrs_knn** out);
 
 /* ---------------------------------------- one process per GPU (rank mode) */
 /* The multi-process form of the engines above: each process drives one GPU

@@ -62,6 +62,7 @@ _STATUS_NAMES = {
     6: "NcclError",
     7: "Timeout",
     8: "OutOfMemory",
+    9: "InvalidFile",
 }
 
 
@@ -150,6 +151,10 @@ def lib() -> ctypes.CDLL:
         L.vrs_ivf_find_top_centroids.argtypes = [c.c_void_p, c.c_void_p, c.c_int64, c.c_int32,
                                                  c.c_void_p, c.c_void_p, P(c.c_int32)]
         L.vrs_ivf_assign.argtypes = [c.c_void_p, c.c_void_p, c.c_int64, c.c_void_p, c.c_void_p]
+        L.vrs_vecrstor_info.argtypes = [c.c_char_p, P(c.c_int64), P(c.c_int64)]
+        L.vrs_vecrstor_write.argtypes = [c.c_char_p, c.c_void_p, c.c_int64, c.c_int64]
+        L.vrs_knn_create_from_file.argtypes = [c.c_char_p, c.c_int32, c.c_int32, c.c_int32,
+                                               P(c.c_void_p)]
         L.vrs_knn_set_stream.argtypes = [c.c_void_p, c.c_void_p]
         L.vrs_profile_enable.argtypes = [c.c_int32]
         L.vrs_profile_read.argtypes = [c.c_char_p, P(c.c_double), P(c.c_int64)]
@@ -227,6 +232,25 @@ class DistributedKnnEngine:
         return cls(h, dimension)
 
     new = try_new
+
+    @classmethod
+    def from_file(cls, path, num_gpus: int, mode: GpuShardMode,
+                  metric: DistanceMetric) -> "DistributedKnnEngine":
+        """try_new over an MmapStorage's rows (crates/vector-index/src/storage/mmap.rs):
+        the VECRSTOR file is validated, mapped and uploaded shard by shard
+        with no host copy of the base."""
+        if num_gpus < 1:
+            raise ValueError("num_gpus must be at least 1")
+        h = ctypes.c_void_p()
+        st = lib().vrs_knn_create_from_file(os.fsencode(path), num_gpus, int(mode), int(metric),
+                                            ctypes.byref(h))
+        fields = {}
+        if st == 1:
+            fields = {"requested": num_gpus, "available": CudaDeviceContext.device_count()}
+        _check(st, **fields)
+        d = ctypes.c_int32(0)
+        _check(lib().vrs_knn_info(h, None, ctypes.byref(d), None, None, None))
+        return cls(h, d.value)
 
     @classmethod
     def create_rank(cls, comm: "Comm", shard, dimension: int, global_offset: int, n_global: int,
@@ -408,6 +432,75 @@ class CudaKMeansEngine(DistributedKMeansEngine):
     @classmethod
     def new(cls) -> "CudaKMeansEngine":
         return cls()
+
+
+# ------------------------------------------------- VECRSTOR vector files
+
+
+class MmapStorage:
+    """crates/vector-index/src/storage/mmap.rs: read-only VECRSTOR vectors.
+    The header is validated by libvrs (vrs_vecrstor_info, the checks of
+    MmapStorage::open); the rows are a numpy memmap, so nothing is copied."""
+
+    HEADER_SIZE = 24
+
+    def __init__(self, path, num_vectors: int, dimension: int):
+        self.path = os.fspath(path)
+        self._n = num_vectors
+        self._d = dimension
+        self._rows = (np.memmap(self.path, np.dtype("<f4"), "r", self.HEADER_SIZE,
+                                (num_vectors, dimension)) if num_vectors * dimension
+                      else np.zeros((num_vectors, dimension), np.float32))
+
+    @classmethod
+    def open(cls, path) -> "MmapStorage":
+        """mmap.rs:171-223."""
+        n, d = ctypes.c_int64(0), ctypes.c_int64(0)
+        _check(lib().vrs_vecrstor_info(os.fsencode(path), ctypes.byref(n), ctypes.byref(d)))
+        return cls(path, n.value, d.value)
+
+    @staticmethod
+    def create(path, dimension: int, vectors: Sequence) -> None:
+        """mmap.rs:90-121: every vector must have `dimension` entries."""
+        for v in vectors:
+            if len(v) != dimension:
+                raise ValueError(f"dimension mismatch: expected {dimension}, got {len(v)}")
+        flat = (np.asarray(vectors, np.float32).reshape(-1) if len(vectors)
+                else np.zeros(0, np.float32))
+        MmapStorage.create_from_flat(path, dimension, flat)
+
+    @staticmethod
+    def create_from_flat(path, dimension: int, flat_data) -> None:
+        """mmap.rs:131-160."""
+        flat = _f32(flat_data).reshape(-1)
+        if dimension < 1 and flat.size:
+            raise ValueError("dimension must be positive")
+        if dimension and flat.size % dimension:
+            raise ValueError(f"dimension mismatch: expected {dimension}, got {flat.size % dimension}")
+        n = flat.size // dimension if dimension else 0
+        _check(lib().vrs_vecrstor_write(os.fsencode(path), _ptr(flat) if flat.size else None,
+                                        n, dimension))
+
+    def __len__(self) -> int:
+        return self._n
+
+    def len(self) -> int:
+        return self._n
+
+    def is_empty(self) -> bool:
+        return self._n == 0
+
+    def dimension(self) -> int:
+        return self._d
+
+    def get(self, i: int) -> np.ndarray:
+        """mmap.rs:237-249: out-of-range ids raise (the reference panics)."""
+        if not 0 <= i < self._n:
+            raise IndexError(f"vector id {i} out of bounds (len={self._n})")
+        return self._rows[i]
+
+    def as_raw_slice(self) -> np.ndarray:
+        return self._rows.reshape(-1)
 
 
 # ------------------------------------------------ IVF coarse quantiser
