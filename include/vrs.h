@@ -173,6 +173,24 @@ VRS_API int vrs_vecrstor_write(const char* path, const float* data, int64_t n, i
 VRS_API int vrs_knn_create_from_file(const char* path, int32_t num_gpus, int32_t mode,
                                      int32_t metric, vrs_knn** out);
 
+/* IvfPqSerializer::save_centroid_file (crates/vector-index/src/ivf/serializer.rs:255-307):
+ * the k-means output (e.g. out_centroids/out_k/out_iters/out_inertia of
+ * vrs_kmeans_fit) as a standalone file: packed little-endian header of 29
+ * bytes -- magic u64 "VRSKMEAN" (0x5652534B4D45414E), version u32 = 1,
+ * metric u8 (vrs_metric codes, serializer.rs:397-410), D u32, K u32,
+ * iterations u32, inertia f32 -- then K x D f32. */
+VRS_API int vrs_centroid_file_write(const char* path, const float* centroids, int64_t d, int64_t k,
+                                    int32_t metric, int64_t iterations, float inertia);
+
+/* IvfPqSerializer::load_centroid_file (serializer.rs:309-370). With
+ * out_centroids NULL only the header is read (to size the buffer); else
+ * K x D floats are read into it (capacity in floats). Wrong magic, version or
+ * metric code (serializer.rs:318-339, 413-430) and short files ->
+ * VRS_ERR_INVALID_FILE with the reference's messages. */
+VRS_API int vrs_centroid_file_read(const char* path, float* out_centroids, int64_t capacity,
+                                   int32_t* metric, int64_t* d, int64_t* k, int64_t* iterations,
+                                   float* inertia);
+
 /* ---------------------------------------- one process per GPU (rank mode) */
 /* The multi-process form of the engines above: each process drives one GPU
  * and owns one row shard; the ranks exchange through NCCL. Replaces the

@@ -147,3 +147,69 @@ def test_engine_from_file_matches_memory(vc, gpu, tmp_path, metric, mode, g):
     ee = vc.DistributedKnnEngine.from_file(e, 1, vc.GpuShardMode.Sharded, M)
     assert ee.num_vectors() == 0 and ee.search(np.zeros(8, np.float32), 5) == []
     ee.close()
+
+
+# ------------------------------------------------------------ centroid files
+# IvfPqSerializer::save_centroid_file / load_centroid_file
+# (crates/vector-index/src/ivf/serializer.rs:255-370), tests after
+# serializer.rs:552-615.
+
+def _pack_centroid_layout(centroids, d, k, metric, iters, inertia):
+    """The packed header the reference writes field by field (serializer.rs:285-302)."""
+    hdr = struct.pack("<QIBIIIf", 0x5652_534B_4D45_414E, 1, metric, d, k, iters, inertia)
+    return hdr + struct.pack(f"<{len(centroids)}f", *centroids)
+
+
+def test_centroid_file_roundtrip(vc, tmp_path):
+    p = tmp_path / "c.bin"
+    c = [1.0, 2.0, 3.0, 4.0, 5.0, 6.0, 7.0, 8.0]
+    vc.IvfPqSerializer.save_centroid_file(p, c, 4, 2, vc.DistanceMetric.L2Squared, 15, 42.5)
+    assert p.read_bytes() == _pack_centroid_layout(c, 4, 2, 0, 15, 42.5)
+    assert len(p.read_bytes()) == 29 + 32
+    ld = vc.IvfPqSerializer.load_centroid_file(p)
+    assert list(ld.centroids.ravel()) == c
+    assert (ld.dimension, ld.k, ld.metric, ld.iterations) == (4, 2, vc.DistanceMetric.L2Squared, 15)
+    assert abs(ld.inertia - 42.5) < 1e-6
+
+
+def test_centroid_file_all_metrics(vc, tmp_path):
+    p = tmp_path / "m.bin"
+    for m in vc.DistanceMetric:
+        vc.IvfPqSerializer.save_centroid_file(p, [1.0, 2.0], 2, 1, m, 1, 0.0)
+        assert vc.IvfPqSerializer.load_centroid_file(p).metric == m
+
+
+def test_centroid_file_invalid_magic(vc, tmp_path):
+    p = tmp_path / "bad.bin"
+    p.write_bytes(b"NOTCENTR12345678")
+    with pytest.raises(vc.CudaError) as e:
+        vc.IvfPqSerializer.load_centroid_file(p)
+    assert e.value.status == 9 and "expected centroid magic" in str(e.value)
+
+
+def test_centroid_file_bad_version_metric_and_truncation(vc, tmp_path):
+    good = _pack_centroid_layout([1.0, 2.0, 3.0, 4.0], 2, 2, 3, 7, 1.25)
+    p = tmp_path / "v.bin"
+    p.write_bytes(good[:8] + struct.pack("<I", 2) + good[12:])
+    with pytest.raises(vc.CudaError, match="unsupported centroid file version: 2"):
+        vc.IvfPqSerializer.load_centroid_file(p)
+    p.write_bytes(good[:12] + bytes([10]) + good[13:])
+    with pytest.raises(vc.CudaError, match="invalid metric code: 10"):
+        vc.IvfPqSerializer.load_centroid_file(p)
+    for cut in (5, 20, 29 + 6):
+        p.write_bytes(good[:cut])
+        with pytest.raises(vc.CudaError) as e:
+            vc.IvfPqSerializer.load_centroid_file(p)
+        assert e.value.status == 9
+    p.write_bytes(good)
+    ld = vc.IvfPqSerializer.load_centroid_file(p)
+    assert ld.metric == vc.DistanceMetric.Manhattan and ld.centroids.shape == (2, 2)
+
+
+def test_centroid_file_empty_and_size_check(vc, tmp_path):
+    p = tmp_path / "e.bin"
+    vc.IvfPqSerializer.save_centroid_file(p, [], 16, 0, vc.DistanceMetric.CosineSimilarity, 0, 0.0)
+    ld = vc.IvfPqSerializer.load_centroid_file(p)
+    assert ld.k == 0 and ld.dimension == 16 and ld.centroids.shape == (0, 16)
+    with pytest.raises(ValueError):
+        vc.IvfPqSerializer.save_centroid_file(p, [1.0, 2.0, 3.0], 2, 2, vc.DistanceMetric.L2Squared, 1, 0.0)

@@ -140,3 +140,100 @@ extern "C" int vrs_knn_create_from_file(const char* path, int32_t num_gpus, int3
   // The mapping lives until the engine holds its copy on the GPUs.
   return vrs_knn_create(v.data, (int64_t)v.n, (int32_t)v.d, num_gpus, mode, metric, out);
 }
+
+// ----------------------------------------------------------------------------
+// Standalone centroid file (IvfPqSerializer::save_centroid_file /
+// load_centroid_file, crates/vector-index/src/ivf/serializer.rs:255-370): the
+// output of k-means training for later IVF builds. Packed little-endian:
+// magic u64 0x5652534B4D45414E ("VRSKMEAN"), version u32 = 1, metric u8
+// (serializer.rs:397-430, the same codes as vrs_metric), dimension u32, K u32,
+// iterations u32, inertia f32, then K x D f32 (29-byte header).
+// ----------------------------------------------------------------------------
+
+namespace {
+constexpr uint64_t kCentroidMagic = 0x5652534B4D45414Eull;
+constexpr uint32_t kCentroidVersion = 1;
+constexpr size_t kCentroidHeader = 29;
+}  // namespace
+
+extern "C" int vrs_centroid_file_write(const char* path, const float* centroids, int64_t d,
+                                       int64_t k, int32_t metric, int64_t iterations,
+                                       float inertia) {
+  if (!path || d < 0 || k < 0 || iterations < 0 || d > UINT32_MAX || k > UINT32_MAX ||
+      iterations > UINT32_MAX || metric < 0 || metric > 9 || (d * k > 0 && !centroids)) {
+    vrs::set_error(VRS_ERR_INVALID_CONFIG, "vrs_centroid_file_write: bad arguments");
+    return VRS_ERR_INVALID_CONFIG;
+  }
+  unsigned char h[kCentroidHeader];
+  const uint32_t dd = (uint32_t)d, kk = (uint32_t)k, it = (uint32_t)iterations;
+  memcpy(h + 0, &kCentroidMagic, 8);
+  memcpy(h + 8, &kCentroidVersion, 4);
+  h[12] = (unsigned char)metric;
+  memcpy(h + 13, &dd, 4);
+  memcpy(h + 17, &kk, 4);
+  memcpy(h + 21, &it, 4);
+  memcpy(h + 25, &inertia, 4);
+  FILE* f = fopen(path, "wb");
+  if (!f) return file_error(std::string(path) + ": " + strerror(errno));
+  bool ok = fwrite(h, 1, sizeof(h), f) == sizeof(h);
+  const size_t total = (size_t)d * (size_t)k;
+  if (ok && total) ok = fwrite(centroids, sizeof(float), total, f) == total;
+  ok = (fclose(f) == 0) && ok;
+  if (!ok) return file_error(std::string(path) + ": write failed: " + strerror(errno));
+  return VRS_OK;
+}
+
+extern "C" int vrs_centroid_file_read(const char* path, float* out_centroids, int64_t capacity,
+                                      int32_t* metric, int64_t* d, int64_t* k, int64_t* iterations,
+                                      float* inertia) {
+  if (!path) return file_error("null path");
+  FILE* f = fopen(path, "rb");
+  if (!f) return file_error(std::string(path) + ": " + strerror(errno));
+  struct Closer {
+    FILE* f;
+    ~Closer() { fclose(f); }
+  } closer{f};
+  unsigned char h[kCentroidHeader];
+  const size_t got = fread(h, 1, sizeof(h), f);
+  uint64_t magic = 0;
+  if (got >= 8) memcpy(&magic, h, 8);
+  if (got < 8) return file_error(std::string(path) + ": unexpected end of file");
+  if (magic != kCentroidMagic) {
+    char buf[96];
+    snprintf(buf, sizeof(buf), "expected centroid magic 0x%llX, got 0x%llX",
+             (unsigned long long)kCentroidMagic, (unsigned long long)magic);
+    return file_error(std::string(path) + ": invalid header: " + buf);
+  }
+  if (got < 12) return file_error(std::string(path) + ": unexpected end of file");
+  uint32_t version;
+  memcpy(&version, h + 8, 4);
+  if (version != kCentroidVersion)
+    return file_error(std::string(path) + ": invalid header: unsupported centroid file version: " +
+                      std::to_string(version));
+  if (got < 13) return file_error(std::string(path) + ": unexpected end of file");
+  if (h[12] > 9)
+    return file_error(std::string(path) + ": invalid header: invalid metric code: " + std::to_string(h[12]));
+  if (got < sizeof(h)) return file_error(std::string(path) + ": unexpected end of file");
+  uint32_t dd, kk, it;
+  float in;
+  memcpy(&dd, h + 13, 4);
+  memcpy(&kk, h + 17, 4);
+  memcpy(&it, h + 21, 4);
+  memcpy(&in, h + 25, 4);
+  const uint64_t total = (uint64_t)dd * kk;
+  if (out_centroids) {
+    if ((uint64_t)capacity < total) {
+      vrs::set_error(VRS_ERR_INVALID_CONFIG, "vrs_centroid_file_read: capacity " + std::to_string(capacity) +
+                                                 " < K x D = " + std::to_string(total));
+      return VRS_ERR_INVALID_CONFIG;
+    }
+    if (total && fread(out_centroids, sizeof(float), (size_t)total, f) != total)
+      return file_error(std::string(path) + ": unexpected end of file");
+  }
+  if (metric) *metric = h[12];
+  if (d) *d = dd;
+  if (k) *k = kk;
+  if (iterations) *iterations = it;
+  if (inertia) *inertia = in;
+  return VRS_OK;
+}

@@ -155,6 +155,11 @@ def lib() -> ctypes.CDLL:
         L.vrs_vecrstor_write.argtypes = [c.c_char_p, c.c_void_p, c.c_int64, c.c_int64]
         L.vrs_knn_create_from_file.argtypes = [c.c_char_p, c.c_int32, c.c_int32, c.c_int32,
                                                P(c.c_void_p)]
+        L.vrs_centroid_file_write.argtypes = [c.c_char_p, c.c_void_p, c.c_int64, c.c_int64,
+                                              c.c_int32, c.c_int64, c.c_float]
+        L.vrs_centroid_file_read.argtypes = [c.c_char_p, c.c_void_p, c.c_int64, P(c.c_int32),
+                                             P(c.c_int64), P(c.c_int64), P(c.c_int64),
+                                             P(c.c_float)]
         L.vrs_knn_set_stream.argtypes = [c.c_void_p, c.c_void_p]
         L.vrs_profile_enable.argtypes = [c.c_int32]
         L.vrs_profile_read.argtypes = [c.c_char_p, P(c.c_double), P(c.c_int64)]
@@ -501,6 +506,44 @@ class MmapStorage:
 
     def as_raw_slice(self) -> np.ndarray:
         return self._rows.reshape(-1)
+
+
+@dataclass
+class CentroidFileData:
+    """crates/vector-index/src/ivf/serializer.rs:378-395."""
+
+    centroids: np.ndarray
+    dimension: int
+    k: int
+    metric: DistanceMetric
+    iterations: int
+    inertia: float
+
+
+class IvfPqSerializer:
+    """The standalone centroid file of crates/vector-index/src/ivf/serializer.rs:255-370,
+    written and read by libvrs (vrs_centroid_file_write / _read)."""
+
+    @staticmethod
+    def save_centroid_file(path, centroids, dimension: int, k: int, metric: DistanceMetric,
+                           iterations: int, inertia: float) -> None:
+        c = _f32(centroids).reshape(-1)
+        if c.size != dimension * k:
+            raise ValueError(f"centroids hold {c.size} values, expected k x dimension = {k * dimension}")
+        _check(lib().vrs_centroid_file_write(os.fsencode(path), _ptr(c) if c.size else None,
+                                             dimension, k, int(metric), iterations, inertia))
+
+    @staticmethod
+    def load_centroid_file(path) -> CentroidFileData:
+        m, d, k, it = ctypes.c_int32(0), ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int64(0)
+        inertia = ctypes.c_float(0.0)
+        L, fp = lib(), os.fsencode(path)
+        _check(L.vrs_centroid_file_read(fp, None, 0, ctypes.byref(m), ctypes.byref(d),
+                                        ctypes.byref(k), ctypes.byref(it), ctypes.byref(inertia)))
+        out = np.empty(max(d.value * k.value, 1), np.float32)
+        _check(L.vrs_centroid_file_read(fp, _ptr(out), out.size, None, None, None, None, None))
+        return CentroidFileData(out[:d.value * k.value].reshape(k.value, d.value), d.value, k.value,
+                                DistanceMetric(m.value), it.value, float(inertia.value))
 
 
 # ------------------------------------------------ IVF coarse quantiser
