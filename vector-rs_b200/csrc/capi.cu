@@ -272,6 +272,73 @@ namespace {
 
 int valid_metric(int m) { return m >= 0 && m <= 9; }
 
+// memcpy split over up to 8 host threads (one when the copy is small or a
+// thread cannot be started): pageable or file-mapped rows reach the pinned
+// staging buffer at several times one core's copy rate.
+void par_memcpy(void* dst, const void* src, size_t bytes) {
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const size_t nt = std::min<size_t>({8, hw, std::max<size_t>(1, bytes / (4u << 20))});
+  if (nt <= 1) {
+    memcpy(dst, src, bytes);
+    return;
+  }
+  const size_t per = ((bytes + nt - 1) / nt + 63) & ~(size_t)63;
+  std::vector<std::thread> th;
+  for (size_t o = 0; o < bytes; o += per) {
+    const size_t n = std::min(per, bytes - o);
+    char* d = static_cast<char*>(dst) + o;
+    const char* sp = static_cast<const char*>(src) + o;
+    try {
+      th.emplace_back([d, sp, n] { memcpy(d, sp, n); });
+    } catch (...) {
+      memcpy(d, sp, n);
+    }
+  }
+  for (auto& t : th) t.join();
+}
+
+// Host rows reach the shard through two pinned staging slots of 64 MB: while
+// one slot's rows are copied to the device and padded (on the shard stream),
+// the next chunk is copied from the caller's (pageable or mapped) memory into
+// the other slot. A slot is refilled only after the event recorded behind its
+// last device copy has completed.
+int upload_host_rows(vrs_knn* h, KnnShard* s, const float* rows, int transform) {
+  const size_t row_bytes = (size_t)h->d * sizeof(float);
+  const int64_t chunk = std::max<int64_t>(1, (int64_t)(64ll << 20) / (int64_t)row_bytes);
+  const int64_t nchunks = (s->n_local + chunk - 1) / chunk;
+  const size_t slot_bytes = (size_t)std::min<int64_t>(chunk, s->n_local) * row_bytes;
+  struct Slots {
+    HBuf pin[2];
+    DBuf dev[2];
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    cudaStream_t st = nullptr;
+    ~Slots() {
+      if (st) cudaStreamSynchronize(st);  // no copy may still read a slot being freed
+      for (auto& e : ev)
+        if (e) cudaEventDestroy(e);
+    }
+  } sl;
+  sl.st = s->stream;
+  for (int j = 0; j < 2 && j < nchunks; j++) {
+    VRS_TRY(sl.pin[j].reserve(slot_bytes));
+    VRS_TRY(sl.dev[j].reserve(slot_bytes));
+    VRS_CUDA(cudaEventCreateWithFlags(&sl.ev[j], cudaEventDisableTiming));
+  }
+  for (int64_t c = 0; c < nchunks; c++) {
+    const int j = (int)(c & 1);
+    const int64_t r0 = c * chunk, rc = std::min(chunk, s->n_local - r0);
+    const size_t bytes = (size_t)rc * row_bytes;
+    if (c >= 2) VRS_CUDA(cudaEventSynchronize(sl.ev[j]));
+    par_memcpy(sl.pin[j].p, rows + r0 * h->d, bytes);
+    VRS_CUDA(cudaMemcpyAsync(sl.dev[j].p, sl.pin[j].p, bytes, cudaMemcpyHostToDevice, s->stream));
+    VRS_TRY(launch_pad_rows(sl.dev[j].as<float>(), rc, h->d, h->dp, s->base.as<float>() + r0 * h->dp,
+                            transform, s->stream));
+    VRS_CUDA(cudaEventRecord(sl.ev[j], s->stream));
+  }
+  VRS_CUDA(cudaStreamSynchronize(s->stream));
+  return VRS_OK;
+}
+
 // Uploads (or copies) one shard's rows into the padded layout.
 int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
   VRS_CUDA(cudaSetDevice(s->device));
@@ -280,24 +347,18 @@ int shard_upload(vrs_knn* h, KnnShard* s, const float* rows, int mem) {
   VRS_TRY(s->base_aux.reserve((size_t)std::max<int64_t>(s->n_local, 1) * sizeof(float)));
   if (s->n_local == 0) return VRS_OK;
   const int transform = h->metric == vrs_exact::kHell ? 1 : 0;
-  // Stage in chunks to bound the temporary buffer.
-  const int64_t chunk = std::max<int64_t>(1, (int64_t)(256ll << 20) / (h->d * (int64_t)sizeof(float)));
-  DBuf stage;
-  for (int64_t r0 = 0; r0 < s->n_local; r0 += chunk) {
-    int64_t rows_c = std::min(chunk, s->n_local - r0);
-    const float* src = rows + r0 * h->d;
-    if (mem == VRS_MEM_HOST) {
-      int st = stage.reserve((size_t)rows_c * h->d * sizeof(float));
-      if (st) return st;
-      VRS_CUDA(cudaMemcpyAsync(stage.p, src, (size_t)rows_c * h->d * sizeof(float),
-                               cudaMemcpyHostToDevice, s->stream));
-      src = stage.as<float>();
+  if (mem == VRS_MEM_HOST) {
+    VRS_TRY(upload_host_rows(h, s, rows, transform));
+  } else {
+    // Device rows: padded in chunks that bound each launch.
+    const int64_t chunk = std::max<int64_t>(1, (int64_t)(256ll << 20) / (h->d * (int64_t)sizeof(float)));
+    for (int64_t r0 = 0; r0 < s->n_local; r0 += chunk) {
+      const int64_t rows_c = std::min(chunk, s->n_local - r0);
+      VRS_TRY(launch_pad_rows(rows + r0 * h->d, rows_c, h->d, h->dp, s->base.as<float>() + r0 * h->dp,
+                              transform, s->stream));
+      VRS_CUDA(cudaStreamSynchronize(s->stream));
     }
-    VRS_TRY(launch_pad_rows(src, rows_c, h->d, h->dp, s->base.as<float>() + r0 * h->dp, transform,
-                            s->stream));
-    VRS_CUDA(cudaStreamSynchronize(s->stream));
   }
-  stage.release();
   if (h->metric == vrs_exact::kCos)
     VRS_TRY(launch_cos_norms(s->base.as<float>(), s->n_local, h->d, h->dp, s->base_aux.as<float>(),
                              s->stream));

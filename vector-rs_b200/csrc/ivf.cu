@@ -54,7 +54,30 @@ int bad(const std::string& m) {
 int probe_chunk(vrs_knn* h, int64_t K, int metric, const float* q, int64_t nb, int32_t p,
                 float* score, int64_t* idx, std::vector<float>& dist, std::vector<uint32_t>& ids) {
   const bool re_sort = rooted(metric);
-  int32_t fetch = re_sort ? (int32_t)std::min<int64_t>({K, (int64_t)p + kRootSlack, kMaxFetch}) : p;
+  if (!re_sort) {
+    // The engine's order is already the reference's: search straight into the
+    // caller's buffers, the u32 ids into the low half of out_idx, then widen
+    // them in place from the last entry down (entry i's 8 bytes cover u32
+    // slots 2i and 2i+1, both >= i, so both were read before i is written).
+    uint32_t* ids32 = reinterpret_cast<uint32_t*>(idx);
+    int32_t got = 0;
+    int st = vrs_knn_search(h, q, nb, p, score, ids32, &got);
+    if (st != VRS_OK) return st;
+    if (got != p) return bad("ivf probe: search returned " + std::to_string(got) + " of " +
+                             std::to_string(p) + " neighbours");
+    // Byte copies: the buffer is read as u32 and written as i64 (no aliasing
+    // of the two pointer types, and the compiler keeps each read before the
+    // write that may cover it).
+    char* raw = reinterpret_cast<char*>(idx);
+    for (int64_t i = nb * (int64_t)p - 1; i >= 0; i--) {
+      uint32_t v;
+      memcpy(&v, raw + 4 * i, 4);
+      const int64_t w = v;
+      memcpy(raw + 8 * i, &w, 8);
+    }
+    return VRS_OK;
+  }
+  int32_t fetch = (int32_t)std::min<int64_t>({K, (int64_t)p + kRootSlack, kMaxFetch});
   for (;;) {
     dist.resize((size_t)nb * fetch);
     ids.resize((size_t)nb * fetch);
