@@ -555,7 +555,28 @@ __global__ void __launch_bounds__(256) tc_tau_kernel(const float* __restrict__ v
     }
   }
   __syncthreads();
-  const uint32_t kth = sel::block_select(buf, total, k, s_hist, s_res);
+  uint32_t kth;
+  if (total <= (int)blockDim.x) {
+    // Few minima (small shards, e.g. IVF quantisers): one minimum per thread,
+    // ranked by counting (ties by position, so the ranks are 0..total-1); the
+    // thread of rank k-1 holds the k-th smallest key, the value block_select
+    // returns, in one pass instead of four radix passes.
+    __shared__ uint32_t s_kth;
+    const int t = threadIdx.x;
+    if (t < total) {
+      const uint32_t mine = ord_key(buf[t].hs);
+      int r = 0;
+      for (int u = 0; u < total; u++) {
+        const uint32_t o = ord_key(buf[u].hs);
+        r += (o < mine) || (o == mine && u < t);
+      }
+      if (r == k - 1) s_kth = mine;
+    }
+    __syncthreads();
+    kth = s_kth;
+  } else {
+    kth = sel::block_select(buf, total, k, s_hist, s_res);
+  }
   if (threadIdx.x == 0) {
     const float tau = ord_inv(kth);
     init_bound[q] = isfinite(tau) ? __fadd_ru(tau, absm[q]) : INFINITY;
