@@ -138,7 +138,9 @@ VRS_API int vrs_kmeans_fit(const float* x, int64_t n, int32_t d, int32_t k, cons
  * entries per query, row stride P: out_score[nq*P], out_idx[nq*P], best
  * first (ascending distance, descending similarity); exactly equal values
  * keep index order, as the reference's stable sort does (kmeans.rs:345-350).
- * nprobe == 0 or K == 0 -> *out_p = 0. P > 2048 is rejected. */
+ * nprobe == 0 or K == 0 -> *out_p = 0. P > 2048 is rejected, and for
+ * Minkowski, Mahalanobis and Hellinger P = 2048 < K as well (the entry after
+ * the boundary must be fetched to order equal roots by index). */
 VRS_API int vrs_ivf_find_top_centroids(vrs_knn* centroids, const float* queries, int64_t nq,
                                        int32_t nprobe, float* out_score, int64_t* out_idx,
                                        int32_t* out_p);

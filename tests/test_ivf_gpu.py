@@ -173,3 +173,22 @@ def test_train_save_load_probe_loop(vc, orc, gpu, tmp_path, metric):
         lit = orc.find_top_centroids(q[r], ld.centroids, 8, metric)
         assert [i for i, _ in lit] == list(ig[r])
     cq.close()
+
+
+def test_nprobe_at_the_search_limit(vc, orc, gpu):
+    # One search returns at most 2048 neighbours. Plain metrics probe 2048 of
+    # 3000 centroids directly; the rooted metrics need the entry after the
+    # boundary, so 2048 < K is refused with InvalidConfig and 2047 works.
+    K, d, nq = 3000, 16, 5
+    c = _rows(vc, L2, K, d, 77, 0)
+    q = _rows(vc, L2, nq, d, 77, 1)
+    for metric, p in ((L2, 2048), (MAHA, 2047)):
+        cq = vc.CoarseQuantizer(c, d, vc.DistanceMetric(metric))
+        sg, ig = cq.find_top_centroids(q, p)
+        so, io = orc.find_top_centroids_batch(q, c, p, metric)
+        _assert_probe(metric, sg, ig, so, io, f"metric={metric} nprobe={p}")
+        if metric == MAHA:
+            with pytest.raises(vc.CudaError) as e:
+                cq.find_top_centroids(q, 2048)
+            assert e.value.status == 5
+        cq.close()

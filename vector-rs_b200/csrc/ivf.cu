@@ -144,6 +144,11 @@ extern "C" int vrs_ivf_find_top_centroids(vrs_knn* centroids, const float* queri
     return VRS_OK;
   }
   if (p > kMaxFetch) return bad("vrs_ivf_find_top_centroids: nprobe' > 2048 is not supported");
+  // The rooted metrics check the entry after the boundary for an equal root;
+  // one search returns at most 2048, so P = 2048 < K leaves no room for it.
+  if (rooted(metric) && p >= kMaxFetch && p < K)
+    return bad("vrs_ivf_find_top_centroids: Minkowski, Mahalanobis and Hellinger support nprobe' <= 2047 "
+               "when there are more centroids");
   if (!queries || !out_score || !out_idx) return bad("vrs_ivf_find_top_centroids: null buffer");
   std::vector<float> dist;
   std::vector<uint32_t> ids;
