@@ -122,6 +122,26 @@ def test_missing_file(vc, tmp_path):
     assert e.value.status == 9
 
 
+def test_engine_from_bad_file_fails_before_the_gpu(vc, tmp_path):
+    # File problems surface as InvalidFile (status 9), a zero dimension as
+    # InvalidConfig (status 5), both before any device work.
+    M, Sm = vc.DistanceMetric.L2Squared, vc.GpuShardMode.Sharded
+    with pytest.raises(vc.CudaError) as e:
+        vc.DistributedKnnEngine.from_file(tmp_path / "missing.bin", 1, Sm, M)
+    assert e.value.status == 9
+    bad = tmp_path / "short.bin"
+    bad.write_bytes(struct.pack("<QQQ", MAGIC, 3, 4) + bytes(8))
+    with pytest.raises(vc.CudaError) as e:
+        vc.DistributedKnnEngine.from_file(bad, 1, Sm, M)
+    assert e.value.status == 9 and "size mismatch" in str(e.value)
+    zero = tmp_path / "zero_dim.bin"
+    zero.write_bytes(struct.pack("<QQQ", MAGIC, 5, 0))
+    assert vc.MmapStorage.open(zero).len() == 5  # valid storage, empty rows
+    with pytest.raises(vc.CudaError) as e:
+        vc.DistributedKnnEngine.from_file(zero, 1, Sm, M)
+    assert e.value.status == 5
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("metric,mode,g", [(0, 0, 1), (2, 0, 1), (3, 1, 1), (0, 0, 2)])
 def test_engine_from_file_matches_memory(vc, gpu, tmp_path, metric, mode, g):
