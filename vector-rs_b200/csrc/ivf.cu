@@ -53,8 +53,7 @@ int bad(const std::string& m) {
 // Top-p centroids of nb queries into score/idx (row stride p).
 int probe_chunk(vrs_knn* h, int64_t K, int metric, const float* q, int64_t nb, int32_t p,
                 float* score, int64_t* idx, std::vector<float>& dist, std::vector<uint32_t>& ids) {
-  const bool re_sort = rooted(metric);
-  if (!re_sort) {
+  if (!rooted(metric)) {
     // The engine's order is already the reference's: search straight into the
     // caller's buffers, the u32 ids into the low half of out_idx, then widen
     // them in place from the last entry down (entry i's 8 bytes cover u32
@@ -86,16 +85,10 @@ int probe_chunk(vrs_knn* h, int64_t K, int metric, const float* q, int64_t nb, i
     if (st != VRS_OK) return st;
     if (got != fetch) return bad("ivf probe: search returned " + std::to_string(got) + " of " +
                                  std::to_string(fetch) + " neighbours");
-    if (!re_sort) {
-      for (int64_t i = 0; i < nb * (int64_t)p; i++) {
-        score[i] = dist[i];
-        idx[i] = ids[i];
-      }
-      return VRS_OK;
-    }
     // A run of equal reported values that reaches the last fetched entry may
-    // continue past it: fetch more for the whole chunk (rare: needs two
-    // distinct sums with one rounded root at the probe boundary).
+    // continue past it: fetch more for the whole chunk (needs a run longer
+    // than the slack at the probe boundary: duplicated centroids, or distinct
+    // sums whose roots round equal).
     bool widen = false;
     if (fetch < K) {
       for (int64_t r = 0; r < nb && !widen; r++)
