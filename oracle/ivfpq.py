@@ -9,7 +9,9 @@ restatement), for small cases:
 * ``pq_distance_with_lut`` -- ProductQuantizer::compute_distance_with_lut (pq.rs:270-296):
   4-way chunks summed as (d0 + d1) + (d2 + d3), then the remainder, in f32
 * ``ivf_pq_search``    -- IvfPqIndex::search (crates/vector-index/src/ivf/mod.rs:265-345)
-  given trained coarse centroids, codebooks and inverted lists.
+  given trained coarse centroids, codebooks and inverted lists;
+  ``ivf_pq_search_c`` is the same search in C (``orc_ivfpq_search``) for
+  larger cases, cross-checked against this one.
 
 The search keeps its k best candidates in Rust's ``std::collections::BinaryHeap``
 ordered by heap score alone (mod.rs:28-54: equal scores compare Equal, no id
@@ -171,3 +173,34 @@ def ivf_pq_search(query, k: int, nprobe: int, coarse_centroids, lists, codebooks
         out.append((vid, dist))
     out.reverse()
     return out
+
+
+def ivf_pq_search_c(query, k: int, nprobe: int, coarse_centroids, lists, codebooks,
+                    num_subvectors: int, sub_clusters: int, metric: int, use_simd: int = -1):
+    """The same search in C (``orc_ivfpq_search`` in vrs_oracle.c), for sizes the
+    Python loops cannot reach. Returns (distances f32[c], ids u32[c])."""
+    import ctypes
+    L = oracle.lib()
+    q = np.ascontiguousarray(query, np.float32)
+    cc = np.ascontiguousarray(coarse_centroids, np.float32)
+    nlist = cc.shape[0] if cc.ndim == 2 else 0
+    off = np.zeros(nlist + 1, np.int64)
+    for c in range(nlist):
+        off[c + 1] = off[c] + len(lists[c][0])
+    ids = np.ascontiguousarray(np.concatenate([np.asarray(l[0], np.uint32) for l in lists])
+                               if nlist else np.zeros(0, np.uint32), dtype=np.uint32)
+    codes = np.ascontiguousarray(
+        np.concatenate([np.asarray(l[1], np.uint8).reshape(-1, num_subvectors) for l in lists])
+        if nlist else np.zeros((0, num_subvectors), np.uint8), dtype=np.uint8)
+    cb = np.ascontiguousarray(codebooks, np.float32)
+    out_d = np.zeros(max(k, 1), np.float32)
+    out_i = np.zeros(max(k, 1), np.uint32)
+    P = ctypes.c_void_p
+    fn = L.orc_ivfpq_search
+    fn.restype = ctypes.c_int
+    fn.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, ctypes.c_int, P, P, P, P,
+                   ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P]
+    n = fn(q.ctypes.data, q.size, int(k), int(nprobe), cc.ctypes.data if nlist else None, nlist,
+           off.ctypes.data, ids.ctypes.data, codes.ctypes.data, cb.ctypes.data, num_subvectors,
+           sub_clusters, int(metric), use_simd, out_d.ctypes.data, out_i.ctypes.data)
+    return out_d[:n], out_i[:n]

@@ -814,3 +814,135 @@ int orc_kmeans_fit(const float* x, int64_t n, int d, int k, const float* init,
     free(cent); free(assign); free(sums); free(counts);
     return kk;
 }
+
+/* ---------------------------------------------------------------------- */
+/* IVF-PQ ADC search on a trained index: IvfPqIndex::search               */
+/* (crates/vector-index/src/ivf/mod.rs:265-345) with ProductQuantizer's    */
+/* compute_adc_lut and compute_distance_with_lut (ivf/pq.rs:233-296). The  */
+/* k best candidates live in a restatement of std's BinaryHeap compared on */
+/* the heap score alone (mod.rs:28-54): push = append + sift_up; pop =     */
+/* last element into the root, sift_down_to_bottom (towards the larger     */
+/* child, the right one when left <= right), then sift_up. Inverted list c */
+/* holds entries [list_off[c], list_off[c+1]) of ids and M-byte codes.     */
+/* Finite scores assumed (the reference's comparator maps NaN to Equal).   */
+/* ---------------------------------------------------------------------- */
+
+typedef struct { float hs; float dist; uint32_t id; } pq_cand_t;
+typedef struct { float v; int idx; int desc; } pq_rank_t;
+
+static int pq_le(float a, float b) { return !(a > b); } /* partial_cmp != Greater */
+
+static void pq_sift_up(pq_cand_t* h, int start, int pos) {
+    pq_cand_t e = h[pos];
+    while (pos > start) {
+        int parent = (pos - 1) / 2;
+        if (pq_le(e.hs, h[parent].hs)) break;
+        h[pos] = h[parent];
+        pos = parent;
+    }
+    h[pos] = e;
+}
+
+static void pq_sift_down_to_bottom(pq_cand_t* h, int end, int pos) {
+    const int start = pos;
+    pq_cand_t e = h[pos];
+    int child = 2 * pos + 1;
+    while (child <= end - 2) {
+        if (pq_le(h[child].hs, h[child + 1].hs)) child++;
+        h[pos] = h[child];
+        pos = child;
+        child = 2 * pos + 1;
+    }
+    if (child == end - 1) {
+        h[pos] = h[child];
+        pos = child;
+    }
+    h[pos] = e;
+    pq_sift_up(h, start, pos);
+}
+
+/* Stable order of find_top_centroids (kmeans.rs:345-350): by value (descending
+ * for similarities), equal values by index. */
+static int pq_rank_cmp(const void* pa, const void* pb) {
+    const pq_rank_t* a = (const pq_rank_t*)pa;
+    const pq_rank_t* b = (const pq_rank_t*)pb;
+    float x = a->desc ? b->v : a->v, y = a->desc ? a->v : b->v;
+    if (x < y) return -1;
+    if (x > y) return 1;
+    return (a->idx > b->idx) - (a->idx < b->idx);
+}
+
+int orc_ivfpq_search(const float* q, int d, int k, int nprobe, const float* coarse, int nlist,
+                     const int64_t* list_off, const uint32_t* ids, const uint8_t* codes,
+                     const float* codebooks, int M, int ksub, int metric, int use_simd,
+                     float* out_dist, uint32_t* out_id) {
+    if (k <= 0 || nlist <= 0) return 0;
+    const int simd = pick_simd(use_simd);
+    const int hib = orc_higher_is_better(metric);
+    const int ds = d / M;
+    int eff = nprobe < nlist ? nprobe : nlist;
+    if (eff < 1) eff = 1;
+    pq_rank_t* rk = (pq_rank_t*)malloc(sizeof(pq_rank_t) * (size_t)nlist);
+    for (int c = 0; c < nlist; c++) {
+        rk[c].v = finish(metric, rank_key(metric, q, coarse + (size_t)c * d, d, simd));
+        rk[c].idx = c;
+        rk[c].desc = hib;
+    }
+    qsort(rk, (size_t)nlist, sizeof(pq_rank_t), pq_rank_cmp);
+    float* resid = (float*)malloc(sizeof(float) * (size_t)d);
+    float* lut = (float*)malloc(sizeof(float) * (size_t)M * ksub);
+    pq_cand_t* heap = (pq_cand_t*)malloc(sizeof(pq_cand_t) * ((size_t)k + 1));
+    int hn = 0;
+    for (int t = 0; t < eff; t++) {
+        const int c = rk[t].idx;
+        const int64_t b = list_off[c], e = list_off[c + 1];
+        if (e <= b) continue;
+        for (int j = 0; j < d; j++) resid[j] = q[j] - coarse[(size_t)c * d + j];
+        for (int m = 0; m < M; m++)
+            for (int s = 0; s < ksub; s++)
+                lut[m * ksub + s] = finish(metric, rank_key(metric, resid + m * ds,
+                                                            codebooks + ((size_t)m * ksub + s) * ds, ds, simd));
+        for (int64_t i = b; i < e; i++) {
+            const uint8_t* code = codes + (size_t)i * M;
+            float total = 0.0f;
+            int m = 0;
+            for (; m + 4 <= M; m += 4) {
+                const float d0 = lut[m * ksub + code[m]], d1 = lut[(m + 1) * ksub + code[m + 1]];
+                const float d2 = lut[(m + 2) * ksub + code[m + 2]], d3 = lut[(m + 3) * ksub + code[m + 3]];
+                total = total + ((d0 + d1) + (d2 + d3));
+            }
+            for (; m < M; m++) total = total + lut[m * ksub + code[m]];
+            const float hs = hib ? -total : total;
+            pq_cand_t cand = {hs, total, ids[i]};
+            if (hn < k) {
+                heap[hn] = cand;
+                pq_sift_up(heap, 0, hn);
+                hn++;
+            } else if (hs < heap[0].hs) {
+                /* pop the worst, then push */
+                pq_cand_t last = heap[--hn];
+                if (hn > 0) {
+                    heap[0] = last;
+                    pq_sift_down_to_bottom(heap, hn, 0);
+                }
+                heap[hn] = cand;
+                pq_sift_up(heap, 0, hn);
+                hn++;
+            }
+        }
+    }
+    /* pop worst to best, written back to front: best first */
+    const int count = hn;
+    while (hn > 0) {
+        pq_cand_t top = heap[0];
+        pq_cand_t last = heap[--hn];
+        if (hn > 0) {
+            heap[0] = last;
+            pq_sift_down_to_bottom(heap, hn, 0);
+        }
+        out_dist[hn] = top.dist;
+        out_id[hn] = top.id;
+    }
+    free(rk); free(resid); free(lut); free(heap);
+    return count;
+}

@@ -119,3 +119,27 @@ def test_encode(pq):
     assert list(pq.pq_encode([1, 1, 2, 2], cb, 2, 2, L2)) == [1, 1]
     assert list(pq.pq_encode([0.1, 0.0, 0.4, 0.5], cb, 2, 2, L2)) == [0, 0]
     assert list(pq.pq_encode([0.5, 0.5, 1.0, 1.0], cb, 2, 2, L2)) == [0, 0]  # ties -> 0
+
+
+@pytest.mark.parametrize("metric", [L2, DOT, COS, 3])
+@pytest.mark.parametrize("ksub", [2, 16])
+def test_c_search_matches_python(pq, orc, metric, ksub):
+    # The C form (for large parity cases) against the Python restatement, on
+    # indexes with many exact ADC ties (ksub = 2: few distinct codes) and
+    # without, for several k and nprobe.
+    rng = np.random.default_rng(100 * ksub + metric)
+    d, M, nlist = 12, 6, 7
+    cb = rng.standard_normal(M * ksub * (d // M)).astype(np.float32)
+    coarse = rng.standard_normal((nlist, d)).astype(np.float32)
+    lists, nid = [], 0
+    for c in range(nlist):
+        n = int(rng.integers(0, 40)) if c != 2 else 0  # list 2 stays empty
+        lists.append((np.arange(nid, nid + n), rng.integers(0, ksub, (n, M)).astype(np.uint8)))
+        nid += n
+    for t in range(4):
+        q = rng.standard_normal(d).astype(np.float32)
+        for k, nprobe in ((1, 1), (7, 3), (25, 7), (500, 0)):
+            py = pq.ivf_pq_search(q, k, nprobe, coarse, lists, cb, M, ksub, metric)
+            dc, ic = pq.ivf_pq_search_c(q, k, nprobe, coarse, lists, cb, M, ksub, metric)
+            assert [(int(i), np.float32(v)) for i, v in zip(ic, dc)] == \
+                [(i, np.float32(v)) for i, v in py], (metric, ksub, k, nprobe, t)
