@@ -3,7 +3,7 @@
  * two GPU hot paths: exact batch flat kNN and Lloyd k-means.
  *
  * This is the boundary the reference's Rust crate `vector-cuda` would bind
- * (one `extern "C"` block; see INTEGRATION.md). Plain pointers and sizes
+ * (one `extern "C"` block). Plain pointers and sizes
  * only. Every function returns a vrs_status; on failure a thread-local
  * message is available from vrs_last_error(). There is no CPU fallback:
  * a missing or failing GPU is an error, never a silent slow path (the
@@ -236,8 +236,11 @@ VRS_API int vrs_kmeans_fit_rank(vrs_comm* comm, const float* x_local, int64_t n_
  * device, held until exit; a batch whose candidate lists do not fit is
  * rejected with VRS_ERR_INVALID_CONFIG (split it). The first call on a
  * device looks up that array's address, so make it before any stream
- * capture. Calls that overlap on the GPU share the array and race.
- * Cosine and Hellinger are rejected (they need per-row norms or roots). */
+ * capture. That address is cached for the life of the process, so do not
+ * use this entry point across a cudaDeviceReset (or any other teardown of
+ * the device's primary context). Calls that overlap on the GPU share the
+ * array and race. Cosine and Hellinger are rejected (they need per-row
+ * norms or roots). */
 VRS_API int vrs_knn_search_noalloc(const float* base, int64_t n, int32_t d, const float* queries,
                                    int64_t nq, int32_t k, int32_t metric, float* out_dist,
                                    uint32_t* out_id, int32_t* out_k, void* cuda_stream);

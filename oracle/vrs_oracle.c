@@ -39,7 +39,7 @@
  *   - Hellinger: one FMA accumulator of (sqrt|a|-sqrt|b|)^2 (:581-610).
  *   - _mm512_reduce_add_ps is the halving tree lanes i+8, i+4, i+2, i+1.
  *
- * Deliberate deviations (all documented in DESIGN.md):
+ * Deliberate deviations (the GPU path makes the same ones):
  *   - k-means starts from caller-supplied centroids instead of the unseeded
  *     k-means++ (kmeans.rs:409-460), which cannot be reproduced;
  *   - an empty cluster keeps its centroid (as the reference GPU kernel,

@@ -66,3 +66,18 @@ def test_metric_higher_is_better(vc):
     assert [L.vrs_metric_higher_is_better(m) for m in range(10)] == [0, 1, 1, 0, 0, 0, 0, 0, 0, 0]
     assert [vc.DistanceMetric(m).higher_is_better() for m in range(10)] == \
         [False, True, True] + [False] * 7
+
+
+def test_noalloc_refuses_huge_query_count_on_cpu(vc):
+    # The allocation-free entry point refuses a query count that no scratch
+    # layout can hold before any size arithmetic or CUDA call, so this runs
+    # without a GPU (and a count that would wrap 64-bit sizes is refused too).
+    f = vc.lib().vrs_knn_search_noalloc
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+                  ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                  ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p]
+    kk = ctypes.c_int32(7)
+    for nq in (2 ** 61 + 300, 2 ** 63 - 1, 2044):
+        assert f(None, 1000, 16, None, nq, 100, 0, None, None, ctypes.byref(kk), None) == 5
+        assert b"no-alloc scratch" in vc.lib().vrs_last_error()
+        assert kk.value == 0

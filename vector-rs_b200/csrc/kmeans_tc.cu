@@ -1,14 +1,16 @@
 // kmeans_tc.cu -- tensor-core (tcgen05) k-means assignment for the GEMM-form
 // metrics (squared L2, Mahalanobis, dot, cosine).
 //
-// Persistent CTAs loop over tiles of 256 points (two M=128 bf16 operand
+// Persistent CTAs loop over tiles of 256 points (two M=128 fp16 operand
 // tiles, loaded by TMA); the K centroids stream through a 4-stage TMA ring
-// as 128-row bf16 tiles; one thread issues tcgen05.mma into two 128x128 f32
-// TMEM accumulators (double-buffered). Sixteen epilogue warps (one thread =
-// one point, two warps per point splitting each tile's columns) keep the
-// approximate best centroid and every centroid whose approximate score is
-// within the point's error margin of it (at most 4, else the point is
-// flagged). kmeans_finalize then picks the exact argmin among those
+// as 128-row fp16 tiles; one thread issues tcgen05.mma (kind::f16) into two
+// 128x128 f32 TMEM accumulators (double-buffered). Sixteen epilogue warps
+// (one thread = one point, two warps per point splitting each tile's
+// columns) keep the approximate best centroid and every centroid whose
+// approximate score is within the point's error margin of it (the NCAND = 8
+// best such per column half, plus the smallest score that did not fit, so a
+// point whose dropped candidate is still in bound is flagged for an exact
+// scan). kmeans_finalize then picks the exact argmin among those
 // candidates in the reference's f32 arithmetic (find_nearest,
 // crates/vector-cuda/src/kmeans.rs:361-407: strict comparison, lowest index
 // wins ties) and records the exact distance for the inertia.
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t d = tmem + acc * 256 + b * BN;
 #pragma unroll
             for (int ks = 0; ks < MAX_KBLK * 4; ks++)
-              if (ks < ksteps) mma_bf16(d, ad[acc][ks], bd[ks], idesc, ks > 0 ? 1u : 0u);
+              if (ks < ksteps) mma_f16(d, ad[acc][ks], bd[ks], idesc, ks > 0 ? 1u : 0u);
           }
           mma_commit(&empty[s]);
           mma_commit(&tfull[b]);

@@ -85,6 +85,15 @@ extern "C" int vrs_knn_search_noalloc(const float* base, int64_t n, int32_t d, c
     set_error(VRS_ERR_INVALID_CONFIG, "ids are u32: n must be < 2^32-1");
     return VRS_ERR_INVALID_CONFIG;
   }
+  // No batch can hold more queries than the scratch fits at the smallest
+  // list (512 candidates, one segment, one count and one flag each). Checked
+  // before any size arithmetic, so the products below cannot wrap and nq
+  // stays far inside int range.
+  if (nq > (int64_t)((kNoAllocScratchBytes - 256) / (2 * sizeof(int) + 512 * sizeof(Cand)))) {
+    set_error(VRS_ERR_INVALID_CONFIG, "vrs_knn_search_noalloc: " + std::to_string(nq) +
+                                          " queries exceed the no-alloc scratch at any k; split the batch");
+    return VRS_ERR_INVALID_CONFIG;
+  }
   void* scratch = nullptr;
   VRS_TRY(scratch_address(&scratch));  // first call on a device: set-up
   if (nq == 0 || k == 0 || n == 0) return VRS_OK;
@@ -121,6 +130,17 @@ extern "C" int vrs_knn_search_noalloc(const float* base, int64_t n, int32_t d, c
   int64_t seg_len = (n + nseg - 1) / nseg;
   seg_len = (seg_len + 63) / 64 * 64;
   nseg = (int)((n + seg_len - 1) / seg_len);
+  // The select flags a query (and leaves its output row untouched) only
+  // when its survivors exceed max_sort. The exact scan keeps at most k'
+  // entries per segment and nseg <= 16384 / k' above, so nseg * k' <=
+  // max_sort <= 16384 and every query's row is written; checked here,
+  // before any launch, so a change to the plan cannot break it silently.
+  const int ms = next_pow2(nseg * kk > 256 ? nseg * kk : 256);
+  const int max_sort = ms > 16384 ? 16384 : ms;
+  if (nseg * kk > max_sort) {
+    set_error(VRS_ERR_DRIVER, "vrs_knn_search_noalloc: segment plan exceeds the select's sort capacity");
+    return VRS_ERR_DRIVER;
+  }
 
   unsigned char* sp = static_cast<unsigned char*>(scratch);
   int* ovf = reinterpret_cast<int*>(sp);
@@ -176,8 +196,7 @@ extern "C" int vrs_knn_search_noalloc(const float* base, int64_t n, int32_t d, c
   sa.out_dist = out_dist;
   sa.out_id = out_id;
   sa.out_pairs = nullptr;
-  int ms = next_pow2(nseg * kk > 256 ? nseg * kk : 256);
-  sa.max_sort = ms > 16384 ? 16384 : ms;
+  sa.max_sort = max_sort;
   sa.tiny = nullptr;
   sa.n_tiny = 0;
   VRS_TRY(launch_knn_select(sa, s));

@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t d = tmem + acc * 256 + b * BN;
 #pragma unroll
           for (int ks = 0; ks < MAX_KBLK * 4; ks++)
-            if (ks < ksteps) mma_bf16(d, ad[acc][ks], bd[ks], idesc, ks > 0 ? 1u : 0u);
+            if (ks < ksteps) mma_f16(d, ad[acc][ks], bd[ks], idesc, ks > 0 ? 1u : 0u);
         }
         mma_commit(&empty[s]);
         mma_commit(&tfull[b]);

@@ -139,7 +139,7 @@ __device__ __forceinline__ void tc_fence_after() {
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16: 16-bit operands
 // (fp16 or bf16, as the instruction descriptor says), f32 accumulate.
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
