@@ -4,18 +4,25 @@ k-means iterations/s (default C3) on B200, through libvrs's C ABI.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload c1|c2|c4-l1|c4-linf|c4-hell|c5a] [--km-workload c3|c5b]
+                    [--no-scale] [--km-parity-iters I]
 
 N > 1 is launched by torchrun (one process per GPU); each rank holds a row
-shard of the base (GpuShardMode::Sharded) and the ranks meet in an NCCL
-all-gather + GPU merge inside vrs_knn_search. Prints one JSON line on rank 0.
+shard of the base (GpuShardMode::Sharded) and the ranks meet in NCCL
+collectives and a GPU merge inside vrs_knn_search. Prints one JSON line on
+rank 0.
 
 A step is one vrs_knn_search of the 10,000 C2 queries against the whole
 (sharded) 1,000,000 x 128 base. `value` times steps whose queries and
 results stay in HBM; `e2e` times the same call with pinned host buffers
-(H2D of the queries and D2H of the results inside the timed region).
-The base (512 MB of f32) is larger than L2, so no flush is needed between
-steps. Inputs are seeded Philox4x32-10 draws generated on the device, the
-same bits the CPU oracle consumes.
+(H2D of the queries and D2H of the results inside the timed region);
+`sustained` repeats the step for at least a second under its own clock
+record. The base (512 MB of f32) is larger than L2, so no flush is needed
+between steps. Inputs are seeded Philox4x32-10 draws generated on the
+device, the same bits the CPU oracle consumes. At every N rank 0 checks a
+query sample of the merged results, and a k-means fit of the same init,
+against the oracle on the whole base. The north star's scale configs (C5a:
+100M x 96 squared-L2 kNN; C5b: 10M x 96, K = 16384 k-means) ride along as
+the keys `c5a` and `c5b`.
 """
 from __future__ import annotations
 
@@ -97,6 +104,10 @@ def parse():
     ap.add_argument("--n-query", type=int, default=None, help="override the workload's query count")
     ap.add_argument("--km-n", type=int, default=None, help="override the k-means point count")
     ap.add_argument("--km-iters", type=int, default=None)
+    ap.add_argument("--km-parity-iters", type=int, default=2,
+                    help="Lloyd iterations of the k-means oracle comparison on all points (0: skip)")
+    ap.add_argument("--no-scale", action="store_true",
+                    help="skip the north-star scale configs (C5a kNN, C5b k-means) that ride along as keys")
     return ap.parse_args()
 
 
@@ -172,7 +183,7 @@ class ClockSampler:
 
 
 def host_gen(vc, kind, seed, stream, rows, d, threads=None):
-    """Host copy of generator rows, produced in parallel chunks."""
+    """Host copy of generator rows from the product library, in parallel chunks."""
     from concurrent.futures import ThreadPoolExecutor
     out = np.empty((rows, d), np.float32)
     nt = threads or os.cpu_count() or 1
@@ -187,20 +198,20 @@ def host_gen(vc, kind, seed, stream, rows, d, threads=None):
     return out
 
 
-def cpu_leg(w, base, queries, sample):
-    """Timed oracle (restated reference CPU path) on a query sample."""
+def oracle_mod():
+    """The CPU oracle (restated reference CPU path): the parity checker and
+    the CPU baseline, never the measured GPU path."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     oracle.build()
-    cores = os.cpu_count() or 1
-    qs = queries[:sample]
-    t0 = time.perf_counter()
-    d, i = oracle.knn_search(base, qs, w["k"], w["metric"], nthreads=cores)
-    dt = time.perf_counter() - t0
-    return {"value": sample / dt, "unit": "queries/s", "cores": cores, "kind": "port",
-            "sample": f"{sample} of the {w['nq']} queries against the full {len(base)}-row base "
-                      f"(AVX-512 restatement of search_batch_cpu, {cores} threads)",
-            "seconds": dt}, (d, i)
+    return oracle
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def workload(args):
@@ -212,12 +223,13 @@ def workload(args):
     return w
 
 
-def km_workload(args):
-    w = dict(KM_WORKLOADS[args.km_workload])
-    if args.km_n:
-        w["n"] = args.km_n
-    if args.km_iters:
-        w["iters"] = args.km_iters
+def km_workload(args, name=None):
+    w = dict(KM_WORKLOADS[name or args.km_workload])
+    if name is None:
+        if args.km_n:
+            w["n"] = args.km_n
+        if args.km_iters:
+            w["iters"] = args.km_iters
     return w
 
 
@@ -233,45 +245,119 @@ def metric_label(w):
     return f"flat kNN queries/s ({fmt_count(w['n'])} x {w['d']} {METRIC_NAMES[w['metric']]}, k={w['k']})"
 
 
+def knn_config(w, world):
+    n_loc = -(-w["n"] // world)
+    big = n_loc * w["d"] * 4 > 126e6
+    return {"workload": w["name"], "n_base": w["n"], "queries_per_step": w["nq"], "k": w["k"], "dim": w["d"],
+            "parallelism": f"row-sharded x{world} + NCCL all-gather merge",
+            "l2": ("inputs larger than L2 (f32 base shard %.0f MB), no flush" % (n_loc * w["d"] * 4 / 1e6))
+                  if big else "base shard smaller than L2: steps see a warm L2"}
+
+
+def parity_stats(gd, gi, od, oi):
+    """Per-position comparison with the oracle: ids, distance bits, and the
+    largest relative distance error (the north star allows 1e-4)."""
+    gd, od = np.asarray(gd, np.float32), np.asarray(od, np.float32)
+    den = np.maximum(np.abs(od.astype(np.float64)), 1.0)
+    rel = np.abs(gd.astype(np.float64) - od.astype(np.float64)) / den
+    return {"queries": int(len(gi)), "ids_equal_frac": float((np.asarray(gi) == np.asarray(oi)).mean()),
+            "dist_bit_equal_frac": float((gd.view(np.uint32) == od.view(np.uint32)).mean()),
+            "max_rel_dist_err": float(rel.max()) if rel.size else 0.0}
+
+
+def oracle_topk_streamed(orc, vc, torch, dev, w, seed, kind, q_host, chunk_rows=2_000_000):
+    """Oracle top-k of a few queries over a base too large for one host copy:
+    rows are generated on this GPU chunk by chunk (the same bits the shards
+    hold), copied to pinned host memory and searched by the row-split oracle
+    with global ids; the per-chunk lists merge per query in (score, id)
+    order. Squared L2, dot and cosine only (their reported values order
+    like the ranking key)."""
+    n, D, K, metric = w["n"], w["d"], w["k"], w["metric"]
+    assert metric in (L2, DOT, COS)
+    sign = -1.0 if metric in (DOT, COS) else 1.0
+    rows = min(chunk_rows, n)
+    buf = torch.empty((rows, D), dtype=torch.float32, device=dev)
+    pin = torch.empty((rows, D), dtype=torch.float32, pin_memory=True)
+    run_d = run_i = None
+    for r0 in range(0, n, rows):
+        rc = min(rows, n - r0)
+        vc.gen_rows_device(kind, seed, 0, r0, rc, D, buf.data_ptr())
+        torch.cuda.synchronize(dev)
+        pin[:rc].copy_(buf[:rc])
+        d, i = orc.knn_search_rows(pin[:rc].numpy(), q_host, K, metric, nthreads=host_cores(), id_offset=r0)
+        if run_d is None:
+            run_d, run_i = d.copy(), i.copy()
+            continue
+        cd = np.concatenate([run_d, d], 1)
+        ci = np.concatenate([run_i, i], 1)
+        for r in range(cd.shape[0]):
+            o = np.lexsort((ci[r].astype(np.int64), sign * cd[r].astype(np.float64)))[:K]
+            run_d[r], run_i[r] = cd[r][o], ci[r][o]
+    del buf
+    return run_d, run_i
+
+
 def reference_arm(args):
-    """The reference's CPU path (oracle restatement of search_batch_cpu, all
-    host threads) on the same workload, a bounded query sample per step."""
+    """The reference's CPU path (the oracle's restatement of
+    search_batch_cpu, all host threads) on the same workload, a bounded query
+    sample per step; inputs from the oracle's own generator (the same bits
+    as the GPU arm's), so this process never loads libvrs. Also times the
+    restated fit_cpu for one Lloyd iteration of the k-means config."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import vector_cuda as vc
+    orc = oracle_mod()
+    cores = host_cores()
     w = workload(args)
-    seed = vc.config_seed(w["seed"])
-    kind = getattr(vc, w["gen"])
-    base = host_gen(vc, kind, seed, 0, w["n"], w["d"])
-    queries = host_gen(vc, kind, seed, 1, min(w["nq"], 2000), w["d"])
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
-    oracle.build()
-    cores = os.cpu_count() or 1
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    seed = orc.config_seed(w["seed"])
+    kind = getattr(orc, w["gen"])
+    base = orc.gen_rows(kind, seed, 0, 0, w["n"], w["d"], nthreads=cores)
+    queries = orc.gen_rows(kind, seed, 1, 0, min(w["nq"], 2000), w["d"], nthreads=cores)
     per_step = max(1, min(100, w["cpu_sample"]))
     for _ in range(args.warmup):
-        oracle.knn_search(base, queries[:16], w["k"], w["metric"], nthreads=cores)
+        orc.knn_search(base, queries[:16], w["k"], w["metric"], nthreads=cores)
     t0 = time.perf_counter()
     for s in range(args.steps):
         q0 = (s * per_step) % (len(queries) - per_step + 1)
-        oracle.knn_search(base, queries[q0:q0 + per_step], w["k"], w["metric"], nthreads=cores)
+        orc.knn_search(base, queries[q0:q0 + per_step], w["k"], w["metric"], nthreads=cores)
     dt = time.perf_counter() - t0
     v = per_step * args.steps / dt
+    sample = (f"{per_step} of the {w['nq']} queries per step against the full {w['n']}-row base, "
+              f"{cores} threads (the reference's Rust cannot build here: no cargo; oracle restatement "
+              "of search_batch_cpu)")
     line = {
         "impl": "reference", "metric": metric_label(w), "value": v,
         "unit": "queries/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": w["data"].replace("generated on device", "host"),
-        "config": {"workload": w["name"], "n_base": w["n"], "queries_per_step": per_step, "k": w["k"]},
-        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": cores, "kind": "port",
-                         "sample": f"{per_step} queries per step against the full base, "
-                                   f"{cores} threads (reference Rust cannot build here: "
-                                   "no cargo; oracle restatement of search_batch_cpu)"},
+        "config": knn_config(w, world), "sample": sample,
+        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    del base
+    if not args.no_kmeans:
+        kw = km_workload(args)
+        ks = orc.config_seed(kw["seed"])
+        cent = orc.gen_rows(orc.GEN_NORMAL, ks, kw["stream_c"], 0, kw["K"], kw["d"])
+        x = orc.gen_rows(orc.GEN_MIXTURE, ks, kw["stream_x"], 0, kw["n"], kw["d"], cent, kw["K"], kw["sigma"],
+                         nthreads=cores)
+        t0 = time.perf_counter()
+        _, _, it, _ = orc.kmeans_fit(x, kw["K"], x[:kw["K"]], 1, 0.0, L2, nthreads=cores)
+        ks_dt = time.perf_counter() - t0
+        line["kmeans"] = {"metric": f"k-means iterations/s ({kw['name']})", "value": it / ks_dt,
+                          "unit": "iterations/s", "cores": cores, "kind": "port",
+                          "sample": f"{it} Lloyd iteration(s) of the {kw['iters']} on all {kw['n']} points "
+                                    "(oracle restatement of fit_cpu)"}
     print(json.dumps(line), flush=True)
     return 0
+
+
+class Ctx:
+    """Per-process bench state shared by the workload runners."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
 
 
 def main():
@@ -290,7 +376,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=dev)
     uid = [vc.Comm.unique_id() if rank == 0 else None]
     if dist:
@@ -310,24 +396,50 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def gather_rows(t):
+        """Rank-ordered concatenation of every rank's rows (rank 0 uses it)."""
+        if not dist:
+            return t
+        n = torch.tensor([t.shape[0]], dtype=torch.int64, device=dev)
+        ns = [torch.zeros_like(n) for _ in range(world)]
+        dist.all_gather(ns, n)
+        m = int(max(x.item() for x in ns))
+        pad = torch.zeros((m,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
+        pad[:t.shape[0]] = t
+        outs = [torch.empty_like(pad) for _ in range(world)]
+        dist.all_gather(outs, pad)
+        return torch.cat([o[:int(c.item())] for o, c in zip(outs, ns)])
+
     pk, pk_kind = peaks()
-    peak_tc = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    ctx = Ctx(args=args, vc=vc, torch=torch, comm=comm, dev=dev, world=world, rank=rank, local=local,
+              stream=stream, barrier=barrier, max_over_ranks=max_over_ranks, gather_rows=gather_rows,
+              pk=pk, pk_kind=pk_kind, peak_burst=pk.get("bf16_tflops", 1590.0),
+              peak_sus=pk.get("bf16_tflops_sustained", pk.get("bf16_tflops", 1400.0)))
     line = None
     if args.ivf:
-        line = ivf_bench(args, vc, torch, dev, peak_tc) if rank == 0 else None
+        line = ivf_bench(args, vc, torch, dev, ctx.peak_burst) if rank == 0 else None
         args.no_knn = args.no_kmeans = True
     if args.storage:
         line = storage_bench(args, vc, torch, dev, pk) if rank == 0 else None
         args.no_knn = args.no_kmeans = True
     if not args.no_knn:
-        line = knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, max_over_ranks,
-                         pk, pk_kind, peak_tc)
+        w = workload(args)
+        line = knn_bench(ctx, w, args.steps, args.warmup, parity_queries=min(w["cpu_sample"], w["nq"]),
+                         cpu_leg=not args.no_cpu, sustained=True)
     if not args.no_kmeans:
-        km = kmeans_bench(args, vc, torch, comm, dev, world, rank, barrier, max_over_ranks, peak_tc)
+        km = kmeans_bench(ctx, km_workload(args), parity_iters=args.km_parity_iters, cpu_leg=not args.no_cpu)
         if line is None:
             line = km
         else:
             line["kmeans"] = km
+    # The north star's scale configs ride along as extra keys of the default
+    # line (few steps each), so every scaling run records them too.
+    if line is not None and not args.no_scale and not args.ivf and not args.storage:
+        c5a = dict(WORKLOADS["c5a"])
+        line["c5a"] = knn_bench(ctx, c5a, min(args.steps, 5), min(args.warmup, 2), parity_queries=20,
+                                cpu_leg=False, sustained=False, e2e_steps=2)
+        line["c5b"] = kmeans_bench(ctx, km_workload(args, "c5b"), parity_iters=1, cpu_leg=False,
+                                   parity_sample=20_000, sustained=False, e2e=False)
     comm.close()
     if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
@@ -336,59 +448,80 @@ def main():
     return 0
 
 
-def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, max_over_ranks,
-              pk, pk_kind, peak_tc):
-    w = workload(args)
+def knn_bench(ctx, w, steps, warmup, parity_queries, cpu_leg, sustained, e2e_steps=None):
+    vc, torch, dev, world, rank = ctx.vc, ctx.torch, ctx.dev, ctx.world, ctx.rank
+    stream, barrier, max_over_ranks = ctx.stream, ctx.barrier, ctx.max_over_ranks
     n_base, n_q, D, K, metric = w["n"], w["nq"], w["d"], w["k"], w["metric"]
     seed = vc.config_seed(w["seed"])
     kind = getattr(vc, w["gen"])
     r0, r1 = vc.shard_rows(n_base, world, rank)
-    shard = torch.empty((max(r1 - r0, 1), D), dtype=torch.float32, device=dev)
-    vc.gen_rows_device(kind, seed, 0, r0, r1 - r0, D, shard.data_ptr())
+    n_loc = r1 - r0
+    shard = torch.empty((max(n_loc, 1), D), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(kind, seed, 0, r0, n_loc, D, shard.data_ptr())
     q_dev = torch.empty((n_q, D), dtype=torch.float32, device=dev)
     vc.gen_rows_device(kind, seed, 1, 0, n_q, D, q_dev.data_ptr())
     torch.cuda.synchronize()
-    eng = vc.DistributedKnnEngine.create_rank(comm, None, D, r0, n_base, vc.GpuShardMode.Sharded,
+    eng = vc.DistributedKnnEngine.create_rank(ctx.comm, None, D, r0, n_base, vc.GpuShardMode.Sharded,
                                               vc.DistanceMetric(metric),
-                                              device_ptr=shard.data_ptr(), n_local=r1 - r0)
+                                              device_ptr=shard.data_ptr(), n_local=n_loc)
     eng.set_stream(stream.cuda_stream)
+    keep_shard = world == 1 and n_base * D * 4 <= 4e9 and rank == 0  # host copy for the oracle
+    base_h = shard[:n_loc].cpu().numpy() if keep_shard else None
+    del shard  # the engine holds its own padded copy
+    torch.cuda.empty_cache()
     out_d = torch.empty((n_q, K), dtype=torch.float32, device=dev)
     out_i = torch.empty((n_q, K), dtype=torch.int32, device=dev)
 
     def step_dev():
         return eng.search_device(q_dev.data_ptr(), n_q, K, out_d.data_ptr(), out_i.data_ptr())
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step_dev()
     barrier()
     vc.profile_reset()  # the launch counter covers the timed steps
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(ctx.local) as clk:
         barrier()
         ev0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step_dev()
         ev1.record(stream)
         barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     launches = vc.profile_read("*")[1]
+    # Results of the timed steps, for the parity check (every rank holds
+    # the merged top-k').
+    res_i = out_i.cpu().numpy().view(np.uint32).copy() if rank == 0 else None
+    res_d = out_d.cpu().numpy().copy() if rank == 0 else None
     # Per-kernel breakdown from the same steps run again with the library's
     # CUDA-event profiling on (its events cost host time per launch, so the
     # timed loop above runs without it).
     vc.profile_reset()
     vc.profile_enable(True)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step_dev()
     barrier()
     vc.profile_enable(False)
-    scan_ms, scan_n = vc.profile_read("knn_scan")
-    sel_ms, sel_n = vc.profile_read("knn_select")
-    merge_ms, merge_n = vc.profile_read("knn_merge")
-    piv_ms, piv_n = vc.profile_read("knn_pivot")
-    fb_ms, fb_n = vc.profile_read("knn_fallback")
-    prep_ms, _ = vc.profile_read("knn_prep")
-    gath_ms, _ = vc.profile_read("knn_gather")
-    value = n_q * args.steps / (ms / 1e3)
+    st = {nm: vc.profile_read(nm) for nm in ("knn_scan", "knn_select", "knn_merge", "knn_pivot", "knn_fallback",
+                                             "knn_prep", "knn_gather")}
+    value = n_q * steps / (ms / 1e3)
+
+    # Sustained: the same step repeated for at least one second (its own
+    # clock record), so the clocks seen under a longer load are on file.
+    sus = None
+    if sustained:
+        n_sus = max(steps, int(np.ceil(1000.0 / max(ms / steps, 1e-3))))
+        n_sus = int(max_over_ranks(float(n_sus)))
+        with ClockSampler(ctx.local) as clk_s:
+            barrier()
+            ev0.record(stream)
+            for _ in range(n_sus):
+                step_dev()
+            ev1.record(stream)
+            barrier()
+        ms_s = max_over_ranks(ev0.elapsed_time(ev1))
+        sus = {"steps": n_sus, "seconds": ms_s / 1e3, "value": n_q * n_sus / (ms_s / 1e3),
+               "ms_per_step": ms_s / n_sus, "clocks": clk_s.summary()}
 
     # ----------------------------------------------------------- e2e (host)
     q_host = torch.empty((n_q, D), dtype=torch.float32, pin_memory=True)
@@ -397,46 +530,46 @@ def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, m
     hi = torch.empty((n_q, K), dtype=torch.int32, pin_memory=True)
 
     def step_host():
-        kk = np.ctypeslib.ctypes.c_int32()
+        kk = vc.ctypes.c_int32()
         vc._check(vc.lib().vrs_knn_search_ex(eng._h, vc.ctypes.c_void_p(q_host.data_ptr()), n_q, K,
                                             vc.ctypes.c_void_p(hd.data_ptr()),
                                             vc.ctypes.c_void_p(hi.data_ptr()),
                                             vc.ctypes.byref(kk), 0))
 
-    for _ in range(max(1, args.warmup // 2)):
+    ne = e2e_steps or steps
+    for _ in range(max(1, warmup // 2)):
         step_host()
-    with ClockSampler(local) as clk2:
+    with ClockSampler(ctx.local) as clk2:
         # Ranks meet after their samplers start, so no rank's first
         # collective waits out another rank's sampler start-up.
         barrier()
         ev0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(ne):
             step_host()
         ev1.record(stream)
         barrier()
     ms_e2e = max_over_ranks(ev0.elapsed_time(ev1))
-    e2e = n_q * args.steps / (ms_e2e / 1e3)
+    e2e = n_q * ne / (ms_e2e / 1e3)
 
-    # ------------------------------------------------------------ roofline
-    n_loc = r1 - r0
+    # ------------------------------------------------------------- roofline
+    scan_ms, scan_n = st["knn_scan"]
     per_launch_ms = scan_ms / max(scan_n, 1)
-    breakdown = {"pivot": piv_ms / args.steps, "scan": scan_ms / args.steps,
-                 "select": sel_ms / args.steps, "merge": merge_ms / args.steps,
-                 "query_prep": prep_ms / args.steps, "all_gathers": gath_ms / args.steps,
-                 # exact re-search of queries whose scan bound failed verification
-                 "fallback": fb_ms / args.steps, "fallback_launches": fb_n}
+    breakdown = {k.replace("knn_", ""): v[0] / steps for k, v in st.items()}
+    breakdown["fallback_launches"] = st["knn_fallback"][1]
     if metric in TC_METRICS and D <= 128:
         flops_per_launch = 2.0 * n_loc * D * n_q  # algorithmic: 2*N_local*D per query
         achieved = flops_per_launch / (per_launch_ms / 1e3) / 1e12
-        is_c2 = args.workload == "c2" and n_base == WORKLOADS["c2"]["n"] and n_q == WORKLOADS["c2"]["nq"]
-        roofline = {"bound": "tensor", "kernel": "knn_scan", "achieved": achieved, "peak": peak_tc,
-                    "unit": "TFLOP/s", "frac": achieved / peak_tc,
-                    "peak_source": f"{pk_kind} bf16 dense (sustained)",
+        is_c2 = w["name"] == WORKLOADS["c2"]["name"] and n_base == WORKLOADS["c2"]["n"] and \
+            n_q == WORKLOADS["c2"]["nq"]
+        roofline = {"bound": "tensor", "kernel": "knn_scan", "achieved": achieved, "peak": ctx.peak_burst,
+                    "unit": "TFLOP/s", "frac": achieved / ctx.peak_burst,
+                    "peak_source": f"{ctx.pk_kind} bf16 dense, burst (the scan is timed in a short region)",
+                    "frac_of_sustained": achieved / ctx.peak_sus,
                     "per_launch_ms": per_launch_ms, "launches": scan_n,
                     "flops_per_launch": flops_per_launch,
                     "traffic": SCAN_DRAM_BYTES_C2 * n_loc / n_base if is_c2 else None,
                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size "
-                                      "C2 launch, scaled by rows scanned per GPU",
+                                      "C2 launch, scaled by rows scanned per GPU" if is_c2 else None,
                     "breakdown_ms_per_step": breakdown,
                     "note": "knn_scan = tcgen05 fp16 distance GEMM fused with thresholded candidate "
                             "lists (pivot-seeded bound); survivors re-ranked exactly in f32"}
@@ -448,8 +581,8 @@ def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, m
         clock_mhz = clk.summary().get("sm_mhz") or 1965.0
         fp32_peak = 148 * 128 * clock_mhz * 1e6 / 1e12  # FP32 lanes x clock, T ops/s
         ach_ops = ops / (per_launch_ms / 1e3) / 1e12
-        roofline = {"bound": "hbm", "kernel": "knn_scan", "achieved": gbs, "peak": pk["hbm_gbs"],
-                    "unit": "GB/s", "frac": gbs / pk["hbm_gbs"], "peak_source": f"{pk_kind} HBM copy",
+        roofline = {"bound": "hbm", "kernel": "knn_scan", "achieved": gbs, "peak": ctx.pk["hbm_gbs"],
+                    "unit": "GB/s", "frac": gbs / ctx.pk["hbm_gbs"], "peak_source": f"{ctx.pk_kind} HBM copy",
                     "per_launch_ms": per_launch_ms, "launches": scan_n,
                     "bytes_per_launch": bytes_per_launch, "traffic": None,
                     "binding": {"pipe": "fp32 CUDA cores", "achieved": ach_ops, "unit": "T ops/s",
@@ -460,69 +593,98 @@ def knn_bench(args, vc, torch, comm, dev, world, rank, local, stream, barrier, m
                     "note": "knn_scan = register-blocked CUDA-core scan (2 FP32 ops per element pair) "
                             "with pivot-seeded bounds; survivors re-ranked exactly"}
         dtype = "f32 CUDA-core scan + f32 exact re-rank"
-    big = n_loc * D * 4 > 126e6
     line = {
         "metric": metric_label(w), "value": value,
-        "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "unit": "queries/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": dtype, "data": w["data"],
-        "config": {"workload": w["name"], "n_base": n_base, "queries_per_step": n_q, "k": K, "dim": D,
-                   "parallelism": f"row-sharded x{world} + NCCL all-gather merge",
-                   "l2": ("inputs larger than L2 (f32 base shard %.0f MB), no flush" % (n_loc * D * 4 / 1e6))
-                         if big else "base shard smaller than L2: steps see a warm L2"},
+        "config": knn_config(w, world),
         "roofline": roofline,
         "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": n_q * D * 4,
-                "d2h_bytes_per_step": n_q * K * 8, "ms_per_step": ms_e2e / args.steps},
+                "d2h_bytes_per_step": n_q * K * 8, "ms_per_step": ms_e2e / ne, "steps": ne},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
         "clocks_e2e": clk2.summary(),
     }
-    # ------------------------------------------------------- CPU baseline
-    if rank == 0 and world == 1 and not args.no_cpu:
-        sample = min(w["cpu_sample"], n_q)
-        base_h = shard[:n_loc].cpu().numpy()
-        q_h = q_dev[:sample].cpu().numpy()
-        cb, (do, io) = cpu_leg(w, base_h, q_h, sample)
-        line["cpu_baseline"] = cb
-        gi = out_i[:sample].cpu().numpy().view(np.uint32)
-        gd = out_d[:sample].cpu().numpy()
-        line["parity_sample"] = {
-            "queries": sample,
-            "ids_equal_frac": float((gi == io).mean()),
-            "dist_bit_equal_frac": float((gd.view(np.uint32) == do.view(np.uint32)).mean())}
+    if sus:
+        line["sustained"] = sus
+    del q_host, hd, hi
     eng.close()
-    del shard, q_dev
     torch.cuda.empty_cache()
+
+    # ------------------------------------- parity (every N) and CPU baseline
+    # Rank 0 checks the merged results of the timed steps against the
+    # oracle on the whole base; the other ranks wait at the barrier.
+    if rank == 0 and parity_queries > 0:
+        orc = oracle_mod()
+        cores = host_cores()
+        sample = min(parity_queries, n_q)
+        q_h = q_dev[:sample].cpu().numpy()
+        if base_h is None and n_base * D * 4 <= 4e9:
+            full = torch.empty((n_base, D), dtype=torch.float32, device=dev)
+            vc.gen_rows_device(kind, seed, 0, 0, n_base, D, full.data_ptr())
+            torch.cuda.synchronize()
+            base_h = full.cpu().numpy()
+            del full
+        if base_h is not None:
+            t0 = time.perf_counter()
+            do, io = orc.knn_search(base_h, q_h, K, metric, nthreads=cores)
+            dt = time.perf_counter() - t0
+            how = "oracle knn_search over the whole base (host copy)"
+        else:
+            t0 = time.perf_counter()
+            do, io = oracle_topk_streamed(orc, vc, torch, dev, w, seed, kind, q_h)
+            dt = time.perf_counter() - t0
+            how = "oracle over the whole base, regenerated chunk by chunk on GPU 0 and merged by (score, id)"
+        line["parity_sample"] = dict(parity_stats(res_d[:sample], res_i[:sample], do, io), how=how,
+                                     n_gpus=world)
+        if cpu_leg and world == 1 and base_h is not None:
+            line["cpu_baseline"] = {
+                "value": sample / dt, "unit": "queries/s", "cores": cores, "kind": "port",
+                "sample": f"{sample} of the {n_q} queries against the full {n_base}-row base "
+                          f"(AVX-512 restatement of search_batch_cpu, {cores} threads)",
+                "seconds": dt}
+        torch.cuda.empty_cache()
+    del q_dev, base_h
+    barrier()
     return line
 
 
-def kmeans_bench(args, vc, torch, comm, dev, world, rank, barrier, max_over_ranks, peak_tc):
-    w = km_workload(args)
+def kmeans_bench(ctx, w, parity_iters, cpu_leg, parity_sample=None, sustained=True, e2e=True):
+    vc, torch, dev, world, rank = ctx.vc, ctx.torch, ctx.dev, ctx.world, ctx.rank
+    barrier, max_over_ranks = ctx.barrier, ctx.max_over_ranks
     KMN, KM_D, KM_K = w["n"], w["d"], w["K"]
     km_seed = vc.config_seed(w["seed"])
     k0, k1 = vc.shard_rows(KMN, world, rank)
+    n_loc = k1 - k0
     cent = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)
     vc.gen_rows_device(vc.GEN_NORMAL, km_seed, w["stream_c"], 0, KM_K, KM_D, cent.data_ptr())
-    xs = torch.empty((max(k1 - k0, 1), KM_D), dtype=torch.float32, device=dev)
-    vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, w["stream_x"], k0, k1 - k0, KM_D, xs.data_ptr(),
+    xs = torch.empty((max(n_loc, 1), KM_D), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, w["stream_x"], k0, n_loc, KM_D, xs.data_ptr(),
                        cent.data_ptr(), KM_K, w["sigma"])
     init = torch.empty((KM_K, KM_D), dtype=torch.float32, device=dev)  # the first K points
     vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, w["stream_x"], 0, KM_K, KM_D, init.data_ptr(),
                        cent.data_ptr(), KM_K, w["sigma"])
     init_h = init.cpu().numpy()
     torch.cuda.synchronize()
-    vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, 2, 0.0,
-                       vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(), n_local=k1 - k0)
+    M = vc.DistanceMetric.L2Squared
+
+    def fit(iters):
+        return vc.kmeans_fit_rank(ctx.comm, None, KMN, KM_D, KM_K, init_h, iters, 0.0, M,
+                                  device_ptr=xs.data_ptr(), n_local=n_loc)
+
+    fit(2)
     barrier()
     # Timed fit: only the whole Lloyd loop is bracketed by events (per-stage
     # events would add host work to every iteration).
     vc.profile_reset()
     vc.profile_enable(2)
-    t0 = time.perf_counter()
-    res = vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, w["iters"], 0.0,
-                             vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(), n_local=k1 - k0)
-    barrier()
-    km_s = max_over_ranks(time.perf_counter() - t0)
+    with ClockSampler(ctx.local) as clk:
+        barrier()
+        t0 = time.perf_counter()
+        res = fit(w["iters"])
+        barrier()
+        km_s = max_over_ranks(time.perf_counter() - t0)
     vc.profile_enable(False)
     loop_ms, _ = vc.profile_read("kmeans_loop")
     loop_s = max_over_ranks(loop_ms / 1e3)
@@ -530,15 +692,14 @@ def kmeans_bench(args, vc, torch, comm, dev, world, rank, barrier, max_over_rank
     barrier()
     vc.profile_reset()
     vc.profile_enable(True)
-    vc.kmeans_fit_rank(comm, None, KMN, KM_D, KM_K, init_h, w["iters"], 0.0,
-                       vc.DistanceMetric.L2Squared, device_ptr=xs.data_ptr(), n_local=k1 - k0)
+    fit(w["iters"])
     barrier()
     vc.profile_enable(False)
     a_ms, a_n = vc.profile_read("kmeans_assign")
     u_ms, u_n = vc.profile_read("kmeans_update")
     f_ms, f_n = vc.profile_read("kmeans_finalize")
     s_ms, s_n = vc.profile_read("kmeans_sums")
-    a_flops = 2.0 * (k1 - k0) * KM_K * KM_D
+    a_flops = 2.0 * n_loc * KM_K * KM_D
     a_ach = a_flops / (a_ms / max(a_n, 1) / 1e3) / 1e12
     out = {
         "metric": f"k-means iterations/s ({w['name']})",
@@ -546,23 +707,113 @@ def kmeans_bench(args, vc, torch, comm, dev, world, rank, barrier, max_over_rank
         "n_gpus": world, "iterations": res.iterations, "inertia": res.inertia, "loop_seconds": loop_s,
         "fit_call_seconds": km_s, "fit_call_iterations_per_s": res.iterations / km_s,
         "config": {"workload": w["name"], "n": KMN, "dim": KM_D, "K": KM_K, "sigma": w["sigma"],
-                   "init": "the first K points", "tol": 0.0},
+                   "init": "the first K points", "tol": 0.0,
+                   "parallelism": f"row-sharded x{world} + NCCL all-reduce of the sums"},
         "timing": "CUDA events around the Lloyd loop inside vrs_kmeans_fit_rank (points resident "
                   "in HBM; the loop includes each iteration's convergence readback; upload, operand "
                   "prep and initial centroids excluded), max over ranks; "
                   "fit_call_* times the whole call on the host",
-        "assign_roofline": {"bound": "tensor", "achieved": a_ach, "peak": peak_tc,
-                            "unit": "TFLOP/s", "frac": a_ach / peak_tc,
+        "assign_roofline": {"bound": "tensor", "achieved": a_ach, "peak": ctx.peak_burst,
+                            "unit": "TFLOP/s", "frac": a_ach / ctx.peak_burst,
+                            "peak_source": f"{ctx.pk_kind} bf16 dense, burst",
+                            "frac_of_sustained": a_ach / ctx.peak_sus,
+                            "flops_per_launch": a_flops,
                             "per_launch_ms": a_ms / max(a_n, 1), "launches": a_n},
         "update_ms_per_launch": u_ms / max(u_n, 1),
         "finalize_ms_per_launch": f_ms / max(f_n, 1),
-        "sums_ms_per_launch": s_ms / max(s_n, 1)}
+        "sums_ms_per_launch": s_ms / max(s_n, 1),
+        "clocks": clk.summary()}
+
+    if sustained:
+        # Whole fits back to back until at least one second of Lloyd loop.
+        vc.profile_reset()
+        vc.profile_enable(2)
+        n_fit = max(1, int(np.ceil(1.0 / max(loop_s, 1e-4))))
+        n_fit = int(max_over_ranks(float(n_fit)))
+        iters = 0
+        with ClockSampler(ctx.local) as clk_s:
+            barrier()
+            for _ in range(n_fit):
+                iters += fit(w["iters"]).iterations
+            barrier()
+        vc.profile_enable(False)
+        ls = max_over_ranks(vc.profile_read("kmeans_loop")[0] / 1e3)
+        out["sustained"] = {"fits": n_fit, "iterations": iters, "loop_seconds": ls, "value": iters / ls,
+                            "clocks": clk_s.summary()}
+
+    if e2e:
+        # Through the C ABI with host buffers: every rank's points are read
+        # from host memory and the centroids and its assignments come back to
+        # host memory inside the timed call (operand prep included).
+        x_host = xs[:n_loc].cpu().numpy()
+        vc.kmeans_fit_rank(ctx.comm, x_host, KMN, KM_D, KM_K, init_h, 1, 0.0, M)
+        with ClockSampler(ctx.local) as clk_e:
+            barrier()
+            t0 = time.perf_counter()
+            r_e = vc.kmeans_fit_rank(ctx.comm, x_host, KMN, KM_D, KM_K, init_h, w["iters"], 0.0, M)
+            e_s = max_over_ranks(time.perf_counter() - t0)
+            barrier()
+        out["e2e"] = {"value": r_e.iterations / e_s, "unit": "iterations/s", "seconds": e_s,
+                      "h2d_bytes_per_step": KMN * KM_D * 4 + world * KM_K * KM_D * 4,
+                      "d2h_bytes_per_step": world * KM_K * KM_D * 4 + KMN * 4,
+                      "how": "one vrs_kmeans_fit_rank per rank on host buffers (points, init in; centroids "
+                             "and assignments out), host clock around the call, max over ranks",
+                      "clocks": clk_e.summary()}
+        del x_host
+
+    # ------------------------------------- parity (every N) and CPU baseline
+    if parity_iters > 0:
+        r_p = fit(parity_iters)
+        a_local = torch.from_numpy(r_p.assignments.astype(np.int32)).to(dev)
+        if parity_sample:
+            a_all = a_local[:parity_sample] if rank == 0 else None  # rank 0's first rows are global rows
+        else:
+            a_all = ctx.gather_rows(a_local)
+        if rank == 0:
+            orc = oracle_mod()
+            cores = host_cores()
+            nx = parity_sample or KMN
+            full = torch.empty((nx, KM_D), dtype=torch.float32, device=dev)
+            vc.gen_rows_device(vc.GEN_MIXTURE, km_seed, w["stream_x"], 0, nx, KM_D, full.data_ptr(),
+                               cent.data_ptr(), KM_K, w["sigma"])
+            torch.cuda.synchronize()
+            x_h = full.cpu().numpy()
+            del full
+            g_assign = a_all.cpu().numpy()
+            t0 = time.perf_counter()
+            if parity_sample:
+                o_assign, _, _, _ = orc.kmeans_local(x_h, init_h, L2, nthreads=cores)
+                dt = time.perf_counter() - t0
+                out["parity"] = {"iterations": 1, "points": nx,
+                                 "assign_equal_frac": float((g_assign[:nx] == o_assign).mean()),
+                                 "n_gpus": world,
+                                 "how": "assignments of the first Lloyd step (against the initial "
+                                        f"centroids) for the first {nx} points vs the oracle"}
+            else:
+                c_o, o_assign, it_o, in_o = orc.kmeans_fit(x_h, KM_K, init_h, parity_iters, 0.0, L2,
+                                                           nthreads=cores)
+                dt = time.perf_counter() - t0
+                out["parity"] = {
+                    "iterations": int(it_o), "points": nx, "n_gpus": world,
+                    "assign_equal_frac": float((g_assign == o_assign).mean()),
+                    "inertia_gpu": r_p.inertia, "inertia_oracle": in_o,
+                    "inertia_rel_err": abs(r_p.inertia - in_o) / max(abs(in_o), 1e-30),
+                    "centroid_max_abs_err": float(np.abs(r_p.centroids - c_o).max()),
+                    "how": f"same init, {parity_iters} Lloyd iterations on all points, oracle fit_cpu restatement"}
+                if cpu_leg and world == 1:
+                    out["cpu_baseline"] = {
+                        "value": it_o / dt, "unit": "iterations/s", "cores": cores, "kind": "port",
+                        "sample": f"{it_o} of the {w['iters']} Lloyd iterations on all {nx} points "
+                                  f"(AVX-512 restatement of fit_cpu, {cores} threads)",
+                        "seconds": dt}
+        del a_local, a_all
     del xs, cent, init
     torch.cuda.empty_cache()
+    barrier()
     return out
 
 
-def ivf_bench(args, vc, torch, dev, peak_tc):
+def ivf_bench(args, vc, torch, dev, peak_tc):  # peak_tc: bf16 burst
     """IVF coarse quantiser on the C5b shape (the quantiser C5b trains):
     nlist = 16,384 centroids x 96, squared L2. Probes 10,000 queries at
     nprobe = 32 (KMeans::find_top_centroids per query in IvfPqIndex::search,

@@ -245,6 +245,14 @@ VRS_API int vrs_knn_search_noalloc(const float* base, int64_t n, int32_t d, cons
                                    int64_t nq, int32_t k, int32_t metric, float* out_dist,
                                    uint32_t* out_id, int32_t* out_k, void* cuda_stream);
 
+/* No counterpart in the reference (its kernels have no bounded waits).
+ * Self-test of the device-side bounded wait every tensor-core pipeline
+ * uses: one thread on the current device waits on an mbarrier that nothing
+ * arrives on, through the same helper, for limit_ns (1 us .. 1 s). Returns
+ * VRS_ERR_TIMEOUT with the stage code in vrs_last_error() when the wait gave
+ * up as designed, and leaves the device usable. */
+VRS_API int vrs_selftest_bounded_wait(int64_t limit_ns);
+
 /* ------------------------------------------------------ streams, profiling */
 /* Makes a single-GPU or rank-mode handle issue its work on `cuda_stream`
  * (a cudaStream_t of the handle's device; NULL restores the handle's own).

@@ -58,6 +58,14 @@ def lib():
                                      ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, _f32p, ctypes.c_void_p,
                                      ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_double)]
+        L.orc_knn_search_rows.restype = ctypes.c_int
+        L.orc_knn_search_rows.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, _f32p, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_uint32, _f32p, _u32p, ctypes.POINTER(ctypes.c_int)]
+        L.orc_gen_rows.restype = ctypes.c_int
+        L.orc_gen_rows.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int64,
+                                   ctypes.c_int64, ctypes.c_int, _f32p, ctypes.c_void_p, ctypes.c_uint32,
+                                   ctypes.c_double, ctypes.c_int]
         L.orc_kmeans_local.restype = None
         L.orc_kmeans_local.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _f32p,
                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
@@ -101,6 +109,48 @@ def knn_search(base, queries, k: int, metric: int, nthreads: int | None = None, 
     lib().orc_knn_search(base, n, d, queries, nq, int(k), int(metric),
                          int(nthreads or os.cpu_count() or 1), use_simd, out_d, out_i, ctypes.byref(ok))
     return out_d[:, :ok.value], out_i[:, :ok.value]
+
+
+def knn_search_rows(base, queries, k: int, metric: int, nthreads: int | None = None, use_simd: int = -1,
+                    id_offset: int = 0):
+    """knn_search for a few queries over many rows (threads split the rows;
+    identical results). Ids are row index + id_offset."""
+    base, queries = _f32(base), _f32(queries)
+    n, d = base.shape
+    nq = queries.shape[0]
+    kk = max(0, min(k, n))
+    out_d = np.zeros((nq, max(kk, 1)), np.float32)
+    out_i = np.zeros((nq, max(kk, 1)), np.uint32)
+    ok = ctypes.c_int(0)
+    lib().orc_knn_search_rows(base, n, d, queries, nq, int(k), int(metric), int(nthreads or os.cpu_count() or 1),
+                              use_simd, int(id_offset), out_d, out_i, ctypes.byref(ok))
+    return out_d[:, :ok.value], out_i[:, :ok.value]
+
+
+# Generator kinds (the product's VRS_GEN_* values).
+GEN_NORMAL, GEN_NORMAL_UNIT, GEN_UNIFORM, GEN_UNIFORM_SUM1, GEN_MIXTURE = 0, 1, 2, 3, 4
+
+
+def gen_rows(kind: int, seed: int, stream: int, row0: int, rows: int, d: int, centres=None, K: int = 0,
+             sigma: float = 0.0, nthreads: int | None = None) -> np.ndarray:
+    """Rows [row0, row0 + rows) of a seeded synthetic matrix (orc_gen.c), the
+    same bits the product's generator gives, without loading libvrs."""
+    out = np.empty((rows, d), np.float32)
+    cp = None
+    if centres is not None:
+        centres = _f32(centres)
+        cp = centres.ctypes.data
+    if rows > 0:
+        st = lib().orc_gen_rows(int(kind), int(seed), int(stream), int(row0), int(rows), int(d), out, cp,
+                                int(K), float(sigma), int(nthreads or os.cpu_count() or 1))
+        if st != 0:
+            raise ValueError("orc_gen_rows: bad arguments")
+    return out
+
+
+def config_seed(index: int) -> int:
+    """Seed of benchmark config `index`: "VRS_B001" as a 64-bit integer + index."""
+    return 0x5652535F42303031 + int(index)
 
 
 def topk_reduce(lists, k: int, metric: int):

@@ -667,6 +667,90 @@ int orc_knn_search(const float* base, int64_t n, int d, const float* q, int64_t 
     return 0;
 }
 
+/* The same search for a few queries over many rows: threads split the ROWS
+ * (each keeps k' per query over its row range, reading every row once for
+ * all queries), then the per-thread lists are merged per query in
+ * (heap score, id) order. The sequential heap above keeps exactly the k'
+ * smallest (heap score, id) pairs -- a later row with an equal score has a
+ * larger id and never displaces the root -- so the merged result is the
+ * same. Ids are row index + id_offset (for a base fed in chunks). */
+typedef struct {
+    const float* base; int64_t r0, r1; int d;
+    const float* q; int nq; int k; int metric; int simd; uint32_t id_offset;
+    cand_t* heaps; int* counts;
+} knn_rows_job_t;
+
+static void* knn_rows_worker(void* arg) {
+    knn_rows_job_t* j = arg;
+    int hib = orc_higher_is_better(j->metric);
+    for (int64_t x = j->r0; x < j->r1; x++) {
+        const float* xv = j->base + x * j->d;
+        for (int qi = 0; qi < j->nq; qi++) {
+            cand_t* heap = j->heaps + (size_t)qi * j->k;
+            int hn = j->counts[qi];
+            float key = rank_key(j->metric, j->q + (int64_t)qi * j->d, xv, j->d, j->simd);
+            cand_t c = { hib ? -key : key, 0.0f, (uint32_t)x + j->id_offset };
+            if (hn < j->k) {
+                c.dist = finish(j->metric, key);
+                heap[hn++] = c;
+                sift_up(heap, hn - 1);
+                j->counts[qi] = hn;
+            } else if (cand_less(&c, &heap[0])) {
+                c.dist = finish(j->metric, key);
+                heap[0] = c;
+                sift_down(heap, hn, 0);
+            }
+        }
+    }
+    return NULL;
+}
+
+int orc_knn_search_rows(const float* base, int64_t n, int d, const float* q, int nq, int k, int metric,
+                        int nthreads, int use_simd, uint32_t id_offset, float* out_dist, uint32_t* out_id,
+                        int* out_k) {
+    int kk = (int)(k < n ? k : n);
+    if (kk < 0) kk = 0;
+    *out_k = kk;
+    if (nq <= 0 || kk == 0) return 0;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    if (n < (int64_t)nthreads * 64) nthreads = 1;
+    int simd = pick_simd(use_simd);
+    cand_t* heaps = malloc(sizeof(cand_t) * (size_t)nthreads * nq * kk);
+    int* counts = calloc((size_t)nthreads * nq, sizeof(int));
+    pthread_t th[256];
+    knn_rows_job_t jobs[256];
+    int64_t per = (n + nthreads - 1) / nthreads;
+    int started = 0;
+    for (int t = 0; t < nthreads; t++) {
+        int64_t r0 = t * per, r1 = r0 + per < n ? r0 + per : n;
+        jobs[t] = (knn_rows_job_t){ base, r0 < n ? r0 : n, r1 > r0 ? r1 : r0, d, q, nq, kk, metric, simd,
+                                    id_offset, heaps + (size_t)t * nq * kk, counts + (size_t)t * nq };
+        pthread_create(&th[t], NULL, knn_rows_worker, &jobs[t]);
+        started++;
+    }
+    for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
+    cand_t* all = malloc(sizeof(cand_t) * (size_t)nthreads * kk);
+    for (int qi = 0; qi < nq; qi++) {
+        int m = 0;
+        for (int t = 0; t < started; t++) {
+            const cand_t* h = heaps + ((size_t)t * nq + qi) * kk;
+            int c = counts[(size_t)t * nq + qi];
+            memcpy(all + m, h, sizeof(cand_t) * (size_t)c);
+            m += c;
+        }
+        qsort(all, m, sizeof(cand_t), cmp_cand);
+        for (int r = 0; r < kk && r < m; r++) {
+            out_dist[(int64_t)qi * kk + r] = all[r].dist;
+            out_id[(int64_t)qi * kk + r] = all[r].id;
+        }
+    }
+    free(all);
+    free(heaps);
+    free(counts);
+    return 0;
+}
+
 /* CollectiveOps::top_k_reduce (collective.rs:115-159): lists concatenated in
  * rank order, same strict heap rule, output best-first. lens[r] entries per
  * list; returns the merged count. */

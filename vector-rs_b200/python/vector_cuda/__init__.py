@@ -169,6 +169,7 @@ def lib() -> ctypes.CDLL:
         L.vrs_gen_rows_device.argtypes = [c.c_int32, c.c_uint64, c.c_uint32, c.c_int64, c.c_int64,
                                           c.c_int32, c.c_int64, c.c_void_p, c.c_void_p, c.c_uint32,
                                           c.c_double, c.c_void_p]
+        L.vrs_selftest_bounded_wait.argtypes = [c.c_int64]
         _lib_handle = L
     return _lib_handle
 
