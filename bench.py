@@ -249,7 +249,8 @@ def knn_config(w, world):
     n_loc = -(-w["n"] // world)
     big = n_loc * w["d"] * 4 > 126e6
     return {"workload": w["name"], "n_base": w["n"], "queries_per_step": w["nq"], "k": w["k"], "dim": w["d"],
-            "parallelism": f"row-sharded x{world} + NCCL all-gather merge",
+            "parallelism": f"row-sharded x{world}; queries broadcast from rank 0, per-query-slice "
+                           "NCCL exchange + GPU merge, results to rank 0",
             "l2": ("inputs larger than L2 (f32 base shard %.0f MB), no flush" % (n_loc * w["d"] * 4 / 1e6))
                   if big else "base shard smaller than L2: steps see a warm L2"}
 
@@ -472,8 +473,14 @@ def knn_bench(ctx, w, steps, warmup, parity_queries, cpu_leg, sustained, e2e_ste
     out_d = torch.empty((n_q, K), dtype=torch.float32, device=dev)
     out_i = torch.empty((n_q, K), dtype=torch.int32, device=dev)
 
+    # Root I/O: rank 0 alone supplies the queries (broadcast to the other
+    # ranks over NVLink) and receives the merged results, like the one
+    # caller of search_batch; the other ranks pass no buffers.
+    root = rank == 0
+
     def step_dev():
-        return eng.search_device(q_dev.data_ptr(), n_q, K, out_d.data_ptr(), out_i.data_ptr())
+        return eng.search_device(q_dev.data_ptr() if root else 0, n_q, K, out_d.data_ptr() if root else 0,
+                                 out_i.data_ptr() if root else 0, root=True)
 
     for _ in range(warmup):
         step_dev()
@@ -489,8 +496,7 @@ def knn_bench(ctx, w, steps, warmup, parity_queries, cpu_leg, sustained, e2e_ste
         barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     launches = vc.profile_read("*")[1]
-    # Results of the timed steps, for the parity check (every rank holds
-    # the merged top-k').
+    # Results of the timed steps (on rank 0), for the parity check.
     res_i = out_i.cpu().numpy().view(np.uint32).copy() if rank == 0 else None
     res_d = out_d.cpu().numpy().copy() if rank == 0 else None
     # Per-kernel breakdown from the same steps run again with the library's
@@ -531,10 +537,9 @@ def knn_bench(ctx, w, steps, warmup, parity_queries, cpu_leg, sustained, e2e_ste
 
     def step_host():
         kk = vc.ctypes.c_int32()
-        vc._check(vc.lib().vrs_knn_search_ex(eng._h, vc.ctypes.c_void_p(q_host.data_ptr()), n_q, K,
-                                            vc.ctypes.c_void_p(hd.data_ptr()),
-                                            vc.ctypes.c_void_p(hi.data_ptr()),
-                                            vc.ctypes.byref(kk), 0))
+        vp = (lambda t: vc.ctypes.c_void_p(t.data_ptr())) if root else (lambda t: None)
+        vc._check(vc.lib().vrs_knn_search_ex(eng._h, vp(q_host), n_q, K, vp(hd), vp(hi), vc.ctypes.byref(kk),
+                                            vc.MEM_ROOT))
 
     ne = e2e_steps or steps
     for _ in range(max(1, warmup // 2)):

@@ -63,6 +63,14 @@ typedef enum vrs_shard_mode { VRS_SHARDED = 0, VRS_REPLICATED = 1 } vrs_shard_mo
 /* Buffer location flags for the *_ex calls. */
 #define VRS_MEM_HOST 0
 #define VRS_MEM_DEVICE 1
+/* vrs_knn_search_ex only, OR'ed with one of the above: in rank mode, only
+ * rank 0's query and output pointers are used (the others may be NULL);
+ * the queries travel to the other ranks by NCCL broadcast and the merged
+ * results come back to rank 0 alone, as to the one caller of
+ * search_batch (crates/vector-cuda/src/ddp/distributed_knn.rs:155-231).
+ * Without it every rank passes the same queries and receives all results.
+ * Ignored by single-process handles (their caller is the root). */
+#define VRS_MEM_ROOT 2
 
 /* Replaces CudaDeviceContext::device_count (crates/vector-cuda/src/device.rs:110-118).
  * Writes 0 (and returns VRS_OK) when no driver or GPU is present. */
@@ -99,7 +107,8 @@ VRS_API int vrs_knn_search(vrs_knn* h, const float* queries, int64_t nq, int32_t
                    uint32_t* out_id, int32_t* out_k);
 
 /* As vrs_knn_search; mem = VRS_MEM_DEVICE means queries/out_* are device
- * pointers on the handle's first GPU (rank mode: the rank's GPU). */
+ * pointers on the handle's first GPU (rank mode: the rank's GPU);
+ * VRS_MEM_ROOT (rank mode) reads queries and writes results on rank 0 only. */
 VRS_API int vrs_knn_search_ex(vrs_knn* h, const float* queries, int64_t nq, int32_t k, float* out_dist,
                       uint32_t* out_id, int32_t* out_k, int32_t mem);
 

@@ -111,6 +111,12 @@ def _rank_worker(rank, world, uid, out_q):
                                                   vc.GpuShardMode.Sharded,
                                                   vc.DistanceMetric.L2Squared)
         d, i = eng.search_arrays(qs, 64)
+        # Root I/O: rank 0 alone passes queries and receives the results.
+        root = eng.search_root(qs if rank == 0 else None, 64, nq=len(qs))
+        ok_root = (root is None) == (rank != 0)
+        if rank == 0:
+            ok_root = ok_root and np.array_equal(root[1], i) and np.array_equal(root[0].view(np.uint32),
+                                                                               d.view(np.uint32))
         eng.close()
         s = vc.config_seed(830)
         cent = vc.gen_rows_host(vc.GEN_NORMAL, s, 2, 0, 32, 24)
@@ -119,7 +125,7 @@ def _rank_worker(rank, world, uid, out_q):
         res = vc.kmeans_fit_rank(comm, x[k0:k1], len(x), 24, 32, x[:32], 5, 0.0,
                                  vc.DistanceMetric.L2Squared)
         comm.close()
-        out_q.put((rank, d, i, res.centroids, res.assignments, res.iterations, res.inertia))
+        out_q.put((rank, d, i, res.centroids, res.assignments, res.iterations, res.inertia, ok_root))
     except Exception as e:  # noqa: BLE001 - reported to the parent
         out_q.put((rank, "error", repr(e)))
 
@@ -148,6 +154,7 @@ def test_rank_mode_knn_and_kmeans(vc, orc, two):
     do, io = orc.knn_search(base, qs, 64, L2)
     for r in range(world):
         _same(got[r][1], got[r][2], do, io)
+        assert got[r][7], f"rank {r}: root I/O search"
     s = vc.config_seed(830)
     cent = vc.gen_rows_host(vc.GEN_NORMAL, s, 2, 0, 32, 24)
     x = vc.gen_rows_host(vc.GEN_MIXTURE, s, 0, 0, 20_003, 24, cent, 32, 0.1)

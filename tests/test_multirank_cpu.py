@@ -8,6 +8,9 @@ single-process oracle:
   with global ids (local id + r0), an all-gather, and the reference's
   top_k_reduce merge in rank order (ddp/collective.rs:115-152) give exactly
   the unsharded search, ties by lower id included;
+* the same search as libvrs runs it in rank mode: queries broadcast from
+  rank 0, every rank's lists exchanged so that each rank merges one slice
+  of the queries, merged slices gathered on rank 0;
 * GpuShardMode::Replicated -- query chunks by `query_chunk`, concatenated in
   rank order (ddp/distributed_knn.rs:201-229);
 * distributed Lloyd -- per-rank assignment, sums and counts, an all-reduce,
@@ -82,6 +85,57 @@ def _sharded_knn(rank, world, port, out_q):
                     ok &= bool(np.array_equal(md.view(np.uint32), d_full[qi].view(np.uint32)))
     if rank == 0:
         out_q.put(("sharded", ok))
+    dist.destroy_process_group()
+
+
+def _sliced_merge_knn(rank, world, port, out_q):
+    """The merge protocol of a row-sharded search in rank mode: rank 0 alone
+    holds the queries and broadcasts them; each rank's top-k' lists (global
+    ids) are padded to world * c rows (c = ceil(nq / world)) and exchanged so
+    that rank p holds every rank's lists for queries [p c, (p+1) c); rank p
+    merges that slice in rank order; the merged slices are gathered on rank
+    0 alone. The result must be the unsharded search."""
+    _paths()
+    import torch
+    import oracle
+    import vector_cuda as vc
+    dist = _init(rank, world, port)
+    ok = True
+    for metric, n, nq in ((L2, 1001, 13), (COS, 640, 8), (HAM, 999, 5)):
+        base, qs_all = _knn_data(vc, metric, n, nq, 9, 20 + metric)
+        k = 7
+        q = torch.from_numpy(qs_all.copy()) if rank == 0 else torch.zeros((nq, 9), dtype=torch.float32)
+        dist.broadcast(q, src=0)
+        qs = q.numpy()
+        r0, r1 = vc.shard_rows(n, world, rank)
+        d_loc, i_loc = oracle.knn_search(base[r0:r1], qs, k, metric, nthreads=2)
+        c = -(-nq // world)
+        pad_d = np.full((world * c, k), np.nan, np.float32)
+        pad_i = np.full((world * c, k), 0xFFFFFFFF, np.uint32)
+        pad_d[:nq], pad_i[:nq] = d_loc, i_loc + np.uint32(r0)
+        recv_d = torch.empty((world * c, k), dtype=torch.float32)
+        recv_i = torch.empty((world * c, k), dtype=torch.int64)
+        dist.all_to_all_single(recv_d, torch.from_numpy(pad_d))
+        dist.all_to_all_single(recv_i, torch.from_numpy(pad_i.astype(np.int64)))
+        rd, ri = recv_d.numpy().reshape(world, c, k), recv_i.numpy().reshape(world, c, k).astype(np.uint32)
+        md = np.full((c, k), np.nan, np.float32)
+        mi = np.full((c, k), 0xFFFFFFFF, np.uint32)
+        for j in range(c):
+            if rank * c + j >= nq:
+                continue  # padding query
+            lists = [(rd[g, j], ri[g, j]) for g in range(world)]
+            dd, ii = oracle.topk_reduce(lists, k, metric)
+            md[j, :len(dd)], mi[j, :len(ii)] = dd, ii
+        slices = [None] * world
+        dist.all_gather_object(slices, (md, mi))
+        if rank == 0:
+            gd = np.concatenate([x[0] for x in slices])[:nq]
+            gi = np.concatenate([x[1] for x in slices])[:nq]
+            d_full, i_full = oracle.knn_search(base, qs_all, k, metric, nthreads=2)
+            ok &= bool(np.array_equal(gi, i_full))
+            ok &= bool(np.array_equal(gd.view(np.uint32), d_full.view(np.uint32)))
+    if rank == 0:
+        out_q.put(("sliced", ok))
     dist.destroy_process_group()
 
 
@@ -180,8 +234,8 @@ def _run(fn, timeout=240):
     return res
 
 
-@pytest.mark.parametrize("fn,name", [(_sharded_knn, "sharded"), (_replicated_knn, "replicated"),
-                                     (_distributed_lloyd, "lloyd")])
+@pytest.mark.parametrize("fn,name", [(_sharded_knn, "sharded"), (_sliced_merge_knn, "sliced"),
+                                     (_replicated_knn, "replicated"), (_distributed_lloyd, "lloyd")])
 def test_two_rank_semantics(fn, name):
     got = _run(fn)
     assert got == (name, True)

@@ -80,18 +80,22 @@ def test_noalloc_largest_batch_at_k_2048(vc, gpu):
 
 
 def test_noalloc_rejects_oversized_batch(vc, gpu):
+    # Every buffer is sized for the full request, so nothing would be read or
+    # written out of bounds even if a batch were accepted.
     import torch
     fn = _noalloc(vc)
-    n, d, nq, k = 1000, 16, 200000, 100
+    n, d = 5000, 16
     db = torch.zeros((n, d), dtype=torch.float32, device="cuda")
-    dq = torch.zeros((8, d), dtype=torch.float32, device="cuda")
     kk = ctypes.c_int32(0)
-    st = fn(db.data_ptr(), n, d, dq.data_ptr(), nq, k, 0, dq.data_ptr(), dq.data_ptr(), ctypes.byref(kk), None)
-    assert st == 5 and b"no-alloc scratch" in vc.lib().vrs_last_error()
-    # One query more than fits at k' = 2048 is refused too.
-    st = fn(db.data_ptr(), n, d, dq.data_ptr(), 128, 2048, 0, dq.data_ptr(), dq.data_ptr(), ctypes.byref(kk),
-            None)
-    assert st == 5 and b"no-alloc scratch" in vc.lib().vrs_last_error()
+    for nq, k in ((3000, 100), (128, 2048)):  # 2043 and 127 queries fit at these k'
+        dq = torch.zeros((nq, d), dtype=torch.float32, device="cuda")
+        od = torch.zeros((nq, k), dtype=torch.float32, device="cuda")
+        oi = torch.zeros((nq, k), dtype=torch.int32, device="cuda")
+        st = fn(db.data_ptr(), n, d, dq.data_ptr(), nq, k, 0, od.data_ptr(), oi.data_ptr(), ctypes.byref(kk),
+                None)
+        assert st == 5 and b"no-alloc scratch" in vc.lib().vrs_last_error()
+        assert kk.value == 0
+    torch.cuda.synchronize()
 
 
 def test_noalloc_rejects_huge_query_count_before_device_work(vc, gpu):

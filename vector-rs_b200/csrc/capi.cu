@@ -230,7 +230,10 @@ struct KnnShard {
   // per-search scratch
   DBuf q_in, q, q_aux, cand, cnt, overflow, pairs, gathered, out_dist, out_id;
   DBuf qb, absm, err, qindex;
-  DBuf mflags;                  // [nq] queries whose merged top-k' holds a sentinel
+  DBuf mflags;                  // [c] queries of this shard's merge slice whose top-k' holds a sentinel
+  DBuf all_flags;               // [G * c] every slice's flags (all-gathered)
+  DBuf sl_dist, sl_id;          // [c][k'] this shard's merged slice
+  DBuf q_root;                  // [nq][d] queries broadcast from rank 0 (root I/O)
   HBuf hstat;                   // pinned: [nq] flags, then the scan's error word
   int last_nq = 0, last_kk = 0, last_nseg = 0, last_cap = 0;
 };
@@ -259,7 +262,8 @@ struct vrs_knn {
       for (DBuf* b : {&s->base, &s->base_aux, &s->q_in, &s->q, &s->q_aux, &s->cand, &s->cnt,
                       &s->overflow, &s->pairs, &s->gathered, &s->out_dist, &s->out_id, &s->xb,
                       &s->xn, &s->xmax, &s->tiny, &s->ntiny, &s->qb, &s->absm, &s->err, &s->qindex, &s->pb,
-                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all, &s->qscale, &s->mflags})
+                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all, &s->qscale, &s->mflags,
+                      &s->all_flags, &s->sl_dist, &s->sl_id, &s->q_root})
         b->release();
       s->hstat.release();
       if (s->own_stream) cudaStreamDestroy(s->own_stream);
@@ -297,16 +301,17 @@ void par_memcpy(void* dst, const void* src, size_t bytes) {
   for (auto& t : th) t.join();
 }
 
-// Host rows reach the shard through two pinned staging slots of 64 MB: while
-// one slot's rows are copied to the device and padded (on the shard stream),
-// the next chunk is copied from the caller's (pageable or mapped) memory into
-// the other slot. A slot is refilled only after the event recorded behind its
-// last device copy has completed.
-int upload_host_rows(vrs_knn* h, KnnShard* s, const float* rows, int transform) {
-  const size_t row_bytes = (size_t)h->d * sizeof(float);
+// Host rows reach the device through two pinned staging slots of 64 MB:
+// while one slot's rows are copied to the device and padded (on `st`), the
+// next chunk is copied from the caller's (pageable or mapped) memory into
+// the other slot. A slot is refilled only after the event recorded behind
+// its last device copy has completed. dst: n rows of dp floats.
+int stage_host_rows(const float* rows, int64_t n, int d, int dp, float* dst, int transform, cudaStream_t st) {
+  if (n <= 0) return VRS_OK;
+  const size_t row_bytes = (size_t)d * sizeof(float);
   const int64_t chunk = std::max<int64_t>(1, (int64_t)(64ll << 20) / (int64_t)row_bytes);
-  const int64_t nchunks = (s->n_local + chunk - 1) / chunk;
-  const size_t slot_bytes = (size_t)std::min<int64_t>(chunk, s->n_local) * row_bytes;
+  const int64_t nchunks = (n + chunk - 1) / chunk;
+  const size_t slot_bytes = (size_t)std::min<int64_t>(chunk, n) * row_bytes;
   struct Slots {
     HBuf pin[2];
     DBuf dev[2];
@@ -318,7 +323,7 @@ int upload_host_rows(vrs_knn* h, KnnShard* s, const float* rows, int transform) 
         if (e) cudaEventDestroy(e);
     }
   } sl;
-  sl.st = s->stream;
+  sl.st = st;
   for (int j = 0; j < 2 && j < nchunks; j++) {
     VRS_TRY(sl.pin[j].reserve(slot_bytes));
     VRS_TRY(sl.dev[j].reserve(slot_bytes));
@@ -326,17 +331,20 @@ int upload_host_rows(vrs_knn* h, KnnShard* s, const float* rows, int transform) 
   }
   for (int64_t c = 0; c < nchunks; c++) {
     const int j = (int)(c & 1);
-    const int64_t r0 = c * chunk, rc = std::min(chunk, s->n_local - r0);
+    const int64_t r0 = c * chunk, rc = std::min(chunk, n - r0);
     const size_t bytes = (size_t)rc * row_bytes;
     if (c >= 2) VRS_CUDA(cudaEventSynchronize(sl.ev[j]));
-    par_memcpy(sl.pin[j].p, rows + r0 * h->d, bytes);
-    VRS_CUDA(cudaMemcpyAsync(sl.dev[j].p, sl.pin[j].p, bytes, cudaMemcpyHostToDevice, s->stream));
-    VRS_TRY(launch_pad_rows(sl.dev[j].as<float>(), rc, h->d, h->dp, s->base.as<float>() + r0 * h->dp,
-                            transform, s->stream));
-    VRS_CUDA(cudaEventRecord(sl.ev[j], s->stream));
+    par_memcpy(sl.pin[j].p, rows + r0 * d, bytes);
+    VRS_CUDA(cudaMemcpyAsync(sl.dev[j].p, sl.pin[j].p, bytes, cudaMemcpyHostToDevice, st));
+    VRS_TRY(launch_pad_rows(sl.dev[j].as<float>(), rc, d, dp, dst + r0 * dp, transform, st));
+    VRS_CUDA(cudaEventRecord(sl.ev[j], st));
   }
-  VRS_CUDA(cudaStreamSynchronize(s->stream));
+  VRS_CUDA(cudaStreamSynchronize(st));
   return VRS_OK;
+}
+
+int upload_host_rows(vrs_knn* h, KnnShard* s, const float* rows, int transform) {
+  return stage_host_rows(rows, s->n_local, h->d, h->dp, s->base.as<float>(), transform, s->stream);
 }
 
 // Uploads (or copies) one shard's rows into the padded layout.
@@ -838,42 +846,95 @@ int64_t query_batch(int kk) {
   return 16384;
 }
 
-// Row-sharded merge: slots a shard flagged become sentinel pairs, every
-// shard's pairs are all-gathered, and the merge (GPU 0 of a clique, every
-// rank in rank mode, so every rank sees the same flags) marks the queries
-// whose top-k' holds a sentinel.
-int sharded_merge(vrs_knn* h, int nb, int kk, double tmo) {
+// Queries each merge participant owns: slice p is rows [p*c, (p+1)*c) of a
+// batch of nb, c = ceil(nb / nranks); the pair lists are padded to
+// nranks * c rows so every slice has the same size.
+int slice_rows(int nb, int nranks) { return (nb + nranks - 1) / nranks; }
+
+// Participant index of shard r: the GPU's position in a clique, the rank in
+// rank mode.
+int participant(const vrs_knn* h, int r) { return h->rank_mode ? h->comm->rank : r; }
+
+// Row-sharded merge, split by query. Slots a shard flagged become sentinel
+// pairs; participant p receives every shard's pairs for its own query slice
+// (grouped NCCL sends and receives, its own slice by a device copy), merges
+// that slice G ways in (score, id, rank) order and flags the queries whose
+// top-k' holds a sentinel. The flags are all-gathered (every shard learns
+// which queries to search again); the merged slices go to participant 0
+// (root_only: the clique, or a rank-mode call whose results only rank 0
+// reads) or to every participant. Per shard this moves 2 (G-1)/G of one
+// shard's pair lists instead of receiving all G of them, and merges nb/G
+// queries instead of nb.
+int sharded_merge(vrs_knn* h, int nb, int kk, bool root_only, double tmo) {
   const int G = (int)h->shards.size();
   const int nranks = h->rank_mode ? h->comm->nranks : G;
-  for (int r = 0; r < G; r++) {
-    KnnShard* s = h->shards[r].get();
-    VRS_CUDA(cudaSetDevice(s->device));
-    VRS_TRY(launch_flag_pairs(s->overflow.as<int>(), nb, kk, s->pairs.as<Cand>(), s->stream));
-  }
+  const int c = slice_rows(nb, nranks);
+  const size_t sl = (size_t)c * kk;  // pairs in one slice
   std::vector<ProfToken> tg(G);
   for (int r = 0; r < G; r++) {
-    VRS_CUDA(cudaSetDevice(h->shards[r]->device));
-    tg[r] = prof_begin("knn_gather", h->shards[r]->stream);
+    KnnShard* s = h->shards[r].get();
+    const int p = participant(h, r);
+    VRS_CUDA(cudaSetDevice(s->device));
+    VRS_TRY(launch_flag_pairs(s->overflow.as<int>(), nb, kk, s->pairs.as<Cand>(), s->stream));
+    VRS_TRY(s->gathered.reserve((size_t)nranks * sl * sizeof(Cand)));
+    VRS_TRY(s->sl_dist.reserve(sl * sizeof(float)));
+    VRS_TRY(s->sl_id.reserve(sl * sizeof(uint32_t)));
+    VRS_TRY(s->mflags.reserve((size_t)c * sizeof(int)));
+    VRS_TRY(s->all_flags.reserve((size_t)nranks * c * sizeof(int)));
+    VRS_TRY(s->out_dist.reserve((size_t)nranks * sl * sizeof(float)));
+    VRS_TRY(s->out_id.reserve((size_t)nranks * sl * sizeof(uint32_t)));
+    VRS_CUDA(cudaMemsetAsync(s->mflags.p, 0, (size_t)c * sizeof(int), s->stream));
+    tg[r] = prof_begin("knn_gather", s->stream);
+    VRS_CUDA(cudaMemcpyAsync(s->gathered.as<Cand>() + (size_t)p * sl, s->pairs.as<Cand>() + (size_t)p * sl,
+                             sl * sizeof(Cand), cudaMemcpyDeviceToDevice, s->stream));
   }
   VRS_NCCL(ncclGroupStart());
   for (int r = 0; r < G; r++) {
     KnnShard* s = h->shards[r].get();
-    VRS_NCCL(ncclAllGather(s->pairs.p, s->gathered.p, (size_t)nb * kk, ncclUint64, s->comm, s->stream));
+    const int p = participant(h, r);
+    for (int j = 0; j < nranks; j++) {
+      if (j == p) continue;
+      VRS_NCCL(ncclSend(s->pairs.as<Cand>() + (size_t)j * sl, sl, ncclUint64, j, s->comm, s->stream));
+      VRS_NCCL(ncclRecv(s->gathered.as<Cand>() + (size_t)j * sl, sl, ncclUint64, j, s->comm, s->stream));
+    }
   }
   VRS_NCCL(ncclGroupEnd());
-  for (int r = 0; r < G; r++) {
-    VRS_CUDA(cudaSetDevice(h->shards[r]->device));
-    prof_end(tg[r], h->shards[r]->stream);
-  }
   for (int r = 0; r < G; r++) VRS_TRY(nccl_ready(h->shards[r]->comm, tmo));
-  KnnShard* s0 = h->shards[0].get();
-  VRS_CUDA(cudaSetDevice(s0->device));
-  VRS_TRY(s0->mflags.reserve((size_t)nb * sizeof(int)));
-  VRS_CUDA(cudaMemsetAsync(s0->mflags.p, 0, (size_t)nb * sizeof(int), s0->stream));
-  ProfToken t = prof_begin("knn_merge", s0->stream);
-  VRS_TRY(launch_merge_pairs(s0->gathered.as<Cand>(), nranks, nb, kk, h->metric, s0->out_dist.as<float>(),
-                             s0->out_id.as<uint32_t>(), s0->mflags.as<int>(), s0->stream));
-  prof_end(t, s0->stream);
+  for (int r = 0; r < G; r++) {
+    KnnShard* s = h->shards[r].get();
+    VRS_CUDA(cudaSetDevice(s->device));
+    prof_end(tg[r], s->stream);
+    ProfToken t = prof_begin("knn_merge", s->stream);
+    VRS_TRY(launch_merge_pairs(s->gathered.as<Cand>(), nranks, c, kk, h->metric, s->sl_dist.as<float>(),
+                               s->sl_id.as<uint32_t>(), s->mflags.as<int>(), s->stream));
+    prof_end(t, s->stream);
+    if (root_only && participant(h, r) == 0) {
+      VRS_CUDA(cudaMemcpyAsync(s->out_dist.p, s->sl_dist.p, sl * sizeof(float), cudaMemcpyDeviceToDevice,
+                               s->stream));
+      VRS_CUDA(cudaMemcpyAsync(s->out_id.p, s->sl_id.p, sl * sizeof(uint32_t), cudaMemcpyDeviceToDevice,
+                               s->stream));
+    }
+  }
+  VRS_NCCL(ncclGroupStart());
+  for (int r = 0; r < G; r++) {
+    KnnShard* s = h->shards[r].get();
+    const int p = participant(h, r);
+    VRS_NCCL(ncclAllGather(s->mflags.p, s->all_flags.p, (size_t)c, ncclInt32, s->comm, s->stream));
+    if (!root_only) {
+      VRS_NCCL(ncclAllGather(s->sl_dist.p, s->out_dist.p, sl, ncclFloat32, s->comm, s->stream));
+      VRS_NCCL(ncclAllGather(s->sl_id.p, s->out_id.p, sl, ncclUint32, s->comm, s->stream));
+    } else if (p != 0) {
+      VRS_NCCL(ncclSend(s->sl_dist.p, sl, ncclFloat32, 0, s->comm, s->stream));
+      VRS_NCCL(ncclSend(s->sl_id.p, sl, ncclUint32, 0, s->comm, s->stream));
+    } else {
+      for (int j = 1; j < nranks; j++) {
+        VRS_NCCL(ncclRecv(s->out_dist.as<float>() + (size_t)j * sl, sl, ncclFloat32, j, s->comm, s->stream));
+        VRS_NCCL(ncclRecv(s->out_id.as<uint32_t>() + (size_t)j * sl, sl, ncclUint32, j, s->comm, s->stream));
+      }
+    }
+  }
+  VRS_NCCL(ncclGroupEnd());
+  for (int r = 0; r < G; r++) VRS_TRY(nccl_ready(h->shards[r]->comm, tmo));
   return VRS_OK;
 }
 
@@ -882,13 +943,18 @@ int sharded_merge(vrs_knn* h, int nb, int kk, double tmo) {
 // bounded wait per shard. Flagged queries (a list overflowed, a bound failed
 // its check, a near-zero cosine query) are searched again with the exact
 // scan on every shard and merged again; that second pass must come out
-// clean. No host round trip sits between the scan and the merge.
-int sharded_finish(vrs_knn* h, int nb, int kk, float* odst, uint32_t* oid, cudaMemcpyKind d2h, double tmo) {
+// clean. No host round trip sits between the scan and the merge. Results
+// reach odst/oid from the root shard (shard 0 of a clique; rank 0 in rank
+// mode with root_only) or, in rank mode without it, on every rank.
+int sharded_finish(vrs_knn* h, int nb, int kk, float* odst, uint32_t* oid, cudaMemcpyKind d2h, bool root_only,
+                   double tmo) {
   const int G = (int)h->shards.size();
   const int nranks = h->rank_mode ? h->comm->nranks : G;
+  const bool merged = nranks > 1;
+  const bool root = !h->rank_mode || !root_only || h->comm->rank == 0;
   KnnShard* s0 = h->shards[0].get();
   for (int pass = 0; pass < 2; pass++) {
-    if (nranks > 1) VRS_TRY(sharded_merge(h, nb, kk, tmo));
+    if (merged) VRS_TRY(sharded_merge(h, nb, kk, root_only || !h->rank_mode, tmo));
     for (int r = 0; r < G; r++) {
       KnnShard* s = h->shards[r].get();
       VRS_CUDA(cudaSetDevice(s->device));
@@ -898,16 +964,18 @@ int sharded_finish(vrs_knn* h, int nb, int kk, float* odst, uint32_t* oid, cudaM
       if (s->use_tc && s->last_nq > 0)
         VRS_CUDA(cudaMemcpyAsync(hs + nb, s->err.p, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
       if (r == 0) {
-        const int* dflags = nranks > 1 ? s0->mflags.as<int>() : s0->overflow.as<int>();
+        const int* dflags = merged ? s0->all_flags.as<int>() : s0->overflow.as<int>();
         VRS_CUDA(cudaMemcpyAsync(hs, dflags, (size_t)nb * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
-        VRS_CUDA(cudaMemcpyAsync(odst, s0->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s->stream));
-        VRS_CUDA(cudaMemcpyAsync(oid, s0->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s->stream));
+        if (root) {
+          VRS_CUDA(cudaMemcpyAsync(odst, s0->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s->stream));
+          VRS_CUDA(cudaMemcpyAsync(oid, s0->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s->stream));
+        }
       }
     }
     for (int r = 0; r < G; r++) {
       KnnShard* s = h->shards[r].get();
       VRS_CUDA(cudaSetDevice(s->device));
-      VRS_TRY(stream_wait(s->stream, nranks > 1 ? s->comm : nullptr, tmo));
+      VRS_TRY(stream_wait(s->stream, merged ? s->comm : nullptr, tmo));
     }
     for (int r = 0; r < G; r++) {
       const int e = h->shards[r]->hstat.as<int>()[nb];
@@ -931,7 +999,7 @@ int sharded_finish(vrs_knn* h, int nb, int kk, float* odst, uint32_t* oid, cudaM
                                s->stream));
       int* ovf = s->overflow.as<int>();
       VRS_CUDA(cudaMemsetAsync(ovf, 0, (size_t)(nb + nf) * sizeof(int), s->stream));
-      if (nranks == 1)
+      if (!merged)
         VRS_TRY(launch_exact_search(h, s, nf, kk, s->qindex.as<int>(), ovf + nb, s->out_dist.as<float>(),
                                     s->out_id.as<uint32_t>(), nullptr, true));
       else
@@ -953,8 +1021,13 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
   if (nq == 0 || k == 0 || h->n_global == 0) return VRS_OK;
   const int kk = (int)std::min<int64_t>(k, h->n_global);
   if (kk > 2048) return fail(VRS_ERR_INVALID_CONFIG, "k' > 2048 is not supported");
-  if (!queries || !out_dist || !out_id) return fail(VRS_ERR_INVALID_CONFIG, "null buffer");
-  const bool dev_io = mem == VRS_MEM_DEVICE;
+  const bool dev_io = (mem & VRS_MEM_DEVICE) != 0;
+  // Root I/O (rank mode only): rank 0 alone holds the queries and receives
+  // the results, as the one caller of the reference's search_batch does;
+  // the queries reach the other ranks by an NCCL broadcast.
+  const bool root_io = (mem & VRS_MEM_ROOT) != 0 && h->rank_mode && h->comm->nranks > 1;
+  const bool is_root = !root_io || h->comm->rank == 0;
+  if (is_root && (!queries || !out_dist || !out_id)) return fail(VRS_ERR_INVALID_CONFIG, "null buffer");
   if (dev_io && !h->rank_mode && h->shards.size() > 1)
     return fail(VRS_ERR_INVALID_CONFIG, "device buffers need a single-GPU or rank-mode handle");
   const cudaMemcpyKind h2d = dev_io ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
@@ -966,9 +1039,24 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
 
   for (int64_t q0 = 0; q0 < nq; q0 += QB) {
     const int nb = (int)std::min<int64_t>(QB, nq - q0);
-    const float* qsrc = queries + q0 * h->d;
-    float* odst = out_dist + q0 * kk;
-    uint32_t* oid = out_id + q0 * kk;
+    const float* qsrc = is_root ? queries + q0 * h->d : nullptr;
+    float* odst = is_root ? out_dist + q0 * kk : nullptr;
+    uint32_t* oid = is_root ? out_id + q0 * kk : nullptr;
+    cudaMemcpyKind qkind = h2d;
+    if (root_io) {
+      // The batch's queries from rank 0 to every rank, then read as device rows.
+      KnnShard* s = h->shards[0].get();
+      VRS_CUDA(cudaSetDevice(s->device));
+      VRS_TRY(s->q_root.reserve((size_t)nb * h->d * sizeof(float)));
+      if (is_root)
+        VRS_CUDA(cudaMemcpyAsync(s->q_root.p, qsrc, (size_t)nb * h->d * sizeof(float), h2d, s->stream));
+      ProfToken tb = prof_begin("knn_gather", s->stream);
+      VRS_NCCL(ncclBroadcast(s->q_root.p, s->q_root.p, (size_t)nb * h->d, ncclFloat32, 0, s->comm, s->stream));
+      VRS_TRY(nccl_ready(s->comm, tmo));
+      prof_end(tb, s->stream);
+      qsrc = s->q_root.as<float>();
+      qkind = cudaMemcpyDeviceToDevice;
+    }
     if (h->mode == VRS_SHARDED) {
       // Every shard scores all queries; per-shard top-k' lists meet in an
       // all-gather and a G-way merge. With pooled pivot minima the shards
@@ -979,14 +1067,19 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         KnnShard* s = h->shards[r].get();
         VRS_CUDA(cudaSetDevice(s->device));
         VRS_TRY(s->q_in.reserve((size_t)nb * h->d * sizeof(float)));
-        VRS_CUDA(cudaMemcpyAsync(s->q_in.p, qsrc, (size_t)nb * h->d * sizeof(float), h2d, s->stream));
+        VRS_CUDA(cudaMemcpyAsync(s->q_in.p, qsrc, (size_t)nb * h->d * sizeof(float), qkind, s->stream));
         VRS_TRY(s->out_dist.reserve((size_t)nb * kk * sizeof(float)));
         VRS_TRY(s->out_id.reserve((size_t)nb * kk * sizeof(uint32_t)));
         if (nranks == 1) {
           VRS_TRY(shard_search_launch(h, s, nb, kk, s->out_dist.as<float>(), s->out_id.as<uint32_t>(), nullptr));
         } else {
-          VRS_TRY(s->pairs.reserve((size_t)nb * kk * sizeof(Cand)));
-          VRS_TRY(s->gathered.reserve((size_t)nranks * nb * kk * sizeof(Cand)));
+          // Pair lists padded to whole merge slices; the padding rows hold
+          // empty pairs (all bits set) whose merged rows are never read.
+          const int rows = nranks * slice_rows(nb, nranks);
+          VRS_TRY(s->pairs.reserve((size_t)rows * kk * sizeof(Cand)));
+          if (rows > nb)
+            VRS_CUDA(cudaMemsetAsync(s->pairs.as<Cand>() + (size_t)nb * kk, 0xff,
+                                     (size_t)(rows - nb) * kk * sizeof(Cand), s->stream));
           VRS_TRY(shard_search_launch(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>(),
                                       pooled ? kPhasePivot : kPhaseAll));
         }
@@ -1020,7 +1113,7 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
           VRS_TRY(shard_search_launch(h, s, nb, kk, nullptr, nullptr, s->pairs.as<Cand>(), kPhaseMain));
         }
       }
-      VRS_TRY(sharded_finish(h, nb, kk, odst, oid, d2h, tmo));
+      VRS_TRY(sharded_finish(h, nb, kk, odst, oid, d2h, root_io, tmo));
     } else {
       // Replicated: query chunks of ceil(nb / ranks) (distributed_knn.rs:201-229).
       const int chunk = (nb + nranks - 1) / nranks;
@@ -1036,7 +1129,7 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         VRS_TRY(s->pairs.reserve((size_t)std::max(chunk, 1) * kk * sizeof(Cand)));
         if (nc > 0)
           VRS_CUDA(cudaMemcpyAsync(s->q_in.p, qsrc + (int64_t)c0 * h->d, (size_t)nc * h->d * sizeof(float),
-                                   h2d, s->stream));
+                                   qkind, s->stream));
         s->last_nq = 0;
         if (!h->rank_mode) {
           if (nc > 0)
@@ -1070,8 +1163,10 @@ int knn_search_impl(vrs_knn* h, const float* queries, int64_t nq, int32_t k, flo
         VRS_CUDA(cudaSetDevice(s->device));
         VRS_TRY(stream_wait(s->stream, h->rank_mode ? s->comm : nullptr, tmo));
         if (h->rank_mode) {
-          VRS_CUDA(cudaMemcpyAsync(odst, s->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s->stream));
-          VRS_CUDA(cudaMemcpyAsync(oid, s->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s->stream));
+          if (is_root) {
+            VRS_CUDA(cudaMemcpyAsync(odst, s->out_dist.p, (size_t)nb * kk * sizeof(float), d2h, s->stream));
+            VRS_CUDA(cudaMemcpyAsync(oid, s->out_id.p, (size_t)nb * kk * sizeof(uint32_t), d2h, s->stream));
+          }
         } else if (c1 > c0) {
           VRS_CUDA(cudaMemcpyAsync(odst + (int64_t)c0 * kk, s->out_dist.p, (size_t)(c1 - c0) * kk * sizeof(float),
                                    d2h, s->stream));
@@ -1171,7 +1266,7 @@ int vrs_knn_search(vrs_knn* h, const float* queries, int64_t nq, int32_t k, floa
 
 int vrs_knn_search_ex(vrs_knn* h, const float* queries, int64_t nq, int32_t k, float* out_dist,
                       uint32_t* out_id, int32_t* out_k, int32_t mem) {
-  if (mem != VRS_MEM_HOST && mem != VRS_MEM_DEVICE) return fail(VRS_ERR_INVALID_CONFIG, "bad mem flag");
+  if (mem & ~(VRS_MEM_DEVICE | VRS_MEM_ROOT)) return fail(VRS_ERR_INVALID_CONFIG, "bad mem flag");
   return knn_search_impl(h, queries, nq, k, out_dist, out_id, out_k, mem);
 }
 
@@ -1347,17 +1442,13 @@ int km_prepare_shard(const KmParams& P, KmShard* s, const float* rows, int mem) 
   VRS_TRY(s->scal.reserve(4 * sizeof(float)));
   VRS_TRY(s->red.reserve(kSumSlots * sizeof(double)));
   if (s->n_local > 0) {
-    const float* src = rows;
-    DBuf stage;
     if (mem == VRS_MEM_HOST) {
-      VRS_TRY(stage.reserve((size_t)s->n_local * P.d * sizeof(float)));
-      VRS_CUDA(cudaMemcpyAsync(stage.p, rows, (size_t)s->n_local * P.d * sizeof(float),
-                               cudaMemcpyHostToDevice, s->stream));
-      src = stage.as<float>();
+      // Pinned staging slots with a multi-threaded host copy (as the kNN upload).
+      VRS_TRY(stage_host_rows(rows, s->n_local, P.d, P.dp, s->x.as<float>(), 0, s->stream));
+    } else {
+      VRS_TRY(launch_pad_rows(rows, s->n_local, P.d, P.dp, s->x.as<float>(), 0, s->stream));
+      VRS_CUDA(cudaStreamSynchronize(s->stream));
     }
-    VRS_TRY(launch_pad_rows(src, s->n_local, P.d, P.dp, s->x.as<float>(), 0, s->stream));
-    VRS_CUDA(cudaStreamSynchronize(s->stream));
-    stage.release();
     if (P.metric == vrs_exact::kHell) {
       VRS_TRY(s->xr.reserve(nx * P.dp * sizeof(float)));
       VRS_TRY(launch_pad_rows(s->x.as<float>(), s->n_local, P.dp, P.dp, s->xr.as<float>(), 1, s->stream));

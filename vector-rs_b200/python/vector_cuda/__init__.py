@@ -303,12 +303,33 @@ class DistributedKnnEngine:
         kk = kk.value
         return dist[:nq * kk].reshape(nq, kk), ids[:nq * kk].reshape(nq, kk)
 
-    def search_device(self, q_ptr: int, nq: int, k: int, dist_ptr: int, id_ptr: int) -> int:
+    def search_root(self, queries, k: int, nq: Optional[int] = None):
+        """Rank mode, root I/O (VRS_MEM_ROOT): rank 0 passes the queries and
+        receives (dist[nq, k'], ids[nq, k']); every other rank passes None
+        with the same nq and receives None. The queries reach the other
+        ranks by NCCL broadcast and only rank 0's buffers are written."""
+        kk = ctypes.c_int32(0)
+        if queries is not None:
+            q = _f32(queries).reshape(-1)
+            nq = q.size // self._dim
+            cap = max(nq * max(k, 0), 1)
+            dist = np.empty(cap, np.float32)
+            ids = np.empty(cap, np.uint32)
+            _check(lib().vrs_knn_search_ex(self._h, _ptr(q), nq, int(k), _ptr(dist), _ptr(ids),
+                                           ctypes.byref(kk), MEM_ROOT))
+            kk = kk.value
+            return dist[:nq * kk].reshape(nq, kk), ids[:nq * kk].reshape(nq, kk)
+        _check(lib().vrs_knn_search_ex(self._h, None, int(nq), int(k), None, None, ctypes.byref(kk), MEM_ROOT))
+        return None
+
+    def search_device(self, q_ptr: int, nq: int, k: int, dist_ptr: int, id_ptr: int,
+                      root: bool = False) -> int:
         """Device-resident queries and outputs (raw device pointers)."""
         kk = ctypes.c_int32(0)
-        _check(lib().vrs_knn_search_ex(self._h, ctypes.c_void_p(q_ptr), nq, int(k),
-                                       ctypes.c_void_p(dist_ptr), ctypes.c_void_p(id_ptr),
-                                       ctypes.byref(kk), 1))
+        _check(lib().vrs_knn_search_ex(self._h, ctypes.c_void_p(q_ptr) if q_ptr else None, nq, int(k),
+                                       ctypes.c_void_p(dist_ptr) if dist_ptr else None,
+                                       ctypes.c_void_p(id_ptr) if id_ptr else None,
+                                       ctypes.byref(kk), 1 | (MEM_ROOT if root else 0)))
         return kk.value
 
     def set_stream(self, cuda_stream: Optional[int]):
@@ -723,6 +744,9 @@ def query_chunk(nq: int, world: int, rank: int) -> Tuple[int, int]:
     """Queries [q0, q1) answered by `rank` under GpuShardMode::Replicated:
     chunks of ceil(nq / world) in query order (ddp/distributed_knn.rs:203-229)."""
     return shard_rows(nq, world, rank)
+
+
+MEM_ROOT = 2  # VRS_MEM_ROOT
 
 
 def config_seed(index: int) -> int:
