@@ -163,6 +163,34 @@ VRS_API int vrs_ivf_find_top_centroids(vrs_knn* centroids, const float* queries,
 VRS_API int vrs_ivf_assign(vrs_knn* centroids, const float* x, int64_t n, int64_t* out_idx,
                            float* out_score);
 
+/* ------------------------------------------------------ IVF-PQ ADC search */
+/* A trained IVF-PQ index held on the current device: nlist coarse centroids
+ * (nlist x d), the product quantizer's codebooks (num_subvectors x
+ * sub_clusters sub-centroids of d / num_subvectors floats, the layout of
+ * ProductQuantizer, crates/vector-index/src/ivf/pq.rs), and the inverted
+ * lists back to back: list c holds entries [list_offsets[c],
+ * list_offsets[c+1]) of ids (u32) and codes (num_subvectors bytes each, as
+ * InvertedList, crates/vector-index/src/ivf/inverted_list.rs:9-15).
+ * sub_clusters <= 256; num_subvectors * sub_clusters <= 16384; d <= 4096
+ * and a multiple of num_subvectors. Copies everything; the caller keeps its
+ * buffers. */
+typedef struct vrs_ivfpq vrs_ivfpq;
+VRS_API int vrs_ivfpq_create(const float* coarse_centroids, int64_t nlist, int32_t d, const float* codebooks,
+                             int32_t num_subvectors, int32_t sub_clusters, const int64_t* list_offsets,
+                             const uint32_t* ids, const uint8_t* codes, int32_t metric, vrs_ivfpq** out);
+
+/* Replaces IvfPqIndex::search_with_nprobe (crates/vector-index/src/ivf/mod.rs:
+ * 265-345) for nq queries (host buffers): coarse probe of nprobe' =
+ * max(1, min(nprobe, nlist)) lists (find_top_centroids order), per list the
+ * residual's ADC table (pq.rs:233-268) and the four-way f32 sums of
+ * compute_distance_with_lut (pq.rs:270-296), the k best kept exactly as the
+ * reference's BinaryHeap keeps them (equal scores included). Row q of
+ * out_dist/out_id (stride k) holds out_count[q] <= k results, best first;
+ * k == 0 or an empty index gives counts of 0. k <= 2048. */
+VRS_API int vrs_ivfpq_search(vrs_ivfpq* h, const float* queries, int64_t nq, int32_t k, int32_t nprobe,
+                             float* out_dist, uint32_t* out_id, int32_t* out_count);
+VRS_API void vrs_ivfpq_destroy(vrs_ivfpq* h);
+
 /* --------------------------------------------------- VECRSTOR vector files */
 /* Format of crates/vector-index/src/storage/mmap.rs:7-16: three little-endian
  * u64 (magic 0x5645435253544F52 "VECRSTOR", N, D), then N x D f32 rows. */

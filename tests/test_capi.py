@@ -81,3 +81,27 @@ def test_noalloc_refuses_huge_query_count_on_cpu(vc):
         assert f(None, 1000, 16, None, nq, 100, 0, None, None, ctypes.byref(kk), None) == 5
         assert b"no-alloc scratch" in vc.lib().vrs_last_error()
         assert kk.value == 0
+
+
+def test_ivfpq_create_rejects_bad_index_on_cpu(vc):
+    # Argument checks run before any device work.
+    L = vc.lib()
+    h = ctypes.c_void_p()
+    cc = np.zeros(8, np.float32)
+    cb = np.zeros(64, np.float32)
+    off = np.array([0, 2], np.int64)
+    ids = np.array([1, 2], np.uint32)
+    codes = np.array([[0, 1], [1, 0]], np.uint8)
+    P = lambda a: a.ctypes.data  # noqa: E731
+    # d not a multiple of num_subvectors
+    assert L.vrs_ivfpq_create(P(cc), 1, 7, P(cb), 2, 2, P(off), P(ids), P(codes), 0, ctypes.byref(h)) == 5
+    # more than 256 sub-centroids (u8 codes)
+    assert L.vrs_ivfpq_create(P(cc), 1, 8, P(cb), 2, 257, P(off), P(ids), P(codes), 0, ctypes.byref(h)) == 5
+    # decreasing offsets
+    bad_off = np.array([0, -1], np.int64)
+    assert L.vrs_ivfpq_create(P(cc), 1, 8, P(cb), 2, 2, P(bad_off), P(ids), P(codes), 0, ctypes.byref(h)) == 5
+    # a code not below sub_clusters
+    bad_codes = np.array([[0, 2], [1, 0]], np.uint8)
+    assert L.vrs_ivfpq_create(P(cc), 1, 8, P(cb), 2, 2, P(off), P(ids), P(bad_codes), 0, ctypes.byref(h)) == 5
+    assert b"sub_clusters" in L.vrs_last_error()
+    assert not h.value

@@ -35,18 +35,24 @@ namespace {
 
 using namespace vrs::tc;
 
-constexpr int BM = 128, NACC = 2, BN = 128, KBW = 64, MAX_KBLK = 2, STAGES = 4;
+// ABUF point-tile buffers: the next point tile's operands load while the
+// current one's MMAs run (one buffer left the tensor pipe idle through every
+// reload, K / BN tiles apart). The centroid tiles come from L2, so a
+// 2-stage ring keeps them ahead.
+constexpr int BM = 128, NACC = 2, BN = 128, KBW = 64, MAX_KBLK = 2, STAGES = 2, ABUF = 2;
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + EPI_WARPS * 32;
 constexpr int HALF_COLS = BN / 2;
 constexpr int NCAND = 8;
 constexpr uint32_t BLK = BM * 128;
-constexpr size_t SMEM_A = (size_t)NACC * MAX_KBLK * BLK;
+constexpr size_t SMEM_A = (size_t)ABUF * NACC * MAX_KBLK * BLK;
 constexpr size_t SMEM_B = (size_t)STAGES * MAX_KBLK * BLK;
 constexpr size_t SMEM_CAND = (size_t)EPI_WARPS * 32 * NCAND * sizeof(Cand);
 constexpr size_t SMEM_CN = 2 * BN * sizeof(float);  // |c|^2 of the tile in each TMEM buffer
 constexpr size_t SMEM_BAR = 256;
 constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_CAND + SMEM_CN + SMEM_BAR;
+static_assert(SMEM_TOTAL <= 232448, "dynamic shared memory above the 227 KB per-block limit");
+static_assert((2 * STAGES + 4 + 2 * ABUF) * 8 + 8 <= SMEM_BAR, "barrier region too small");
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -109,9 +115,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* tempty = tfull + 2;
-  uint64_t* afull = tempty + 2;
-  uint64_t* aempty = afull + 1;
-  uint32_t* s_tmem = (uint32_t*)(aempty + 1);
+  uint64_t* afull = tempty + 2;   // [ABUF]
+  uint64_t* aempty = afull + ABUF;  // [ABUF]
+  uint32_t* s_tmem = (uint32_t*)(aempty + ABUF);
   volatile int* s_abort = (volatile int*)(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -127,8 +133,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], EPI_WARPS);
     }
-    mbar_init(afull, 1);
-    mbar_init(aempty, 1);
+    for (int b = 0; b < ABUF; b++) {
+      mbar_init(&afull[b], 1);
+      mbar_init(&aempty[b], 1);
+    }
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -145,15 +153,22 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ---------------------------------------------------- TMA producer
     if (lane == 0) {
-      uint32_t g = 0;
-      int lp = 0;
-      bool ok = true;
-      for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x, lp++) {
-        if (!mbar_wait(aempty, (lp & 1) ^ 1, s_abort, a.err, 11, WAIT_NS)) break;
-        mbar_expect_tx(afull, (uint32_t)(NACC * a.kblk) * BLK);
+      // Point tile of local index lp goes to A buffer lp % ABUF; its use
+      // number u = lp / ABUF waits for the buffer's previous phase.
+      auto load_a = [&](int pt, int lp) -> bool {
+        const int ab = lp % ABUF, u = lp / ABUF;
+        if (!mbar_wait(&aempty[ab], (u & 1) ^ 1, s_abort, a.err, 11, WAIT_NS)) return false;
+        mbar_expect_tx(&afull[ab], (uint32_t)(NACC * a.kblk) * BLK);
         for (int acc = 0; acc < NACC; acc++)
           for (int kb = 0; kb < a.kblk; kb++)
-            tma_load_2d(sA + (acc * MAX_KBLK + kb) * BLK, &tmA, kb * KBW, pt * BM * NACC + acc * BM, afull);
+            tma_load_2d(sA + ((ab * NACC + acc) * MAX_KBLK + kb) * BLK, &tmA, kb * KBW,
+                        pt * BM * NACC + acc * BM, &afull[ab]);
+        return true;
+      };
+      uint32_t g = 0;
+      int lp = 0;
+      bool ok = blockIdx.x >= nptiles || load_a(blockIdx.x, 0);
+      for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x, lp++) {
         for (int j = 0; j < kt; j++, g++) {
           const int s = g % STAGES;
           if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, s_abort, a.err, 12, WAIT_NS)) {
@@ -163,6 +178,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_expect_tx(&full[s], (uint32_t)a.kblk * BLK);
           for (int kb = 0; kb < a.kblk; kb++)
             tma_load_2d(sB + (s * MAX_KBLK + kb) * BLK, &tmB, kb * KBW, j * BN, &full[s]);
+          // The next point tile's operands, as soon as this tile's first
+          // centroid tile is queued (its buffer frees when the MMAs of the
+          // tile before this one complete).
+          if (j == 0 && pt + (int)gridDim.x < nptiles && !load_a(pt + gridDim.x, lp + 1)) {
+            ok = false;
+            break;
+          }
         }
       }
     }
@@ -170,23 +192,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(BM, BN);
-      // The A descriptors are fixed for the CTA (registers); the B ones are
-      // formed per tile before the waits. Descriptors differ only in the
-      // masked start-address field.
+      // Descriptors differ only in the masked start-address field: the A
+      // ones are formed per point tile (for its buffer), the B ones per
+      // centroid tile, both before the waits.
       const DescSw128 a_desc(sA), b_desc(sB);
       const int ksteps = a.ksteps;
-      uint64_t ad[NACC][MAX_KBLK * 4];
-#pragma unroll
-      for (int acc = 0; acc < NACC; acc++)
-#pragma unroll
-        for (int ks = 0; ks < MAX_KBLK * 4; ks++)
-          ad[acc][ks] = a_desc.at((uint32_t)(acc * MAX_KBLK * BLK + (ks >> 2) * BLK + (ks & 3) * 32) >> 4);
       uint32_t g = 0;
       int lp = 0;
       bool ok = true;
       int64_t last = -1;
       for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x, lp++) {
-        if (!mbar_wait(afull, lp & 1, s_abort, a.err, 13, WAIT_NS)) break;
+        const int ab = lp % ABUF, u = lp / ABUF;
+        uint64_t ad[NACC][MAX_KBLK * 4];
+#pragma unroll
+        for (int acc = 0; acc < NACC; acc++)
+#pragma unroll
+          for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+            ad[acc][ks] = a_desc.at((uint32_t)((ab * NACC + acc) * MAX_KBLK * BLK + (ks >> 2) * BLK +
+                                               (ks & 3) * 32) >> 4);
+        if (!mbar_wait(&afull[ab], u & 1, s_abort, a.err, 13, WAIT_NS)) break;
         tc_fence_after();
         for (int j = 0; j < kt; j++, g++) {
           const int s = g % STAGES, b = g & 1;
@@ -217,7 +241,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           mma_commit(&tfull[b]);
           last = g;
         }
-        if (ok) mma_commit(aempty);
+        if (ok) mma_commit(&aempty[ab]);
       }
       if (*s_abort && last >= 0) {
         volatile int dummy = 0;

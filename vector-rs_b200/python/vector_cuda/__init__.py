@@ -170,6 +170,12 @@ def lib() -> ctypes.CDLL:
                                           c.c_int32, c.c_int64, c.c_void_p, c.c_void_p, c.c_uint32,
                                           c.c_double, c.c_void_p]
         L.vrs_selftest_bounded_wait.argtypes = [c.c_int64]
+        L.vrs_ivfpq_create.argtypes = [c.c_void_p, c.c_int64, c.c_int32, c.c_void_p, c.c_int32, c.c_int32,
+                                       c.c_void_p, c.c_void_p, c.c_void_p, c.c_int32, P(c.c_void_p)]
+        L.vrs_ivfpq_search.argtypes = [c.c_void_p, c.c_void_p, c.c_int64, c.c_int32, c.c_int32, c.c_void_p,
+                                       c.c_void_p, c.c_void_p]
+        L.vrs_ivfpq_destroy.argtypes = [c.c_void_p]
+        L.vrs_ivfpq_destroy.restype = None
         _lib_handle = L
     return _lib_handle
 
@@ -651,6 +657,59 @@ class KMeans:
 
 
 # ---------------------------------------------------- rank mode (NCCL)
+
+
+class IvfPqIndex:
+    """A trained IVF-PQ index on the GPU (IvfPqIndex of
+    crates/vector-index/src/ivf/mod.rs): coarse centroids, product-quantizer
+    codebooks and inverted lists (ids, u8 codes) uploaded once;
+    search_batch is search_with_nprobe for many queries."""
+
+    def __init__(self, coarse_centroids, dimension: int, codebooks, num_subvectors: int, sub_clusters: int,
+                 lists, metric: DistanceMetric):
+        """lists: sequence of (ids, codes[len, num_subvectors]) per coarse centroid."""
+        cc = _f32(coarse_centroids).reshape(-1)
+        nlist = cc.size // dimension
+        off = np.zeros(nlist + 1, np.int64)
+        for c in range(nlist):
+            off[c + 1] = off[c] + len(lists[c][0])
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(l[0], np.uint32) for l in lists])
+                                   if nlist else np.zeros(0, np.uint32), dtype=np.uint32)
+        codes = np.ascontiguousarray(
+            np.concatenate([np.asarray(l[1], np.uint8).reshape(-1, num_subvectors) for l in lists])
+            if nlist else np.zeros((0, num_subvectors), np.uint8), dtype=np.uint8)
+        cb = _f32(codebooks).reshape(-1)
+        h = ctypes.c_void_p()
+        _check(lib().vrs_ivfpq_create(_ptr(cc) if nlist else None, nlist, dimension, _ptr(cb), num_subvectors,
+                                      sub_clusters, _ptr(off), _ptr(ids) if ids.size else None,
+                                      _ptr(codes) if codes.size else None, int(metric), ctypes.byref(h)))
+        self._h, self._dim = h, dimension
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().vrs_ivfpq_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def search_batch(self, queries, k: int, nprobe: int):
+        """Returns (dist[nq, k], ids[nq, k], count[nq]): row q holds count[q]
+        results best first."""
+        q = _f32(queries).reshape(-1)
+        nq = q.size // self._dim
+        dist = np.zeros(max(nq * k, 1), np.float32)
+        ids = np.zeros(max(nq * k, 1), np.uint32)
+        cnt = np.zeros(max(nq, 1), np.int32)
+        _check(lib().vrs_ivfpq_search(self._h, _ptr(q), nq, int(k), int(nprobe), _ptr(dist), _ptr(ids), _ptr(cnt)))
+        return dist[:nq * k].reshape(nq, k), ids[:nq * k].reshape(nq, k), cnt[:nq]
+
+    def search_with_nprobe(self, query, k: int, nprobe: int) -> List[SearchResult]:
+        d, i, c = self.search_batch(query, k, nprobe)
+        return [SearchResult(int(i[0, r]), float(d[0, r])) for r in range(int(c[0]))]
 
 
 class Comm:
