@@ -7,6 +7,7 @@ number of candidates, and a C5b-sized quantiser."""
 import numpy as np
 import pytest
 
+pytestmark = pytest.mark.gpu
 L2, DOT, COS, L1, MINK, CHEB, HAM, MAHA, JAC, HELL = range(10)
 
 
