@@ -98,6 +98,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--ivf", action="store_true",
                     help="IVF coarse probe/assign line only (1 GPU; not part of the default run)")
+    ap.add_argument("--ivfpq", action="store_true",
+                    help="IVF-PQ ADC search line only (1 GPU; not part of the default run)")
     ap.add_argument("--storage", action="store_true",
                     help="VECRSTOR file -> GPU engine load line only (1 GPU; not part of the default run)")
     ap.add_argument("--n-base", type=int, default=None, help="override the workload's base rows")
@@ -423,6 +425,9 @@ def main():
     if args.storage:
         line = storage_bench(args, vc, torch, dev, pk) if rank == 0 else None
         args.no_knn = args.no_kmeans = True
+    if args.ivfpq:
+        line = ivfpq_bench(args, vc, torch, dev, pk, pk_kind) if rank == 0 else None
+        args.no_knn = args.no_kmeans = True
     if not args.no_knn:
         w = workload(args)
         line = knn_bench(ctx, w, args.steps, args.warmup, parity_queries=min(w["cpu_sample"], w["nq"]),
@@ -435,7 +440,7 @@ def main():
             line["kmeans"] = km
     # The north star's scale configs ride along as extra keys of the default
     # line (few steps each), so every scaling run records them too.
-    if line is not None and not args.no_scale and not args.ivf and not args.storage:
+    if line is not None and not args.no_scale and not args.ivf and not args.storage and not args.ivfpq:
         c5a = dict(WORKLOADS["c5a"])
         line["c5a"] = knn_bench(ctx, c5a, min(args.steps, 5), min(args.warmup, 2), parity_queries=20,
                                 cpu_leg=False, sustained=False, e2e_steps=2)
@@ -899,6 +904,102 @@ def ivf_bench(args, vc, torch, dev, peak_tc):  # peak_tc: bf16 burst
                          "sample": f"{S} queries, oracle batch kNN at k = nprobe over all centroids"},
         "clocks": clk.summary(),
         "gpu_launches": sum(v["launches"] for v in stages.values()),
+    }
+
+
+def ivfpq_bench(args, vc, torch, dev, pk, pk_kind):
+    """IVF-PQ ADC search (IvfPqIndex::search_with_nprobe,
+    crates/vector-index/src/ivf/mod.rs:265-345) on an index of the C5b shape:
+    nlist = 16,384 coarse centroids over d = 96 (the quantiser C5b trains),
+    10,000,000 encoded rows with M = 16 sub-spaces of 256 sub-centroids;
+    10,000 queries per step around the centroids, nprobe = 32, k = 100. One
+    step = one vrs_ivfpq_search on host buffers (coarse probe, ADC tables,
+    scores, heaps, copies). Codes are drawn uniformly and list sizes from a
+    uniform multinomial (the ADC work does not depend on code values)."""
+    K, D, M, KS, N, NQ, P, KK = 16_384, 96, 16, 256, 10_000_000, 10_000, 32, 100
+    seed = vc.config_seed(4)
+    rng = np.random.default_rng(seed & 0xFFFFFFFF)
+    cent = torch.empty((K, D), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(vc.GEN_NORMAL, seed, 5, 0, K, D, cent.data_ptr())
+    q = torch.empty((NQ, D), dtype=torch.float32, device=dev)
+    vc.gen_rows_device(vc.GEN_MIXTURE, seed, 7, 0, NQ, D, q.data_ptr(), cent.data_ptr(), K, 0.05)
+    cent_h, q_h = cent.cpu().numpy(), q.cpu().numpy()
+    del cent, q
+    cb = (0.05 * rng.standard_normal(M * KS * (D // M))).astype(np.float32)
+    sizes = rng.multinomial(N, np.full(K, 1.0 / K))
+    off = np.zeros(K + 1, np.int64)
+    off[1:] = np.cumsum(sizes)
+    ids = rng.permutation(N).astype(np.uint32)
+    codes = rng.integers(0, KS, (N, M), dtype=np.uint8)
+    lists = [(ids[off[c]:off[c + 1]], codes[off[c]:off[c + 1]]) for c in range(K)]
+    ids_flat, codes_flat = ids, codes  # lists back to back already
+    idx = vc.IvfPqIndex(cent_h, D, cb, M, KS, lists, vc.DistanceMetric.L2Squared)
+    for _ in range(max(args.warmup, 3)):
+        idx.search_batch(q_h, KK, P)
+    steps = max(args.steps, 1)
+    with ClockSampler(dev.index or 0) as clk:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            gd, gi, gc = idx.search_batch(q_h, KK, P)
+        step_s = (time.perf_counter() - t0) / steps
+    vc.profile_reset()
+    vc.profile_enable(True)
+    idx.search_batch(q_h, KK, P)
+    vc.profile_enable(False)
+    adc_ms, adc_n = vc.profile_read("ivfpq_adc")
+    stages = {nm: dict(zip(("ms", "launches"), vc.profile_read(nm)))
+              for nm in ("knn_prep", "knn_pivot", "knn_scan", "knn_select", "ivfpq_adc")}
+    launches = sum(v["launches"] for v in stages.values())
+    idx.close()
+    # Parity sample and CPU baseline: the oracle's C restatement of the
+    # reference search, one query per call, calls spread over host threads.
+    orc = oracle_mod()
+    import ivfpq
+    from concurrent.futures import ThreadPoolExecutor
+    S = 64
+    cores = host_cores()
+
+    def one(i):
+        return ivfpq.ivf_pq_search_c_flat(q_h[i], KK, P, cent_h, off, ids_flat, codes_flat, cb, M, KS, L2)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(cores) as ex:
+        ref = list(ex.map(one, range(S)))
+    cpu_s = time.perf_counter() - t0
+    ids_eq = np.mean([np.array_equal(gi[i, :gc[i]], ref[i][1]) for i in range(S)])
+    dist_eq = np.mean([np.array_equal(gd[i, :gc[i]].view(np.uint32), ref[i][0].view(np.uint32)) for i in range(S)])
+    cand = float(np.mean([sizes[c] for c in range(K)])) * P
+    bytes_q = cand * (M + 4)  # codes + ids of the probed lists
+    ach = bytes_q * NQ / (adc_ms / max(adc_n, 1) / 1e3) / 1e9
+    del orc
+    return {
+        "metric": "IVF-PQ ADC search queries/s (nlist 16384, d 96, M 16 x 256, 10M rows, nprobe 32, k 100)",
+        "value": NQ / step_s, "unit": "queries/s", "higher_is_better": True, "n_gpus": 1,
+        "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": step_s * 1e3,
+        "dtype": "f32 tables and sums (the reference's arithmetic)", "data": "synthetic",
+        "config": {"workload": "IVF-PQ index of the C5b shape: coarse centroids N(0,1), queries a mixture "
+                               "around them (sigma 0.05), codebooks N(0, 0.05^2), uniform codes, list sizes "
+                               "multinomial(10M, uniform)",
+                   "nlist": K, "dim": D, "num_subvectors": M, "sub_clusters": KS, "rows": N,
+                   "queries_per_step": NQ, "nprobe": P, "k": KK,
+                   "l2": "codes + ids 200 MB, larger than L2; queries from host memory every call"},
+        "timing": "host clock around the synchronous vrs_ivfpq_search on host buffers (probe, ADC, copies)",
+        "e2e": {"value": NQ / step_s, "unit": "queries/s", "h2d_bytes_per_step": NQ * D * 4 * 2 + NQ * P * 4,
+                "d2h_bytes_per_step": NQ * (KK * 8 + 4) + NQ * P * 12},
+        "stages": stages,
+        "roofline": {"bound": "hbm", "kernel": "ivfpq_adc", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": ach / pk["hbm_gbs"], "peak_source": f"{pk_kind} HBM copy",
+                     "bytes_per_query": bytes_q, "traffic": None,
+                     "note": "algorithmic bytes = codes + ids of the probed lists per query; lists shared by "
+                             "queries are re-read from L2, so the kernel is bound by its table builds and "
+                             "shared-memory lookups rather than HBM"},
+        "parity": {"queries": S, "ids_equal_frac": float(ids_eq), "dist_bit_equal_frac": float(dist_eq)},
+        "cpu_baseline": {"value": S / cpu_s, "unit": "queries/s", "cores": cores, "kind": "port",
+                         "sample": f"{S} queries, oracle C restatement of search_with_nprobe, one query per call "
+                                   f"on {cores} threads"},
+        "clocks": clk.summary(),
+        "gpu_launches": launches,
     }
 
 

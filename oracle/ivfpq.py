@@ -175,15 +175,9 @@ def ivf_pq_search(query, k: int, nprobe: int, coarse_centroids, lists, codebooks
     return out
 
 
-def ivf_pq_search_c(query, k: int, nprobe: int, coarse_centroids, lists, codebooks,
-                    num_subvectors: int, sub_clusters: int, metric: int, use_simd: int = -1):
-    """The same search in C (``orc_ivfpq_search`` in vrs_oracle.c), for sizes the
-    Python loops cannot reach. Returns (distances f32[c], ids u32[c])."""
-    import ctypes
-    L = oracle.lib()
-    q = np.ascontiguousarray(query, np.float32)
-    cc = np.ascontiguousarray(coarse_centroids, np.float32)
-    nlist = cc.shape[0] if cc.ndim == 2 else 0
+def flatten_lists(lists, num_subvectors: int):
+    """(offsets[nlist + 1] i64, ids u32, codes [total][M] u8) of per-list (ids, codes)."""
+    nlist = len(lists)
     off = np.zeros(nlist + 1, np.int64)
     for c in range(nlist):
         off[c + 1] = off[c] + len(lists[c][0])
@@ -192,6 +186,27 @@ def ivf_pq_search_c(query, k: int, nprobe: int, coarse_centroids, lists, codeboo
     codes = np.ascontiguousarray(
         np.concatenate([np.asarray(l[1], np.uint8).reshape(-1, num_subvectors) for l in lists])
         if nlist else np.zeros((0, num_subvectors), np.uint8), dtype=np.uint8)
+    return off, ids, codes
+
+
+def ivf_pq_search_c(query, k: int, nprobe: int, coarse_centroids, lists, codebooks,
+                    num_subvectors: int, sub_clusters: int, metric: int, use_simd: int = -1):
+    """The same search in C (``orc_ivfpq_search`` in vrs_oracle.c), for sizes the
+    Python loops cannot reach. Returns (distances f32[c], ids u32[c])."""
+    off, ids, codes = flatten_lists(lists, num_subvectors)
+    return ivf_pq_search_c_flat(query, k, nprobe, coarse_centroids, off, ids, codes, codebooks,
+                                num_subvectors, sub_clusters, metric, use_simd)
+
+
+def ivf_pq_search_c_flat(query, k: int, nprobe: int, coarse_centroids, off, ids, codes, codebooks,
+                         num_subvectors: int, sub_clusters: int, metric: int, use_simd: int = -1):
+    """ivf_pq_search_c on lists already flattened by flatten_lists (arrays
+    C-contiguous: offsets i64, ids u32, codes u8)."""
+    import ctypes
+    L = oracle.lib()
+    q = np.ascontiguousarray(query, np.float32)
+    cc = np.ascontiguousarray(coarse_centroids, np.float32)
+    nlist = cc.shape[0] if cc.ndim == 2 else 0
     cb = np.ascontiguousarray(codebooks, np.float32)
     out_d = np.zeros(max(k, 1), np.float32)
     out_i = np.zeros(max(k, 1), np.uint32)

@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -306,41 +307,66 @@ void par_memcpy(void* dst, const void* src, size_t bytes) {
 // next chunk is copied from the caller's (pageable or mapped) memory into
 // the other slot. A slot is refilled only after the event recorded behind
 // its last device copy has completed. dst: n rows of dp floats.
+// The slots (pinned host, device, events) are kept per device for the life
+// of the process and reused by every upload (pinning 128 MB costs tens of
+// ms, more than a whole k-means fit of 1M rows); uploads to one device take
+// turns on its slots.
+constexpr size_t kStageSlot = 64ull << 20;
+struct StageSlots {
+  std::mutex mu;
+  HBuf pin[2];
+  DBuf dev[2];
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+};
+
+StageSlots* stage_slots(int device) {
+  static std::mutex g_mu;
+  static StageSlots* g_slots[128] = {nullptr};  // never freed: live until exit
+  if (device < 0 || device >= 128) return nullptr;
+  std::lock_guard<std::mutex> g(g_mu);
+  if (!g_slots[device]) g_slots[device] = new StageSlots();
+  return g_slots[device];
+}
+
 int stage_host_rows(const float* rows, int64_t n, int d, int dp, float* dst, int transform, cudaStream_t st) {
   if (n <= 0) return VRS_OK;
+  int device = 0;
+  VRS_CUDA(cudaGetDevice(&device));
+  StageSlots* sl = stage_slots(device);
+  if (!sl) return fail(VRS_ERR_DEVICE_NOT_FOUND, "device ordinal out of range for the staging slots");
+  std::lock_guard<std::mutex> lk(sl->mu);
   const size_t row_bytes = (size_t)d * sizeof(float);
-  const int64_t chunk = std::max<int64_t>(1, (int64_t)(64ll << 20) / (int64_t)row_bytes);
+  const int64_t chunk = std::max<int64_t>(1, (int64_t)kStageSlot / (int64_t)row_bytes);
   const int64_t nchunks = (n + chunk - 1) / chunk;
-  const size_t slot_bytes = (size_t)std::min<int64_t>(chunk, n) * row_bytes;
-  struct Slots {
-    HBuf pin[2];
-    DBuf dev[2];
-    cudaEvent_t ev[2] = {nullptr, nullptr};
-    cudaStream_t st = nullptr;
-    ~Slots() {
-      if (st) cudaStreamSynchronize(st);  // no copy may still read a slot being freed
-      for (auto& e : ev)
-        if (e) cudaEventDestroy(e);
-    }
-  } sl;
-  sl.st = st;
+  const size_t slot_bytes = std::max(kStageSlot, (size_t)chunk * row_bytes);
   for (int j = 0; j < 2 && j < nchunks; j++) {
-    VRS_TRY(sl.pin[j].reserve(slot_bytes));
-    VRS_TRY(sl.dev[j].reserve(slot_bytes));
-    VRS_CUDA(cudaEventCreateWithFlags(&sl.ev[j], cudaEventDisableTiming));
+    VRS_TRY(sl->pin[j].reserve(slot_bytes));
+    VRS_TRY(sl->dev[j].reserve(slot_bytes));
+    if (!sl->ev[j]) VRS_CUDA(cudaEventCreateWithFlags(&sl->ev[j], cudaEventDisableTiming));
   }
-  for (int64_t c = 0; c < nchunks; c++) {
+  int rc = VRS_OK;
+  for (int64_t c = 0; c < nchunks && rc == VRS_OK; c++) {
     const int j = (int)(c & 1);
-    const int64_t r0 = c * chunk, rc = std::min(chunk, n - r0);
-    const size_t bytes = (size_t)rc * row_bytes;
-    if (c >= 2) VRS_CUDA(cudaEventSynchronize(sl.ev[j]));
-    par_memcpy(sl.pin[j].p, rows + r0 * d, bytes);
-    VRS_CUDA(cudaMemcpyAsync(sl.dev[j].p, sl.pin[j].p, bytes, cudaMemcpyHostToDevice, st));
-    VRS_TRY(launch_pad_rows(sl.dev[j].as<float>(), rc, d, dp, dst + r0 * dp, transform, st));
-    VRS_CUDA(cudaEventRecord(sl.ev[j], st));
+    const int64_t r0 = c * chunk, rc_rows = std::min(chunk, n - r0);
+    const size_t bytes = (size_t)rc_rows * row_bytes;
+    // The slot's previous copy (this upload's or an earlier one's) is done.
+    if (cudaEventQuery(sl->ev[j]) != cudaSuccess) {
+      cudaError_t e = cudaEventSynchronize(sl->ev[j]);
+      if (e != cudaSuccess) return fail(cuda_status(e), std::string("staging: ") + cudaGetErrorString(e));
+    }
+    par_memcpy(sl->pin[j].p, rows + r0 * d, bytes);
+    cudaError_t e = cudaMemcpyAsync(sl->dev[j].p, sl->pin[j].p, bytes, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return fail(cuda_status(e), std::string("staging copy: ") + cudaGetErrorString(e));
+    rc = launch_pad_rows(sl->dev[j].as<float>(), rc_rows, d, dp, dst + r0 * dp, transform, st);
+    if (rc == VRS_OK) {
+      e = cudaEventRecord(sl->ev[j], st);
+      if (e != cudaSuccess) return fail(cuda_status(e), std::string("staging event: ") + cudaGetErrorString(e));
+    }
   }
-  VRS_CUDA(cudaStreamSynchronize(st));
-  return VRS_OK;
+  // The slots are free again once `st` has run the last pad.
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (rc == VRS_OK && e != cudaSuccess) return fail(cuda_status(e), std::string("staging: ") + cudaGetErrorString(e));
+  return rc;
 }
 
 int upload_host_rows(vrs_knn* h, KnnShard* s, const float* rows, int transform) {
@@ -531,8 +557,11 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   cudaStream_t st = s->stream;
   const int d16 = tc::tc_d16(h->metric, h->d);
   const int nq_alloc = (nq + 255) / 256 * 256;
-  tc::TcPlan p = tc::tc_plan(s->n_local, nq, kk, s->num_sms);
-  const int nlists = 2 * p.nseg;
+  // The candidate pass runs on CTA pairs (cta_group::2, four lists per
+  // segment); VRS_SCAN_1SM=1 selects the one-SM kernel (two lists).
+  const bool pair_scan = !getenv("VRS_SCAN_1SM");
+  tc::TcPlan p = pair_scan ? tc::tc_plan2(s->n_local, nq, kk, s->num_sms) : tc::tc_plan(s->n_local, nq, kk, s->num_sms);
+  const int nlists = (pair_scan ? 4 : 2) * p.nseg;
   // The starting bound comes from a pivot rank below k (tc_optimistic_rank)
   // and is checked by the select: a single shard's failures are flagged for
   // the exact re-search; merge pairs carry a sentinel instead and the merge
@@ -592,10 +621,15 @@ main_phase:
   VRS_CUDA(cudaMemsetAsync(s->cnt.p, 0, (size_t)nlists * nq * sizeof(int), st));
   if (s->n_local > 0) {
     ProfToken t = prof_begin("knn_scan", st);
-    VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, s->xb.p, s->n_local, h->d, s->xn.as<float>(), h->metric, nq, kk,
-                        p, s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(),
-                        s->absm.as<float>(), s->err.as<int>(), nullptr, s->ibound.as<float>(), s->qscale.as<float>(),
-                        s->xscale, st));
+    if (pair_scan)
+      VRS_TRY(tc::tc_scan2(s->qb.p, nq_alloc, s->xb.p, s->n_local, h->d, s->xn.as<float>(), h->metric, nq, kk, p,
+                           s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(), s->absm.as<float>(),
+                           s->err.as<int>(), s->ibound.as<float>(), s->qscale.as<float>(), s->xscale, st));
+    else
+      VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, s->xb.p, s->n_local, h->d, s->xn.as<float>(), h->metric, nq, kk,
+                          p, s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(),
+                          s->absm.as<float>(), s->err.as<int>(), nullptr, s->ibound.as<float>(),
+                          s->qscale.as<float>(), s->xscale, st));
     prof_end(t, st);
   }
   KnnSelectArgs sa{};

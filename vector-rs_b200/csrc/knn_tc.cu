@@ -352,6 +352,262 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ------------------------------------------------- 2-SM scan (cta_group::2)
+// The candidate pass on CTA pairs. A cluster of two CTAs on two SMs owns 256
+// queries (128 per CTA, its A tile) and streams 256-row base tiles, each CTA
+// loading its 128-row half. The even CTA's one thread issues
+// tcgen05.mma.cta_group::2 with M = 256, N = 256: every CTA's TMEM receives
+// its 128 queries x the tile's 256 rows, double-buffered (2 x 256 = 512
+// columns). Per SM and MMA the operands read from shared memory halve
+// against the 1-SM M = 128 x N = 128 tile (one A and one half-B K-slice for
+// twice the products), which is what capped that kernel's MMA stream.
+//   * TMA: both CTAs' loads complete on the even CTA's `full` / `afull`
+//     barriers (armed by the even CTA with both halves' bytes); a stage is
+//     refilled after the MMA commit arrives on that CTA's own `empty`
+//     (multicast to both CTAs).
+//   * The MMA commit also arrives on both CTAs' `tfull`; each CTA's 16
+//     epilogue warps (TMEM lane quadrant x 64-column quarter: one thread =
+//     one query, 64 columns per tile, the epilogue of the 1-SM kernel) then
+//     arrive on the even CTA's `tempty`.
+//   * Lists: one per (segment, column quarter, query).
+// Every wait is bounded; both CTAs meet in a cluster barrier before TMEM
+// is released and before either exits.
+constexpr int P_BM = 128;           // queries per CTA (M = 256 per pair)
+constexpr int P_BN = 256;           // base rows per pair tile (N)
+constexpr int P_HALF = P_BN / 2;    // rows each CTA loads
+constexpr int P_STAGES = 5;
+constexpr int P_QUARTER = 64;       // columns per epilogue warp
+constexpr uint32_t P_BLK = 128 * 128;  // bytes of one K-block of a 128-row tile
+constexpr size_t P_SMEM_A = (size_t)MAX_KBLK * P_BLK;
+constexpr size_t P_SMEM_B = (size_t)P_STAGES * MAX_KBLK * P_BLK;
+constexpr size_t P_SMEM_TOTAL = 1024 + P_SMEM_A + P_SMEM_B + SMEM_HIST + SMEM_BAR;
+static_assert(P_SMEM_TOTAL <= 232448, "2-SM scan: shared memory above the per-block limit");
+static_assert((3 * P_STAGES + 2 + 2 + 1) * 8 + 8 <= SMEM_BAR, "2-SM scan: barrier region too small");
+
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    knn_scan_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        TcScanArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + P_SMEM_A;
+  int* s_hist = (int*)(sB + P_SMEM_B);
+  uint64_t* bars = (uint64_t*)((uint8_t*)s_hist + SMEM_HIST);
+  uint64_t* full = bars;                  // [P_STAGES] even CTA: both halves' bytes
+  uint64_t* empty = bars + P_STAGES;      // [P_STAGES] each CTA: MMA commit
+  uint64_t* tfull = bars + 2 * P_STAGES;  // [2] each CTA: MMA commit
+  uint64_t* tempty = tfull + 2;           // [2] even CTA: both CTAs' epilogue warps
+  uint64_t* afull = tempty + 2;           // even CTA: both A tiles
+  uint32_t* s_tmem = (uint32_t*)(afull + 1);
+  volatile int* s_abort = (volatile int*)(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();
+  const bool lead = cta == 0;
+  const int q0 = (blockIdx.x >> 1) * (2 * P_BM) + (int)cta * P_BM;
+  const int seg = blockIdx.y;
+  const int64_t row_begin = (int64_t)seg * a.seg_len;
+  const int64_t row_end = min(a.n, row_begin + a.seg_len);
+  const int ntiles = row_end > row_begin ? (int)((row_end - row_begin + P_BN - 1) / P_BN) : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * EPI_WARPS);
+    }
+    mbar_init(afull, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(s_tmem, TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    // ---------------------------------------------------- TMA producer
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t afull_lead = mapa_shared(afull, 0);
+      if (lead) mbar_expect_tx(afull, (uint32_t)(2 * a.kblk) * P_BLK);
+      for (int kb = 0; kb < a.kblk; kb++) tma_load_2d_pair(sA + kb * P_BLK, &tmA, kb * KBW, q0, afull_lead);
+      int issued = 0;
+      for (int t = 0; t < ntiles; t++) {
+        const int s = t % P_STAGES;
+        if (!mbar_wait(&empty[s], ((t / P_STAGES) & 1) ^ 1, s_abort, a.err, 21, WAIT_NS)) break;
+        if (lead) mbar_expect_tx(&full[s], (uint32_t)(2 * a.kblk) * P_BLK);
+        const uint32_t full_lead = mapa_shared(&full[s], 0);
+        const int y = (int)(row_begin + (int64_t)t * P_BN + (int)cta * P_HALF);
+        for (int kb = 0; kb < a.kblk; kb++)
+          tma_load_2d_pair(sB + (s * MAX_KBLK + kb) * P_BLK, &tmB, kb * KBW, y, full_lead);
+        issued = t + 1;
+      }
+      if (*s_abort && lead) {
+        // Drain (bounded): both CTAs' loads complete on these barriers.
+        volatile int dummy = 0;
+        for (int t = max(0, issued - P_STAGES); t < issued; t++)
+          mbar_wait(&full[t % P_STAGES], (t / P_STAGES) & 1, &dummy, a.err, 0, WAIT_NS / 4);
+        mbar_wait(afull, 0, &dummy, a.err, 0, WAIT_NS / 4);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------- MMA issuer (even CTA)
+    if (lane == 0 && lead && ntiles > 0) {
+      const uint32_t idesc = a.idesc;
+      const DescSw128 a_desc(sA), b_desc(sB);
+      const int ksteps = a.ksteps;
+      uint64_t ad[MAX_KBLK * 4];
+#pragma unroll
+      for (int ks = 0; ks < MAX_KBLK * 4; ks++) ad[ks] = a_desc.at((uint32_t)((ks >> 2) * P_BLK + (ks & 3) * 32) >> 4);
+      bool ok = mbar_wait(afull, 0, s_abort, a.err, 22, WAIT_NS);
+      tc_fence_after();
+      int last = -1;
+      for (int t = 0; ok && t < ntiles; t++) {
+        const int s = t % P_STAGES, b = t & 1;
+        uint64_t bd[MAX_KBLK * 4];
+#pragma unroll
+        for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+          bd[ks] = b_desc.at((uint32_t)(s * MAX_KBLK * P_BLK + (ks >> 2) * P_BLK + (ks & 3) * 32) >> 4);
+        if (!mbar_wait(&full[s], (t / P_STAGES) & 1, s_abort, a.err, 23, WAIT_NS)) break;
+        if (!mbar_wait(&tempty[b], ((t >> 1) & 1) ^ 1, s_abort, a.err, 24, WAIT_NS)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * P_BN;
+#pragma unroll
+        for (int ks = 0; ks < MAX_KBLK * 4; ks++)
+          if (ks < ksteps) mma_f16_pair(d, ad[ks], bd[ks], idesc, ks > 0 ? 1u : 0u);
+        mma_commit_pair(&empty[s], 0x3);
+        mma_commit_pair(&tfull[b], 0x3);
+        last = t;
+      }
+      if (*s_abort && last >= 0) {
+        volatile int dummy = 0;
+        mbar_wait(&tfull[last & 1], (last >> 1) & 1, &dummy, a.err, 0, WAIT_NS / 4);
+      }
+    }
+  } else {
+    // ---------------------------------------------------- epilogue
+    const int ew = warp - 2;
+    const int quarter = ew >> 2;
+    const int quad = warp & 3;
+    const int q = q0 + quad * 32 + lane;
+    const bool vq = q < a.nq;
+    const int64_t list_id = ((int64_t)blockIdx.y * 4 + quarter) * a.nq + (vq ? q : 0);
+    Cand* list = a.cand + list_id * a.cap;
+    int count = 0;
+    float bound = vq ? (a.init_bound ? a.init_bound[q] : INFINITY) : -INFINITY;
+    const float ks = vq ? a.qscale[q] * a.xscale : 1.0f;
+    const float inv_ks = 1.0f / ks;
+    const float f2 = -2.0f * inv_ks;
+    const float absm = vq ? a.absm[q] : 0.0f;
+    int* hist = s_hist + ew * 256;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const uint32_t tempty_lead0 = mapa_shared(&tempty[0], 0), tempty_lead1 = mapa_shared(&tempty[1], 0);
+    for (int t = 0; t < ntiles; t++) {
+      const int b = t & 1;
+      const bool ok = mbar_wait(&tfull[b], (t >> 1) & 1, s_abort, a.err, 25, WAIT_NS);
+      if (!__all_sync(sel::kFull, ok)) break;
+      tc_fence_after();
+      const int64_t n0 = row_begin + (int64_t)t * P_BN + quarter * P_QUARTER;
+      if (MODE == 0 && t + 1 < ntiles && lane < 2)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(a.xn + n0 + P_BN + lane * 32));
+      const int64_t rem_cols = row_end - n0;
+      const int valid_cols = rem_cols < P_QUARTER ? (int)(rem_cols > 0 ? rem_cols : 0) : P_QUARTER;
+      const float thr = MODE == 0 ? bound : MODE == 1 ? -bound * ks : -0.5f * bound * ks;
+      float v[P_QUARTER];
+      tmem_ld64(tmem + lane_base + b * P_BN + quarter * P_QUARTER, v);
+      if (MODE == 0) {
+        const float4* xp = reinterpret_cast<const float4*>(a.xn + n0);
+#pragma unroll
+        for (int j4 = 0; j4 < P_QUARTER / 4; j4++) {
+          if (j4 % 4 == 0) asm volatile("" ::: "memory");
+          const float4 x4 = __ldg(xp + j4);
+          v[4 * j4 + 0] = fmaf(f2, v[4 * j4 + 0], x4.x);
+          v[4 * j4 + 1] = fmaf(f2, v[4 * j4 + 1], x4.y);
+          v[4 * j4 + 2] = fmaf(f2, v[4 * j4 + 2], x4.z);
+          v[4 * j4 + 3] = fmaf(f2, v[4 * j4 + 3], x4.w);
+        }
+      }
+      if (valid_cols < P_QUARTER) {
+        // Columns past the segment end: NaN fails every comparison.
+#pragma unroll
+        for (int j = 0; j < P_QUARTER; j++)
+          if (j >= valid_cols) v[j] = __int_as_float(0x7fffffff);
+      }
+      float g[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float* w = v + 8 * i;
+        g[i] = MODE == 0 ? fmin3(fmin3(w[0], w[1], w[2]), fmin3(w[3], w[4], w[5]), fminf(w[6], w[7]))
+                         : fmax3(fmax3(w[0], w[1], w[2]), fmax3(w[3], w[4], w[5]), fmaxf(w[6], w[7]));
+      }
+      const float best = MODE == 0 ? fmin3(fmin3(g[0], g[1], g[2]), fmin3(g[3], g[4], g[5]), fminf(g[6], g[7]))
+                                   : fmax3(fmax3(g[0], g[1], g[2]), fmax3(g[3], g[4], g[5]), fmaxf(g[6], g[7]));
+      if (MODE == 0 ? best <= thr : best >= thr) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (MODE == 0 ? g[i] <= thr : g[i] >= thr) {
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+              const float sc = MODE == 0 ? v[8 * i + jj] : MODE == 1 ? -inv_ks * v[8 * i + jj] : f2 * v[8 * i + jj];
+              if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + 8 * i + jj)};
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (lead)
+          mbar_arrive(&tempty[b]);
+        else
+          mbar_arrive_cluster(b ? tempty_lead1 : tempty_lead0);
+      }
+      // Shrink lists that could overflow on the next tile.
+      unsigned need = __ballot_sync(sel::kFull, vq && count > a.cap - P_QUARTER);
+      while (need) {
+        const int l = __ffs(need) - 1;
+        need &= need - 1;
+        const int lc = __shfl_sync(sel::kFull, count, l);
+        const float la = __shfl_sync(sel::kFull, absm, l);
+        Cand* ll = reinterpret_cast<Cand*>(
+            __shfl_sync(sel::kFull, reinterpret_cast<unsigned long long>(list), l));
+        __syncwarp();
+        int less;
+        const uint32_t kth = sel::warp_select<false>(ll, lc, a.k, 0, hist, &less);
+        const float bnd = __fadd_ru(ord_inv(kth), la);
+        const int nc = sel::warp_filter(ll, lc, sel::KeepBound{bnd});
+        if (lane == l) {
+          count = nc;
+          bound = bnd;
+          if (nc > a.cap - P_QUARTER) {
+            a.overflow[q] = 1;
+            count = 0;
+            bound = -INFINITY;
+          }
+        }
+      }
+    }
+    if (vq) a.cnt[list_id] = count;
+    if (vq && *s_abort) a.overflow[q] = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no MMA, load or remote arrival of either CTA is still pending
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ prep
 // Base rows -> fp16 operand rows (cosine: unit-normalised), |x|^2 for the L2
 // epilogue, max |x| for the margins, and the list of near-zero cosine rows.
@@ -767,6 +1023,93 @@ TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms, int align_tiles) {
   p.seg_len = std::max<int64_t>(1, tiles_per_seg) * BN;
   p.nseg = (int)std::max<int64_t>(1, (n + p.seg_len - 1) / p.seg_len);
   return p;
+}
+
+// Plan of the 2-SM candidate pass: pairs of 256 queries x segments of
+// 256-row tiles, at most 8 segments (4 lists each: the warp select takes at
+// most 32 lists per query), chosen like tc_plan for whole waves of SM pairs.
+TcPlan tc_plan2(int64_t n, int nq, int kk, int num_sms) {
+  TcPlan p;
+  p.qtiles = (nq + 2 * P_BM - 1) / (2 * P_BM);
+  p.cap = 1024;
+  while (p.cap < 2 * kk + 2 * BN) p.cap *= 2;
+  const int pairs = std::max(1, num_sms / 2);
+  const int64_t ntile_total = (n + P_BN - 1) / P_BN;
+  double best = 1e30;
+  p.nseg = 1;
+  for (int s = 1; s <= 8; s++) {
+    if (s > 1 && ntile_total / s < 4) break;
+    const double waves = (double)p.qtiles * s / pairs;
+    const double cost = std::ceil(waves) / waves + 0.003 * s;
+    if (cost < best - 1e-9) {
+      best = cost;
+      p.nseg = s;
+    }
+  }
+  const int64_t tiles_per_seg = std::max<int64_t>(1, (ntile_total + p.nseg - 1) / p.nseg);
+  p.seg_len = tiles_per_seg * P_BN;
+  p.nseg = (int)std::max<int64_t>(1, (n + p.seg_len - 1) / p.seg_len);
+  return p;
+}
+
+// Candidate pass on CTA pairs (knn_scan_tc2_kernel): lists [4 * nseg][nq][cap].
+int tc_scan2(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn, int metric,
+             int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow, const float* absm, int* err,
+             const float* init_bound, const float* qscale, float xscale, cudaStream_t s) {
+  if (n == 0 || nq == 0) return VRS_OK;
+  if (nq_rows_alloc % (2 * P_BM) != 0) {
+    set_error(VRS_ERR_INVALID_CONFIG, "2-SM scan: query operand rows must be a multiple of 256");
+    return VRS_ERR_INVALID_CONFIG;
+  }
+  const int d16 = tc_d16(metric, d);
+  CUtensorMap tmA, tmB;
+  const bool f16 = tc_fp16(metric);
+  VRS_TRY(make_tmap(&tmA, qb, nq_rows_alloc, d16, f16));
+  VRS_TRY(make_tmap(&tmB, xb, n, d16, f16));
+  TcScanArgs a;
+  a.xn = xn;
+  a.n = n;
+  a.nq = nq;
+  a.ksteps = d16 / 16;
+  a.kblk = (d16 + KBW - 1) / KBW;
+  a.seg_len = p.seg_len;
+  a.cand = cand;
+  a.cnt = cnt;
+  a.overflow = overflow;
+  a.cap = p.cap;
+  a.k = kk;
+  a.absm = absm;
+  a.err = err;
+  a.tmin = nullptr;
+  a.tmin_stride = 0;
+  a.idesc = f16 ? idesc_f16(2 * P_BM, P_BN) : idesc_bf16(2 * P_BM, P_BN);
+  a.qscale = qscale;
+  a.xscale = xscale;
+  a.init_bound = init_bound;
+  const bool l2 = metric == vrs_exact::kL2 || metric == vrs_exact::kMaha;
+  auto kern = tc_fold(metric, d) ? knn_scan_tc2_kernel<2> : l2 ? knn_scan_tc2_kernel<0> : knn_scan_tc2_kernel<1>;
+  static std::once_flag attr_once[64];
+  int dev = 0;
+  VRS_CUDA(cudaGetDevice(&dev));
+  int attr_err = 0;
+  if (dev < 64) {
+    std::call_once(attr_once[dev], [&] {
+      for (auto f : {knn_scan_tc2_kernel<0>, knn_scan_tc2_kernel<1>, knn_scan_tc2_kernel<2>})
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM_TOTAL) != cudaSuccess)
+          attr_err = 1;
+    });
+  } else {
+    VRS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM_TOTAL));
+  }
+  if (attr_err) {
+    set_error(VRS_ERR_DRIVER, "cudaFuncSetAttribute(knn_scan_tc2_kernel) failed");
+    return VRS_ERR_DRIVER;
+  }
+  dim3 grid(2 * p.qtiles, p.nseg);  // x: two CTAs (one cluster) per 256 queries
+  kern<<<grid, THREADS, P_SMEM_TOTAL, s>>>(tmA, tmB, a);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
 }
 
 int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn,

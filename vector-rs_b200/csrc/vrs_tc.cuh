@@ -66,6 +66,12 @@ inline int tc_fold_exponent(int d, float xscale, float maxabs) {
 // align_tiles: segments hold a multiple of this many 128-row tiles (the
 // pivot pass passes kPivotGroup).
 TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms, int align_tiles = 1);
+// The candidate pass on CTA pairs (cta_group::2, M = N = 256): its plan and
+// launch; its lists are [4 * nseg][nq][cap] (one per 64-column quarter).
+TcPlan tc_plan2(int64_t n, int nq, int kk, int num_sms);
+int tc_scan2(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn, int metric,
+             int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow, const float* absm, int* err,
+             const float* init_bound, const float* qscale, float xscale, cudaStream_t s);
 // The pivot pass reports one minimum per column half of every group of
 // kPivotGroup 128-row tiles (256 pivot rows per value): fewer values to
 // store and to select from, each still the score of a distinct row.
