@@ -179,6 +179,30 @@ struct PqHeap {
 };
 
 
+// Sub-vectors shorter than 16 elements: the reference's AVX-512 kernels
+// never fill a 16-lane register, their lane reductions add or take the
+// maximum of zeros (+0), and only the scalar tail remains -- a sequential
+// f32 sum (or maximum) from +0 with separate multiply and add, exactly as
+// the general functions of vrs_exact.cuh compute it for such lengths.
+template <int METRIC>
+__device__ __forceinline__ float short_key(const float* x, const float* c, int n) {
+  float r = 0.0f;
+  for (int i = 0; i < n; i++) {
+    if (METRIC == vrs_exact::kL2 || METRIC == vrs_exact::kMaha) {
+      const float d = __fsub_rn(x[i], c[i]);
+      r = __fadd_rn(r, __fmul_rn(d, d));
+    } else if (METRIC == vrs_exact::kDot) {
+      r = __fadd_rn(r, __fmul_rn(x[i], c[i]));
+    } else if (METRIC == vrs_exact::kL1) {
+      r = __fadd_rn(r, fabsf(__fsub_rn(x[i], c[i])));
+    } else {  // kCheb
+      const float d = fabsf(__fsub_rn(x[i], c[i]));
+      if (d > r) r = d;
+    }
+  }
+  return r;
+}
+
 // Table value lut[t], t = m * ksub + s: the reference's pair function of
 // sub-vector m of the residual and sub-centroid (m, s), reported value.
 template <int METRIC>
@@ -186,6 +210,9 @@ __device__ __forceinline__ float lut_value(const AdcArgs& a, const float* resid,
   const int m = t / a.ksub;
   const float* x = resid + m * a.ds;
   const float* c = a.cb + (size_t)t * a.ds;
+  constexpr bool kShort = METRIC == vrs_exact::kL2 || METRIC == vrs_exact::kMaha || METRIC == vrs_exact::kDot ||
+                          METRIC == vrs_exact::kL1 || METRIC == vrs_exact::kCheb;
+  if (kShort && a.ds < 16) return vrs_exact::finish(METRIC, short_key<METRIC>(x, c, a.ds));
   float key;
   if (METRIC == vrs_exact::kCos) {
     key = vrs_exact::cos_finish(vrs_exact::cos_dot(x, c, a.ds), raux[m], a.cb_aux[t]);
