@@ -1441,12 +1441,14 @@ struct KmShard {
   DBuf segws;  // counting-sort workspace of the centroid sums
   HBuf hstat;  // pinned: {assignment error word, max centroid shift} per iteration
   DBuf cent_prev;        // centroids the latest assignment was made against
+  DBuf pscore, ibound;   // squared L2: score bound of each point's assignment; next step's starting bound
   bool last_tc = false;  // the latest assignment took the tensor-core path
   ~KmShard() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     for (DBuf* b : {&x, &xr, &x_aux, &assign, &dist, &acc, &cent, &cent_r, &cent_aux, &shift, &scal, &red, &xb,
-                    &xq, &xtiny, &cb, &cn, &cmax, &res, &cands, &err, &ctiny, &segws, &flags, &cent_prev})
+                    &xq, &xtiny, &cb, &cn, &cmax, &res, &cands, &err, &ctiny, &segws, &flags, &cent_prev, &pscore,
+                    &ibound})
       b->release();
     hstat.release();
     if (stream) cudaStreamDestroy(stream);
@@ -1505,6 +1507,10 @@ int km_prepare_shard(const KmParams& P, KmShard* s, const float* rows, int mem) 
     VRS_TRY(s->cands.reserve(nx * 2 * 8 * sizeof(Cand)));
     VRS_TRY(s->flags.reserve((2 * nx + 2) * sizeof(int)));
     VRS_TRY(s->err.reserve(sizeof(int)));
+    if (P.metric == vrs_exact::kL2 || P.metric == vrs_exact::kMaha) {
+      VRS_TRY(s->pscore.reserve(nx * sizeof(float)));
+      VRS_TRY(s->ibound.reserve(nx * sizeof(float)));
+    }
     VRS_CUDA(cudaMemsetAsync(s->cn.p, 0, (size_t)kpad * sizeof(float), s->stream));
     s->use_tc = true;  // point operands are prepared in km_run, once the global max |x| is known
   }
@@ -1611,11 +1617,18 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
         }
         if (!any_tiny) {
           VRS_CUDA(cudaMemsetAsync(s->err.p, 0, sizeof(int), s->stream));
+          // Squared L2 after a tensor-core step: every point starts from the
+          // bound its last assignment and that centroid's shift give.
+          const bool l2 = P.metric == vrs_exact::kL2 || P.metric == vrs_exact::kMaha;
+          const bool start = l2 && it > 0 && s->last_tc;
           ProfToken t = prof_begin("kmeans_assign", s->stream);
+          if (start)
+            VRS_TRY(kmtc::start_bound(s->n_local, s->assign.as<int32_t>(), s->pscore.as<float>(),
+                                      s->xq.as<float>(), s->shift.as<float>(), s->ibound.as<float>(), s->stream));
           VRS_TRY(kmtc::assign(s->xb.p, s->n_local, s->cb.p, P.k, P.d, s->cn.as<float>(), s->xq.as<float>(),
                                s->cmax.as<unsigned int>(), P.metric, op_scale, s->res.as<kmtc::Res>(),
-                               s->cands.as<Cand>(),
-                               s->err.as<int>(), s->num_sms, s->stream));
+                               s->cands.as<Cand>(), s->err.as<int>(), s->num_sms,
+                               start ? s->ibound.as<float>() : nullptr, s->stream));
           prof_end(t, s->stream);
           ProfToken t2 = prof_begin("kmeans_finalize", s->stream);
           VRS_TRY(kmtc::finalize(s->x.as<float>(), s->n_local, P.d, P.dp, s->cent.as<float>(),
@@ -1624,7 +1637,7 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
                                  s->cands.as<Cand>(),
                                  P.metric == vrs_exact::kCos ? s->xtiny.as<int>() : nullptr,
                                  s->assign.as<int32_t>(), s->dist.as<float>(), s->flags.as<int>(), s->num_sms,
-                                 op_scale, s->stream));
+                                 op_scale, l2 ? s->pscore.as<float>() : nullptr, s->stream));
           prof_end(t2, s->stream);
           tc_done = true;
         }

@@ -71,6 +71,9 @@ struct AssignArgs {
   Res* res;                 // [n][2] per (point, column half)
   Cand* cands;              // [n][2][NCAND]
   int* err;
+  // Upper bound on each point's best approximate score (MODE 0, from the
+  // previous Lloyd step; null: none): candidates start within it.
+  const float* init_bound;
 };
 
 // Acceptance margin of one point in score units (same bound as the kNN
@@ -265,7 +268,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float absm = vp ? point_margin(a.metric, a.d, a.xq[p], X, a.inv_scale) : 0.0f;
       const float f2 = -2.0f * a.acc_scale, f1 = -a.acc_scale;
       float best = INFINITY;
-      float bound = vp ? INFINITY : -INFINITY;  // padding points keep nothing
+      // Padding points keep nothing; with a starting bound s (>= the exact
+      // score of some centroid), best approx <= s + e and e < absm / 2, so
+      // s + 1.5 absm >= best approx + absm keeps every candidate the
+      // unbounded sweep would keep at the end.
+      float bound = !vp ? -INFINITY : a.init_bound ? __fadd_ru(a.init_bound[p], 1.5f * absm) : INFINITY;
       float lost = INFINITY;  // smallest score pushed out of a full buffer
       int cnt = 0;
       // Keeps the NCAND best candidates; remembers the best score dropped.
@@ -326,9 +333,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float cmn = fmin3(fmin3(gm[0], gm[1], gm[2]), fmin3(gm[3], gm[4], gm[5]), fminf(gm[6], gm[7]));
           // A better chunk minimum tightens the bound; drop candidates that
           // fall outside it.
-          if (vp && cmn < best) {
+          if (vp && cmn < best && cmn <= bound) {
             best = cmn;
-            bound = __fadd_ru(best, absm);
+            bound = fminf(bound, __fadd_ru(best, absm));
             int k2 = 0;
             for (int e = 0; e < cnt; e++) {
               const Cand ce = buf[e];
@@ -397,7 +404,7 @@ template <int METRIC>
 __global__ void __launch_bounds__(256) kmeans_triage_kernel(
     int64_t n, int d, const float* __restrict__ xq, const unsigned int* __restrict__ cmax,
     const Res* __restrict__ res, const Cand* __restrict__ cands, const int* __restrict__ force_full,
-    int32_t* __restrict__ assign, int* __restrict__ flags, float inv_scale) {
+    int32_t* __restrict__ assign, int* __restrict__ flags, float inv_scale, float* __restrict__ pscore) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= n) return;
   const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
@@ -405,10 +412,12 @@ __global__ void __launch_bounds__(256) kmeans_triage_kernel(
   const float bound = __fadd_ru(fminf(r0.best, r1.best), absm);
   if (r0.lost <= bound || r1.lost <= bound || (force_full && force_full[i])) {
     flags[2 + atomicAdd(&flags[0], 1)] = (int)i;
+    if (pscore) pscore[i] = INFINITY;  // full exact scan: no approximate score kept
     return;
   }
   int nin = 0;
   uint32_t only = 0;
+  float only_hs = 0.0f;
   for (int h = 0; h < 2; h++) {
     const Res r = h ? r1 : r0;
     for (int e = 0; e < r.cnt; e++) {
@@ -416,13 +425,17 @@ __global__ void __launch_bounds__(256) kmeans_triage_kernel(
       if (ce.hs <= bound) {
         nin++;
         only = ce.id;
+        only_hs = ce.hs;
       }
     }
   }
-  if (nin == 1)
+  if (nin == 1) {
     assign[i] = (int)only;
-  else
+    // exact score of the assigned centroid <= approx + e, e < absm / 2
+    if (pscore) pscore[i] = __fadd_ru(only_hs, 0.5f * absm);
+  } else {
     flags[2 + n + atomicAdd(&flags[1], 1)] = (int)i;
+  }
 }
 
 // Finalize, step 2: the points of list M, one half-warp per point (its 16
@@ -434,7 +447,8 @@ __global__ void __launch_bounds__(128) kmeans_multi_kernel(
     const float* __restrict__ x, int64_t n, int d, int dp, const float* __restrict__ cent,
     const float* __restrict__ cent_aux, const float* __restrict__ x_aux, const float* __restrict__ xq,
     const unsigned int* __restrict__ cmax, const Res* __restrict__ res, const Cand* __restrict__ cands,
-    const int* __restrict__ flags, int32_t* __restrict__ assign, float* __restrict__ dist, float inv_scale) {
+    const int* __restrict__ flags, int32_t* __restrict__ assign, float* __restrict__ dist, float inv_scale,
+    float* __restrict__ pscore) {
   const int hl = threadIdx.x & 15;
   const unsigned mask = 0xffffu << (threadIdx.x & 16);
   const bool hib = vrs_exact::higher_is_better(METRIC);
@@ -450,6 +464,7 @@ __global__ void __launch_bounds__(128) kmeans_multi_kernel(
     const float bound = __fadd_ru(fminf(r0.best, r1.best), absm);
     int best = 0x7fffffff;
     float best_key = hib ? -INFINITY : INFINITY;
+    float best_hs = INFINITY;  // approximate score of the winner
     for (int h = 0; h < 2; h++) {
       const Res r = h ? r1 : r0;
       for (int e = 0; e < r.cnt; e++) {
@@ -463,12 +478,14 @@ __global__ void __launch_bounds__(128) kmeans_multi_kernel(
         if (better) {
           best_key = key;
           best = (int)c;
+          best_hs = ce.hs;
         }
       }
     }
     if (hl == 0) {
       assign[i] = best;
       dist[i] = vrs_exact::finish(METRIC, best_key);
+      if (pscore) pscore[i] = __fadd_ru(best_hs, 0.5f * absm);
     }
   }
 }
@@ -628,13 +645,14 @@ template <int M>
 int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
                  const float* x_aux, int k, const float* xq, const unsigned int* cmax, const Res* res,
                  const Cand* cands, const int* force_full, int32_t* assign, float* dist, int* flags,
-                 int num_sms, float inv_scale, cudaStream_t s) {
+                 int num_sms, float inv_scale, float* pscore, cudaStream_t s) {
   VRS_CUDA(cudaMemsetAsync(flags, 0, 2 * sizeof(int), s));
   kmeans_triage_kernel<M><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, d, xq, cmax, res, cands, force_full,
-                                                                        assign, flags, inv_scale);
+                                                                        assign, flags, inv_scale, pscore);
   VRS_CUDA(cudaGetLastError());
   kmeans_multi_kernel<M><<<(unsigned)(num_sms * 8), 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, xq, cmax,
-                                                                 res, cands, flags, assign, dist, inv_scale);
+                                                                 res, cands, flags, assign, dist, inv_scale,
+                                                                 pscore);
   VRS_CUDA(cudaGetLastError());
   kmeans_flagged_kernel<M><<<(unsigned)(num_sms * 8), 256, 0, s>>>(x, d, dp, cent, cent_aux, x_aux, k, flags,
                                                                    assign, dist);
@@ -643,7 +661,40 @@ int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, co
   return VRS_OK;
 }
 
+// Starting bound of the next Lloyd step (squared L2, Mahalanobis). Score
+// units are |c|^2 - 2 x.c = |x - c|^2 - |x|^2. With c the point's centroid
+// of the last step, pscore >= its score then and delta = |c_new - c_old|
+// (the update's squared shift), |x - c_new| <= |x - c_old| + delta gives
+// score_new(c) <= (sqrt(pscore + |x|^2) + delta)^2 - |x|^2; evaluated in
+// f64 with a relative allowance for the f32 inputs (|x| and the shift are
+// f32 results) and rounded up.
+__global__ void kmeans_start_bound_kernel(int64_t n, const int32_t* __restrict__ assign,
+                                          const float* __restrict__ pscore, const float* __restrict__ xq,
+                                          const float* __restrict__ shift, float* __restrict__ out) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float ps = pscore[i];
+  if (!(ps < INFINITY)) {
+    out[i] = INFINITY;
+    return;
+  }
+  const double x2 = (double)xq[i] * (double)xq[i];
+  const double r = sqrt(fmax(0.0, ((double)ps + x2) * (1.0 + 1e-6)));
+  const double dl = sqrt((double)shift[assign[i]] * (1.0 + 1e-4));
+  const double ub = (r + dl) * (r + dl) - x2 * (1.0 - 1e-6) + 1e-5 * ((r + dl) * (r + dl) + x2) + 1e-30;
+  out[i] = isfinite(ub) ? __double2float_ru(ub) : INFINITY;
+}
+
 }  // namespace
+
+int start_bound(int64_t n, const int32_t* assign, const float* pscore, const float* xq, const float* shift,
+                float* out, cudaStream_t s) {
+  if (n == 0) return VRS_OK;
+  kmeans_start_bound_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, assign, pscore, xq, shift, out);
+  VRS_CUDA(cudaGetLastError());
+  count_launch();
+  return VRS_OK;
+}
 
 bool supported(int metric, int d) {
   return d >= 1 && d <= 128 &&
@@ -663,7 +714,7 @@ int prep_rows(const float* x, int64_t n, int d, int dp, int metric, float op_sca
 
 int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
            const unsigned int* cmax, int metric, float op_scale, Res* res, Cand* cands, int* err, int num_sms,
-           cudaStream_t s) {
+           const float* init_bound, cudaStream_t s) {
   if (n == 0) return VRS_OK;
   const int d16 = (d + 15) / 16 * 16;
   CUtensorMap tmA, tmB;
@@ -685,6 +736,7 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
   a.res = res;
   a.cands = cands;
   a.err = err;
+  a.init_bound = a.mode == 0 ? init_bound : nullptr;
   auto kern = a.mode == 0 ? kmeans_assign_tc_kernel<0> : kmeans_assign_tc_kernel<1>;
   VRS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL));
   const int nptiles = (int)((n + BM * NACC - 1) / (BM * NACC));
@@ -698,21 +750,24 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
 int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
              const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
              const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
-             float op_scale, cudaStream_t s) {
+             float op_scale, float* pscore, cudaStream_t s) {
   if (n == 0) return VRS_OK;
   switch (metric) {
     case vrs_exact::kL2:
       return finalize_run<vrs_exact::kL2>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full,
-                                          assign_out, dist, flags, num_sms, 1.0f / op_scale, s);
+                                          assign_out, dist, flags, num_sms, 1.0f / op_scale, pscore, s);
     case vrs_exact::kMaha:
       return finalize_run<vrs_exact::kMaha>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                            force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, s);
+                                            force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, pscore,
+                                            s);
     case vrs_exact::kDot:
       return finalize_run<vrs_exact::kDot>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                           force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, s);
+                                           force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, nullptr,
+                                           s);
     case vrs_exact::kCos:
       return finalize_run<vrs_exact::kCos>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
-                                           force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, s);
+                                           force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, nullptr,
+                                           s);
   }
   set_error(VRS_ERR_INVALID_CONFIG, "k-means tensor-core finalize: unsupported metric");
   return VRS_ERR_INVALID_CONFIG;
