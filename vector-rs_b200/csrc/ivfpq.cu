@@ -93,6 +93,7 @@ struct AdcArgs {
   const float* coarse;     // [nlist][d]
   const float* cb;         // [M * ksub][ds]
   const float* cb_aux;     // cosine: [M * ksub] norm sums; Hellinger: [M * ksub][ds] element roots
+  const float* cb_t;       // [M][ds][ksub]: the codebooks with the sub-centroid index fastest
   const int64_t* off;      // [nlist + 1]
   const uint32_t* ids;     // [total]
   const uint8_t* codes;    // [total][M]
@@ -184,19 +185,22 @@ struct PqHeap {
 // maximum of zeros (+0), and only the scalar tail remains -- a sequential
 // f32 sum (or maximum) from +0 with separate multiply and add, exactly as
 // the general functions of vrs_exact.cuh compute it for such lengths.
+// c[i * cstride] is element i of the sub-centroid (the transposed copy:
+// consecutive threads read consecutive sub-centroids).
 template <int METRIC>
-__device__ __forceinline__ float short_key(const float* x, const float* c, int n) {
+__device__ __forceinline__ float short_key(const float* x, const float* c, int n, int cstride) {
   float r = 0.0f;
   for (int i = 0; i < n; i++) {
+    const float ci = c[i * cstride];
     if (METRIC == vrs_exact::kL2 || METRIC == vrs_exact::kMaha) {
-      const float d = __fsub_rn(x[i], c[i]);
+      const float d = __fsub_rn(x[i], ci);
       r = __fadd_rn(r, __fmul_rn(d, d));
     } else if (METRIC == vrs_exact::kDot) {
-      r = __fadd_rn(r, __fmul_rn(x[i], c[i]));
+      r = __fadd_rn(r, __fmul_rn(x[i], ci));
     } else if (METRIC == vrs_exact::kL1) {
-      r = __fadd_rn(r, fabsf(__fsub_rn(x[i], c[i])));
+      r = __fadd_rn(r, fabsf(__fsub_rn(x[i], ci)));
     } else {  // kCheb
-      const float d = fabsf(__fsub_rn(x[i], c[i]));
+      const float d = fabsf(__fsub_rn(x[i], ci));
       if (d > r) r = d;
     }
   }
@@ -212,7 +216,10 @@ __device__ __forceinline__ float lut_value(const AdcArgs& a, const float* resid,
   const float* c = a.cb + (size_t)t * a.ds;
   constexpr bool kShort = METRIC == vrs_exact::kL2 || METRIC == vrs_exact::kMaha || METRIC == vrs_exact::kDot ||
                           METRIC == vrs_exact::kL1 || METRIC == vrs_exact::kCheb;
-  if (kShort && a.ds < 16) return vrs_exact::finish(METRIC, short_key<METRIC>(x, c, a.ds));
+  if (kShort && a.ds < 16) {
+    const int sc = t - m * a.ksub;
+    return vrs_exact::finish(METRIC, short_key<METRIC>(x, a.cb_t + (size_t)m * a.ds * a.ksub + sc, a.ds, a.ksub));
+  }
   float key;
   if (METRIC == vrs_exact::kCos) {
     key = vrs_exact::cos_finish(vrs_exact::cos_dot(x, c, a.ds), raux[m], a.cb_aux[t]);
@@ -269,18 +276,39 @@ __global__ void __launch_bounds__(kAdcThreads) ivfpq_adc_kernel(AdcArgs a) {
       const int cnt = end - i0 < kAdcThreads ? (int)(end - i0) : kAdcThreads;
       if (i < end) {
         // compute_distance_with_lut: quads as (d0 + d1) + (d2 + d3), then
-        // the remainder, all in f32 without contraction.
+        // the remainder, all in f32 without contraction. With M a multiple
+        // of 4 a quad's codes are one aligned 32-bit word (16 bytes at a
+        // time when M is a multiple of 16).
         const uint8_t* code = a.codes + (size_t)i * M;
         float total = 0.0f;
         int m = 0;
-        for (; m + 4 <= M; m += 4) {
-          const float d0 = lut[m * ksub + code[m]];
-          const float d1 = lut[(m + 1) * ksub + code[m + 1]];
-          const float d2 = lut[(m + 2) * ksub + code[m + 2]];
-          const float d3 = lut[(m + 3) * ksub + code[m + 3]];
+        auto quad = [&](uint32_t w, int mq) {
+          const float d0 = lut[mq * ksub + (w & 0xff)];
+          const float d1 = lut[(mq + 1) * ksub + ((w >> 8) & 0xff)];
+          const float d2 = lut[(mq + 2) * ksub + ((w >> 16) & 0xff)];
+          const float d3 = lut[(mq + 3) * ksub + (w >> 24)];
           total = __fadd_rn(total, __fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)));
+        };
+        if ((M & 15) == 0) {
+          for (; m < M; m += 16) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(code + m));
+            quad(w.x, m);
+            quad(w.y, m + 4);
+            quad(w.z, m + 8);
+            quad(w.w, m + 12);
+          }
+        } else if ((M & 3) == 0) {
+          for (; m < M; m += 4) quad(__ldg(reinterpret_cast<const uint32_t*>(code + m)), m);
+        } else {
+          for (; m + 4 <= M; m += 4) {
+            const float d0 = lut[m * ksub + code[m]];
+            const float d1 = lut[(m + 1) * ksub + code[m + 1]];
+            const float d2 = lut[(m + 2) * ksub + code[m + 2]];
+            const float d3 = lut[(m + 3) * ksub + code[m + 3]];
+            total = __fadd_rn(total, __fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)));
+          }
+          for (; m < M; m++) total = __fadd_rn(total, lut[m * ksub + code[m]]);
         }
-        for (; m < M; m++) total = __fadd_rn(total, lut[m * ksub + code[m]]);
         c_hs[tid] = hib ? -total : total;
         c_dist[tid] = total;
         c_id[tid] = a.ids[i];
@@ -384,7 +412,7 @@ struct vrs_ivfpq {
   int d = 0, M = 0, ksub = 0, ds = 0, metric = 0, device = 0;
   vrs_knn* coarse_h = nullptr;  // kNN handle over the coarse centroids (probing)
   cudaStream_t stream = nullptr;
-  vrs::DevArr coarse, cb, cb_aux, off, ids, codes;
+  vrs::DevArr coarse, cb, cb_aux, cb_t, off, ids, codes;
   vrs::DevArr q, probe, odist, oid, ocount;  // per search, grown on demand
   ~vrs_ivfpq() {
     if (stream) {
@@ -449,6 +477,16 @@ extern "C" int vrs_ivfpq_create(const float* coarse_centroids, int64_t nlist, in
   cudaStream_t s = h->stream;
   VRS_TRY(upload(h->coarse, coarse_centroids, (size_t)nlist * d * sizeof(float), s));
   VRS_TRY(upload(h->cb, codebooks, nsub * h->ds * sizeof(float), s));
+  {
+    // [M][ds][ksub] copy for coalesced table builds.
+    std::vector<float> t(nsub * h->ds);
+    for (int m = 0; m < num_subvectors; m++)
+      for (int sc = 0; sc < sub_clusters; sc++)
+        for (int e = 0; e < h->ds; e++)
+          t[((size_t)m * h->ds + e) * sub_clusters + sc] = codebooks[((size_t)m * sub_clusters + sc) * h->ds + e];
+    VRS_TRY(upload(h->cb_t, t.data(), t.size() * sizeof(float), s));
+    VRS_CUDA(cudaStreamSynchronize(s));  // t is freed at the end of this scope
+  }
   VRS_TRY(upload(h->off, list_offsets, nlist > 0 ? (size_t)(nlist + 1) * sizeof(int64_t) : 0, s));
   VRS_TRY(upload(h->ids, ids, (size_t)total * sizeof(uint32_t), s));
   VRS_TRY(upload(h->codes, codes, (size_t)total * num_subvectors, s));
@@ -511,6 +549,7 @@ extern "C" int vrs_ivfpq_search(vrs_ivfpq* h, const float* queries, int64_t nq, 
     a.coarse = h->coarse.as<float>();
     a.cb = h->cb.as<float>();
     a.cb_aux = h->cb_aux.as<float>();
+    a.cb_t = h->cb_t.as<float>();
     a.off = h->off.as<int64_t>();
     a.ids = h->ids.as<uint32_t>();
     a.codes = h->codes.as<uint8_t>();

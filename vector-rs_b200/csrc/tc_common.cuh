@@ -267,9 +267,13 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
   return r;
 }
 
-// Arrive (release, cluster scope) on an mbarrier of either CTA of the pair.
+// Arrive on an mbarrier of either CTA of the pair, with the default
+// release semantics at CTA scope. The epilogue uses it to hand a TMEM buffer
+// back to the MMA issuer in the other CTA: tcgen05.wait::ld has already
+// completed its TMEM reads, so nothing else needs ordering; a cluster-scope
+// release would also wait for the warp's outstanding global stores.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
 }
 
 // 2-D tiled load (no multicast) into this CTA's shared memory whose
