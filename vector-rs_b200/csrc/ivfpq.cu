@@ -44,7 +44,8 @@
 namespace vrs {
 namespace {
 
-constexpr int kAdcThreads = 128;
+constexpr int kAdcChunk = 128;                  // list entries scored per round (one per scorer)
+constexpr int kAdcThreads = kAdcChunk + 32;     // four scorer warps + the replay warp
 constexpr int kMaxK = 2048;           // heap capacity in shared memory
 constexpr int kMaxLut = 16384;        // M * ksub table entries (64 KB)
 constexpr int kMaxDim = 4096;         // residual (and its roots) in shared memory
@@ -231,140 +232,176 @@ __device__ __forceinline__ float lut_value(const AdcArgs& a, const float* resid,
   return vrs_exact::finish(METRIC, key);
 }
 
-// One block per query: probed lists in order, table per list, 128 entries
-// scored per round, warp 0 replays them into the heap.
+// Named barriers: the replay warp and the scorers hand chunk buffers to each
+// other (bar.arrive on one side, bar.sync on the other, kAdcThreads threads).
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+constexpr int kBarFull = 1;   // + buffer: scorers -> replay warp
+constexpr int kBarEmpty = 3;  // + buffer: replay warp -> scorers
+constexpr int kBarTable = 5;  // scorers only: the table is built / no longer read
+
+// One block per query. Warps 0-3 (the scorers) walk the probed lists in
+// order: per list they build the table, then score 128 entries at a time
+// into one of two chunk buffers. Warp 4 replays each filled buffer into the
+// heap in scan order while the scorers fill the other one; both sides walk
+// the same (list, chunk) sequence, so chunk j uses buffer j % 2, the
+// scorers wait for the replay of chunk j - 2 before refilling it, and the
+// replay of the last two chunks is never waited for (no arrive without its
+// sync).
 template <int METRIC>
 __global__ void __launch_bounds__(kAdcThreads) ivfpq_adc_kernel(AdcArgs a) {
   extern __shared__ __align__(16) float smem[];
   const int qi = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31;
   const int M = a.M, ksub = a.ksub, d = a.d, k = a.k;
   float* lut = smem;                          // [M * ksub]
   float* resid = lut + M * ksub;              // [d]
   float* raux = resid + d;                    // [d] roots (Hellinger) / [M] norm sums (cosine)
-  float* c_hs = raux + d;                     // [128] chunk heap scores
-  float* c_dist = c_hs + kAdcThreads;         // [128] chunk values
-  uint32_t* c_id = reinterpret_cast<uint32_t*>(c_dist + kAdcThreads);  // [128]
+  float* c_hs = raux + d;                     // [2][128] chunk heap scores
+  float* c_dist = c_hs + 2 * kAdcChunk;       // [2][128] chunk values
+  uint32_t* c_id = reinterpret_cast<uint32_t*>(c_dist + 2 * kAdcChunk);  // [2][128]
   PqHeap heap;
-  heap.hs = reinterpret_cast<float*>(c_id + kAdcThreads);  // [k]
-  heap.dist = heap.hs + k;                                  // [k]
-  heap.id = reinterpret_cast<uint32_t*>(heap.dist + k);     // [k]
-  __shared__ int s_hn;
-  if (tid == 0) s_hn = 0;
+  heap.hs = reinterpret_cast<float*>(c_id + 2 * kAdcChunk);  // [k]
+  heap.dist = heap.hs + k;                                    // [k]
+  heap.id = reinterpret_cast<uint32_t*>(heap.dist + k);       // [k]
   const bool hib = vrs_exact::higher_is_better(METRIC);
   const float* q = a.q + (size_t)qi * d;
+  const int32_t* probe = a.probe + (size_t)qi * a.P;
+  // Chunks over all probed lists (both sides need the count).
+  int total = 0;
   for (int p = 0; p < a.P; p++) {
-    const int c = a.probe[(size_t)qi * a.P + p];
-    const int64_t beg = a.off[c], end = a.off[c + 1];
-    if (end <= beg) continue;  // empty list: skipped, as the reference does
-    __syncthreads();  // the previous list's table and chunk are no longer read
-    const float* cc = a.coarse + (size_t)c * d;
-    for (int e = tid; e < d; e += kAdcThreads) {
-      const float r = __fsub_rn(q[e], cc[e]);
-      resid[e] = r;
-      if (METRIC == vrs_exact::kHell) raux[e] = vrs_exact::root_abs(r);
-    }
-    __syncthreads();
-    if (METRIC == vrs_exact::kCos) {
-      for (int m = tid; m < M; m += kAdcThreads) raux[m] = vrs_exact::cos_norm_sq(resid + m * a.ds, a.ds);
-      __syncthreads();
-    }
-    for (int t = tid; t < M * ksub; t += kAdcThreads) lut[t] = lut_value<METRIC>(a, resid, raux, t);
-    __syncthreads();
-    for (int64_t i0 = beg; i0 < end; i0 += kAdcThreads) {
-      const int64_t i = i0 + tid;
-      const int cnt = end - i0 < kAdcThreads ? (int)(end - i0) : kAdcThreads;
-      if (i < end) {
-        // compute_distance_with_lut: quads as (d0 + d1) + (d2 + d3), then
-        // the remainder, all in f32 without contraction. With M a multiple
-        // of 4 a quad's codes are one aligned 32-bit word (16 bytes at a
-        // time when M is a multiple of 16).
-        const uint8_t* code = a.codes + (size_t)i * M;
-        float total = 0.0f;
-        int m = 0;
-        auto quad = [&](uint32_t w, int mq) {
-          const float d0 = lut[mq * ksub + (w & 0xff)];
-          const float d1 = lut[(mq + 1) * ksub + ((w >> 8) & 0xff)];
-          const float d2 = lut[(mq + 2) * ksub + ((w >> 16) & 0xff)];
-          const float d3 = lut[(mq + 3) * ksub + (w >> 24)];
-          total = __fadd_rn(total, __fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)));
-        };
-        if ((M & 15) == 0) {
-          for (; m < M; m += 16) {
-            const uint4 w = __ldg(reinterpret_cast<const uint4*>(code + m));
-            quad(w.x, m);
-            quad(w.y, m + 4);
-            quad(w.z, m + 8);
-            quad(w.w, m + 12);
-          }
-        } else if ((M & 3) == 0) {
-          for (; m < M; m += 4) quad(__ldg(reinterpret_cast<const uint32_t*>(code + m)), m);
-        } else {
-          for (; m + 4 <= M; m += 4) {
-            const float d0 = lut[m * ksub + code[m]];
-            const float d1 = lut[(m + 1) * ksub + code[m + 1]];
-            const float d2 = lut[(m + 2) * ksub + code[m + 2]];
-            const float d3 = lut[(m + 3) * ksub + code[m + 3]];
-            total = __fadd_rn(total, __fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)));
-          }
-          for (; m < M; m++) total = __fadd_rn(total, lut[m * ksub + code[m]]);
-        }
-        c_hs[tid] = hib ? -total : total;
-        c_dist[tid] = total;
-        c_id[tid] = a.ids[i];
+    const int c = probe[p];
+    total += (int)((a.off[c + 1] - a.off[c] + kAdcChunk - 1) / kAdcChunk);
+  }
+  if (tid < kAdcChunk) {
+    // ------------------------------------------------------------ scorers
+    int chunk = 0;
+    for (int p = 0; p < a.P; p++) {
+      const int c = probe[p];
+      const int64_t beg = a.off[c], end = a.off[c + 1];
+      if (end <= beg) continue;  // empty list: skipped, as the reference does
+      named_sync(kBarTable, kAdcChunk);  // the previous list's table is no longer read
+      const float* cc = a.coarse + (size_t)c * d;
+      for (int e = tid; e < d; e += kAdcChunk) {
+        const float r = __fsub_rn(q[e], cc[e]);
+        resid[e] = r;
+        if (METRIC == vrs_exact::kHell) raux[e] = vrs_exact::root_abs(r);
       }
-      __syncthreads();
-      if (warp == 0) {
+      named_sync(kBarTable, kAdcChunk);
+      if (METRIC == vrs_exact::kCos) {
+        for (int m = tid; m < M; m += kAdcChunk) raux[m] = vrs_exact::cos_norm_sq(resid + m * a.ds, a.ds);
+        named_sync(kBarTable, kAdcChunk);
+      }
+      for (int t = tid; t < M * ksub; t += kAdcChunk) lut[t] = lut_value<METRIC>(a, resid, raux, t);
+      named_sync(kBarTable, kAdcChunk);
+      for (int64_t i0 = beg; i0 < end; i0 += kAdcChunk, chunk++) {
+        const int b = chunk & 1;
+        if (chunk >= 2) named_sync(kBarEmpty + b, kAdcThreads);
+        const int64_t i = i0 + tid;
+        if (i < end) {
+          // compute_distance_with_lut: quads as (d0 + d1) + (d2 + d3), then
+          // the remainder, all in f32 without contraction. With M a
+          // multiple of 4 a quad's codes are one aligned 32-bit word (16
+          // bytes at a time when M is a multiple of 16).
+          const uint8_t* code = a.codes + (size_t)i * M;
+          float total_s = 0.0f;
+          int m = 0;
+          auto quad = [&](uint32_t w, int mq) {
+            const float d0 = lut[mq * ksub + (w & 0xff)];
+            const float d1 = lut[(mq + 1) * ksub + ((w >> 8) & 0xff)];
+            const float d2 = lut[(mq + 2) * ksub + ((w >> 16) & 0xff)];
+            const float d3 = lut[(mq + 3) * ksub + (w >> 24)];
+            total_s = __fadd_rn(total_s, __fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)));
+          };
+          if ((M & 15) == 0) {
+            for (; m < M; m += 16) {
+              const uint4 w = __ldg(reinterpret_cast<const uint4*>(code + m));
+              quad(w.x, m);
+              quad(w.y, m + 4);
+              quad(w.z, m + 8);
+              quad(w.w, m + 12);
+            }
+          } else if ((M & 3) == 0) {
+            for (; m < M; m += 4) quad(__ldg(reinterpret_cast<const uint32_t*>(code + m)), m);
+          } else {
+            for (; m + 4 <= M; m += 4) {
+              const float d0 = lut[m * ksub + code[m]];
+              const float d1 = lut[(m + 1) * ksub + code[m + 1]];
+              const float d2 = lut[(m + 2) * ksub + code[m + 2]];
+              const float d3 = lut[(m + 3) * ksub + code[m + 3]];
+              total_s = __fadd_rn(total_s, __fadd_rn(__fadd_rn(d0, d1), __fadd_rn(d2, d3)));
+            }
+            for (; m < M; m++) total_s = __fadd_rn(total_s, lut[m * ksub + code[m]]);
+          }
+          c_hs[b * kAdcChunk + tid] = hib ? -total_s : total_s;
+          c_dist[b * kAdcChunk + tid] = total_s;
+          c_id[b * kAdcChunk + tid] = a.ids[i];
+        }
+        named_arrive(kBarFull + b, kAdcThreads);
+      }
+    }
+  } else {
+    // -------------------------------------------------------- replay warp
+    int n = 0;  // heap size (lane 0's view; the ballots read the root)
+    int chunk = 0;
+    for (int p = 0; p < a.P; p++) {
+      const int c = probe[p];
+      const int64_t beg = a.off[c], end = a.off[c + 1];
+      for (int64_t i0 = beg; i0 < end; i0 += kAdcChunk, chunk++) {
+        const int b = chunk & 1;
+        const int cnt = end - i0 < kAdcChunk ? (int)(end - i0) : kAdcChunk;
+        named_sync(kBarFull + b, kAdcThreads);
+        const float* hs_b = c_hs + b * kAdcChunk;
         for (int w = 0; w < cnt; w += 32) {
           const int j = w + lane;
-          const int hn = s_hn;
+          const int hn = __shfl_sync(0xffffffffu, n, 0);
           // Full heap: only entries strictly below the root at the start of
           // these 32 can enter (the root never rises); filling: all of them.
-          const bool cand = j < cnt && (hn < k || c_hs[j] < heap.hs[0]);
+          const bool cand = j < cnt && (hn < k || hs_b[j] < heap.hs[0]);
           unsigned msk = __ballot_sync(0xffffffffu, cand);
           if (lane == 0) {
-            int n = hn;
             while (msk) {
               const int e = w + __ffs(msk) - 1;
               msk &= msk - 1;
-              const float h = c_hs[e];
+              const float h = hs_b[e];
               if (n < k) {
-                heap.push(n, h, c_dist[e], c_id[e]);
+                heap.push(n, h, c_dist[b * kAdcChunk + e], c_id[b * kAdcChunk + e]);
                 n++;
               } else if (h < heap.hs[0]) {
                 float th, td;
                 uint32_t ti;
                 heap.pop(n, &th, &td, &ti);
-                heap.push(n - 1, h, c_dist[e], c_id[e]);
+                heap.push(n - 1, h, c_dist[b * kAdcChunk + e], c_id[b * kAdcChunk + e]);
               }
             }
-            s_hn = n;
           }
           __syncwarp();
         }
+        if (chunk + 2 < total) named_arrive(kBarEmpty + b, kAdcThreads);
       }
-      __syncthreads();
     }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    // Popped worst first; written from the back, so the row is best first.
-    int n = s_hn;
-    const int count = n;
-    while (n > 0) {
-      float th, td;
-      uint32_t ti;
-      heap.pop(n, &th, &td, &ti);
-      n--;
-      a.out_dist[(size_t)qi * k + n] = td;
-      a.out_id[(size_t)qi * k + n] = ti;
+    if (lane == 0) {
+      // Popped worst first; written from the back, so the row is best first.
+      const int count = n;
+      while (n > 0) {
+        float th, td;
+        uint32_t ti;
+        heap.pop(n, &th, &td, &ti);
+        n--;
+        a.out_dist[(size_t)qi * k + n] = td;
+        a.out_id[(size_t)qi * k + n] = ti;
+      }
+      a.out_count[qi] = count;
     }
-    a.out_count[qi] = count;
   }
 }
 
 size_t adc_smem_bytes(int M, int ksub, int d, int k) {
-  return ((size_t)M * ksub + 2 * (size_t)d + 3 * kAdcThreads + 3 * (size_t)k) * sizeof(float);
+  return ((size_t)M * ksub + 2 * (size_t)d + 6 * kAdcChunk + 3 * (size_t)k) * sizeof(float);
 }
 
 template <int METRIC>
