@@ -232,6 +232,48 @@ __device__ __forceinline__ float lut_value(const AdcArgs& a, const float* resid,
   return vrs_exact::finish(METRIC, key);
 }
 
+// Table build for sub-vectors of DS < 16 elements (the common PQ case): per
+// sub-space m the residual slice sits in registers and thread s computes
+// sub-centroids s, s + 128, ... from the transposed codebook, all DS loads
+// of an entry in flight together; the arithmetic is short_key's.
+template <int METRIC, int DS>
+__device__ void build_table_short(const AdcArgs& a, const float* resid, float* lut, int tid) {
+  for (int m = 0; m < a.M; m++) {
+    float xv[DS];
+#pragma unroll
+    for (int e = 0; e < DS; e++) xv[e] = resid[m * DS + e];
+    const float* cbm = a.cb_t + (size_t)m * DS * a.ksub;
+    for (int sc = tid; sc < a.ksub; sc += kAdcChunk) {
+      float cv[DS];
+#pragma unroll
+      for (int e = 0; e < DS; e++) cv[e] = __ldg(cbm + (size_t)e * a.ksub + sc);
+      lut[m * a.ksub + sc] = vrs_exact::finish(METRIC, short_key<METRIC>(xv, cv, DS, 1));
+    }
+  }
+}
+
+// Builds the probed list's table into `lut` (the scorers call it).
+template <int METRIC>
+__device__ void build_table(const AdcArgs& a, const float* resid, const float* raux, float* lut, int tid) {
+  constexpr bool kShort = METRIC == vrs_exact::kL2 || METRIC == vrs_exact::kMaha || METRIC == vrs_exact::kDot ||
+                          METRIC == vrs_exact::kL1 || METRIC == vrs_exact::kCheb;
+  if (kShort) {
+    switch (a.ds) {
+#define VRS_DS_CASE(n) \
+  case n:              \
+    build_table_short<METRIC, n>(a, resid, lut, tid); \
+    return;
+      VRS_DS_CASE(1) VRS_DS_CASE(2) VRS_DS_CASE(3) VRS_DS_CASE(4) VRS_DS_CASE(5) VRS_DS_CASE(6) VRS_DS_CASE(7)
+      VRS_DS_CASE(8) VRS_DS_CASE(9) VRS_DS_CASE(10) VRS_DS_CASE(11) VRS_DS_CASE(12) VRS_DS_CASE(13)
+      VRS_DS_CASE(14) VRS_DS_CASE(15)
+#undef VRS_DS_CASE
+      default:
+        break;
+    }
+  }
+  for (int t = tid; t < a.M * a.ksub; t += kAdcChunk) lut[t] = lut_value<METRIC>(a, resid, raux, t);
+}
+
 // Named barriers: the replay warp and the scorers hand chunk buffers to each
 // other (bar.arrive on one side, bar.sync on the other, kAdcThreads threads).
 __device__ __forceinline__ void named_sync(int id, int count) {
@@ -296,7 +338,7 @@ __global__ void __launch_bounds__(kAdcThreads) ivfpq_adc_kernel(AdcArgs a) {
         for (int m = tid; m < M; m += kAdcChunk) raux[m] = vrs_exact::cos_norm_sq(resid + m * a.ds, a.ds);
         named_sync(kBarTable, kAdcChunk);
       }
-      for (int t = tid; t < M * ksub; t += kAdcChunk) lut[t] = lut_value<METRIC>(a, resid, raux, t);
+      build_table<METRIC>(a, resid, raux, lut, tid);
       named_sync(kBarTable, kAdcChunk);
       for (int64_t i0 = beg; i0 < end; i0 += kAdcChunk, chunk++) {
         const int b = chunk & 1;
