@@ -276,15 +276,32 @@ __device__ void build_table(const AdcArgs& a, const float* resid, const float* r
 
 // Named barriers: the replay warp and the scorers hand chunk buffers to each
 // other (bar.arrive on one side, bar.sync on the other, kAdcThreads threads).
-__device__ __forceinline__ void named_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+// Barrier ids are immediates, so the kernel reserves only the ids it uses
+// (a register id reserves all 16, which limits the blocks per SM).
+template <int ID>
+__device__ __forceinline__ void named_sync(int count) {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "r"(count) : "memory");
 }
-__device__ __forceinline__ void named_arrive(int id, int count) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+template <int ID>
+__device__ __forceinline__ void named_arrive(int count) {
+  asm volatile("bar.arrive %0, %1;" ::"n"(ID), "r"(count) : "memory");
 }
 constexpr int kBarFull = 1;   // + buffer: scorers -> replay warp
 constexpr int kBarEmpty = 3;  // + buffer: replay warp -> scorers
 constexpr int kBarTable = 5;  // scorers only: the table is built / no longer read
+__device__ __forceinline__ void sync_full(int b) {
+  if (b) named_sync<kBarFull + 1>(kAdcThreads); else named_sync<kBarFull>(kAdcThreads);
+}
+__device__ __forceinline__ void arrive_full(int b) {
+  if (b) named_arrive<kBarFull + 1>(kAdcThreads); else named_arrive<kBarFull>(kAdcThreads);
+}
+__device__ __forceinline__ void sync_empty(int b) {
+  if (b) named_sync<kBarEmpty + 1>(kAdcThreads); else named_sync<kBarEmpty>(kAdcThreads);
+}
+__device__ __forceinline__ void arrive_empty(int b) {
+  if (b) named_arrive<kBarEmpty + 1>(kAdcThreads); else named_arrive<kBarEmpty>(kAdcThreads);
+}
+__device__ __forceinline__ void sync_table() { named_sync<kBarTable>(kAdcChunk); }
 
 // One block per query. Warps 0-3 (the scorers) walk the probed lists in
 // order: per list they build the table, then score 128 entries at a time
@@ -295,7 +312,7 @@ constexpr int kBarTable = 5;  // scorers only: the table is built / no longer re
 // replay of the last two chunks is never waited for (no arrive without its
 // sync).
 template <int METRIC>
-__global__ void __launch_bounds__(kAdcThreads) ivfpq_adc_kernel(AdcArgs a) {
+__global__ void __launch_bounds__(kAdcThreads, 6) ivfpq_adc_kernel(AdcArgs a) {
   extern __shared__ __align__(16) float smem[];
   const int qi = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
@@ -326,23 +343,23 @@ __global__ void __launch_bounds__(kAdcThreads) ivfpq_adc_kernel(AdcArgs a) {
       const int c = probe[p];
       const int64_t beg = a.off[c], end = a.off[c + 1];
       if (end <= beg) continue;  // empty list: skipped, as the reference does
-      named_sync(kBarTable, kAdcChunk);  // the previous list's table is no longer read
+      sync_table();  // the previous list's table is no longer read
       const float* cc = a.coarse + (size_t)c * d;
       for (int e = tid; e < d; e += kAdcChunk) {
         const float r = __fsub_rn(q[e], cc[e]);
         resid[e] = r;
         if (METRIC == vrs_exact::kHell) raux[e] = vrs_exact::root_abs(r);
       }
-      named_sync(kBarTable, kAdcChunk);
+      sync_table();
       if (METRIC == vrs_exact::kCos) {
         for (int m = tid; m < M; m += kAdcChunk) raux[m] = vrs_exact::cos_norm_sq(resid + m * a.ds, a.ds);
-        named_sync(kBarTable, kAdcChunk);
+        sync_table();
       }
       build_table<METRIC>(a, resid, raux, lut, tid);
-      named_sync(kBarTable, kAdcChunk);
+      sync_table();
       for (int64_t i0 = beg; i0 < end; i0 += kAdcChunk, chunk++) {
         const int b = chunk & 1;
-        if (chunk >= 2) named_sync(kBarEmpty + b, kAdcThreads);
+        if (chunk >= 2) sync_empty(b);
         const int64_t i = i0 + tid;
         if (i < end) {
           // compute_distance_with_lut: quads as (d0 + d1) + (d2 + d3), then
@@ -383,7 +400,7 @@ __global__ void __launch_bounds__(kAdcThreads) ivfpq_adc_kernel(AdcArgs a) {
           c_dist[b * kAdcChunk + tid] = total_s;
           c_id[b * kAdcChunk + tid] = a.ids[i];
         }
-        named_arrive(kBarFull + b, kAdcThreads);
+        arrive_full(b);
       }
     }
   } else {
@@ -396,7 +413,7 @@ __global__ void __launch_bounds__(kAdcThreads) ivfpq_adc_kernel(AdcArgs a) {
       for (int64_t i0 = beg; i0 < end; i0 += kAdcChunk, chunk++) {
         const int b = chunk & 1;
         const int cnt = end - i0 < kAdcChunk ? (int)(end - i0) : kAdcChunk;
-        named_sync(kBarFull + b, kAdcThreads);
+        sync_full(b);
         const float* hs_b = c_hs + b * kAdcChunk;
         for (int w = 0; w < cnt; w += 32) {
           const int j = w + lane;
@@ -423,7 +440,7 @@ __global__ void __launch_bounds__(kAdcThreads) ivfpq_adc_kernel(AdcArgs a) {
           }
           __syncwarp();
         }
-        if (chunk + 2 < total) named_arrive(kBarEmpty + b, kAdcThreads);
+        if (chunk + 2 < total) arrive_empty(b);
       }
     }
     if (lane == 0) {

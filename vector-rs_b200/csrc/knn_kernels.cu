@@ -398,7 +398,19 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
   const float qa = METRIC == vrs_exact::kCos ? a.q_aux[qrow] : 0.0f;
   const int half = lane >> 4, hl = lane & 15;
   const int RT = R + a.n_tiny;
+  // Rows of step it + 1 -> L2 while step it is scored (16 lanes, one 128-byte
+  // line each: four rows of up to four lines; longer rows are fetched as
+  // they are read).
+  auto prefetch_step = [&](int it) {
+    const int i = 4 * it + (lane >> 2);
+    if (lane < 16 && i < RT && (lane & 3) * 32 < a.d) {
+      const uint32_t row = i < R ? buf[i].id : a.tiny[i - R];
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a.base + (int64_t)row * a.dp + (lane & 3) * 32));
+    }
+  };
+  prefetch_step(0);
   for (int it = 0; 4 * it < RT; it++) {
+    prefetch_step(it + 1);
     const int i0 = 4 * it + half, i1 = 4 * it + 2 + half;
     const bool act0 = i0 < RT, act1 = i1 < RT;
     const int ii0 = act0 ? i0 : 4 * it, ii1 = act1 ? i1 : 4 * it;
