@@ -237,97 +237,76 @@ __global__ void __launch_bounds__(THREADS, 1)
     int* hist = s_hist + ew * 256;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     float run = MODE == 0 ? INFINITY : -INFINITY;  // pivot pass: best key of the current group
-    // The warp's 64-column half of a tile is two 32-column chunks whose TMEM
-    // loads are software-pipelined (chunk 1 loads while chunk 0 is scored,
-    // the next tile's chunk 0 while chunk 1 is); the buffer is handed back
-    // once both chunks have landed. ra / rb: the two chunks' registers.
-    uint32_t ra[32], rb[32];
-    // Scores one chunk in place; returns its best key (pivot minima) and,
-    // in the candidate pass, appends rows within the bound.
-    auto score_chunk = [&](uint32_t (&r)[32], int64_t c0) -> float {
-      const float thr = MODE == 0 ? bound : MODE == 1 ? -bound * ks : -0.5f * bound * ks;
-      if (MODE == 0) {
-        const float4* xp = reinterpret_cast<const float4*>(a.xn + c0);
-#pragma unroll
-        for (int j4 = 0; j4 < 8; j4++) {
-          const float4 x4 = __ldg(xp + j4);
-          r[4 * j4 + 0] = __float_as_uint(fmaf(f2, __uint_as_float(r[4 * j4 + 0]), x4.x));
-          r[4 * j4 + 1] = __float_as_uint(fmaf(f2, __uint_as_float(r[4 * j4 + 1]), x4.y));
-          r[4 * j4 + 2] = __float_as_uint(fmaf(f2, __uint_as_float(r[4 * j4 + 2]), x4.z));
-          r[4 * j4 + 3] = __float_as_uint(fmaf(f2, __uint_as_float(r[4 * j4 + 3]), x4.w));
-        }
-      }
-      const int64_t rem = row_end - c0;
-      if (rem < 32) {
-        // Columns past the segment end (the segment's last tile only): the
-        // worst key for the pivot minima; NaN for the candidate pass, which
-        // fails every comparison (min/max ignore a NaN operand) even when
-        // the bound is infinite.
-        const uint32_t pad = TILEMIN ? __float_as_uint(MODE == 0 ? INFINITY : -INFINITY) : 0x7fffffffu;
-#pragma unroll
-        for (int j = 0; j < 32; j++)
-          if (j >= rem) r[j] = pad;
-      }
-      auto V = [&](int j) { return __uint_as_float(r[j]); };
-      float g[4];
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int o = 8 * i;
-        g[i] = MODE == 0 ? fmin3(fmin3(V(o), V(o + 1), V(o + 2)), fmin3(V(o + 3), V(o + 4), V(o + 5)),
-                                 fminf(V(o + 6), V(o + 7)))
-                         : fmax3(fmax3(V(o), V(o + 1), V(o + 2)), fmax3(V(o + 3), V(o + 4), V(o + 5)),
-                                 fmaxf(V(o + 6), V(o + 7)));
-      }
-      const float best = MODE == 0 ? fminf(fminf(g[0], g[1]), fminf(g[2], g[3]))
-                                   : fmaxf(fmaxf(g[0], g[1]), fmaxf(g[2], g[3]));
-      if (!TILEMIN && (MODE == 0 ? best <= thr : best >= thr)) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          if (MODE == 0 ? g[i] <= thr : g[i] >= thr) {
-#pragma unroll
-            for (int jj = 0; jj < 8; jj++) {
-              const float x = V(8 * i + jj);
-              const float sc = MODE == 0 ? x : MODE == 1 ? -inv_ks * x : f2 * x;
-              if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(c0 + 8 * i + jj)};
-            }
-          }
-        }
-      }
-      return best;
-    };
-    const uint32_t col = lane_base + acc * 256 + ch * HALF_COLS;
-    bool live = ntiles > 0 && __all_sync(sel::kFull, mbar_wait(&tfull[0], 0, s_abort, a.err, 5, WAIT_NS));
-    if (live) {
-      tc_fence_after();
-      tmem_ld32_issue(tmem + col, ra);
-      tmem_ld_wait32(ra);
-    }
-    for (int t = 0; live && t < ntiles; t++) {
+    for (int t = 0; t < ntiles; t++) {
       const int b = t & 1;
+      const bool ok = mbar_wait(&tfull[b], (t >> 1) & 1, s_abort, a.err, 5, WAIT_NS);
+      if (!__all_sync(sel::kFull, ok)) break;
+      tc_fence_after();
       const int64_t n0 = row_begin + (int64_t)t * BN + ch * HALF_COLS;
       if (MODE == 0 && t + 1 < ntiles && lane < 2) {
         // |x|^2 of this warp's columns of the next tile -> L1 (2 lines).
         asm volatile("prefetch.global.L1 [%0];" ::"l"(a.xn + n0 + BN + lane * 32));
       }
-      tmem_ld32_issue(tmem + col + b * BN + 32, rb);
-      const float best0 = score_chunk(ra, n0);
-      tmem_ld_wait32(rb);
-      // Both chunks of tile t are in registers: its buffer is free.
+      const int64_t rem_cols = row_end - n0;
+      const int valid_cols = rem_cols < HALF_COLS ? (int)(rem_cols > 0 ? rem_cols : 0) : HALF_COLS;
+      // Key threshold: MODE 0 passes key <= bound, MODE 1 key >= -bound ks,
+      // MODE 2 key >= -bound ks / 2 (all factors are exact powers of two).
+      const float thr = MODE == 0 ? bound : MODE == 1 ? -bound * ks : -0.5f * bound * ks;
+      // The warp's whole column half: 64 accumulators per thread, one wait.
+      float v[HALF_COLS];
+      tmem_ld64(tmem + lane_base + acc * 256 + b * BN + ch * HALF_COLS, v);
+      if (MODE == 0) {
+        const float4* xp = reinterpret_cast<const float4*>(a.xn + n0);
+#pragma unroll
+        for (int j4 = 0; j4 < HALF_COLS / 4; j4++) {
+          // Four loads in flight at a time keep the register count under
+          // the 96 that 18 warps per SM allow.
+          if (j4 % 4 == 0) asm volatile("" ::: "memory");
+          const float4 x4 = __ldg(xp + j4);
+          v[4 * j4 + 0] = fmaf(f2, v[4 * j4 + 0], x4.x);
+          v[4 * j4 + 1] = fmaf(f2, v[4 * j4 + 1], x4.y);
+          v[4 * j4 + 2] = fmaf(f2, v[4 * j4 + 2], x4.z);
+          v[4 * j4 + 3] = fmaf(f2, v[4 * j4 + 3], x4.w);
+        }
+      }
+      if (valid_cols < HALF_COLS) {
+        // Columns past the segment end (the segment's last tile only): the
+        // worst key for the pivot minima; NaN for the append path, which
+        // fails every comparison (min/max ignore a NaN operand) even when
+        // the bound is infinite.
+        const float pad = TILEMIN ? (MODE == 0 ? INFINITY : -INFINITY) : __int_as_float(0x7fffffff);
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; j++)
+          if (j >= valid_cols) v[j] = pad;
+      }
+      // Best key of each group of 8 columns, then of the half: 36 three-input
+      // min/max for 64 keys. The per-group tests run only in lanes whose
+      // half passes.
+      float g[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float* w = v + 8 * i;
+        g[i] = MODE == 0 ? fmin3(fmin3(w[0], w[1], w[2]), fmin3(w[3], w[4], w[5]), fminf(w[6], w[7]))
+                         : fmax3(fmax3(w[0], w[1], w[2]), fmax3(w[3], w[4], w[5]), fmaxf(w[6], w[7]));
+      }
+      const float best = MODE == 0 ? fmin3(fmin3(g[0], g[1], g[2]), fmin3(g[3], g[4], g[5]), fminf(g[6], g[7]))
+                                   : fmax3(fmax3(g[0], g[1], g[2]), fmax3(g[3], g[4], g[5]), fmaxf(g[6], g[7]));
+      if (!TILEMIN && (MODE == 0 ? best <= thr : best >= thr)) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (MODE == 0 ? g[i] <= thr : g[i] >= thr) {
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+              const float sc = MODE == 0 ? v[8 * i + jj] : MODE == 1 ? -inv_ks * v[8 * i + jj] : f2 * v[8 * i + jj];
+              if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + 8 * i + jj)};
+            }
+          }
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
-      const bool more = t + 1 < ntiles;
-      if (more) {
-        live = __all_sync(sel::kFull, mbar_wait(&tfull[b ^ 1], ((t + 1) >> 1) & 1, s_abort, a.err, 5, WAIT_NS));
-        if (live) {
-          tc_fence_after();
-          tmem_ld32_issue(tmem + col + (b ^ 1) * BN, ra);
-        }
-      }
-      const float best1 = score_chunk(rb, n0 + 32);
-      if (more && live) tmem_ld_wait32(ra);
       if (TILEMIN) {
-        const float best = MODE == 0 ? fminf(best0, best1) : fmaxf(best0, best1);
         run = MODE == 0 ? fminf(run, best) : fmaxf(run, best);
         if ((t + 1) % kPivotGroup == 0 || t == ntiles - 1) {
           if (vq)
@@ -532,78 +511,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     int* hist = s_hist + ew * 256;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const uint32_t tempty_lead0 = mapa_shared(&tempty[0], 0), tempty_lead1 = mapa_shared(&tempty[1], 0);
-    // Each tile's quarter is two 32-column chunks. Their TMEM loads are
-    // software-pipelined: chunk 1 of a tile loads while chunk 0 is scored,
-    // and chunk 0 of the next tile while chunk 1 is; the tile's buffer goes
-    // back to the MMA issuer as soon as both of its chunks have landed. Two
-    // fixed register arrays (ra: chunk 0, rb: chunk 1) hold the loads.
-    uint32_t ra[32], rb[32];
-    // Scores one 32-column chunk: group extrema, one threshold test, and the
-    // appends of groups that pass.
-    // Works in place on the loaded bits (no second 32-register array: the
-    // other chunk's load is in flight meanwhile).
-    auto score_chunk = [&](uint32_t (&r)[32], int64_t c0) {
+    for (int t = 0; t < ntiles; t++) {
+      const int b = t & 1;
+      const bool ok = mbar_wait(&tfull[b], (t >> 1) & 1, s_abort, a.err, 25, WAIT_NS);
+      if (!__all_sync(sel::kFull, ok)) break;
+      tc_fence_after();
+      const int64_t n0 = row_begin + (int64_t)t * P_BN + quarter * P_QUARTER;
+      if (MODE == 0 && t + 1 < ntiles && lane < 2)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(a.xn + n0 + P_BN + lane * 32));
+      const int64_t rem_cols = row_end - n0;
+      const int valid_cols = rem_cols < P_QUARTER ? (int)(rem_cols > 0 ? rem_cols : 0) : P_QUARTER;
       const float thr = MODE == 0 ? bound : MODE == 1 ? -bound * ks : -0.5f * bound * ks;
+      float v[P_QUARTER];
+      tmem_ld64(tmem + lane_base + b * P_BN + quarter * P_QUARTER, v);
       if (MODE == 0) {
-        const float4* xp = reinterpret_cast<const float4*>(a.xn + c0);
+        const float4* xp = reinterpret_cast<const float4*>(a.xn + n0);
 #pragma unroll
-        for (int j4 = 0; j4 < 8; j4++) {
+        for (int j4 = 0; j4 < P_QUARTER / 4; j4++) {
+          if (j4 % 4 == 0) asm volatile("" ::: "memory");
           const float4 x4 = __ldg(xp + j4);
-          r[4 * j4 + 0] = __float_as_uint(fmaf(f2, __uint_as_float(r[4 * j4 + 0]), x4.x));
-          r[4 * j4 + 1] = __float_as_uint(fmaf(f2, __uint_as_float(r[4 * j4 + 1]), x4.y));
-          r[4 * j4 + 2] = __float_as_uint(fmaf(f2, __uint_as_float(r[4 * j4 + 2]), x4.z));
-          r[4 * j4 + 3] = __float_as_uint(fmaf(f2, __uint_as_float(r[4 * j4 + 3]), x4.w));
+          v[4 * j4 + 0] = fmaf(f2, v[4 * j4 + 0], x4.x);
+          v[4 * j4 + 1] = fmaf(f2, v[4 * j4 + 1], x4.y);
+          v[4 * j4 + 2] = fmaf(f2, v[4 * j4 + 2], x4.z);
+          v[4 * j4 + 3] = fmaf(f2, v[4 * j4 + 3], x4.w);
         }
       }
-      const int64_t rem = row_end - c0;
-      if (rem < 32) {
+      if (valid_cols < P_QUARTER) {
         // Columns past the segment end: NaN fails every comparison.
 #pragma unroll
-        for (int j = 0; j < 32; j++)
-          if (j >= rem) r[j] = 0x7fffffffu;
+        for (int j = 0; j < P_QUARTER; j++)
+          if (j >= valid_cols) v[j] = __int_as_float(0x7fffffff);
       }
-      auto V = [&](int j) { return __uint_as_float(r[j]); };
-      float g[4];
+      float g[8];
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int o = 8 * i;
-        g[i] = MODE == 0 ? fmin3(fmin3(V(o), V(o + 1), V(o + 2)), fmin3(V(o + 3), V(o + 4), V(o + 5)),
-                                 fminf(V(o + 6), V(o + 7)))
-                         : fmax3(fmax3(V(o), V(o + 1), V(o + 2)), fmax3(V(o + 3), V(o + 4), V(o + 5)),
-                                 fmaxf(V(o + 6), V(o + 7)));
+      for (int i = 0; i < 8; i++) {
+        const float* w = v + 8 * i;
+        g[i] = MODE == 0 ? fmin3(fmin3(w[0], w[1], w[2]), fmin3(w[3], w[4], w[5]), fminf(w[6], w[7]))
+                         : fmax3(fmax3(w[0], w[1], w[2]), fmax3(w[3], w[4], w[5]), fmaxf(w[6], w[7]));
       }
-      const float best = MODE == 0 ? fminf(fminf(g[0], g[1]), fminf(g[2], g[3]))
-                                   : fmaxf(fmaxf(g[0], g[1]), fmaxf(g[2], g[3]));
+      const float best = MODE == 0 ? fmin3(fmin3(g[0], g[1], g[2]), fmin3(g[3], g[4], g[5]), fminf(g[6], g[7]))
+                                   : fmax3(fmax3(g[0], g[1], g[2]), fmax3(g[3], g[4], g[5]), fmaxf(g[6], g[7]));
       if (MODE == 0 ? best <= thr : best >= thr) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
+        for (int i = 0; i < 8; i++) {
           if (MODE == 0 ? g[i] <= thr : g[i] >= thr) {
 #pragma unroll
             for (int jj = 0; jj < 8; jj++) {
-              const float x = V(8 * i + jj);
-              const float sc = MODE == 0 ? x : MODE == 1 ? -inv_ks * x : f2 * x;
-              if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(c0 + 8 * i + jj)};
+              const float sc = MODE == 0 ? v[8 * i + jj] : MODE == 1 ? -inv_ks * v[8 * i + jj] : f2 * v[8 * i + jj];
+              if (sc <= bound) list[count++] = Cand{sc, (uint32_t)(n0 + 8 * i + jj)};
             }
           }
         }
       }
-    };
-    const uint32_t col = lane_base + quarter * P_QUARTER;
-    bool live = ntiles > 0 && __all_sync(sel::kFull, mbar_wait(&tfull[0], 0, s_abort, a.err, 25, WAIT_NS));
-    if (live) {
-      tc_fence_after();
-      tmem_ld32_issue(tmem + col, ra);
-      tmem_ld_wait32(ra);
-    }
-    for (int t = 0; live && t < ntiles; t++) {
-      const int b = t & 1;
-      const int64_t n0 = row_begin + (int64_t)t * P_BN + quarter * P_QUARTER;
-      if (MODE == 0 && t + 1 < ntiles && lane < 2)
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(a.xn + n0 + P_BN + lane * 32));
-      tmem_ld32_issue(tmem + col + b * P_BN + 32, rb);
-      score_chunk(ra, n0);
-      tmem_ld_wait32(rb);
-      // Both chunks of tile t are in registers: its buffer is free.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -612,16 +571,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         else
           mbar_arrive_cluster(b ? tempty_lead1 : tempty_lead0);
       }
-      const bool more = t + 1 < ntiles;
-      if (more) {
-        live = __all_sync(sel::kFull, mbar_wait(&tfull[b ^ 1], ((t + 1) >> 1) & 1, s_abort, a.err, 25, WAIT_NS));
-        if (live) {
-          tc_fence_after();
-          tmem_ld32_issue(tmem + col + (b ^ 1) * P_BN, ra);
-        }
-      }
-      score_chunk(rb, n0 + 32);
-      if (more && live) tmem_ld_wait32(ra);
       // Shrink lists that could overflow on the next tile.
       unsigned need = __ballot_sync(sel::kFull, vq && count > a.cap - P_QUARTER);
       while (need) {
