@@ -78,11 +78,12 @@ KM_WORKLOADS = {
 METRIC_NAMES = {L2: "squared-L2", DOT: "dot", COS: "cosine", L1: "Manhattan", CHEB: "Chebyshev",
                 HELL: "Hellinger"}
 TC_METRICS = (L2, DOT, COS, 7)
-# DRAM bytes (read + write) of one main-scan launch over the full C2 base,
-# from the ncu capture summarised in profiles/knn_scan_tc_C2.txt; other base
-# sizes scale it by the rows scanned (the traffic is the base re-stream plus
-# the candidate lists, both proportional to the rows).
-SCAN_DRAM_BYTES_C2 = 318.847488e6 + 29.940224e6
+# DRAM bytes (read + write) of one candidate-scan launch (the pair kernel)
+# over the full C2 base, from the ncu capture summarised in
+# profiles/knn_scan_tc2_C2.txt; other base sizes scale it by the rows scanned
+# (the traffic is the base re-stream plus the candidate lists, both
+# proportional to the rows).
+SCAN_DRAM_BYTES_C2 = 381.478912e6 + 35.181312e6
 
 
 def parse():
