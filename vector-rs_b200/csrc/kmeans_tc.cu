@@ -37,22 +37,29 @@ using namespace vrs::tc;
 
 // ABUF point-tile buffers: the next point tile's operands load while the
 // current one's MMAs run (one buffer left the tensor pipe idle through every
-// reload, K / BN tiles apart). The centroid tiles come from L2, so a
-// 2-stage ring keeps them ahead.
-constexpr int BM = 128, NACC = 2, BN = 128, KBW = 64, MAX_KBLK = 2, STAGES = 2, ABUF = 2;
+// reload, K / BN tiles apart). The centroid tiles come from L2 through a
+// ring of SLOTS slots of one 64-column k-block each: a slot frees as soon as
+// the MMAs of its k-block complete, so each load is issued SLOTS - 1
+// k-blocks of MMA time before it is needed (a ring of whole tiles gave a
+// load one tile's MMA time, less than an L2 round trip).
+#ifndef KM_SLOTS
+#define KM_SLOTS 4
+#endif
+constexpr int BM = 128, NACC = 2, BN = 128, KBW = 64, MAX_KBLK = 2, SLOTS = KM_SLOTS, ABUF = 2;
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + EPI_WARPS * 32;
 constexpr int HALF_COLS = BN / 2;
 constexpr int NCAND = 8;
 constexpr uint32_t BLK = BM * 128;
 constexpr size_t SMEM_A = (size_t)ABUF * NACC * MAX_KBLK * BLK;
-constexpr size_t SMEM_B = (size_t)STAGES * MAX_KBLK * BLK;
+constexpr size_t SMEM_B = (size_t)SLOTS * BLK;
 constexpr size_t SMEM_CAND = (size_t)EPI_WARPS * 32 * NCAND * sizeof(Cand);
 constexpr size_t SMEM_CN = 2 * BN * sizeof(float);  // |c|^2 of the tile in each TMEM buffer
 constexpr size_t SMEM_BAR = 256;
 constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_CAND + SMEM_CN + SMEM_BAR;
 static_assert(SMEM_TOTAL <= 232448, "dynamic shared memory above the 227 KB per-block limit");
-static_assert((2 * STAGES + 4 + 2 * ABUF) * 8 + 8 <= SMEM_BAR, "barrier region too small");
+static_assert((2 * SLOTS + 5 + 2 * ABUF) * 8 + 8 <= SMEM_BAR, "barrier region too small");
+static_assert(SLOTS >= 2, "the ring needs two slots");
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -83,16 +90,17 @@ struct AssignArgs {
 // 2^-10 + 2^-22 (relative) of the exact one; elements below fp16's normal
 // range add at most 2^-25 each in scaled units, i.e. 2^-25 sqrt(d) |other| / s
 // per side after unscaling; plus the f32 accumulation of d16 + 2 terms
-// (4 ulps each, allowing truncation).
-__device__ __forceinline__ float point_margin(int metric, int d, float Q, float X, float inv_s) {
+// (4 ulps each, allowing truncation). rd = sqrt((double)d), computed once
+// by the caller (correctly rounded, so every kernel gets the same margin).
+__device__ __forceinline__ float point_margin(int metric, int d, double rd, float Q, float X, float inv_s) {
   const double u = 0x1p-24;
   const int d16 = (d + 15) / 16 * 16;
   const double c_tc = 0x1p-10 + 0x1p-22 + (double)(d16 + 2) * 0x1p-22;
-  const double sub = 0x1p-25 * sqrt((double)d) * ((double)Q + X) * (double)inv_s;
+  const double sub = 0x1p-25 * rd * ((double)Q + X) * (double)inv_s;
   const double g = (double)(d + 4) * u * 1.01;
   double e;
   if (metric == vrs_exact::kCos) {  // unit vectors, s = 1
-    e = c_tc + 0x1p-25 * sqrt((double)d) * 2.0 + 8.0 * u + 4.0 * g;
+    e = c_tc + 0x1p-25 * rd * 2.0 + 8.0 * u + 4.0 * g;
   } else if (metric == vrs_exact::kDot) {
     e = (c_tc + 2.0 * g) * (double)Q * (double)X + sub;
   } else {
@@ -115,12 +123,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   float* s_cn = (float*)((uint8_t*)s_cand + SMEM_CAND);  // [2][BN]
   uint64_t* bars = (uint64_t*)((uint8_t*)s_cn + SMEM_CN);
   uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* empty = bars + SLOTS;
+  uint64_t* tfull = bars + 2 * SLOTS;
   uint64_t* tempty = tfull + 2;
   uint64_t* afull = tempty + 2;   // [ABUF]
   uint64_t* aempty = afull + ABUF;  // [ABUF]
-  uint32_t* s_tmem = (uint32_t*)(aempty + ABUF);
+  uint64_t* drain = aempty + ABUF;  // abort path: all issued MMAs complete
+  uint32_t* s_tmem = (uint32_t*)(drain + 1);
   volatile int* s_abort = (volatile int*)(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -128,7 +137,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int kt = (a.k + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) {
+    for (int s = 0; s < SLOTS; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -140,6 +149,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&afull[b], 1);
       mbar_init(&aempty[b], 1);
     }
+    mbar_init(drain, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -168,26 +178,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                         pt * BM * NACC + acc * BM, &afull[ab]);
         return true;
       };
-      uint32_t g = 0;
+      uint32_t q = 0;  // k-blocks queued so far: slot q % SLOTS, use q / SLOTS
       int lp = 0;
       bool ok = blockIdx.x >= nptiles || load_a(blockIdx.x, 0);
       for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x, lp++) {
-        for (int j = 0; j < kt; j++, g++) {
-          const int s = g % STAGES;
-          if (!mbar_wait(&empty[s], ((g / STAGES) & 1) ^ 1, s_abort, a.err, 12, WAIT_NS)) {
-            ok = false;
-            break;
+        for (int j = 0; ok && j < kt; j++) {
+          for (int kb = 0; kb < a.kblk; kb++, q++) {
+            const int s = (int)(q % SLOTS);
+            if (!mbar_wait(&empty[s], ((q / SLOTS) & 1) ^ 1, s_abort, a.err, 12, WAIT_NS)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&full[s], BLK);
+            tma_load_2d(sB + s * BLK, &tmB, kb * KBW, j * BN, &full[s]);
           }
-          mbar_expect_tx(&full[s], (uint32_t)a.kblk * BLK);
-          for (int kb = 0; kb < a.kblk; kb++)
-            tma_load_2d(sB + (s * MAX_KBLK + kb) * BLK, &tmB, kb * KBW, j * BN, &full[s]);
           // The next point tile's operands, as soon as this tile's first
           // centroid tile is queued (its buffer frees when the MMAs of the
           // tile before this one complete).
-          if (j == 0 && pt + (int)gridDim.x < nptiles && !load_a(pt + gridDim.x, lp + 1)) {
-            ok = false;
-            break;
-          }
+          if (ok && j == 0 && pt + (int)gridDim.x < nptiles && !load_a(pt + gridDim.x, lp + 1)) ok = false;
         }
       }
     }
@@ -197,13 +205,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t idesc = idesc_f16(BM, BN);
       // Descriptors differ only in the masked start-address field: the A
       // ones are formed per point tile (for its buffer), the B ones per
-      // centroid tile, both before the waits.
+      // slot.
       const DescSw128 a_desc(sA), b_desc(sB);
-      const int ksteps = a.ksteps;
-      uint32_t g = 0;
+      const int ksteps = a.ksteps, kblk = a.kblk;
+      uint32_t g = 0;  // centroid tiles issued: TMEM buffer g & 1
+      uint32_t q = 0;  // k-blocks consumed: slot q % SLOTS
       int lp = 0;
-      bool ok = true;
-      int64_t last = -1;
+      bool ok = true, issued = false;
       for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x, lp++) {
         const int ab = lp % ABUF, u = lp / ABUF;
         uint64_t ad[NACC][MAX_KBLK * 4];
@@ -216,13 +224,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(&afull[ab], u & 1, s_abort, a.err, 13, WAIT_NS)) break;
         tc_fence_after();
         for (int j = 0; j < kt; j++, g++) {
-          const int s = g % STAGES, b = g & 1;
-          uint64_t bd[MAX_KBLK * 4];
-#pragma unroll
-          for (int ks = 0; ks < MAX_KBLK * 4; ks++)
-            bd[ks] = b_desc.at((uint32_t)(s * MAX_KBLK * BLK + (ks >> 2) * BLK + (ks & 3) * 32) >> 4);
-          if (!mbar_wait(&full[s], (g / STAGES) & 1, s_abort, a.err, 14, WAIT_NS) ||
-              !mbar_wait(&tempty[b], ((g >> 1) & 1) ^ 1, s_abort, a.err, 15, WAIT_NS)) {
+          const int b = g & 1;
+          if (!mbar_wait(&tempty[b], ((g >> 1) & 1) ^ 1, s_abort, a.err, 15, WAIT_NS)) {
             ok = false;
             break;
           }
@@ -232,23 +235,39 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_expect_tx_only(&tfull[b], BN * sizeof(float));
             bulk_copy_g2s(s_cn + b * BN, a.cn + (int64_t)j * BN, BN * sizeof(float), &tfull[b]);
           }
-          tc_fence_after();
 #pragma unroll
-          for (int acc = 0; acc < NACC; acc++) {
-            const uint32_t d = tmem + acc * 256 + b * BN;
+          for (int kb = 0; kb < MAX_KBLK; kb++) {
+            if (kb >= kblk) break;
+            const int s = (int)(q % SLOTS);
+            if (!mbar_wait(&full[s], (q / SLOTS) & 1, s_abort, a.err, 14, WAIT_NS)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
-            for (int ks = 0; ks < MAX_KBLK * 4; ks++)
-              if (ks < ksteps) mma_f16(d, ad[acc][ks], bd[ks], idesc, ks > 0 ? 1u : 0u);
+            for (int acc = 0; acc < NACC; acc++) {
+              const uint32_t d = tmem + acc * 256 + b * BN;
+#pragma unroll
+              for (int ks = 0; ks < 4; ks++)
+                if (kb * 4 + ks < ksteps)
+                  mma_f16(d, ad[acc][kb * 4 + ks], b_desc.at((uint32_t)(s * BLK + ks * 32) >> 4), idesc,
+                          kb * 4 + ks > 0 ? 1u : 0u);
+            }
+            issued = true;
+            mma_commit(&empty[s]);
+            q++;
           }
-          mma_commit(&empty[s]);
+          if (!ok) break;
           mma_commit(&tfull[b]);
-          last = g;
         }
         if (ok) mma_commit(&aempty[ab]);
       }
-      if (*s_abort && last >= 0) {
+      if (*s_abort && issued) {
+        // A tile may have stopped between k-blocks: wait (bounded) for every
+        // MMA issued so far before the TMEM is released.
         volatile int dummy = 0;
-        mbar_wait(&tfull[last & 1], (uint32_t)((last >> 1) & 1), &dummy, a.err, 0, WAIT_NS / 4);
+        mma_commit(drain);
+        mbar_wait(drain, 0, &dummy, a.err, 0, WAIT_NS / 4);
       }
     }
   } else {
@@ -260,19 +279,33 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     Cand* buf = s_cand + (ew * 32 + lane) * NCAND;
     const float X = __uint_as_float(*a.cmax);
+    const double rd = sqrt((double)a.d);
+    // The point's |x| and starting bound for the next point tile are loaded
+    // one tile ahead, off the path between the MMAs and this warp.
+    const int64_t poff = acc * BM + quad * 32 + lane;
+    auto load_point = [&](int pt, float* xq, float* ib) {
+      const int64_t p = (int64_t)pt * BM * NACC + poff;
+      const bool in = pt < nptiles && p < a.n;
+      *xq = in ? a.xq[p] : 0.0f;
+      *ib = in && a.init_bound ? a.init_bound[p] : INFINITY;
+    };
+    float nxq, nib;
+    load_point(blockIdx.x, &nxq, &nib);
     uint32_t g = 0;
     bool ok = true;
     for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x) {
-      const int64_t p = (int64_t)pt * BM * NACC + acc * BM + quad * 32 + lane;
+      const int64_t p = (int64_t)pt * BM * NACC + poff;
       const bool vp = p < a.n;
-      const float absm = vp ? point_margin(a.metric, a.d, a.xq[p], X, a.inv_scale) : 0.0f;
+      const float pxq = nxq, pib = nib;
+      load_point(pt + gridDim.x, &nxq, &nib);
+      const float absm = vp ? point_margin(a.metric, a.d, rd, pxq, X, a.inv_scale) : 0.0f;
       const float f2 = -2.0f * a.acc_scale, f1 = -a.acc_scale;
       float best = INFINITY;
       // Padding points keep nothing; with a starting bound s (>= the exact
       // score of some centroid), best approx <= s + e and e < absm / 2, so
       // s + 1.5 absm >= best approx + absm keeps every candidate the
       // unbounded sweep would keep at the end.
-      float bound = !vp ? -INFINITY : a.init_bound ? __fadd_ru(a.init_bound[p], 1.5f * absm) : INFINITY;
+      float bound = !vp ? -INFINITY : a.init_bound ? __fadd_ru(pib, 1.5f * absm) : INFINITY;
       float lost = INFINITY;  // smallest score pushed out of a full buffer
       int cnt = 0;
       // Keeps the NCAND best candidates; remembers the best score dropped.
@@ -322,6 +355,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 32; i++) v[i] = f1 * v[i];
           }
+          if (c == HALF_COLS / 32 - 1) {
+            // The tile's last columns are in registers and its |c|^2 read:
+            // hand the TMEM buffer (and its |c|^2 slot) back to the MMA
+            // issuer before the selection work.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+          }
           if (cb < 32) {
 #pragma unroll
             for (int i = 0; i < 32; i++)
@@ -331,23 +372,21 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 8; i++) gm[i] = fmin3(v[4 * i], v[4 * i + 1], fminf(v[4 * i + 2], v[4 * i + 3]));
           const float cmn = fmin3(fmin3(gm[0], gm[1], gm[2]), fmin3(gm[3], gm[4], gm[5]), fminf(gm[6], gm[7]));
-          // A better chunk minimum tightens the bound; drop candidates that
-          // fall outside it.
-          if (vp && cmn < best && cmn <= bound) {
-            best = cmn;
-            bound = fminf(bound, __fadd_ru(best, absm));
-            int k2 = 0;
-            for (int e = 0; e < cnt; e++) {
-              const Cand ce = buf[e];
-              if (ce.hs <= bound) buf[k2++] = ce;
+          // Padding points have bound -inf and never hit. Most chunks hold
+          // no candidate of any of the warp's points: one vote skips them.
+          const bool hit = cmn <= bound;
+          if (__any_sync(sel::kFull, hit) && hit) {
+            // A better chunk minimum tightens the bound. Entries already
+            // kept stay; those now outside the bound are ignored by the
+            // triage and are the first to go when the buffer is full.
+            if (cmn < best) {
+              best = cmn;
+              bound = fminf(bound, __fadd_ru(best, absm));
             }
-            cnt = k2;
-          }
-          unsigned m = 0;
+            unsigned m = 0;
 #pragma unroll
-          for (int i = 0; i < 8; i++) m |= gm[i] <= bound ? (1u << i) : 0u;
-          // One vote per chunk; static register indices for the groups.
-          if (__any_sync(sel::kFull, m != 0)) {
+            for (int i = 0; i < 8; i++) m |= gm[i] <= bound ? (1u << i) : 0u;
+            // Static register indices: each group, then each of its four.
 #pragma unroll
             for (int i = 0; i < 8; i++) {
               if ((m >> i) & 1u) {
@@ -358,15 +397,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                   w0 = w1;
                   w1 = w2;
                   w2 = w3;
-                  if (4 * i + jj < cb && sc <= bound) insert(sc, (uint32_t)(c0 + c * 32 + 4 * i + jj));
+                  if (sc <= bound && 4 * i + jj < cb) insert(sc, (uint32_t)(c0 + c * 32 + 4 * i + jj));
                 }
               }
             }
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[b]);
       }
       if (!ok) break;
       if (vp) {
@@ -400,48 +436,67 @@ __global__ void __launch_bounds__(THREADS, 1)
 //    exact distance (kmeans_dist_kernel fills distances in after the loop);
 //  * several -> list M (flags[1] = count, indices from flags + 2 + n):
 //    scored exactly by kmeans_multi_kernel.
+// Appends `value` to list[] for every lane with `take` set: one atomic per
+// warp on the list's counter (every lane of the warp must call together).
+__device__ __forceinline__ void warp_append(int* counter, int* list, bool take, int value) {
+  const unsigned m = __ballot_sync(0xffffffffu, take);
+  if (!m) return;
+  const int lane = threadIdx.x & 31, leader = __ffs(m) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(counter, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (take) list[base + __popc(m & ((1u << lane) - 1u))] = value;
+}
+
 template <int METRIC>
 __global__ void __launch_bounds__(256) kmeans_triage_kernel(
     int64_t n, int d, const float* __restrict__ xq, const unsigned int* __restrict__ cmax,
     const Res* __restrict__ res, const Cand* __restrict__ cands, const int* __restrict__ force_full,
     int32_t* __restrict__ assign, int* __restrict__ flags, float inv_scale, float* __restrict__ pscore) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
-  const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax), inv_scale);
-  const float bound = __fadd_ru(fminf(r0.best, r1.best), absm);
-  if (r0.lost <= bound || r1.lost <= bound || (force_full && force_full[i])) {
-    flags[2 + atomicAdd(&flags[0], 1)] = (int)i;
-    if (pscore) pscore[i] = INFINITY;  // full exact scan: no approximate score kept
-    return;
-  }
-  int nin = 0;
-  uint32_t only = 0;
-  float only_hs = 0.0f;
-  for (int h = 0; h < 2; h++) {
-    const Res r = h ? r1 : r0;
-    for (int e = 0; e < r.cnt; e++) {
-      const Cand ce = cands[(i * 2 + h) * NCAND + e];
-      if (ce.hs <= bound) {
-        nin++;
-        only = ce.id;
-        only_hs = ce.hs;
+  int cls = 0;  // 0: assigned here (or past the end), 1: list F, 2: list M
+  if (i < n) {
+    const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
+    const float absm = point_margin(METRIC, d, sqrt((double)d), xq[i], __uint_as_float(*cmax), inv_scale);
+    const float bound = __fadd_ru(fminf(r0.best, r1.best), absm);
+    if (r0.lost <= bound || r1.lost <= bound || (force_full && force_full[i])) {
+      cls = 1;
+      if (pscore) pscore[i] = INFINITY;  // full exact scan: no approximate score kept
+    } else {
+      int nin = 0;
+      uint32_t only = 0;
+      float only_hs = 0.0f;
+      for (int h = 0; h < 2; h++) {
+        const Res r = h ? r1 : r0;
+        for (int e = 0; e < r.cnt; e++) {
+          const Cand ce = cands[(i * 2 + h) * NCAND + e];
+          if (ce.hs <= bound) {
+            nin++;
+            only = ce.id;
+            only_hs = ce.hs;
+          }
+        }
+      }
+      if (nin == 1) {
+        assign[i] = (int)only;
+        // exact score of the assigned centroid <= approx + e, e < absm / 2
+        if (pscore) pscore[i] = __fadd_ru(only_hs, 0.5f * absm);
+      } else {
+        cls = 2;
       }
     }
   }
-  if (nin == 1) {
-    assign[i] = (int)only;
-    // exact score of the assigned centroid <= approx + e, e < absm / 2
-    if (pscore) pscore[i] = __fadd_ru(only_hs, 0.5f * absm);
-  } else {
-    flags[2 + n + atomicAdd(&flags[1], 1)] = (int)i;
-  }
+  // The lists' order is immaterial: every listed point is scored on its own.
+  warp_append(&flags[0], flags + 2, cls == 1, (int)i);
+  warp_append(&flags[1], flags + 2 + n, cls == 2, (int)i);
 }
 
 // Finalize, step 2: the points of list M, one half-warp per point (its 16
-// lanes are the reference's 16 SIMD lanes), striding over the list: exact
-// argmin among the candidates within the bound (lowest index on ties), with
-// the exact distance.
+// lanes are the reference's 16 SIMD lanes), striding over the list. Lane l
+// loads candidate l & 7 of column half l >> 3, so all of a point's
+// candidates are read at once; those within the bound are then scored two
+// at a time (rank_key2: both rows' loads in flight) for the exact argmin,
+// lowest index on ties, with the exact distance.
 template <int METRIC>
 __global__ void __launch_bounds__(128) kmeans_multi_kernel(
     const float* __restrict__ x, int64_t n, int d, int dp, const float* __restrict__ cent,
@@ -449,8 +504,10 @@ __global__ void __launch_bounds__(128) kmeans_multi_kernel(
     const unsigned int* __restrict__ cmax, const Res* __restrict__ res, const Cand* __restrict__ cands,
     const int* __restrict__ flags, int32_t* __restrict__ assign, float* __restrict__ dist, float inv_scale,
     float* __restrict__ pscore) {
+  static_assert(2 * NCAND == 16, "one candidate slot per lane of a half-warp");
   const int hl = threadIdx.x & 15;
-  const unsigned mask = 0xffffu << (threadIdx.x & 16);
+  const int hsh = threadIdx.x & 16;
+  const unsigned mask = 0xffffu << hsh;
   const bool hib = vrs_exact::higher_is_better(METRIC);
   const int count = flags[1];
   const int* list = flags + 2 + n;
@@ -460,26 +517,40 @@ __global__ void __launch_bounds__(128) kmeans_multi_kernel(
     const float* v = x + i * dp;
     const float va = METRIC == vrs_exact::kCos ? x_aux[i] : 0.0f;
     const Res r0 = res[i * 2], r1 = res[i * 2 + 1];
-    const float absm = point_margin(METRIC, d, xq[i], __uint_as_float(*cmax), inv_scale);
+    const float absm = point_margin(METRIC, d, sqrt((double)d), xq[i], __uint_as_float(*cmax), inv_scale);
     const float bound = __fadd_ru(fminf(r0.best, r1.best), absm);
+    const int h = hl >> 3, e = hl & 7;
+    Cand ce{INFINITY, 0u};
+    if (e < (h ? r1.cnt : r0.cnt)) ce = cands[(i * 2 + h) * NCAND + e];
+    unsigned in = (__ballot_sync(mask, ce.hs <= bound) >> hsh) & 0xffffu;
     int best = 0x7fffffff;
     float best_key = hib ? -INFINITY : INFINITY;
     float best_hs = INFINITY;  // approximate score of the winner
-    for (int h = 0; h < 2; h++) {
-      const Res r = h ? r1 : r0;
-      for (int e = 0; e < r.cnt; e++) {
-        const Cand ce = cands[(i * 2 + h) * NCAND + e];
-        if (!(ce.hs <= bound)) continue;
-        const uint32_t c = ce.id;
-        const float ca = METRIC == vrs_exact::kCos ? cent_aux[c] : 0.0f;
-        const float key = vrs_exact::lanes::rank_key(METRIC, v, cent + (int64_t)c * dp, d, va, ca, hl, mask);
-        const bool better = hib ? (key > best_key || (key == best_key && (int)c < best))
-                                : (key < best_key || (key == best_key && (int)c < best));
-        if (better) {
-          best_key = key;
-          best = (int)c;
-          best_hs = ce.hs;
-        }
+    while (in) {
+      const int l0 = __ffs(in) - 1;
+      in &= in - 1;
+      const int l1 = in ? __ffs(in) - 1 : l0;
+      if (in) in &= in - 1;
+      const uint32_t c0 = __shfl_sync(mask, ce.id, l0, 16), c1 = __shfl_sync(mask, ce.id, l1, 16);
+      const float h0 = __shfl_sync(mask, ce.hs, l0, 16), h1 = __shfl_sync(mask, ce.hs, l1, 16);
+      const float ca0 = METRIC == vrs_exact::kCos ? cent_aux[c0] : 0.0f;
+      const float ca1 = METRIC == vrs_exact::kCos ? cent_aux[c1] : 0.0f;
+      float k0, k1;
+      vrs_exact::lanes::rank_key2(METRIC, v, cent + (int64_t)c0 * dp, cent + (int64_t)c1 * dp, d, va, ca0, ca1, hl,
+                                  mask, &k0, &k1);
+      const bool b0 = hib ? (k0 > best_key || (k0 == best_key && (int)c0 < best))
+                          : (k0 < best_key || (k0 == best_key && (int)c0 < best));
+      if (b0) {
+        best_key = k0;
+        best = (int)c0;
+        best_hs = h0;
+      }
+      const bool b1 = hib ? (k1 > best_key || (k1 == best_key && (int)c1 < best))
+                          : (k1 < best_key || (k1 == best_key && (int)c1 < best));
+      if (b1) {
+        best_key = k1;
+        best = (int)c1;
+        best_hs = h1;
       }
     }
     if (hl == 0) {
@@ -650,7 +721,7 @@ int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, co
   kmeans_triage_kernel<M><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, d, xq, cmax, res, cands, force_full,
                                                                         assign, flags, inv_scale, pscore);
   VRS_CUDA(cudaGetLastError());
-  kmeans_multi_kernel<M><<<(unsigned)(num_sms * 8), 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, xq, cmax,
+  kmeans_multi_kernel<M><<<(unsigned)(num_sms * 16), 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, xq, cmax,
                                                                  res, cands, flags, assign, dist, inv_scale,
                                                                  pscore);
   VRS_CUDA(cudaGetLastError());
