@@ -255,6 +255,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       // The warp's whole column half: 64 accumulators per thread, one wait.
       float v[HALF_COLS];
       tmem_ld64(tmem + lane_base + acc * 256 + b * BN + ch * HALF_COLS, v);
+      // The tile's columns are in registers: hand the TMEM buffer back to
+      // the MMA issuer now, so the selection below overlaps the next MMAs.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
       if (MODE == 0) {
         const float4* xp = reinterpret_cast<const float4*>(a.xn + n0);
 #pragma unroll
@@ -303,9 +308,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
       if (TILEMIN) {
         run = MODE == 0 ? fminf(run, best) : fmaxf(run, best);
         if ((t + 1) % kPivotGroup == 0 || t == ntiles - 1) {
@@ -524,6 +526,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const float thr = MODE == 0 ? bound : MODE == 1 ? -bound * ks : -0.5f * bound * ks;
       float v[P_QUARTER];
       tmem_ld64(tmem + lane_base + b * P_BN + quarter * P_QUARTER, v);
+      // The tile's columns are in registers: hand the TMEM buffer back to
+      // the MMA issuer now, so the selection below overlaps the next MMAs.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (lead)
+          mbar_arrive(&tempty[b]);
+        else
+          mbar_arrive_cluster(b ? tempty_lead1 : tempty_lead0);
+      }
       if (MODE == 0) {
         const float4* xp = reinterpret_cast<const float4*>(a.xn + n0);
 #pragma unroll
@@ -562,14 +574,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             }
           }
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (lead)
-          mbar_arrive(&tempty[b]);
-        else
-          mbar_arrive_cluster(b ? tempty_lead1 : tempty_lead0);
       }
       // Shrink lists that could overflow on the next tile.
       unsigned need = __ballot_sync(sel::kFull, vq && count > a.cap - P_QUARTER);
