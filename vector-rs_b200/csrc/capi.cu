@@ -1504,7 +1504,7 @@ int km_prepare_shard(const KmParams& P, KmShard* s, const float* rows, int mem) 
     VRS_TRY(s->cmax.reserve(2 * sizeof(unsigned int)));
     VRS_TRY(s->ctiny.reserve(sizeof(int)));
     VRS_TRY(s->res.reserve(nx * 2 * sizeof(kmtc::Res)));
-    VRS_TRY(s->cands.reserve(nx * 2 * 8 * sizeof(Cand)));
+    VRS_TRY(s->cands.reserve(kmtc::group_bytes(nx)));
     VRS_TRY(s->flags.reserve((2 * nx + 2) * sizeof(int)));
     VRS_TRY(s->err.reserve(sizeof(int)));
     if (P.metric == vrs_exact::kL2 || P.metric == vrs_exact::kMaha) {
@@ -1627,14 +1627,14 @@ int km_run(const KmParams& P, std::vector<KmShard*>& shards, const float* init_h
                                       s->xq.as<float>(), s->shift.as<float>(), s->ibound.as<float>(), s->stream));
           VRS_TRY(kmtc::assign(s->xb.p, s->n_local, s->cb.p, P.k, P.d, s->cn.as<float>(), s->xq.as<float>(),
                                s->cmax.as<unsigned int>(), P.metric, op_scale, s->res.as<kmtc::Res>(),
-                               s->cands.as<Cand>(), s->err.as<int>(), s->num_sms,
+                               s->cands.p, s->err.as<int>(), s->num_sms,
                                start ? s->ibound.as<float>() : nullptr, s->stream));
           prof_end(t, s->stream);
           ProfToken t2 = prof_begin("kmeans_finalize", s->stream);
           VRS_TRY(kmtc::finalize(s->x.as<float>(), s->n_local, P.d, P.dp, s->cent.as<float>(),
                                  s->cent_aux.as<float>(), s->x_aux.as<float>(), P.k, s->xq.as<float>(),
                                  s->cmax.as<unsigned int>(), P.metric, s->res.as<kmtc::Res>(),
-                                 s->cands.as<Cand>(),
+                                 s->cands.p,
                                  P.metric == vrs_exact::kCos ? s->xtiny.as<int>() : nullptr,
                                  s->assign.as<int32_t>(), s->dist.as<float>(), s->flags.as<int>(), s->num_sms,
                                  op_scale, l2 ? s->pscore.as<float>() : nullptr, s->stream));

@@ -6,10 +6,11 @@
 // as 128-row fp16 tiles; one thread issues tcgen05.mma (kind::f16) into two
 // 128x128 f32 TMEM accumulators (double-buffered). Sixteen epilogue warps
 // (one thread = one point, two warps per point splitting each tile's
-// columns) keep the approximate best centroid and every centroid whose
-// approximate score is within the point's error margin of it (the NCAND = 8
-// best such per column half, plus the smallest score that did not fit, so a
-// point whose dropped candidate is still in bound is flagged for an exact
+// columns) keep the approximate best score and every group of four
+// centroids whose smallest approximate score is within the point's bound
+// (up to kGroupSlots groups per column half, stored straight to global
+// memory, plus the smallest group minimum that did not fit, so a point
+// whose dropped group may hold its nearest centroid is flagged for an exact
 // scan). kmeans_finalize then picks the exact argmin among those
 // candidates in the reference's f32 arithmetic (find_nearest,
 // crates/vector-cuda/src/kmeans.rs:361-407: strict comparison, lowest index
@@ -43,20 +44,19 @@ using namespace vrs::tc;
 // k-blocks of MMA time before it is needed (a ring of whole tiles gave a
 // load one tile's MMA time, less than an L2 round trip).
 #ifndef KM_SLOTS
-#define KM_SLOTS 4
+#define KM_SLOTS 6
 #endif
 constexpr int BM = 128, NACC = 2, BN = 128, KBW = 64, MAX_KBLK = 2, SLOTS = KM_SLOTS, ABUF = 2;
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + EPI_WARPS * 32;
 constexpr int HALF_COLS = BN / 2;
-constexpr int NCAND = 8;
+constexpr int NG = kGroupSlots;
 constexpr uint32_t BLK = BM * 128;
 constexpr size_t SMEM_A = (size_t)ABUF * NACC * MAX_KBLK * BLK;
 constexpr size_t SMEM_B = (size_t)SLOTS * BLK;
-constexpr size_t SMEM_CAND = (size_t)EPI_WARPS * 32 * NCAND * sizeof(Cand);
 constexpr size_t SMEM_CN = 2 * BN * sizeof(float);  // |c|^2 of the tile in each TMEM buffer
 constexpr size_t SMEM_BAR = 256;
-constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_CAND + SMEM_CN + SMEM_BAR;
+constexpr size_t SMEM_TOTAL = 1024 + SMEM_A + SMEM_B + SMEM_CN + SMEM_BAR;
 static_assert(SMEM_TOTAL <= 232448, "dynamic shared memory above the 227 KB per-block limit");
 static_assert((2 * SLOTS + 5 + 2 * ABUF) * 8 + 8 <= SMEM_BAR, "barrier region too small");
 static_assert(SLOTS >= 2, "the ring needs two slots");
@@ -76,7 +76,7 @@ struct AssignArgs {
   float acc_scale;          // 1 / (operand scale)^2: unscales the accumulator
   float inv_scale;          // 1 / operand scale (margins)
   Res* res;                 // [n][2] per (point, column half)
-  Cand* cands;              // [n][2][NCAND]
+  Groups groups;            // candidate groups, [n][2][NG] slots
   int* err;
   // Upper bound on each point's best approximate score (MODE 0, from the
   // previous Lloyd step; null: none): candidates start within it.
@@ -119,8 +119,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + SMEM_A;
-  Cand* s_cand = (Cand*)(sB + SMEM_B);
-  float* s_cn = (float*)((uint8_t*)s_cand + SMEM_CAND);  // [2][BN]
+  float* s_cn = (float*)(sB + SMEM_B);  // [2][BN]
   uint64_t* bars = (uint64_t*)((uint8_t*)s_cn + SMEM_CN);
   uint64_t* full = bars;
   uint64_t* empty = bars + SLOTS;
@@ -182,6 +181,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       int lp = 0;
       bool ok = blockIdx.x >= nptiles || load_a(blockIdx.x, 0);
       for (int pt = blockIdx.x; ok && pt < nptiles; pt += gridDim.x, lp++) {
+        // The next point tile's operands go into the buffer of the tile
+        // before this one, free once that tile's MMAs complete: issued as
+        // soon as a non-blocking test sees it free, so the centroid tiles
+        // keep flowing meanwhile (waiting for it held the ring one tile
+        // deep at every point-tile boundary); at the tile's last centroid
+        // tile at the latest.
+        bool a_next = pt + (int)gridDim.x >= nptiles;
+        const int nb = (lp + 1) % ABUF;
+        const uint32_t npar = (uint32_t)(((lp + 1) / ABUF) & 1) ^ 1u;
         for (int j = 0; ok && j < kt; j++) {
           for (int kb = 0; kb < a.kblk; kb++, q++) {
             const int s = (int)(q % SLOTS);
@@ -192,10 +200,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_expect_tx(&full[s], BLK);
             tma_load_2d(sB + s * BLK, &tmB, kb * KBW, j * BN, &full[s]);
           }
-          // The next point tile's operands, as soon as this tile's first
-          // centroid tile is queued (its buffer frees when the MMAs of the
-          // tile before this one complete).
-          if (ok && j == 0 && pt + (int)gridDim.x < nptiles && !load_a(pt + gridDim.x, lp + 1)) ok = false;
+          if (ok && !a_next && (j == kt - 1 || mbar_test(&aempty[nb], npar))) {
+            if (!load_a(pt + gridDim.x, lp + 1)) ok = false;
+            a_next = true;
+          }
         }
       }
     }
@@ -277,7 +285,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int ch = ew >> 3;
     const int quad = warp & 3;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    Cand* buf = s_cand + (ew * 32 + lane) * NCAND;
     const float X = __uint_as_float(*a.cmax);
     const double rd = sqrt((double)a.d);
     // The point's |x| and starting bound for the next point tile are loaded
@@ -306,24 +313,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       // s + 1.5 absm >= best approx + absm keeps every candidate the
       // unbounded sweep would keep at the end.
       float bound = !vp ? -INFINITY : a.init_bound ? __fadd_ru(pib, 1.5f * absm) : INFINITY;
-      float lost = INFINITY;  // smallest score pushed out of a full buffer
-      int cnt = 0;
-      // Keeps the NCAND best candidates; remembers the best score dropped.
-      auto insert = [&](float sc, uint32_t id) {
-        if (cnt < NCAND) {
-          buf[cnt++] = Cand{sc, id};
-          return;
-        }
-        int wi = 0;
-        for (int e = 1; e < NCAND; e++)
-          if (buf[e].hs > buf[wi].hs) wi = e;
-        if (sc < buf[wi].hs) {
-          lost = fminf(lost, buf[wi].hs);
-          buf[wi] = Cand{sc, id};
-        } else {
-          lost = fminf(lost, sc);
-        }
-      };
+      float lost = INFINITY;  // smallest minimum of a group that found the slots full
+      int cnt = 0;            // groups kept
+      const int64_t slot0 = (p * 2 + ch) * NG;
       for (int j = 0; j < kt; j++, g++) {
         const int b = g & 1;
         const bool w = mbar_wait(&tfull[b], (g >> 1) & 1, s_abort, a.err, 16, WAIT_NS);
@@ -372,34 +364,51 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 8; i++) gm[i] = fmin3(v[4 * i], v[4 * i + 1], fminf(v[4 * i + 2], v[4 * i + 3]));
           const float cmn = fmin3(fmin3(gm[0], gm[1], gm[2]), fmin3(gm[3], gm[4], gm[5]), fminf(gm[6], gm[7]));
-          // Padding points have bound -inf and never hit. Most chunks hold
+          // Padding points have bound -inf and never hit; a chunk of
+          // columns past K only (+inf) never hits either. Most chunks hold
           // no candidate of any of the warp's points: one vote skips them.
-          const bool hit = cmn <= bound;
+          const bool hit = cmn <= bound && cmn < INFINITY;
           if (__any_sync(sel::kFull, hit) && hit) {
-            // A better chunk minimum tightens the bound. Entries already
-            // kept stay; those now outside the bound are ignored by the
-            // triage and are the first to go when the buffer is full.
+            // A better chunk minimum tightens the bound. Groups already
+            // kept stay; the triage filters their scores by the final
+            // bound.
             if (cmn < best) {
               best = cmn;
               bound = fminf(bound, __fadd_ru(best, absm));
             }
-            unsigned m = 0;
-#pragma unroll
-            for (int i = 0; i < 8; i++) m |= gm[i] <= bound ? (1u << i) : 0u;
-            // Static register indices: each group, then each of its four.
+            // Each group of four whose minimum passes: its four scores in
+            // one 16-byte store and its first column (static register
+            // indices, predicated; only a warp's hitting lanes run this).
+            // Columns past K inside a kept group score +inf and are never
+            // chosen.
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-              if ((m >> i) & 1u) {
-                float w0 = v[4 * i], w1 = v[4 * i + 1], w2 = v[4 * i + 2], w3 = v[4 * i + 3];
-#pragma unroll 1
-                for (int jj = 0; jj < 4; jj++) {
-                  const float sc = w0;
-                  w0 = w1;
-                  w1 = w2;
-                  w2 = w3;
-                  if (sc <= bound && 4 * i + jj < cb) insert(sc, (uint32_t)(c0 + c * 32 + 4 * i + jj));
+              if (gm[i] <= bound) {
+                if (cnt < NG) {
+                  a.groups.sc[slot0 + cnt] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                  a.groups.col[slot0 + cnt] = (uint32_t)(c0 + c * 32 + 4 * i);
+                  cnt++;
+                } else {
+                  lost = fminf(lost, gm[i]);
                 }
               }
+            }
+            if (cnt >= NG - 1) {
+              // Make room for the next hit (rarely needed): drop kept groups
+              // the bound has passed. This thread wrote the slots, so it
+              // reads them back; the chunk's scores are no longer live.
+              int k2 = 0;
+              for (int e = 0; e < cnt; e++) {
+                const float4 s4 = a.groups.sc[slot0 + e];
+                if (fminf(fminf(s4.x, s4.y), fminf(s4.z, s4.w)) <= bound) {
+                  if (k2 != e) {
+                    a.groups.sc[slot0 + k2] = s4;
+                    a.groups.col[slot0 + k2] = a.groups.col[slot0 + e];
+                  }
+                  k2++;
+                }
+              }
+              cnt = k2;
             }
           }
         }
@@ -408,11 +417,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (vp) {
         Res r;
         r.best = best;
-        r.bi = cnt > 0 ? buf[0].id : 0xffffffffu;
+        r.bi = 0;
         r.cnt = cnt;
         r.lost = lost;
         a.res[p * 2 + ch] = r;
-        for (int e = 0; e < cnt; e++) a.cands[(p * 2 + ch) * NCAND + e] = buf[e];
       }
     }
   }
@@ -451,7 +459,7 @@ __device__ __forceinline__ void warp_append(int* counter, int* list, bool take, 
 template <int METRIC>
 __global__ void __launch_bounds__(256) kmeans_triage_kernel(
     int64_t n, int d, const float* __restrict__ xq, const unsigned int* __restrict__ cmax,
-    const Res* __restrict__ res, const Cand* __restrict__ cands, const int* __restrict__ force_full,
+    const Res* __restrict__ res, Groups groups, const int* __restrict__ force_full,
     int32_t* __restrict__ assign, int* __restrict__ flags, float inv_scale, float* __restrict__ pscore) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   int cls = 0;  // 0: assigned here (or past the end), 1: list F, 2: list M
@@ -469,11 +477,17 @@ __global__ void __launch_bounds__(256) kmeans_triage_kernel(
       for (int h = 0; h < 2; h++) {
         const Res r = h ? r1 : r0;
         for (int e = 0; e < r.cnt; e++) {
-          const Cand ce = cands[(i * 2 + h) * NCAND + e];
-          if (ce.hs <= bound) {
-            nin++;
-            only = ce.id;
-            only_hs = ce.hs;
+          const int64_t sl = (i * 2 + h) * NG + e;
+          const float4 s4 = groups.sc[sl];
+          const uint32_t col = groups.col[sl];
+          const float sc[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+          for (int jj = 0; jj < 4; jj++) {
+            if (sc[jj] <= bound) {
+              nin++;
+              only = col + jj;
+              only_hs = sc[jj];
+            }
           }
         }
       }
@@ -493,18 +507,19 @@ __global__ void __launch_bounds__(256) kmeans_triage_kernel(
 
 // Finalize, step 2: the points of list M, one half-warp per point (its 16
 // lanes are the reference's 16 SIMD lanes), striding over the list. Lane l
-// loads candidate l & 7 of column half l >> 3, so all of a point's
-// candidates are read at once; those within the bound are then scored two
-// at a time (rank_key2: both rows' loads in flight) for the exact argmin,
-// lowest index on ties, with the exact distance.
+// loads group slot l & 7 of column half l >> 3, so all of a point's groups
+// are read at once; the scores within the bound are then taken two at a
+// time (lowest lane, lowest column first) and scored exactly (rank_key2:
+// both rows' loads in flight) for the exact argmin, lowest index on ties,
+// with the exact distance.
 template <int METRIC>
 __global__ void __launch_bounds__(128) kmeans_multi_kernel(
     const float* __restrict__ x, int64_t n, int d, int dp, const float* __restrict__ cent,
     const float* __restrict__ cent_aux, const float* __restrict__ x_aux, const float* __restrict__ xq,
-    const unsigned int* __restrict__ cmax, const Res* __restrict__ res, const Cand* __restrict__ cands,
+    const unsigned int* __restrict__ cmax, const Res* __restrict__ res, Groups groups,
     const int* __restrict__ flags, int32_t* __restrict__ assign, float* __restrict__ dist, float inv_scale,
     float* __restrict__ pscore) {
-  static_assert(2 * NCAND == 16, "one candidate slot per lane of a half-warp");
+  static_assert(2 * NG == 16, "one group slot per lane of a half-warp");
   const int hl = threadIdx.x & 15;
   const int hsh = threadIdx.x & 16;
   const unsigned mask = 0xffffu << hsh;
@@ -520,19 +535,38 @@ __global__ void __launch_bounds__(128) kmeans_multi_kernel(
     const float absm = point_margin(METRIC, d, sqrt((double)d), xq[i], __uint_as_float(*cmax), inv_scale);
     const float bound = __fadd_ru(fminf(r0.best, r1.best), absm);
     const int h = hl >> 3, e = hl & 7;
-    Cand ce{INFINITY, 0u};
-    if (e < (h ? r1.cnt : r0.cnt)) ce = cands[(i * 2 + h) * NCAND + e];
-    unsigned in = (__ballot_sync(mask, ce.hs <= bound) >> hsh) & 0xffffu;
+    float4 s4 = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+    uint32_t col = 0;
+    if (e < (h ? r1.cnt : r0.cnt)) {
+      s4 = groups.sc[(i * 2 + h) * NG + e];
+      col = groups.col[(i * 2 + h) * NG + e];
+    }
+    // This lane's scores within the bound, one bit per column of its group.
+    unsigned mine = (s4.x <= bound ? 1u : 0u) | (s4.y <= bound ? 2u : 0u) | (s4.z <= bound ? 4u : 0u) |
+                    (s4.w <= bound ? 8u : 0u);
+    // Next candidate (id, approximate score): the lowest remaining bit of
+    // the lowest lane that has one; false when none is left.
+    auto next = [&](uint32_t* id, float* hs) -> bool {
+      const unsigned lm = (__ballot_sync(mask, mine != 0) >> hsh) & 0xffffu;
+      if (!lm) return false;
+      const int l = __ffs(lm) - 1;
+      const int jb = __ffs(__shfl_sync(mask, mine, l, 16)) - 1;
+      const float sv = jb == 0 ? s4.x : jb == 1 ? s4.y : jb == 2 ? s4.z : s4.w;
+      *hs = __shfl_sync(mask, sv, l, 16);
+      *id = __shfl_sync(mask, col, l, 16) + (uint32_t)jb;
+      if (hl == l) mine &= mine - 1;
+      return true;
+    };
     int best = 0x7fffffff;
     float best_key = hib ? -INFINITY : INFINITY;
     float best_hs = INFINITY;  // approximate score of the winner
-    while (in) {
-      const int l0 = __ffs(in) - 1;
-      in &= in - 1;
-      const int l1 = in ? __ffs(in) - 1 : l0;
-      if (in) in &= in - 1;
-      const uint32_t c0 = __shfl_sync(mask, ce.id, l0, 16), c1 = __shfl_sync(mask, ce.id, l1, 16);
-      const float h0 = __shfl_sync(mask, ce.hs, l0, 16), h1 = __shfl_sync(mask, ce.hs, l1, 16);
+    uint32_t c0, c1;
+    float h0, h1;
+    while (next(&c0, &h0)) {
+      if (!next(&c1, &h1)) {
+        c1 = c0;
+        h1 = h0;
+      }
       const float ca0 = METRIC == vrs_exact::kCos ? cent_aux[c0] : 0.0f;
       const float ca1 = METRIC == vrs_exact::kCos ? cent_aux[c1] : 0.0f;
       float k0, k1;
@@ -715,14 +749,15 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16) {
 template <int M>
 int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
                  const float* x_aux, int k, const float* xq, const unsigned int* cmax, const Res* res,
-                 const Cand* cands, const int* force_full, int32_t* assign, float* dist, int* flags,
+                 void* groups, const int* force_full, int32_t* assign, float* dist, int* flags,
                  int num_sms, float inv_scale, float* pscore, cudaStream_t s) {
+  const Groups gr = groups_at(groups, n);
   VRS_CUDA(cudaMemsetAsync(flags, 0, 2 * sizeof(int), s));
-  kmeans_triage_kernel<M><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, d, xq, cmax, res, cands, force_full,
+  kmeans_triage_kernel<M><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, d, xq, cmax, res, gr, force_full,
                                                                         assign, flags, inv_scale, pscore);
   VRS_CUDA(cudaGetLastError());
   kmeans_multi_kernel<M><<<(unsigned)(num_sms * 16), 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, xq, cmax,
-                                                                 res, cands, flags, assign, dist, inv_scale,
+                                                                 res, gr, flags, assign, dist, inv_scale,
                                                                  pscore);
   VRS_CUDA(cudaGetLastError());
   kmeans_flagged_kernel<M><<<(unsigned)(num_sms * 8), 256, 0, s>>>(x, d, dp, cent, cent_aux, x_aux, k, flags,
@@ -784,7 +819,7 @@ int prep_rows(const float* x, int64_t n, int d, int dp, int metric, float op_sca
 }
 
 int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
-           const unsigned int* cmax, int metric, float op_scale, Res* res, Cand* cands, int* err, int num_sms,
+           const unsigned int* cmax, int metric, float op_scale, Res* res, void* groups, int* err, int num_sms,
            const float* init_bound, cudaStream_t s) {
   if (n == 0) return VRS_OK;
   const int d16 = (d + 15) / 16 * 16;
@@ -805,7 +840,7 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
   a.inv_scale = 1.0f / op_scale;
   a.metric = metric;
   a.res = res;
-  a.cands = cands;
+  a.groups = groups_at(groups, n);
   a.err = err;
   a.init_bound = a.mode == 0 ? init_bound : nullptr;
   auto kern = a.mode == 0 ? kmeans_assign_tc_kernel<0> : kmeans_assign_tc_kernel<1>;
@@ -820,23 +855,23 @@ int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float*
 
 int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
              const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
-             const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
+             void* groups, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
              float op_scale, float* pscore, cudaStream_t s) {
   if (n == 0) return VRS_OK;
   switch (metric) {
     case vrs_exact::kL2:
-      return finalize_run<vrs_exact::kL2>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands, force_full,
+      return finalize_run<vrs_exact::kL2>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, groups, force_full,
                                           assign_out, dist, flags, num_sms, 1.0f / op_scale, pscore, s);
     case vrs_exact::kMaha:
-      return finalize_run<vrs_exact::kMaha>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
+      return finalize_run<vrs_exact::kMaha>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, groups,
                                             force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, pscore,
                                             s);
     case vrs_exact::kDot:
-      return finalize_run<vrs_exact::kDot>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
+      return finalize_run<vrs_exact::kDot>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, groups,
                                            force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, nullptr,
                                            s);
     case vrs_exact::kCos:
-      return finalize_run<vrs_exact::kCos>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, cands,
+      return finalize_run<vrs_exact::kCos>(x, n, d, dp, cent, cent_aux, x_aux, k, xq, cmax, res, groups,
                                            force_full, assign_out, dist, flags, num_sms, 1.0f / op_scale, nullptr,
                                            s);
   }

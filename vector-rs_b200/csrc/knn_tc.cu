@@ -374,17 +374,25 @@ __global__ void __launch_bounds__(THREADS, 1)
 //   * Lists: one per (segment, column quarter, query).
 // Every wait is bounded; both CTAs meet in a cluster barrier before TMEM
 // is released and before either exits.
-constexpr int P_BM = 128;           // queries per CTA (M = 256 per pair)
-constexpr int P_BN = 256;           // base rows per pair tile (N)
-constexpr int P_HALF = P_BN / 2;    // rows each CTA loads
-constexpr int P_STAGES = 5;
-constexpr int P_QUARTER = 64;       // columns per epilogue warp
-constexpr uint32_t P_BLK = 128 * 128;  // bytes of one K-block of a 128-row tile
+#ifndef KNN_P_BN
+#define KNN_P_BN 256
+#endif
+constexpr int P_BM = 128;             // queries per CTA (M = 256 per pair)
+constexpr int P_BN = KNN_P_BN;        // base rows per pair tile (N)
+constexpr int P_HALF = P_BN / 2;      // rows each CTA loads
+constexpr int P_NBUF = 512 / P_BN;    // accumulator buffers in TMEM
+constexpr int P_QUARTER = P_BN / 4;   // columns per epilogue warp
+constexpr uint32_t P_BLK = 128 * 128;        // bytes of one K-block of the 128-row A tile
+constexpr uint32_t P_BLK_B = P_HALF * 128;   // bytes of one K-block of a CTA's B half
+constexpr int P_STAGES = (int)((160u * 1024u) / (MAX_KBLK * P_BLK_B));
+constexpr size_t P_SMEM_BAR = 512;
 constexpr size_t P_SMEM_A = (size_t)MAX_KBLK * P_BLK;
-constexpr size_t P_SMEM_B = (size_t)P_STAGES * MAX_KBLK * P_BLK;
-constexpr size_t P_SMEM_TOTAL = 1024 + P_SMEM_A + P_SMEM_B + SMEM_HIST + SMEM_BAR;
+constexpr size_t P_SMEM_B = (size_t)P_STAGES * MAX_KBLK * P_BLK_B;
+constexpr size_t P_SMEM_TOTAL = 1024 + P_SMEM_A + P_SMEM_B + SMEM_HIST + P_SMEM_BAR;
+static_assert(P_BN == 128 || P_BN == 256, "2-SM scan: pair tiles are 128 or 256 rows");
+static_assert(P_QUARTER % 32 == 0, "2-SM scan: epilogue columns come in 32-column loads");
 static_assert(P_SMEM_TOTAL <= 232448, "2-SM scan: shared memory above the per-block limit");
-static_assert((3 * P_STAGES + 2 + 2 + 1) * 8 + 8 <= SMEM_BAR, "2-SM scan: barrier region too small");
+static_assert((2 * P_STAGES + 2 * P_NBUF + 1) * 8 + 8 <= P_SMEM_BAR, "2-SM scan: barrier region too small");
 
 template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
@@ -398,9 +406,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   uint64_t* bars = (uint64_t*)((uint8_t*)s_hist + SMEM_HIST);
   uint64_t* full = bars;                  // [P_STAGES] even CTA: both halves' bytes
   uint64_t* empty = bars + P_STAGES;      // [P_STAGES] each CTA: MMA commit
-  uint64_t* tfull = bars + 2 * P_STAGES;  // [2] each CTA: MMA commit
-  uint64_t* tempty = tfull + 2;           // [2] even CTA: both CTAs' epilogue warps
-  uint64_t* afull = tempty + 2;           // even CTA: both A tiles
+  uint64_t* tfull = bars + 2 * P_STAGES;  // [P_NBUF] each CTA: MMA commit
+  uint64_t* tempty = tfull + P_NBUF;      // [P_NBUF] even CTA: both CTAs' epilogue warps
+  uint64_t* afull = tempty + P_NBUF;      // even CTA: both A tiles
   uint32_t* s_tmem = (uint32_t*)(afull + 1);
   volatile int* s_abort = (volatile int*)(s_tmem + 1);
 
@@ -418,7 +426,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; b++) {
+    for (int b = 0; b < P_NBUF; b++) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 2 * EPI_WARPS);
     }
@@ -446,11 +454,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       for (int t = 0; t < ntiles; t++) {
         const int s = t % P_STAGES;
         if (!mbar_wait(&empty[s], ((t / P_STAGES) & 1) ^ 1, s_abort, a.err, 21, WAIT_NS)) break;
-        if (lead) mbar_expect_tx(&full[s], (uint32_t)(2 * a.kblk) * P_BLK);
+        if (lead) mbar_expect_tx(&full[s], (uint32_t)(2 * a.kblk) * P_BLK_B);
         const uint32_t full_lead = mapa_shared(&full[s], 0);
         const int y = (int)(row_begin + (int64_t)t * P_BN + (int)cta * P_HALF);
         for (int kb = 0; kb < a.kblk; kb++)
-          tma_load_2d_pair(sB + (s * MAX_KBLK + kb) * P_BLK, &tmB, kb * KBW, y, full_lead);
+          tma_load_2d_pair(sB + (s * MAX_KBLK + kb) * P_BLK_B, &tmB, kb * KBW, y, full_lead);
         issued = t + 1;
       }
       if (*s_abort && lead) {
@@ -474,13 +482,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       int last = -1;
       for (int t = 0; ok && t < ntiles; t++) {
-        const int s = t % P_STAGES, b = t & 1;
+        const int s = t % P_STAGES, b = t % P_NBUF;
         uint64_t bd[MAX_KBLK * 4];
 #pragma unroll
         for (int ks = 0; ks < MAX_KBLK * 4; ks++)
-          bd[ks] = b_desc.at((uint32_t)(s * MAX_KBLK * P_BLK + (ks >> 2) * P_BLK + (ks & 3) * 32) >> 4);
+          bd[ks] = b_desc.at((uint32_t)(s * MAX_KBLK * P_BLK_B + (ks >> 2) * P_BLK_B + (ks & 3) * 32) >> 4);
         if (!mbar_wait(&full[s], (t / P_STAGES) & 1, s_abort, a.err, 23, WAIT_NS)) break;
-        if (!mbar_wait(&tempty[b], ((t >> 1) & 1) ^ 1, s_abort, a.err, 24, WAIT_NS)) break;
+        if (!mbar_wait(&tempty[b], ((t / P_NBUF) & 1) ^ 1, s_abort, a.err, 24, WAIT_NS)) break;
         tc_fence_after();
         const uint32_t d = tmem + b * P_BN;
 #pragma unroll
@@ -492,7 +500,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
       if (*s_abort && last >= 0) {
         volatile int dummy = 0;
-        mbar_wait(&tfull[last & 1], (last >> 1) & 1, &dummy, a.err, 0, WAIT_NS / 4);
+        mbar_wait(&tfull[last % P_NBUF], (last / P_NBUF) & 1, &dummy, a.err, 0, WAIT_NS / 4);
       }
     }
   } else {
@@ -512,20 +520,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const float absm = vq ? a.absm[q] : 0.0f;
     int* hist = s_hist + ew * 256;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    const uint32_t tempty_lead0 = mapa_shared(&tempty[0], 0), tempty_lead1 = mapa_shared(&tempty[1], 0);
+    constexpr int NGR = P_QUARTER / 8;  // groups of 8 columns per warp and tile
     for (int t = 0; t < ntiles; t++) {
-      const int b = t & 1;
-      const bool ok = mbar_wait(&tfull[b], (t >> 1) & 1, s_abort, a.err, 25, WAIT_NS);
+      const int b = t % P_NBUF;
+      const bool ok = mbar_wait(&tfull[b], (t / P_NBUF) & 1, s_abort, a.err, 25, WAIT_NS);
       if (!__all_sync(sel::kFull, ok)) break;
       tc_fence_after();
       const int64_t n0 = row_begin + (int64_t)t * P_BN + quarter * P_QUARTER;
-      if (MODE == 0 && t + 1 < ntiles && lane < 2)
+      if (MODE == 0 && t + 1 < ntiles && lane < P_QUARTER / 32)
         asm volatile("prefetch.global.L1 [%0];" ::"l"(a.xn + n0 + P_BN + lane * 32));
       const int64_t rem_cols = row_end - n0;
       const int valid_cols = rem_cols < P_QUARTER ? (int)(rem_cols > 0 ? rem_cols : 0) : P_QUARTER;
       const float thr = MODE == 0 ? bound : MODE == 1 ? -bound * ks : -0.5f * bound * ks;
       float v[P_QUARTER];
-      tmem_ld64(tmem + lane_base + b * P_BN + quarter * P_QUARTER, v);
+      if constexpr (P_QUARTER == 64)
+        tmem_ld64(tmem + lane_base + b * P_BN + quarter * P_QUARTER, v);
+      else
+        tmem_ld32(tmem + lane_base + b * P_BN + quarter * P_QUARTER, v);
       // The tile's columns are in registers: hand the TMEM buffer back to
       // the MMA issuer now, so the selection below overlaps the next MMAs.
       tc_fence_before();
@@ -534,7 +545,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (lead)
           mbar_arrive(&tempty[b]);
         else
-          mbar_arrive_cluster(b ? tempty_lead1 : tempty_lead0);
+          mbar_arrive_cluster(mapa_shared(&tempty[b], 0));
       }
       if (MODE == 0) {
         const float4* xp = reinterpret_cast<const float4*>(a.xn + n0);
@@ -554,18 +565,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         for (int j = 0; j < P_QUARTER; j++)
           if (j >= valid_cols) v[j] = __int_as_float(0x7fffffff);
       }
-      float g[8];
+      float g[NGR];
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
+      for (int i = 0; i < NGR; i++) {
         const float* w = v + 8 * i;
         g[i] = MODE == 0 ? fmin3(fmin3(w[0], w[1], w[2]), fmin3(w[3], w[4], w[5]), fminf(w[6], w[7]))
                          : fmax3(fmax3(w[0], w[1], w[2]), fmax3(w[3], w[4], w[5]), fmaxf(w[6], w[7]));
       }
-      const float best = MODE == 0 ? fmin3(fmin3(g[0], g[1], g[2]), fmin3(g[3], g[4], g[5]), fminf(g[6], g[7]))
-                                   : fmax3(fmax3(g[0], g[1], g[2]), fmax3(g[3], g[4], g[5]), fmaxf(g[6], g[7]));
+      float best;
+      if constexpr (NGR == 8)
+        best = MODE == 0 ? fmin3(fmin3(g[0], g[1], g[2]), fmin3(g[3], g[4], g[5]), fminf(g[6], g[7]))
+                         : fmax3(fmax3(g[0], g[1], g[2]), fmax3(g[3], g[4], g[5]), fmaxf(g[6], g[7]));
+      else
+        best = MODE == 0 ? fminf(fmin3(g[0], g[1], g[2]), g[3]) : fmaxf(fmax3(g[0], g[1], g[2]), g[3]);
       if (MODE == 0 ? best <= thr : best >= thr) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
+        for (int i = 0; i < NGR; i++) {
           if (MODE == 0 ? g[i] <= thr : g[i] >= thr) {
 #pragma unroll
             for (int jj = 0; jj < 8; jj++) {
@@ -908,8 +923,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 16-bit [rows][d16] row-major, box 64 x 128, 128-byte swizzle, zero OOB fill.
-int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16, bool f16) {
+// 16-bit [rows][d16] row-major, box 64 x box_rows, 128-byte swizzle, zero OOB fill.
+int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16, bool f16, int box_rows = BM) {
   auto fn = encode_fn();
   if (!fn) {
     set_error(VRS_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
@@ -917,7 +932,7 @@ int make_tmap(CUtensorMap* m, const void* base, int64_t rows, int d16, bool f16)
   }
   cuuint64_t dims[2] = {(cuuint64_t)d16, (cuuint64_t)std::max<int64_t>(rows, 1)};
   cuuint64_t strides[1] = {(cuuint64_t)d16 * 2};
-  cuuint32_t box[2] = {(cuuint32_t)KBW, (cuuint32_t)BM};
+  cuuint32_t box[2] = {(cuuint32_t)KBW, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                   const_cast<void*>(base), dims, strides, box,
@@ -1069,7 +1084,7 @@ int tc_scan2(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d
   CUtensorMap tmA, tmB;
   const bool f16 = tc_fp16(metric);
   VRS_TRY(make_tmap(&tmA, qb, nq_rows_alloc, d16, f16));
-  VRS_TRY(make_tmap(&tmB, xb, n, d16, f16));
+  VRS_TRY(make_tmap(&tmB, xb, n, d16, f16, P_HALF));
   TcScanArgs a;
   a.xn = xn;
   a.n = n;

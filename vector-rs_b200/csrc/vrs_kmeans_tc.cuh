@@ -7,14 +7,35 @@ namespace vrs {
 namespace kmtc {
 
 // Per (point, column half) result of the tensor-core pass: approximate best
-// score and centroid, number of kept candidates (at most 8, the best within
-// the margin), and the smallest score that did not fit (+inf if none).
+// score, number of kept candidate groups (at most kGroupSlots), and the
+// smallest group minimum that did not fit (+inf if none).
 struct Res {
   float best;
-  uint32_t bi;
+  uint32_t bi;  // unused
   int cnt;
   float lost;
 };
+
+// Candidate groups: the pass keeps, per (point, column half), up to
+// kGroupSlots groups of four consecutive centroids whose smallest
+// approximate score was within the point's bound when seen: their four
+// scores (sc) and first centroid index (col). Record r = 2 * point + half
+// owns slots [r * kGroupSlots, (r + 1) * kGroupSlots). One allocation of
+// group_bytes(n) holds both arrays.
+constexpr int kGroupSlots = 8;
+struct Groups {
+  float4* sc;
+  uint32_t* col;
+};
+inline size_t group_bytes(int64_t n) {
+  return (size_t)n * 2 * kGroupSlots * (sizeof(float4) + sizeof(uint32_t));
+}
+inline Groups groups_at(void* base, int64_t n) {
+  Groups g;
+  g.sc = static_cast<float4*>(base);
+  g.col = reinterpret_cast<uint32_t*>(static_cast<char*>(base) + (size_t)n * 2 * kGroupSlots * sizeof(float4));
+  return g;
+}
 
 bool supported(int metric, int d);
 // fp16 operand rows, |row|^2 (sq, nullable), |row| (nrm, nullable), max |row|
@@ -27,16 +48,17 @@ int prep_rows(const float* x, int64_t n, int d, int dp, int metric, float op_sca
 // init_bound (nullable; squared L2 / Mahalanobis only): per point an upper
 // bound on some centroid's score |c|^2 - 2 x.c (start_bound).
 int assign(const void* xb, int64_t n, const void* cb, int k, int d, const float* cn, const float* xq,
-           const unsigned int* cmax, int metric, float op_scale, Res* res, Cand* cands, int* err, int num_sms,
+           const unsigned int* cmax, int metric, float op_scale, Res* res, void* groups, int* err, int num_sms,
            const float* init_bound, cudaStream_t s);
-// Exact assignment from the candidates (flags: 2 n + 2 ints of scratch).
+// Exact assignment from the candidate groups (groups: as written by assign
+// for the same n; flags: 2 n + 2 ints of scratch).
 // Points whose candidates may be incomplete are assigned by a full exact
 // scan, one CTA per point; points with several candidates within their
 // bound by exact scoring of those; a point with a single candidate within
 // its bound takes it and gets no exact distance here (fill_dist).
 int finalize(const float* x, int64_t n, int d, int dp, const float* cent, const float* cent_aux,
              const float* x_aux, int k, const float* xq, const unsigned int* cmax, int metric, const Res* res,
-             const Cand* cands, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
+             void* groups, const int* force_full, int32_t* assign_out, float* dist, int* flags, int num_sms,
              float op_scale, float* pscore, cudaStream_t s);
 // pscore (written by finalize, squared L2 / Mahalanobis; +inf for points
 // scanned exactly): an upper bound on each point's score to the centroid it
