@@ -515,7 +515,7 @@ def knn_bench(ctx, w, steps, warmup, parity_queries, cpu_leg, sustained, e2e_ste
     barrier()
     vc.profile_enable(False)
     st = {nm: vc.profile_read(nm) for nm in ("knn_scan", "knn_select", "knn_merge", "knn_pivot", "knn_fallback",
-                                             "knn_prep", "knn_gather")}
+                                             "knn_prep", "knn_gather", "knn_fallback_queries")}
     value = n_q * steps / (ms / 1e3)
 
     # Sustained: the same step repeated for at least one second (its own
@@ -565,8 +565,9 @@ def knn_bench(ctx, w, steps, warmup, parity_queries, cpu_leg, sustained, e2e_ste
     # ------------------------------------------------------------- roofline
     scan_ms, scan_n = st["knn_scan"]
     per_launch_ms = scan_ms / max(scan_n, 1)
-    breakdown = {k.replace("knn_", ""): v[0] / steps for k, v in st.items()}
+    breakdown = {k.replace("knn_", ""): v[0] / steps for k, v in st.items() if k != "knn_fallback_queries"}
     breakdown["fallback_launches"] = st["knn_fallback"][1]
+    breakdown["fallback_queries_per_step"] = st["knn_fallback_queries"][1] / steps
     if metric in TC_METRICS and D <= 128:
         flops_per_launch = 2.0 * n_loc * D * n_q  # algorithmic: 2*N_local*D per query
         achieved = flops_per_launch / (per_launch_ms / 1e3) / 1e12

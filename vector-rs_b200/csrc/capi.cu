@@ -227,6 +227,7 @@ struct KnnShard {
   float xscale = 1.0f;          // tensor-core operand scale of the base rows
   int fold_m = 0;               // exponent of the folded -|x|^2 column
   DBuf qscale;                  // per-search operand scale of each query
+  DBuf qsq;                     // per-search |q|^2 from below (squared L2 / Mahalanobis)
   bool use_simt = false;        // CUDA-core scan (Manhattan, Chebyshev, Hellinger)
   // per-search scratch
   DBuf q_in, q, q_aux, cand, cnt, overflow, pairs, gathered, out_dist, out_id;
@@ -263,7 +264,7 @@ struct vrs_knn {
       for (DBuf* b : {&s->base, &s->base_aux, &s->q_in, &s->q, &s->q_aux, &s->cand, &s->cnt,
                       &s->overflow, &s->pairs, &s->gathered, &s->out_dist, &s->out_id, &s->xb,
                       &s->xn, &s->xmax, &s->tiny, &s->ntiny, &s->qb, &s->absm, &s->err, &s->qindex, &s->pb,
-                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all, &s->qscale, &s->mflags,
+                      &s->pn, &s->tmin, &s->ibound, &s->ptop, &s->ptop_all, &s->qscale, &s->qsq, &s->mflags,
                       &s->all_flags, &s->sl_dist, &s->sl_id, &s->q_root})
         b->release();
       s->hstat.release();
@@ -567,6 +568,8 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
   // the exact re-search; merge pairs carry a sentinel instead and the merge
   // decides (a pooled bound is global, so no shard can check it alone).
   const int tau_rank = pool_len(h, s, kk, phase);
+  // The scan's squared-L2 scores leave |q|^2 out (see KnnSelectArgs::q_sq).
+  const bool l2_scores = h->metric == vrs_exact::kL2 || h->metric == vrs_exact::kMaha;
   if (phase == kPhaseMain) goto main_phase;
   VRS_TRY(s->qb.reserve((size_t)nq_alloc * d16 * 2));
   VRS_TRY(s->absm.reserve((size_t)nq * sizeof(float)));
@@ -575,12 +578,14 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
     VRS_CUDA(cudaMemsetAsync((char*)s->qb.p + (size_t)nq * d16 * 2, 0, (size_t)(nq_alloc - nq) * d16 * 2, st));
   VRS_CUDA(cudaMemsetAsync(s->err.p, 0, sizeof(int), st));
   VRS_TRY(s->qscale.reserve((size_t)nq * sizeof(float)));
+  if (l2_scores) VRS_TRY(s->qsq.reserve((size_t)nq * sizeof(float)));
   {
     ProfToken t = prof_begin("knn_prep", st);
     VRS_TRY(tc::tc_query_prep(s->q_in.as<float>(), nq, h->d, h->dp, h->metric, s->xmax.as<unsigned int>(),
                               s->xscale, s->fold_m, s->q.as<float>(),
                               h->metric == vrs_exact::kCos ? s->q_aux.as<float>() : nullptr, s->qb.p,
-                              s->qscale.as<float>(), s->absm.as<float>(), s->overflow.as<int>(), st));
+                              s->qscale.as<float>(), s->absm.as<float>(), s->overflow.as<int>(),
+                              l2_scores ? s->qsq.as<float>() : nullptr, st));
     prof_end(t, st);
   }
   VRS_TRY(s->ibound.reserve((size_t)nq * sizeof(float)));
@@ -660,6 +665,7 @@ main_phase:
   sa.n_tiny = h->metric == vrs_exact::kCos ? s->n_tiny : 0;
   sa.init_bound = tau_rank < kk ? s->ibound.as<float>() : nullptr;
   sa.certify = out_pairs != nullptr;
+  sa.q_sq = l2_scores ? s->qsq.as<float>() : nullptr;
   ProfToken t = prof_begin("knn_select", st);
   if (nlists <= 32 && kk <= 256 && sa.n_tiny <= 256) {
     VRS_TRY(launch_knn_select_warp(sa, st));
@@ -792,6 +798,7 @@ int shard_search_finish(vrs_knn* h, KnnShard* s, float* out_dist, uint32_t* out_
     if (f[i]) idx.push_back(i);
   if (idx.empty()) return VRS_OK;
   const int nf = (int)idx.size();
+  prof_count("knn_fallback_queries", nf);
   VRS_TRY(s->qindex.reserve((size_t)nf * sizeof(int)));
   VRS_CUDA(cudaMemcpyAsync(s->qindex.p, idx.data(), (size_t)nf * sizeof(int), cudaMemcpyHostToDevice,
                            s->stream));
@@ -1025,6 +1032,7 @@ int sharded_finish(vrs_knn* h, int nb, int kk, float* odst, uint32_t* oid, cudaM
     // Exact re-search of the flagged queries on every shard; results land in
     // their rows (final results for one shard, merge pairs otherwise).
     const int nf = (int)idx.size();
+    prof_count("knn_fallback_queries", nf);
     for (int r = 0; r < G; r++) {
       KnnShard* s = h->shards[r].get();
       VRS_CUDA(cudaSetDevice(s->device));

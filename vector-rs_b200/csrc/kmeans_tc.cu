@@ -444,16 +444,34 @@ __global__ void __launch_bounds__(THREADS, 1)
 //    exact distance (kmeans_dist_kernel fills distances in after the loop);
 //  * several -> list M (flags[1] = count, indices from flags + 2 + n):
 //    scored exactly by kmeans_multi_kernel.
-// Appends `value` to list[] for every lane with `take` set: one atomic per
-// warp on the list's counter (every lane of the warp must call together).
-__device__ __forceinline__ void warp_append(int* counter, int* list, bool take, int value) {
-  const unsigned m = __ballot_sync(0xffffffffu, take);
-  if (!m) return;
-  const int lane = threadIdx.x & 31, leader = __ffs(m) - 1;
-  int base = 0;
-  if (lane == leader) base = atomicAdd(counter, __popc(m));
-  base = __shfl_sync(0xffffffffu, base, leader);
-  if (take) list[base + __popc(m & ((1u << lane) - 1u))] = value;
+// Appends `value` to two lists (list0 for the threads with `take` == 1,
+// list1 for `take` == 2) with one global atomic per block and list: warps
+// count by ballot, a shared prefix orders the warps, thread 0 reserves the
+// block's range. Every thread of the block must call (blockDim = 256).
+__device__ __forceinline__ void block_append2(int* counter0, int* list0, int* counter1, int* list1, int take,
+                                              int value) {
+  __shared__ int s_cnt[2][8];
+  __shared__ int s_base[2];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const unsigned below = (1u << lane) - 1u;
+  const unsigned m0 = __ballot_sync(0xffffffffu, take == 1), m1 = __ballot_sync(0xffffffffu, take == 2);
+  if (lane == 0) {
+    s_cnt[0][w] = __popc(m0);
+    s_cnt[1][w] = __popc(m1);
+  }
+  __syncthreads();
+  if (threadIdx.x < 2) {
+    int tot = 0;
+    for (int i = 0; i < 8; i++) {
+      const int c = s_cnt[threadIdx.x][i];
+      s_cnt[threadIdx.x][i] = tot;  // exclusive prefix over the warps
+      tot += c;
+    }
+    s_base[threadIdx.x] = tot ? atomicAdd(threadIdx.x ? counter1 : counter0, tot) : 0;
+  }
+  __syncthreads();
+  if (take == 1) list0[s_base[0] + s_cnt[0][w] + __popc(m0 & below)] = value;
+  if (take == 2) list1[s_base[1] + s_cnt[1][w] + __popc(m1 & below)] = value;
 }
 
 template <int METRIC>
@@ -501,8 +519,7 @@ __global__ void __launch_bounds__(256) kmeans_triage_kernel(
     }
   }
   // The lists' order is immaterial: every listed point is scored on its own.
-  warp_append(&flags[0], flags + 2, cls == 1, (int)i);
-  warp_append(&flags[1], flags + 2 + n, cls == 2, (int)i);
+  block_append2(&flags[0], flags + 2, &flags[1], flags + 2 + n, cls, (int)i);
 }
 
 // Finalize, step 2: the points of list M, one half-warp per point (its 16

@@ -127,6 +127,17 @@ __global__ void __launch_bounds__(kScanThreads) knn_scan_exact_kernel(KnnScanArg
 }
 
 // ------------------------------------------------------------------ select
+// Certified limit of a slot whose bound could not be checked alone, in
+// exact heap-score units: no unkept row of this shard scores below it. The
+// scan kept every row whose approximate score is within sb, and absm / 2
+// covers the approximate score's error plus the exact score's rounding, so
+// an unkept row's exact score exceeds sb - absm / 2 (plus |q|^2 for the
+// squared-L2 scores, which leave it out); both steps round down.
+__device__ __forceinline__ float certified_limit(const KnnSelectArgs& a, float sb, int qrow) {
+  const float lim = __fsub_rd(sb, 0.5f * a.absm[qrow]);
+  return a.q_sq ? __fadd_rd(lim, a.q_sq[qrow]) : lim;
+}
+
 template <int METRIC>
 __device__ void select_one(const KnnSelectArgs& a, int slot, Cand* sbuf, int* s_hist, int* s_res, int* s_wt,
                            int* s_off) {
@@ -176,7 +187,7 @@ __device__ void select_one(const KnnSelectArgs& a, int slot, Cand* sbuf, int* s_
     }
     cut = true;
   }
-  const float lim = cut ? __fsub_rd(sb, 0.5f * a.absm[qrow]) : INFINITY;
+  const float lim = cut ? certified_limit(a, sb, qrow) : INFINITY;
   // Exact re-rank of approximate survivors in the reference's order.
   if (a.kind != kExactScores) {
     const float* qp = a.q + (int64_t)qrow * a.dp;
@@ -369,7 +380,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) knn_select_warp_kernel(KnnSele
       cut = true;
     }
   }
-  const float lim = cut ? __fsub_rd(sb, 0.5f * a.absm[qrow]) : INFINITY;
+  const float lim = cut ? certified_limit(a, sb, qrow) : INFINITY;
   // Survivors -> shared memory (batched reads of the flattened lists).
   int R = 0;
   for (int j0 = 0; j0 < total; j0 += 32 * kBatch) {

@@ -686,7 +686,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
     tc_query_prep_kernel(const float* __restrict__ q_in, int nq, int d, int dp, int d16, int metric,
                          const unsigned int* __restrict__ xmax_bits, float xscale, int fold_m,
                          float* __restrict__ qpad, float* __restrict__ qaux, uint16_t* __restrict__ qb,
-                         float* __restrict__ qscale, float* __restrict__ absm, int* __restrict__ overflow) {
+                         float* __restrict__ qscale, float* __restrict__ absm, int* __restrict__ overflow,
+                         float* __restrict__ qsq) {
   const int lane = threadIdx.x & 31;
   const int i = blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
   if (i >= nq) return;  // uniform per warp
@@ -768,6 +769,10 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
   }
   if (lane != 0) return;
   qscale[i] = qs;
+  // |q|^2 from below (the squares and their double sum are exact to far
+  // below f32's step; rounded down): the scan's squared-L2 scores leave it
+  // out, the exact heap scores include it.
+  if (qsq) qsq[i] = __double2float_rd(ss * (1.0 - 0x1p-40));
   const double X = (double)__uint_as_float(*xmax_bits);
   const double Q = sqrt(ss);
   const double u = 0x1p-24;
@@ -968,7 +973,7 @@ int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, float xsc
 
 int tc_query_prep(const float* q_in, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
                   float xscale, int fold_m, float* qpad, float* qaux, void* qb, float* qscale, float* absm,
-                  int* overflow, cudaStream_t s) {
+                  int* overflow, float* qsq, cudaStream_t s) {
   if (nq == 0) return VRS_OK;
   if (d > 128) {
     set_error(VRS_ERR_INVALID_CONFIG, "tensor-core query prep needs d <= 128");
@@ -976,7 +981,7 @@ int tc_query_prep(const float* q_in, int nq, int d, int dp, int metric, const un
   }
   tc_query_prep_kernel<<<(nq + kPrepWarps - 1) / kPrepWarps, kPrepWarps * 32, 0, s>>>(
       q_in, nq, d, dp, tc_d16(metric, d), metric, xmax_bits, xscale, fold_m, qpad, qaux, (uint16_t*)qb, qscale,
-      absm, overflow);
+      absm, overflow, qsq);
   VRS_CUDA(cudaGetLastError());
   count_launch();
   return VRS_OK;

@@ -48,6 +48,12 @@ void harvest_locked() {
 
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+void prof_count(const char* name, int64_t n) {
+  std::lock_guard<std::mutex> g(g_mu);
+  if (g_on != 1) return;
+  g_acc[name].second += n;
+}
+
 ProfToken prof_begin(const char* name, cudaStream_t s) {
   ProfToken t;
   {

@@ -42,6 +42,9 @@ ProfToken prof_begin(const char* name, cudaStream_t s);
 void prof_end(ProfToken& t, cudaStream_t s);
 // Counts kernel launches issued by this library (read as profile name "*").
 void count_launch(int n = 1);
+// Adds n to the count of a named event (read back as the "launches" of
+// vrs_profile_read(name); total_ms stays 0); only while every stage is timed.
+void prof_count(const char* name, int64_t n);
 
 // ------------------------------------------------------- candidate lists
 // One candidate of a per-(segment, query) list: heap score (smaller is
@@ -143,6 +146,11 @@ struct KnnSelectArgs {
   // (no unkept row of this shard can score below that) followed by a
   // kSentinelId pair at that score, and the merge decides.
   int certify;
+  // Squared L2 / Mahalanobis: per query row a lower bound of |q|^2. The
+  // scan's scores (|x|^2 - 2 q.x) leave it out and the exact heap scores
+  // include it, so the certified limit above is moved by it before it is
+  // compared with exact scores (null: no offset).
+  const float* q_sq;
 };
 
 // Launchers (knn_kernels.cu).

@@ -44,11 +44,12 @@ int tc_base_prep(const float* x, int64_t n, int d, int dp, int metric, float xsc
 // From the unpadded queries q_in ([nq][d]): the padded f32 rows qpad
 // ([nq][dp], for the exact re-rank), cosine norms in the reference's order
 // (qaux, cosine only), fp16 operand rows, each query's operand scale
-// (qscale) and margin (absm). Near-zero cosine queries and queries whose
-// scale cannot fit the folded column are flagged for the exact scan.
+// (qscale) and margin (absm), and (qsq, nullable) a lower bound of |q|^2 in
+// f32. Near-zero cosine queries and queries whose scale cannot fit the
+// folded column are flagged for the exact scan.
 int tc_query_prep(const float* q_in, int nq, int d, int dp, int metric, const unsigned int* xmax_bits,
                   float xscale, int fold_m, float* qpad, float* qaux, void* qb, float* qscale, float* absm,
-                  int* overflow, cudaStream_t s);
+                  int* overflow, float* qsq, cudaStream_t s);
 // Base operand scale for a base whose largest |element| is maxabs, and the
 // folded column's exponent (|F| = xscale |x|^2 / 2^(m+1) <= 2^14 with
 // |x|^2 <= d maxabs^2).
