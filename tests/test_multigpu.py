@@ -58,6 +58,28 @@ def test_clique_knn(vc, orc, two, metric, mode):
     eng.close()
 
 
+@pytest.mark.parametrize("metric,d", [(L2, 96), (L2, 128), (COS, 96), (DOT, 64)])
+def test_pooled_bound_needs_no_exact_pass(vc, orc, two, metric, d):
+    """Sharded tensor-core search pools the shards' pivot minima into one
+    starting bound; a shard whose candidates fall short of k' certifies a
+    limit in exact-score units and the merge checks it. On ordinary data no
+    query may need the exact re-search (a squared-L2 limit once missed
+    |q|^2 and sent every query there), and results equal the oracle's."""
+    base, qs = _data(vc, metric, 300_000, 512, d, 20 + d)
+    eng = vc.DistributedKnnEngine.try_new(base, d, two, vc.GpuShardMode.Sharded, vc.DistanceMetric(metric))
+    vc.profile_enable(1)
+    vc.profile_reset()
+    try:
+        dg, ig = eng.search_arrays(qs, 100)
+        _, fallback_queries = vc.profile_read("knn_fallback_queries")
+    finally:
+        vc.profile_enable(0)
+    do, io = orc.knn_search(base, qs, 100, metric)
+    _same(dg, ig, do, io)
+    assert fallback_queries == 0
+    eng.close()
+
+
 def test_clique_knn_ties_across_shards(vc, orc, two):
     """Equal rows in every shard: the merge must order equal scores by id."""
     rng = np.random.default_rng(5)
