@@ -83,7 +83,7 @@ TC_METRICS = (L2, DOT, COS, 7)
 # profiles/knn_scan_tc2_C2.txt; other base sizes scale it by the rows scanned
 # (the traffic is the base re-stream plus the candidate lists, both
 # proportional to the rows).
-SCAN_DRAM_BYTES_C2 = 381.478912e6 + 35.181312e6
+SCAN_DRAM_BYTES_C2 = 382.762752e6 + 36.893184e6
 
 
 def parse():
