@@ -595,13 +595,23 @@ int launch_tc_search(vrs_knn* h, KnnShard* s, int nq, int kk, float* out_dist, u
     // pivot_stride-th row.
     const void* pb = s->pivot_stride > 1 ? s->pb.p : s->xb.p;
     const float* pn = s->pivot_stride > 1 ? s->pn.as<float>() : s->xn.as<float>();
-    const int ntile = 2 * (int)tc::tc_pivot_groups(s->pivot_m);
-    tc::TcPlan pp = tc::tc_plan(s->pivot_m, nq, kk, s->num_sms, tc::kPivotGroup);
+    // On CTA pairs like the candidate pass (256-row tiles, four quarters),
+    // or the one-SM kernel (128-row tiles, two halves); 256 rows per value
+    // either way.
+    const int ntile = (int)(pair_scan ? tc::tc_pivot_values2(s->pivot_m) : 2 * tc::tc_pivot_groups(s->pivot_m));
     VRS_TRY(s->tmin.reserve((size_t)ntile * nq * sizeof(float)));
     ProfToken t0 = prof_begin("knn_pivot", st);
-    VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, pb, s->pivot_m, h->d, pn, h->metric, nq, kk, pp, nullptr,
-                        nullptr, s->overflow.as<int>(), s->absm.as<float>(), s->err.as<int>(),
-                        s->tmin.as<float>(), nullptr, s->qscale.as<float>(), s->xscale, st));
+    if (pair_scan) {
+      tc::TcPlan pp = tc::tc_plan2(s->pivot_m, nq, kk, s->num_sms, tc::kPivotGroup);
+      VRS_TRY(tc::tc_scan2(s->qb.p, nq_alloc, pb, s->pivot_m, h->d, pn, h->metric, nq, kk, pp, nullptr, nullptr,
+                           s->overflow.as<int>(), s->absm.as<float>(), s->err.as<int>(), s->tmin.as<float>(),
+                           nullptr, s->qscale.as<float>(), s->xscale, st));
+    } else {
+      tc::TcPlan pp = tc::tc_plan(s->pivot_m, nq, kk, s->num_sms, tc::kPivotGroup);
+      VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, pb, s->pivot_m, h->d, pn, h->metric, nq, kk, pp, nullptr,
+                          nullptr, s->overflow.as<int>(), s->absm.as<float>(), s->err.as<int>(),
+                          s->tmin.as<float>(), nullptr, s->qscale.as<float>(), s->xscale, st));
+    }
     if (phase == kPhasePivot)
       VRS_TRY(tc::tc_pivot_topk(s->tmin.as<float>(), ntile, nq, tau_rank, s->ptop.as<float>(), st));
     else
@@ -629,7 +639,7 @@ main_phase:
     if (pair_scan)
       VRS_TRY(tc::tc_scan2(s->qb.p, nq_alloc, s->xb.p, s->n_local, h->d, s->xn.as<float>(), h->metric, nq, kk, p,
                            s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(), s->absm.as<float>(),
-                           s->err.as<int>(), s->ibound.as<float>(), s->qscale.as<float>(), s->xscale, st));
+                           s->err.as<int>(), nullptr, s->ibound.as<float>(), s->qscale.as<float>(), s->xscale, st));
     else
       VRS_TRY(tc::tc_scan(s->qb.p, nq_alloc, s->xb.p, s->n_local, h->d, s->xn.as<float>(), h->metric, nq, kk,
                           p, s->cand.as<Cand>(), s->cnt.as<int>(), s->overflow.as<int>(),

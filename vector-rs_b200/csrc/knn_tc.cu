@@ -74,11 +74,13 @@ struct TcScanArgs {
   const float* absm; // [nq]
   int* err;          // global error word (0 = ok)
   // Pivot pass: instead of appending, write the minimum score of each
-  // column half of every group of kPivotGroup tiles per query to
-  // tmin[query][2 * group + half] (group = global 128-row tile / kPivotGroup;
-  // segments start on group boundaries).
+  // column part of every group of kPivotGroup tiles per query to
+  // tmin[query][parts * group + part] (one-SM kernel: 128-row tiles, two
+  // 64-column halves; pair kernel: 256-row tiles, four 64-column quarters;
+  // group = global tile / kPivotGroup; segments start on group boundaries).
+  // Every value is the minimum over 256 distinct rows.
   float* tmin;
-  int64_t tmin_stride;  // entries per query row of tmin (2 * groups)
+  int64_t tmin_stride;  // entries per query row of tmin (parts * groups)
   // Starting acceptance bound per query (null: +inf).
   const float* init_bound;
   uint32_t idesc;    // MMA instruction descriptor
@@ -394,7 +396,7 @@ static_assert(P_QUARTER % 32 == 0, "2-SM scan: epilogue columns come in 32-colum
 static_assert(P_SMEM_TOTAL <= 232448, "2-SM scan: shared memory above the per-block limit");
 static_assert((2 * P_STAGES + 2 * P_NBUF + 1) * 8 + 8 <= P_SMEM_BAR, "2-SM scan: barrier region too small");
 
-template <int MODE>
+template <int MODE, bool TILEMIN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     knn_scan_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         TcScanArgs a) {
@@ -511,7 +513,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int q = q0 + quad * 32 + lane;
     const bool vq = q < a.nq;
     const int64_t list_id = ((int64_t)blockIdx.y * 4 + quarter) * a.nq + (vq ? q : 0);
-    Cand* list = a.cand + list_id * a.cap;
+    Cand* list = TILEMIN ? nullptr : a.cand + list_id * a.cap;
     int count = 0;
     float bound = vq ? (a.init_bound ? a.init_bound[q] : INFINITY) : -INFINITY;
     const float ks = vq ? a.qscale[q] * a.xscale : 1.0f;
@@ -521,6 +523,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     int* hist = s_hist + ew * 256;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     constexpr int NGR = P_QUARTER / 8;  // groups of 8 columns per warp and tile
+    float run = MODE == 0 ? INFINITY : -INFINITY;  // pivot pass: best key of the current group
     for (int t = 0; t < ntiles; t++) {
       const int b = t % P_NBUF;
       const bool ok = mbar_wait(&tfull[b], (t / P_NBUF) & 1, s_abort, a.err, 25, WAIT_NS);
@@ -560,10 +563,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
       }
       if (valid_cols < P_QUARTER) {
-        // Columns past the segment end: NaN fails every comparison.
+        // Columns past the segment end: the worst key for the pivot minima;
+        // NaN for the append path, which fails every comparison.
+        const float pad = TILEMIN ? (MODE == 0 ? INFINITY : -INFINITY) : __int_as_float(0x7fffffff);
 #pragma unroll
         for (int j = 0; j < P_QUARTER; j++)
-          if (j >= valid_cols) v[j] = __int_as_float(0x7fffffff);
+          if (j >= valid_cols) v[j] = pad;
       }
       float g[NGR];
 #pragma unroll
@@ -578,6 +583,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                          : fmax3(fmax3(g[0], g[1], g[2]), fmax3(g[3], g[4], g[5]), fmaxf(g[6], g[7]));
       else
         best = MODE == 0 ? fminf(fmin3(g[0], g[1], g[2]), g[3]) : fmaxf(fmax3(g[0], g[1], g[2]), g[3]);
+      if (TILEMIN) {
+        run = MODE == 0 ? fminf(run, best) : fmaxf(run, best);
+        if ((t + 1) % kPivotGroup == 0 || t == ntiles - 1) {
+          if (vq)
+            a.tmin[(int64_t)q * a.tmin_stride + (row_begin / P_BN + t) / kPivotGroup * 4 + quarter] =
+                MODE == 0 ? run : MODE == 1 ? -inv_ks * run : f2 * run;
+          run = MODE == 0 ? INFINITY : -INFINITY;
+        }
+        continue;
+      }
       if (MODE == 0 ? best <= thr : best >= thr) {
 #pragma unroll
         for (int i = 0; i < NGR; i++) {
@@ -615,7 +630,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
       }
     }
-    if (vq) a.cnt[list_id] = count;
+    if (vq && !TILEMIN) a.cnt[list_id] = count;
     if (vq && *s_abort) a.overflow[q] = 1;
   }
   tc_fence_before();
@@ -1052,7 +1067,7 @@ TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms, int align_tiles) {
 // Plan of the 2-SM candidate pass: pairs of 256 queries x segments of
 // 256-row tiles, at most 8 segments (4 lists each: the warp select takes at
 // most 32 lists per query), chosen like tc_plan for whole waves of SM pairs.
-TcPlan tc_plan2(int64_t n, int nq, int kk, int num_sms) {
+TcPlan tc_plan2(int64_t n, int nq, int kk, int num_sms, int align_tiles) {
   TcPlan p;
   p.qtiles = (nq + 2 * P_BM - 1) / (2 * P_BM);
   p.cap = 1024;
@@ -1070,7 +1085,8 @@ TcPlan tc_plan2(int64_t n, int nq, int kk, int num_sms) {
       p.nseg = s;
     }
   }
-  const int64_t tiles_per_seg = std::max<int64_t>(1, (ntile_total + p.nseg - 1) / p.nseg);
+  int64_t tiles_per_seg = std::max<int64_t>(1, (ntile_total + p.nseg - 1) / p.nseg);
+  tiles_per_seg = (tiles_per_seg + align_tiles - 1) / align_tiles * align_tiles;
   p.seg_len = tiles_per_seg * P_BN;
   p.nseg = (int)std::max<int64_t>(1, (n + p.seg_len - 1) / p.seg_len);
   return p;
@@ -1079,7 +1095,7 @@ TcPlan tc_plan2(int64_t n, int nq, int kk, int num_sms) {
 // Candidate pass on CTA pairs (knn_scan_tc2_kernel): lists [4 * nseg][nq][cap].
 int tc_scan2(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn, int metric,
              int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow, const float* absm, int* err,
-             const float* init_bound, const float* qscale, float xscale, cudaStream_t s) {
+             float* tmin, const float* init_bound, const float* qscale, float xscale, cudaStream_t s) {
   if (n == 0 || nq == 0) return VRS_OK;
   if (nq_rows_alloc % (2 * P_BM) != 0) {
     set_error(VRS_ERR_INVALID_CONFIG, "2-SM scan: query operand rows must be a multiple of 256");
@@ -1104,21 +1120,28 @@ int tc_scan2(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d
   a.k = kk;
   a.absm = absm;
   a.err = err;
-  a.tmin = nullptr;
-  a.tmin_stride = 0;
+  a.tmin = tmin;
+  a.tmin_stride = tc_pivot_values2(n);
+  if (tmin && p.seg_len % ((int64_t)kPivotGroup * P_BN) != 0) {
+    set_error(VRS_ERR_INVALID_CONFIG, "pivot segments must start on pivot-group boundaries");
+    return VRS_ERR_INVALID_CONFIG;
+  }
   a.idesc = f16 ? idesc_f16(2 * P_BM, P_BN) : idesc_bf16(2 * P_BM, P_BN);
   a.qscale = qscale;
   a.xscale = xscale;
   a.init_bound = init_bound;
   const bool l2 = metric == vrs_exact::kL2 || metric == vrs_exact::kMaha;
-  auto kern = tc_fold(metric, d) ? knn_scan_tc2_kernel<2> : l2 ? knn_scan_tc2_kernel<0> : knn_scan_tc2_kernel<1>;
+  auto kern = tc_fold(metric, d) ? (tmin ? knn_scan_tc2_kernel<2, true> : knn_scan_tc2_kernel<2, false>)
+              : l2               ? (tmin ? knn_scan_tc2_kernel<0, true> : knn_scan_tc2_kernel<0, false>)
+                                 : (tmin ? knn_scan_tc2_kernel<1, true> : knn_scan_tc2_kernel<1, false>);
   static std::once_flag attr_once[64];
   int dev = 0;
   VRS_CUDA(cudaGetDevice(&dev));
   int attr_err = 0;
   if (dev < 64) {
     std::call_once(attr_once[dev], [&] {
-      for (auto f : {knn_scan_tc2_kernel<0>, knn_scan_tc2_kernel<1>, knn_scan_tc2_kernel<2>})
+      for (auto f : {knn_scan_tc2_kernel<0, false>, knn_scan_tc2_kernel<1, false>, knn_scan_tc2_kernel<2, false>,
+                     knn_scan_tc2_kernel<0, true>, knn_scan_tc2_kernel<1, true>, knn_scan_tc2_kernel<2, true>})
         if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM_TOTAL) != cudaSuccess)
           attr_err = 1;
     });

@@ -67,17 +67,22 @@ inline int tc_fold_exponent(int d, float xscale, float maxabs) {
 // align_tiles: segments hold a multiple of this many 128-row tiles (the
 // pivot pass passes kPivotGroup).
 TcPlan tc_plan(int64_t n, int nq, int kk, int num_sms, int align_tiles = 1);
-// The candidate pass on CTA pairs (cta_group::2, M = N = 256): its plan and
-// launch; its lists are [4 * nseg][nq][cap] (one per 64-column quarter).
-TcPlan tc_plan2(int64_t n, int nq, int kk, int num_sms);
+// The scan on CTA pairs (cta_group::2, M = N = 256): its plan and launch;
+// its lists are [4 * nseg][nq][cap] (one per 64-column quarter). With tmin
+// != null it is the pivot pass (plan aligned to kPivotGroup tiles), writing
+// tc_pivot_values2(n) minima per query.
+TcPlan tc_plan2(int64_t n, int nq, int kk, int num_sms, int align_tiles = 1);
 int tc_scan2(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn, int metric,
              int nq, int kk, const TcPlan& p, Cand* cand, int* cnt, int* overflow, const float* absm, int* err,
-             const float* init_bound, const float* qscale, float xscale, cudaStream_t s);
+             float* tmin, const float* init_bound, const float* qscale, float xscale, cudaStream_t s);
 // The pivot pass reports one minimum per column half of every group of
 // kPivotGroup 128-row tiles (256 pivot rows per value): fewer values to
 // store and to select from, each still the score of a distinct row.
 constexpr int kPivotGroup = 4;
 inline int64_t tc_pivot_groups(int64_t m) { return ((m + 127) / 128 + kPivotGroup - 1) / kPivotGroup; }
+// Minima per query of the pair kernel's pivot pass: four 64-column quarters
+// of every group of kPivotGroup 256-row tiles (256 rows per value).
+inline int64_t tc_pivot_values2(int64_t m) { return 4 * (((m + 255) / 256 + kPivotGroup - 1) / kPivotGroup); }
 // With tmin != null this is the pivot pass (per-tile minima, no appends);
 // init_bound (nullable) seeds each query's acceptance bound.
 int tc_scan(const void* qb, int nq_rows_alloc, const void* xb, int64_t n, int d, const float* xn,
