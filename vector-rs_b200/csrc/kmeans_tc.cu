@@ -773,7 +773,15 @@ int finalize_run(const float* x, int64_t n, int d, int dp, const float* cent, co
   kmeans_triage_kernel<M><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(n, d, xq, cmax, res, gr, force_full,
                                                                         assign, flags, inv_scale, pscore);
   VRS_CUDA(cudaGetLastError());
-  kmeans_multi_kernel<M><<<(unsigned)(num_sms * 16), 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, xq, cmax,
+  // One resident wave (the kernel strides over the list): more blocks than
+  // fit ran as a second wave with a tail.
+  static const int multi_per_sm = [] {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kmeans_multi_kernel<M>, 128, 0) != cudaSuccess || b < 1)
+      b = 4;
+    return b;
+  }();
+  kmeans_multi_kernel<M><<<(unsigned)(num_sms * multi_per_sm), 128, 0, s>>>(x, n, d, dp, cent, cent_aux, x_aux, xq, cmax,
                                                                  res, gr, flags, assign, dist, inv_scale,
                                                                  pscore);
   VRS_CUDA(cudaGetLastError());
