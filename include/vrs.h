@@ -303,7 +303,9 @@ VRS_API int vrs_knn_set_stream(vrs_knn* h, void* cuda_stream);
  * "kmeans_assign", "kmeans_finalize", "kmeans_sums", "kmeans_update",
  * "kmeans_loop" (a whole Lloyd loop). With on = 2 only the whole-loop stage
  * ("kmeans_loop") is timed, so the per-iteration host work stays as with
- * profiling off. "*" reads the count of kernel launches since the reset. */
+ * profiling off. "*" reads the count of kernel launches since the reset;
+ * "knn_fallback_queries" (with on = 1) counts, in `launches`, the queries
+ * that took the exact re-search (total_ms stays 0). */
 VRS_API int vrs_profile_enable(int32_t on);
 VRS_API int vrs_profile_reset(void);
 VRS_API int vrs_profile_read(const char* name, double* total_ms, int64_t* launches);
