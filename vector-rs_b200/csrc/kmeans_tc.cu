@@ -2,9 +2,10 @@
 // metrics (squared L2, Mahalanobis, dot, cosine).
 //
 // Persistent CTAs loop over tiles of 256 points (two M=128 fp16 operand
-// tiles, loaded by TMA); the K centroids stream through a 4-stage TMA ring
-// as 128-row fp16 tiles; one thread issues tcgen05.mma (kind::f16) into two
-// 128x128 f32 TMEM accumulators (double-buffered). Sixteen epilogue warps
+// tiles, loaded by TMA, double-buffered); the K centroids stream as 128-row
+// fp16 tiles through a TMA ring of 64-column k-block slots; one thread
+// issues tcgen05.mma (kind::f16) into two 128x128 f32 TMEM accumulators
+// (double-buffered). Sixteen epilogue warps
 // (one thread = one point, two warps per point splitting each tile's
 // columns) keep the approximate best score and every group of four
 // centroids whose smallest approximate score is within the point's bound
@@ -40,9 +41,8 @@ using namespace vrs::tc;
 // current one's MMAs run (one buffer left the tensor pipe idle through every
 // reload, K / BN tiles apart). The centroid tiles come from L2 through a
 // ring of SLOTS slots of one 64-column k-block each: a slot frees as soon as
-// the MMAs of its k-block complete, so each load is issued SLOTS - 1
-// k-blocks of MMA time before it is needed (a ring of whole tiles gave a
-// load one tile's MMA time, less than an L2 round trip).
+// the MMAs of its k-block complete, so each load is issued up to SLOTS - 1
+// k-blocks of MMA time before it is needed.
 #ifndef KM_SLOTS
 #define KM_SLOTS 6
 #endif
