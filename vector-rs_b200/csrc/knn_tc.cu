@@ -357,23 +357,27 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ------------------------------------------------- 2-SM scan (cta_group::2)
-// The candidate pass on CTA pairs. A cluster of two CTAs on two SMs owns 256
+// The candidate pass, and with TILEMIN the pivot pass, on CTA pairs
+// (N = 256 by default; KNN_P_BN = 128 builds a 128-row pair tile with four
+// accumulator buffers, measured slower on C2). A cluster of two CTAs on two SMs owns 256
 // queries (128 per CTA, its A tile) and streams 256-row base tiles, each CTA
 // loading its 128-row half. The even CTA's one thread issues
 // tcgen05.mma.cta_group::2 with M = 256, N = 256: every CTA's TMEM receives
 // its 128 queries x the tile's 256 rows, double-buffered (2 x 256 = 512
 // columns). Per SM and MMA the operands read from shared memory halve
 // against the 1-SM M = 128 x N = 128 tile (one A and one half-B K-slice for
-// twice the products), which is what capped that kernel's MMA stream.
+// twice the products).
 //   * TMA: both CTAs' loads complete on the even CTA's `full` / `afull`
 //     barriers (armed by the even CTA with both halves' bytes); a stage is
 //     refilled after the MMA commit arrives on that CTA's own `empty`
 //     (multicast to both CTAs).
 //   * The MMA commit also arrives on both CTAs' `tfull`; each CTA's 16
 //     epilogue warps (TMEM lane quadrant x 64-column quarter: one thread =
-//     one query, 64 columns per tile, the epilogue of the 1-SM kernel) then
-//     arrive on the even CTA's `tempty`.
-//   * Lists: one per (segment, column quarter, query).
+//     one query, 64 columns per tile, the epilogue of the 1-SM kernel) load
+//     their columns and at once arrive on the even CTA's `tempty`, then test
+//     and append.
+//   * Lists: one per (segment, column quarter, query); the pivot pass
+//     writes one minimum per (query, quarter, group of kPivotGroup tiles).
 // Every wait is bounded; both CTAs meet in a cluster barrier before TMEM
 // is released and before either exits.
 #ifndef KNN_P_BN
